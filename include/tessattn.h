@@ -1,0 +1,189 @@
+/* tessattn.h -- C ABI of libtessattn.so, the B200 (sm_100a) encoder-attention library.
+ *
+ * This library replaces the attention hot path of Tessery's native Metal runtime
+ * (src/metal_inference/native/runtime.mm, bound over ctypes in
+ * src/metal_inference/metal.py:27-91).  Every entry point below names the reference
+ * interface it stands in for.  Conventions shared by all entry points:
+ *
+ *   - Plain C types only: opaque handles, raw pointers, sizes.  No C++ or framework
+ *     types cross the boundary.
+ *   - Status codes (int): TX_OK (0), TX_EINVAL (1, rejected before any GPU work),
+ *     TX_ECUDA (2, CUDA runtime error), TX_ETIMEOUT (3, a bounded device-side wait gave
+ *     up; the kernel returned and the context stays usable).  tx_last_error() gives a
+ *     one-line, payload-free description for the calling context.
+ *     The reference returns 0/1 from every mi_* call (runtime.mm:81-297); 0 keeps the
+ *     same meaning and every failure is non-zero.
+ *   - The library never aborts the process and never frees caller memory.
+ *   - One context per device; calls on one context are serialised by a mutex, as the
+ *     reference serialises commands per runtime (metal.py:191, 375-414).
+ */
+#ifndef TESSATTN_H
+#define TESSATTN_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  TX_OK = 0,
+  TX_EINVAL = 1,
+  TX_ECUDA = 2,
+  TX_ETIMEOUT = 3
+};
+
+/* Element types of attention inputs/outputs. */
+enum { TX_F32 = 0, TX_BF16 = 1 };
+
+/* ABI version; bumped on any signature change.  The Python loader refuses a library
+ * whose version differs, as metal.py:84-90 refuses a stale native build. */
+uint32_t tx_abi_version(void);
+
+/* ---- lifecycle -------------------------------------------------------------------- */
+
+/* Replaces mi_create (runtime.mm:43-58).  Opens a context on CUDA device `device`
+ * (stream, events, status word).  Returns NULL when no usable sm_100 device exists;
+ * the reason is available from tx_last_error(NULL). */
+void *tx_create(int device);
+
+/* Replaces mi_destroy (runtime.mm:60-62).  Waits for queued work, frees every buffer
+ * and scratch allocation the context owns. */
+void tx_destroy(void *ctx);
+
+/* Payload-free description of the last failure on `ctx` (or of the last failed
+ * tx_create when ctx is NULL).  The string stays valid until the next call on ctx. */
+const char *tx_last_error(void *ctx);
+
+/* Number of streaming multiprocessors of the context's device. */
+int tx_device_sms(void *ctx);
+
+/* Name of the last attention kernel this context launched ("tc_bf16_d128",
+ * "simt", "d32_f32") or "" -- the route a call took, as the reference's tests read
+ * kernel names from MetalRuntime.diagnostics()["dispatches"] (metal.py:208-234). */
+const char *tx_last_kernel(void *ctx);
+
+/* Number of kernels this context has launched since it was created (every entry
+ * point counts its own launches), so callers can report launches per step. */
+uint64_t tx_launch_count(void *ctx);
+
+/* ---- device buffers --------------------------------------------------------------- */
+
+/* Replaces mi_buffer (runtime.mm:65-76).  Allocates `size` bytes of device memory,
+ * copying `host` into it when non-NULL, zero-filled otherwise.  NULL on failure
+ * (size 0 included, as in the reference). */
+void *tx_buffer(void *ctx, const void *host, uint64_t size);
+
+/* Replaces mi_free (runtime.mm:78-80). */
+void tx_free(void *buffer);
+
+/* Replaces mi_read (runtime.mm:81-86): synchronous device-to-host copy of the first
+ * `bytes` bytes.  Returns 1 when bytes exceeds the buffer size. */
+int tx_read(void *buffer, void *out, uint64_t bytes);
+
+/* Host-to-device copy into an existing buffer (the reference writes shared memory
+ * directly; CUDA needs an explicit copy).  Returns 1 when bytes exceeds the size. */
+int tx_write(void *buffer, const void *src, uint64_t bytes);
+
+/* Device address and size of a buffer, for the typed entry points below. */
+void *tx_buffer_device_ptr(void *buffer);
+uint64_t tx_buffer_size(void *buffer);
+
+/* Page-locked host memory for asynchronous copies (e2e measurement, staging). */
+void *tx_host_alloc(uint64_t size);
+void tx_host_free(void *ptr);
+
+/* ---- commands (one stream-ordered batch of dispatches) ---------------------------- */
+
+/* Replaces mi_begin (runtime.mm:88-107).  Returns 1 when a command is already open. */
+int tx_begin(void *ctx);
+
+/* Replaces mi_dispatch (runtime.mm:109-146).  `name` selects a kernel by the
+ * reference's kernel names ("rms_norm", "rope", "attention", "attention_tiled",
+ * "attention_tail_32", "attention_tail_128") plus this library's additions
+ * ("attention_d32", "qk_norm_rope").  `buffers` are tx_buffer handles in the
+ * reference's slot order, `params` is the reference's 64-byte Params block
+ * (kernels.metal:5-8, packed "<12I4f" by metal.py:596-614), and `threads`/`group`
+ * are the reference's Metal grid, from which the row/batch counts are derived exactly
+ * as the reference kernels derive them.  The CUDA grid is chosen by the library. */
+int tx_dispatch(void *ctx, const char *name, void **buffers, uint32_t count,
+                const void *params, uint32_t size, uint64_t threads, uint32_t group);
+
+/* Replaces mi_finish (runtime.mm:217-253): waits for the command, checks CUDA errors
+ * and the device status word, records the command's GPU time. */
+int tx_finish(void *ctx);
+
+/* Replaces mi_abort (runtime.mm:289-297).  CUDA cannot discard launched work, so
+ * abort waits for it, then drops the open command and its timing. */
+void tx_abort(void *ctx);
+
+/* Replaces mi_gpu_seconds (runtime.mm:285-287): device time of the last finished
+ * command (CUDA events), or -1 when unavailable. */
+double tx_gpu_seconds(void *ctx);
+
+/* Replace mi_profile_enable / mi_profile_read (runtime.mm:256-283): per-dispatch
+ * device timings (one CUDA event pair per dispatch) for the next commands. */
+int tx_profile_enable(void *ctx, int enabled);
+int tx_profile_read(void *ctx, double *seconds, uint32_t count);
+
+/* ---- typed attention entry points -------------------------------------------------
+
+ * These replace the Params-block route for callers that hold device pointers.  They
+ * implement the operator reached through MetalRuntime._attention (metal.py:532-569)
+ * and, when `q_norm_w`/`k_norm_w` are non-NULL, the q/k RMSNorm + RoPE calls that
+ * precede it in Qwen3Backend.forward (qwen3.py:216-237).
+ *
+ * Layouts (row-major, d contiguous):
+ *   padded: q/out [batch, seq, heads, dim], k/v [batch, seq, kv_heads, dim]
+ *   varlen: q/out [total, heads, dim],      k/v [total, kv_heads, dim],
+ *           sequence s spans rows cu_seqlens[s] .. cu_seqlens[s+1]-1.
+ * Semantics (kernels.metal:78-103): query row at position p of a sequence of length n
+ * attends to keys [0, causal ? min(p+1, n) : n); padded query rows (p >= n) are
+ * computed too and attend to [0, n); kv head = head / (heads / kv_heads).
+ * `scale` multiplies q.k (the reference passes dim^-0.5).
+ * in_dtype: TX_F32 or TX_BF16 for q, k, v.  out_dtype: TX_F32 or TX_BF16.
+ * q_norm_w / k_norm_w: bf16 bit patterns [dim] (kernels.metal:53-63 reads its weight
+ * as bf16); both NULL means no prologue.  eps/theta as in the reference Params.
+ * Positions for RoPE: the padded index (kernels.metal:68) or the index within the
+ * sequence (varlen).
+ * lengths / cu_seqlens: device arrays read by the kernels.  lengths_host /
+ * cu_seqlens_host: optional host copies; when given, they are validated and used to
+ * build an exact, longest-first work list; when NULL the work list covers every tile
+ * and the kernels skip empty tiles by reading the device array.
+ * stream: a cudaStream_t, or NULL for the context's stream.
+ * Returns TX_OK when the work has been queued; errors from inside kernels are reported
+ * by tx_sync / tx_finish. */
+int tx_attention_padded(void *ctx, const void *q, const void *k, const void *v,
+                        const uint32_t *lengths, const uint32_t *lengths_host, void *out,
+                        uint32_t batch, uint32_t seq, uint32_t heads, uint32_t kv_heads,
+                        uint32_t dim, int in_dtype, int out_dtype, int causal, float scale,
+                        const uint16_t *q_norm_w, const uint16_t *k_norm_w, float eps,
+                        float theta, void *stream);
+
+int tx_attention_varlen(void *ctx, const void *q, const void *k, const void *v,
+                        const int32_t *cu_seqlens, const int32_t *cu_seqlens_host,
+                        uint32_t nseq, uint32_t total, uint32_t max_len, void *out,
+                        uint32_t heads, uint32_t kv_heads, uint32_t dim, int in_dtype,
+                        int out_dtype, int causal, float scale, const uint16_t *q_norm_w,
+                        const uint16_t *k_norm_w, float eps, float theta, void *stream);
+
+/* Standalone fused q/k prologue (qwen3.py:216-237 as one pass): RMSNorm with bf16
+ * weights then split-half RoPE, reading q/k in `in_dtype` and writing bf16 or f32
+ * (`out_dtype`) to q_out/k_out (which may alias q/k when the types match).
+ * positions: padded layout when cu_seqlens is NULL (rows = batch*seq tokens,
+ * position = token % seq), else index within each varlen sequence. */
+int tx_qk_norm_rope(void *ctx, const void *q, const void *k, void *q_out, void *k_out,
+                    uint32_t tokens, uint32_t seq, const int32_t *cu_seqlens, uint32_t nseq,
+                    uint32_t heads, uint32_t kv_heads, uint32_t dim, int in_dtype,
+                    int out_dtype, const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                    float eps, float theta, void *stream);
+
+/* Waits for all work queued on `stream` (NULL: context stream) and reports kernel
+ * errors, including device-side wait timeouts, as a status code. */
+int tx_sync(void *ctx, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TESSATTN_H */

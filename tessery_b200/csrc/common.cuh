@@ -1,0 +1,67 @@
+// Shared device/host helpers for libtessattn (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tx {
+
+// Device status word values (written by kernels whose bounded waits give up).
+// Low byte: kind; bits 8..23: site id (which wait gave up), for the error message.
+enum : int {
+  kStatusOk = 0,
+  kStatusTimeout = 3,
+  kStatusBadArg = 1,
+};
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t bits) {
+  return __uint_as_float(uint32_t(bits) << 16);
+}
+
+// Round-to-nearest-even float -> bf16 bit pattern (NaN kept quiet).
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return uint16_t((u >> 16) | 0x40u);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return uint16_t(u >> 16);
+}
+
+// Two floats -> packed bf16x2 (lo in bits 0..15), round to nearest even.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static __device__ __forceinline__ float load(const float *p, size_t i) { return p[i]; }
+  static __device__ __forceinline__ void store(float *p, size_t i, float v) { p[i] = v; }
+};
+template <> struct Elem<uint16_t> {
+  static __device__ __forceinline__ float load(const uint16_t *p, size_t i) {
+    return bf16_bits_to_f32(p[i]);
+  }
+  static __device__ __forceinline__ void store(uint16_t *p, size_t i, float v) {
+    p[i] = f32_to_bf16_bits(v);
+  }
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Records the first failure in the context's status word.
+__device__ __forceinline__ void report_status(int *status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+}  // namespace tx

@@ -1,0 +1,62 @@
+// Host-side launch interface between the C ABI (runtime.cu) and the kernel files.
+// All launchers enqueue on `stream` and return cudaGetLastError() of the launch.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tx {
+
+// One attention problem, in element units.  Pointers are device addresses.
+struct AttnProblem {
+  const void *q, *k, *v;
+  void *out;
+  const uint32_t *lengths;   // padded layout: [batch] valid lengths (device)
+  const int32_t *cu_seqlens; // varlen layout: [nseq+1] offsets (device); NULL = padded
+  uint32_t batch;            // padded: batch; varlen: nseq
+  uint32_t seq;              // padded: L; varlen: max sequence length
+  uint32_t total;            // varlen: total rows; padded: batch*seq
+  uint32_t heads, kv_heads, dim;
+  int in_dtype, out_dtype;   // TX_F32 / TX_BF16
+  int causal;
+  float scale;
+};
+
+// Reference-semantics kernels (kernels.metal:53-103 restated for CUDA).
+cudaError_t launch_rms_norm(const float *x, const uint16_t *w, float *out, uint32_t rows,
+                            uint32_t cols, float eps, cudaStream_t stream);
+cudaError_t launch_rope(float *x, uint32_t n, uint32_t heads, uint32_t seq, uint32_t dim,
+                        float theta, cudaStream_t stream);
+// General attention: any dim <= 256, f32/bf16 in, f32/bf16 out, padded or varlen.
+cudaError_t launch_attention_simt(const AttnProblem &p, cudaStream_t stream);
+
+// Fused q/k RMSNorm + RoPE prologue.  Rows: tokens*heads (q) and tokens*kv_heads (k).
+struct PrologueProblem {
+  const void *q, *k;
+  void *q_out, *k_out;
+  uint32_t tokens, seq;       // padded: position = token % seq
+  const int32_t *cu_seqlens;  // varlen: position = token - cu_seqlens[seq_of(token)]
+  uint32_t nseq;
+  uint32_t heads, kv_heads, dim;
+  int in_dtype, out_dtype;
+  const uint16_t *q_w, *k_w;
+  float eps, theta;
+};
+cudaError_t launch_qk_norm_rope(const PrologueProblem &p, cudaStream_t stream);
+
+// Bandwidth-oriented fp32 kernel for head_dim 32 (BERT/BGE shapes).
+cudaError_t launch_attention_d32(const AttnProblem &p, cudaStream_t stream);
+
+// tcgen05/TMEM/TMA attention for head_dim 128 with bf16 q/k/v.
+// `units` is a device work list (see attn_tc.cu for the encoding), `status` the
+// context's device status word.
+bool tc_attention_supported(const AttnProblem &p);
+cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uint32_t n_units,
+                                int num_sms, int *status, cudaStream_t stream);
+// Host-side work-list construction for launch_attention_tc.
+// Fills `units` (capacity >= tc_max_units) and returns the count.
+uint32_t tc_max_units(const AttnProblem &p);
+uint32_t tc_build_units(const AttnProblem &p, const uint32_t *lengths_host,
+                        const int32_t *cu_host, uint32_t *units);
+
+}  // namespace tx

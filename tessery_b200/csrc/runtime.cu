@@ -1,0 +1,708 @@
+// C ABI of libtessattn.so: the CUDA counterpart of the reference's Objective-C++ Metal
+// runtime (src/metal_inference/native/runtime.mm) for the attention hot path.
+//
+// A context owns one CUDA stream on one device, a device status word written by
+// kernels whose bounded waits give up, and scratch memory (prologue outputs, the
+// tensor-core work list).  Commands (tx_begin .. tx_finish) bracket dispatches with CUDA
+// events the way mi_begin/mi_finish bracket a Metal command buffer.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "../../include/tessattn.h"
+#include "kernels.h"
+
+namespace {
+
+constexpr uint32_t kAbiVersion = 1;
+
+struct Ctx;
+
+struct Buf {
+  Ctx *ctx;
+  void *dev;
+  uint64_t size;
+};
+
+struct Ctx {
+  int device = 0;
+  int sms = 0;
+  cudaStream_t stream = nullptr;
+  std::recursive_mutex mu;
+  std::string err;
+  // command state
+  bool open = false;
+  cudaEvent_t ev_begin = nullptr, ev_end = nullptr;
+  double last_gpu = -1.0;
+  // per-dispatch profiling
+  bool profile = false;
+  std::vector<cudaEvent_t> prof_events;  // pairs
+  size_t prof_used = 0;
+  std::vector<double> prof_seconds;
+  // device status word
+  int *status = nullptr;
+  // scratch
+  void *qk_scratch = nullptr;
+  size_t qk_bytes = 0;
+  uint32_t *units = nullptr;
+  size_t units_cap = 0;
+  std::vector<uint32_t> units_host;
+  uint64_t units_key = 0;
+  uint32_t units_count = 0;
+  cudaEvent_t scratch_done = nullptr;  // last launch that read scratch
+  std::set<Buf *> buffers;
+  const char *last_kernel = "";
+  uint64_t launches = 0;  // kernels this context has launched
+};
+
+std::mutex g_create_mu;
+std::string g_create_err;
+
+int fail(Ctx *c, int code, const char *msg) {
+  if (c) c->err = msg;
+  return code;
+}
+
+int cuda_fail(Ctx *c, cudaError_t e, const char *what) {
+  if (c) {
+    c->err = std::string(what) + ": " + cudaGetErrorName(e);
+  }
+  return TX_ECUDA;
+}
+
+// Makes `stream` wait for the previous user of the context's scratch memory.
+cudaError_t scratch_acquire(Ctx *c, cudaStream_t stream) {
+  return cudaStreamWaitEvent(stream, c->scratch_done, 0);
+}
+cudaError_t scratch_release(Ctx *c, cudaStream_t stream) {
+  return cudaEventRecord(c->scratch_done, stream);
+}
+
+cudaError_t ensure_qk_scratch(Ctx *c, size_t bytes) {
+  if (c->qk_bytes >= bytes) return cudaSuccess;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return e;
+  if (c->qk_scratch) cudaFree(c->qk_scratch);
+  c->qk_scratch = nullptr;
+  c->qk_bytes = 0;
+  e = cudaMalloc(&c->qk_scratch, bytes);
+  if (e != cudaSuccess) return e;
+  c->qk_bytes = bytes;
+  return cudaSuccess;
+}
+
+cudaError_t ensure_units(Ctx *c, size_t count) {
+  if (c->units_cap >= count) return cudaSuccess;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return e;
+  if (c->units) cudaFree(c->units);
+  c->units = nullptr;
+  c->units_cap = 0;
+  c->units_key = 0;
+  e = cudaMalloc(&c->units, count * sizeof(uint32_t));
+  if (e != cudaSuccess) return e;
+  c->units_cap = count;
+  return cudaSuccess;
+}
+
+uint64_t fnv1a(uint64_t h, const void *data, size_t n) {
+  const uint8_t *p = (const uint8_t *)data;
+  for (size_t i = 0; i < n; ++i) { h ^= p[i]; h *= 1099511628211ull; }
+  return h;
+}
+
+// Reads and clears the device status word after the stream has drained.
+int check_status(Ctx *c) {
+  int st = 0;
+  cudaError_t e = cudaMemcpy(&st, c->status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(c, e, "status read");
+  if (st) {
+    int zero = 0;
+    cudaMemcpy(c->status, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    char msg[128];
+    if ((st & 0xff) == TX_ETIMEOUT) {
+      snprintf(msg, sizeof msg, "device wait timed out (site %d)", (st >> 8) & 0xffff);
+      return fail(c, TX_ETIMEOUT, msg);
+    }
+    snprintf(msg, sizeof msg, "device reported status %d", st);
+    return fail(c, TX_ECUDA, msg);
+  }
+  return TX_OK;
+}
+
+bool buf_ok(Buf *b, Ctx *c) { return b && b->ctx == c && c->buffers.count(b); }
+
+struct Params64 {
+  uint32_t n, rows, cols, k, heads, kv_heads, seq, batch, dim, group, u0, u1;
+  float eps, theta, scale, reserved;
+};
+static_assert(sizeof(Params64) == 64, "Params block is 64 bytes");
+
+// Core of the typed entry points (padded when cu == nullptr).
+int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
+                  const int32_t *cu_host, const uint16_t *q_w, const uint16_t *k_w, float eps,
+                  float theta, cudaStream_t stream) {
+  if (!p.q || !p.k || !p.v || !p.out) return fail(c, TX_EINVAL, "null tensor pointer");
+  if (p.cu_seqlens == nullptr && p.lengths == nullptr)
+    return fail(c, TX_EINVAL, "lengths or cu_seqlens required");
+  if (!p.heads || !p.kv_heads || p.heads % p.kv_heads)
+    return fail(c, TX_EINVAL, "heads must be a positive multiple of kv_heads");
+  if (!p.dim || p.dim > 256) return fail(c, TX_EINVAL, "head_dim must be in 1..256");
+  if (p.in_dtype != TX_F32 && p.in_dtype != TX_BF16) return fail(c, TX_EINVAL, "bad in_dtype");
+  if (p.out_dtype != TX_F32 && p.out_dtype != TX_BF16) return fail(c, TX_EINVAL, "bad out_dtype");
+  if (!std::isfinite(p.scale)) return fail(c, TX_EINVAL, "scale must be finite");
+  if ((q_w == nullptr) != (k_w == nullptr))
+    return fail(c, TX_EINVAL, "q_norm_w and k_norm_w are given together");
+  const bool prologue = q_w != nullptr;
+  if (prologue && !(p.dim == 32 || p.dim == 64 || p.dim == 128 || p.dim == 256))
+    return fail(c, TX_EINVAL, "prologue supports head_dim 32, 64, 128, 256");
+  if (prologue && !(eps >= 0.f && std::isfinite(eps) && std::isfinite(theta) && theta > 0.f))
+    return fail(c, TX_EINVAL, "bad eps/theta");
+  if (p.cu_seqlens) {
+    if (!p.batch) return fail(c, TX_EINVAL, "nseq must be positive");
+    if (cu_host) {
+      if (cu_host[0] != 0) return fail(c, TX_EINVAL, "cu_seqlens[0] must be 0");
+      for (uint32_t s = 0; s < p.batch; ++s) {
+        if (cu_host[s + 1] < cu_host[s]) return fail(c, TX_EINVAL, "cu_seqlens must not decrease");
+        if ((uint32_t)(cu_host[s + 1] - cu_host[s]) > p.seq)
+          return fail(c, TX_EINVAL, "sequence longer than max_len");
+      }
+      if ((uint32_t)cu_host[p.batch] != p.total) return fail(c, TX_EINVAL, "cu_seqlens[nseq] != total");
+    }
+  } else {
+    if (!p.batch || !p.seq) return fail(c, TX_EINVAL, "batch and seq must be positive");
+    if (lengths_host)
+      for (uint32_t b = 0; b < p.batch; ++b)
+        if (lengths_host[b] > p.seq) return fail(c, TX_EINVAL, "length exceeds seq");
+    p.total = p.batch * p.seq;
+  }
+  if (!p.total) return TX_OK;
+  if ((uint64_t)p.total * p.heads * p.dim >= (1ull << 40))
+    return fail(c, TX_EINVAL, "problem too large");
+
+  const bool tc_path = p.in_dtype == TX_BF16 && p.scale > 0.f && tx::tc_attention_supported(p);
+  const bool d32_path = !tc_path && p.in_dtype == TX_F32 && p.out_dtype == TX_F32 && p.dim == 32 &&
+                        p.batch <= 65535u && p.heads <= 65535u &&
+                        (uintptr_t)p.q % 16 == 0 && (uintptr_t)p.k % 16 == 0 &&
+                        (uintptr_t)p.v % 16 == 0 && (uintptr_t)p.out % 16 == 0;
+  cudaError_t e = cudaSetDevice(c->device);
+  if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
+  bool uses_scratch = prologue || tc_path;
+  if (uses_scratch && (e = scratch_acquire(c, stream)) != cudaSuccess)
+    return cuda_fail(c, e, "scratch wait");
+
+  if (prologue) {
+    // Normalised q/k go to scratch in the attention kernel's input type.
+    const int mid = p.in_dtype;
+    const size_t esz = mid == TX_BF16 ? 2 : 4;
+    const size_t qn = (size_t)p.total * p.heads * p.dim, kn = (size_t)p.total * p.kv_heads * p.dim;
+    if ((e = ensure_qk_scratch(c, (qn + kn) * esz + 256)) != cudaSuccess)
+      return cuda_fail(c, e, "scratch allocation");
+    void *qs = c->qk_scratch;
+    void *ks = (uint8_t *)c->qk_scratch + ((qn * esz + 255) & ~(size_t)255);
+    tx::PrologueProblem pp{};
+    pp.q = p.q; pp.k = p.k; pp.q_out = qs; pp.k_out = ks;
+    pp.tokens = p.total; pp.seq = p.cu_seqlens ? p.seq : p.seq;
+    pp.cu_seqlens = p.cu_seqlens; pp.nseq = p.batch;
+    pp.heads = p.heads; pp.kv_heads = p.kv_heads; pp.dim = p.dim;
+    pp.in_dtype = p.in_dtype; pp.out_dtype = mid;
+    pp.q_w = q_w; pp.k_w = k_w; pp.eps = eps; pp.theta = theta;
+    if ((e = tx::launch_qk_norm_rope(pp, stream)) != cudaSuccess)
+      return cuda_fail(c, e, "prologue launch");
+    ++c->launches;
+    p.q = qs;
+    p.k = ks;
+  }
+
+  if (tc_path) {
+    uint32_t cap = tx::tc_max_units(p);
+    uint64_t key = 1469598103934665603ull;
+    uint32_t hdr[8] = {p.batch, p.seq, p.heads, p.kv_heads, (uint32_t)p.causal,
+                       p.cu_seqlens ? 1u : 0u, lengths_host || cu_host ? 1u : 0u, p.total};
+    key = fnv1a(key, hdr, sizeof hdr);
+    if (lengths_host) key = fnv1a(key, lengths_host, sizeof(uint32_t) * p.batch);
+    if (cu_host) key = fnv1a(key, cu_host, sizeof(int32_t) * (p.batch + 1));
+    if (key != c->units_key) {
+      if ((e = ensure_units(c, cap)) != cudaSuccess) return cuda_fail(c, e, "work list allocation");
+      c->units_host.resize(cap);
+      c->units_count = tx::tc_build_units(p, lengths_host, cu_host, c->units_host.data());
+      // Pageable source: the call returns once the data is staged, so the host vector
+      // can be rebuilt by the next call.
+      if (c->units_count &&
+          (e = cudaMemcpyAsync(c->units, c->units_host.data(), c->units_count * sizeof(uint32_t),
+                               cudaMemcpyHostToDevice, stream)) != cudaSuccess)
+        return cuda_fail(c, e, "work list upload");
+      c->units_key = key;
+    }
+    if ((e = tx::launch_attention_tc(p, c->units, c->units_count, c->sms, c->status, stream)) !=
+        cudaSuccess)
+      return cuda_fail(c, e, "attention launch");
+    c->last_kernel = "tc_bf16_d128";
+    ++c->launches;
+  } else if (d32_path) {
+    if ((e = tx::launch_attention_d32(p, stream)) != cudaSuccess)
+      return cuda_fail(c, e, "attention launch");
+    c->last_kernel = "d32_f32";
+    ++c->launches;
+  } else {
+    if ((e = tx::launch_attention_simt(p, stream)) != cudaSuccess)
+      return cuda_fail(c, e, "attention launch");
+    c->last_kernel = "simt";
+    ++c->launches;
+  }
+  if (uses_scratch && (e = scratch_release(c, stream)) != cudaSuccess)
+    return cuda_fail(c, e, "scratch event");
+  return TX_OK;
+}
+
+// Profiling hooks around one dispatch of an open command.
+void prof_begin(Ctx *c) {
+  if (!c->profile) return;
+  if (c->prof_used + 2 > c->prof_events.size()) {
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    c->prof_events.push_back(a);
+    c->prof_events.push_back(b);
+  }
+  cudaEventRecord(c->prof_events[c->prof_used], c->stream);
+}
+void prof_end(Ctx *c) {
+  if (!c->profile) return;
+  cudaEventRecord(c->prof_events[c->prof_used + 1], c->stream);
+  c->prof_used += 2;
+}
+
+}  // namespace
+
+extern "C" {
+
+uint32_t tx_abi_version(void) { return kAbiVersion; }
+
+void *tx_create(int device) {
+  std::lock_guard<std::mutex> g(g_create_mu);
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) {
+    g_create_err = std::string("no CUDA device: ") + cudaGetErrorName(e);
+    return nullptr;
+  }
+  if (device < 0 || device >= count) {
+    g_create_err = "device index out of range";
+    return nullptr;
+  }
+  cudaDeviceProp prop;
+  if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) {
+    g_create_err = std::string("device query: ") + cudaGetErrorName(e);
+    return nullptr;
+  }
+  if (prop.major != 10) {
+    g_create_err = "device is not sm_100 (this library is built for sm_100a only)";
+    return nullptr;
+  }
+  if ((e = cudaSetDevice(device)) != cudaSuccess) {
+    g_create_err = std::string("cudaSetDevice: ") + cudaGetErrorName(e);
+    return nullptr;
+  }
+  Ctx *c = new Ctx();
+  c->device = device;
+  c->sms = prop.multiProcessorCount;
+  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreate(&c->ev_begin) != cudaSuccess || cudaEventCreate(&c->ev_end) != cudaSuccess ||
+      cudaEventCreateWithFlags(&c->scratch_done, cudaEventDisableTiming) != cudaSuccess ||
+      cudaMalloc(&c->status, sizeof(int)) != cudaSuccess ||
+      cudaMemset(c->status, 0, sizeof(int)) != cudaSuccess) {
+    g_create_err = "context resources";
+    tx_destroy(c);
+    return nullptr;
+  }
+  cudaEventRecord(c->scratch_done, c->stream);
+  cudaStreamSynchronize(c->stream);
+  return c;
+}
+
+void tx_destroy(void *ctx) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return;
+  {
+    std::lock_guard<std::recursive_mutex> g(c->mu);
+    cudaSetDevice(c->device);
+    cudaDeviceSynchronize();
+    for (Buf *b : c->buffers) {
+      cudaFree(b->dev);
+      delete b;
+    }
+    c->buffers.clear();
+    if (c->qk_scratch) cudaFree(c->qk_scratch);
+    if (c->units) cudaFree(c->units);
+    if (c->status) cudaFree(c->status);
+    for (cudaEvent_t ev : c->prof_events) cudaEventDestroy(ev);
+    if (c->ev_begin) cudaEventDestroy(c->ev_begin);
+    if (c->ev_end) cudaEventDestroy(c->ev_end);
+    if (c->scratch_done) cudaEventDestroy(c->scratch_done);
+    if (c->stream) cudaStreamDestroy(c->stream);
+  }
+  delete c;
+}
+
+const char *tx_last_error(void *ctx) {
+  if (!ctx) return g_create_err.c_str();
+  return ((Ctx *)ctx)->err.c_str();
+}
+
+int tx_device_sms(void *ctx) { return ctx ? ((Ctx *)ctx)->sms : 0; }
+
+const char *tx_last_kernel(void *ctx) { return ctx ? ((Ctx *)ctx)->last_kernel : ""; }
+
+uint64_t tx_launch_count(void *ctx) { return ctx ? ((Ctx *)ctx)->launches : 0; }
+
+void *tx_buffer(void *ctx, const void *host, uint64_t size) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c || !size || size > (1ull << 40)) {
+    if (c) c->err = "bad buffer size";
+    return nullptr;
+  }
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  cudaSetDevice(c->device);
+  void *d = nullptr;
+  cudaError_t e = cudaMalloc(&d, size);
+  if (e != cudaSuccess) {
+    cuda_fail(c, e, "cudaMalloc");
+    cudaGetLastError();
+    return nullptr;
+  }
+  e = host ? cudaMemcpy(d, host, size, cudaMemcpyHostToDevice) : cudaMemset(d, 0, size);
+  if (e != cudaSuccess) {
+    cuda_fail(c, e, "buffer init");
+    cudaFree(d);
+    return nullptr;
+  }
+  Buf *b = new Buf{c, d, size};
+  c->buffers.insert(b);
+  return b;
+}
+
+void tx_free(void *buffer) {
+  Buf *b = (Buf *)buffer;
+  if (!b) return;
+  Ctx *c = b->ctx;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!c->buffers.count(b)) return;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  cudaFree(b->dev);
+  c->buffers.erase(b);
+  delete b;
+}
+
+int tx_read(void *buffer, void *out, uint64_t bytes) {
+  Buf *b = (Buf *)buffer;
+  if (!b || !out) return TX_EINVAL;
+  Ctx *c = b->ctx;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!buf_ok(b, c)) return TX_EINVAL;
+  if (bytes > b->size) return fail(c, TX_EINVAL, "read beyond buffer");
+  cudaSetDevice(c->device);
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e == cudaSuccess) e = cudaMemcpy(out, b->dev, bytes, cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? TX_OK : cuda_fail(c, e, "read");
+}
+
+int tx_write(void *buffer, const void *src, uint64_t bytes) {
+  Buf *b = (Buf *)buffer;
+  if (!b || !src) return TX_EINVAL;
+  Ctx *c = b->ctx;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!buf_ok(b, c)) return TX_EINVAL;
+  if (bytes > b->size) return fail(c, TX_EINVAL, "write beyond buffer");
+  cudaSetDevice(c->device);
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e == cudaSuccess) e = cudaMemcpy(b->dev, src, bytes, cudaMemcpyHostToDevice);
+  return e == cudaSuccess ? TX_OK : cuda_fail(c, e, "write");
+}
+
+void *tx_buffer_device_ptr(void *buffer) { return buffer ? ((Buf *)buffer)->dev : nullptr; }
+uint64_t tx_buffer_size(void *buffer) { return buffer ? ((Buf *)buffer)->size : 0; }
+
+void *tx_host_alloc(uint64_t size) {
+  void *p = nullptr;
+  if (!size || cudaHostAlloc(&p, size, cudaHostAllocDefault) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return p;
+}
+
+void tx_host_free(void *ptr) {
+  if (ptr) cudaFreeHost(ptr);
+}
+
+int tx_begin(void *ctx) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (c->open) return fail(c, TX_EINVAL, "command already open");
+  cudaSetDevice(c->device);
+  c->prof_used = 0;
+  c->prof_seconds.clear();
+  cudaError_t e = cudaEventRecord(c->ev_begin, c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "begin");
+  c->open = true;
+  return TX_OK;
+}
+
+int tx_dispatch(void *ctx, const char *name, void **buffers, uint32_t count, const void *params,
+                uint32_t size, uint64_t threads, uint32_t group) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!c->open) return fail(c, TX_EINVAL, "no open command");
+  if (!name || !params || size != 64 || count > 8 || !threads || !group)
+    return fail(c, TX_EINVAL, "bad dispatch arguments");
+  Buf *b[8] = {};
+  for (uint32_t i = 0; i < count; ++i) {
+    b[i] = (Buf *)buffers[i];
+    if (!buf_ok(b[i], c)) return fail(c, TX_EINVAL, "foreign or freed buffer");
+  }
+  Params64 pr;
+  memcpy(&pr, params, 64);
+  cudaSetDevice(c->device);
+  cudaError_t e = cudaSuccess;
+  const std::string n(name);
+
+  if (n == "rms_norm") {
+    // threads = rows * group (one threadgroup per row, kernels.metal:53-56)
+    if (count != 3 || threads % group) return fail(c, TX_EINVAL, "rms_norm: bad arguments");
+    uint64_t rows = threads / group;
+    if (!pr.cols || rows * pr.cols * 4 > b[0]->size || rows * pr.cols * 4 > b[2]->size ||
+        (uint64_t)pr.cols * 2 > b[1]->size)
+      return fail(c, TX_EINVAL, "rms_norm: buffer too small");
+    prof_begin(c);
+    e = tx::launch_rms_norm((const float *)b[0]->dev, (const uint16_t *)b[1]->dev,
+                            (float *)b[2]->dev, (uint32_t)rows, pr.cols, pr.eps, c->stream);
+    if (e == cudaSuccess) ++c->launches;
+    prof_end(c);
+  } else if (n == "rope") {
+    // one thread per rotated pair, i < n (kernels.metal:65-67)
+    if (count != 1 || !pr.dim || pr.dim % 2 || !pr.heads || !pr.seq)
+      return fail(c, TX_EINVAL, "rope: bad arguments");
+    uint64_t rows = ((uint64_t)pr.n + pr.dim / 2 - 1) / (pr.dim / 2);
+    if (rows * pr.dim * 4 > b[0]->size) return fail(c, TX_EINVAL, "rope: buffer too small");
+    prof_begin(c);
+    e = tx::launch_rope((float *)b[0]->dev, pr.n, pr.heads, pr.seq, pr.dim, pr.theta, c->stream);
+    if (e == cudaSuccess) ++c->launches;
+    prof_end(c);
+  } else if (n == "attention" || n == "attention_tiled" || n == "attention_tail_32" ||
+             n == "attention_tail_128" || n == "attention_d32") {
+    if (count != 5) return fail(c, TX_EINVAL, "attention: five buffers expected");
+    if (!pr.heads || !pr.kv_heads || pr.heads % pr.kv_heads || !pr.dim || pr.dim > 256 || !pr.seq)
+      return fail(c, TX_EINVAL, "attention: bad shape");
+    // Token count from the reference grid (metal.py:543-569).
+    uint64_t tokens;
+    if (n == "attention" || n == "attention_d32") {
+      if (threads % ((uint64_t)pr.heads * 32)) return fail(c, TX_EINVAL, "attention: bad grid");
+      tokens = threads / 32 / pr.heads;
+    } else if (n == "attention_tiled") {
+      if (threads % ((uint64_t)pr.heads * 128)) return fail(c, TX_EINVAL, "attention: bad grid");
+      tokens = threads / 128 / pr.heads * 8;
+    } else {
+      uint64_t per = (uint64_t)pr.heads * 128 * ((pr.seq + 7) / 8);
+      if (threads % per) return fail(c, TX_EINVAL, "attention: bad grid");
+      tokens = threads / per * pr.seq;
+    }
+    if (!tokens || tokens % pr.seq) return fail(c, TX_EINVAL, "attention: tokens not a multiple of seq");
+    uint64_t batch = tokens / pr.seq;
+    uint64_t qbytes = tokens * pr.heads * pr.dim * 4, kbytes = tokens * pr.kv_heads * pr.dim * 4;
+    if (b[0]->size < qbytes || b[1]->size < kbytes || b[2]->size < kbytes ||
+        b[3]->size < batch * 4 || b[4]->size < qbytes)
+      return fail(c, TX_EINVAL, "attention: buffer too small");
+    tx::AttnProblem p{};
+    p.q = b[0]->dev; p.k = b[1]->dev; p.v = b[2]->dev; p.out = b[4]->dev;
+    p.lengths = (const uint32_t *)b[3]->dev;
+    p.batch = (uint32_t)batch; p.seq = pr.seq; p.total = (uint32_t)tokens;
+    p.heads = pr.heads; p.kv_heads = pr.kv_heads; p.dim = pr.dim;
+    p.in_dtype = TX_F32; p.out_dtype = TX_F32;
+    p.causal = pr.u0 ? 0 : 1;
+    p.scale = pr.scale;
+    prof_begin(c);
+    int rc = run_attention(c, p, nullptr, nullptr, nullptr, nullptr, 0.f, 0.f, c->stream);
+    prof_end(c);
+    if (rc) return rc;
+  } else if (n == "qk_norm_rope") {
+    // buffers: q, k (f32, in place), q_norm weight, k_norm weight (bf16); n = tokens
+    if (count != 4 || !pr.heads || !pr.kv_heads || !pr.seq)
+      return fail(c, TX_EINVAL, "qk_norm_rope: bad arguments");
+    if (!(pr.dim == 32 || pr.dim == 64 || pr.dim == 128 || pr.dim == 256))
+      return fail(c, TX_EINVAL, "qk_norm_rope: head_dim 32, 64, 128 or 256");
+    uint64_t qbytes = (uint64_t)pr.n * pr.heads * pr.dim * 4;
+    uint64_t kbytes = (uint64_t)pr.n * pr.kv_heads * pr.dim * 4;
+    if (b[0]->size < qbytes || b[1]->size < kbytes || b[2]->size < pr.dim * 2u ||
+        b[3]->size < pr.dim * 2u)
+      return fail(c, TX_EINVAL, "qk_norm_rope: buffer too small");
+    tx::PrologueProblem pp{};
+    pp.q = b[0]->dev; pp.k = b[1]->dev; pp.q_out = b[0]->dev; pp.k_out = b[1]->dev;
+    pp.tokens = pr.n; pp.seq = pr.seq; pp.heads = pr.heads; pp.kv_heads = pr.kv_heads;
+    pp.dim = pr.dim; pp.in_dtype = TX_F32; pp.out_dtype = TX_F32;
+    pp.q_w = (const uint16_t *)b[2]->dev; pp.k_w = (const uint16_t *)b[3]->dev;
+    pp.eps = pr.eps; pp.theta = pr.theta;
+    prof_begin(c);
+    e = tx::launch_qk_norm_rope(pp, c->stream);
+    if (e == cudaSuccess) ++c->launches;
+    prof_end(c);
+  } else {
+    return fail(c, TX_EINVAL, "unknown kernel name");
+  }
+  if (e != cudaSuccess) return cuda_fail(c, e, "launch");
+  return TX_OK;
+}
+
+int tx_finish(void *ctx) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!c->open) return fail(c, TX_EINVAL, "no open command");
+  cudaSetDevice(c->device);
+  c->open = false;
+  c->last_gpu = -1.0;
+  cudaError_t e = cudaEventRecord(c->ev_end, c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(c, e, "command");
+  int rc = check_status(c);
+  if (rc) return rc;
+  float ms = 0.f;
+  if (cudaEventElapsedTime(&ms, c->ev_begin, c->ev_end) == cudaSuccess) c->last_gpu = ms * 1e-3;
+  if (c->profile) {
+    for (size_t i = 0; i + 1 < c->prof_used; i += 2) {
+      float t = 0.f;
+      if (cudaEventElapsedTime(&t, c->prof_events[i], c->prof_events[i + 1]) != cudaSuccess) {
+        c->prof_seconds.clear();
+        return fail(c, TX_ECUDA, "profile timing");
+      }
+      c->prof_seconds.push_back(t * 1e-3);
+    }
+  }
+  return TX_OK;
+}
+
+void tx_abort(void *ctx) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  cudaGetLastError();
+  c->open = false;
+  c->prof_used = 0;
+}
+
+double tx_gpu_seconds(void *ctx) { return ctx ? ((Ctx *)ctx)->last_gpu : -1.0; }
+
+int tx_profile_enable(void *ctx, int enabled) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (c->open) return fail(c, TX_EINVAL, "command open");
+  c->profile = enabled != 0;
+  c->prof_used = 0;
+  c->prof_seconds.clear();
+  return TX_OK;
+}
+
+int tx_profile_read(void *ctx, double *seconds, uint32_t count) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (c->open || count != c->prof_seconds.size()) return fail(c, TX_EINVAL, "profile count");
+  if (count) memcpy(seconds, c->prof_seconds.data(), count * sizeof(double));
+  return TX_OK;
+}
+
+int tx_attention_padded(void *ctx, const void *q, const void *k, const void *v,
+                        const uint32_t *lengths, const uint32_t *lengths_host, void *out,
+                        uint32_t batch, uint32_t seq, uint32_t heads, uint32_t kv_heads,
+                        uint32_t dim, int in_dtype, int out_dtype, int causal, float scale,
+                        const uint16_t *q_norm_w, const uint16_t *k_norm_w, float eps,
+                        float theta, void *stream) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  tx::AttnProblem p{};
+  p.q = q; p.k = k; p.v = v; p.out = out; p.lengths = lengths; p.cu_seqlens = nullptr;
+  p.batch = batch; p.seq = seq; p.heads = heads; p.kv_heads = kv_heads; p.dim = dim;
+  p.in_dtype = in_dtype; p.out_dtype = out_dtype; p.causal = causal ? 1 : 0; p.scale = scale;
+  if (!lengths) return fail(c, TX_EINVAL, "lengths required");
+  if ((uint64_t)batch * seq > 0xffffffffull) return fail(c, TX_EINVAL, "too many tokens");
+  return run_attention(c, p, lengths_host, nullptr, q_norm_w, k_norm_w, eps, theta,
+                       stream ? (cudaStream_t)stream : c->stream);
+}
+
+int tx_attention_varlen(void *ctx, const void *q, const void *k, const void *v,
+                        const int32_t *cu_seqlens, const int32_t *cu_seqlens_host, uint32_t nseq,
+                        uint32_t total, uint32_t max_len, void *out, uint32_t heads,
+                        uint32_t kv_heads, uint32_t dim, int in_dtype, int out_dtype, int causal,
+                        float scale, const uint16_t *q_norm_w, const uint16_t *k_norm_w, float eps,
+                        float theta, void *stream) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!cu_seqlens) return fail(c, TX_EINVAL, "cu_seqlens required");
+  if (!max_len) return fail(c, TX_EINVAL, "max_len must be positive");
+  tx::AttnProblem p{};
+  p.q = q; p.k = k; p.v = v; p.out = out; p.lengths = nullptr; p.cu_seqlens = cu_seqlens;
+  p.batch = nseq; p.seq = max_len; p.total = total; p.heads = heads; p.kv_heads = kv_heads;
+  p.dim = dim; p.in_dtype = in_dtype; p.out_dtype = out_dtype; p.causal = causal ? 1 : 0;
+  p.scale = scale;
+  return run_attention(c, p, nullptr, cu_seqlens_host, q_norm_w, k_norm_w, eps, theta,
+                       stream ? (cudaStream_t)stream : c->stream);
+}
+
+int tx_qk_norm_rope(void *ctx, const void *q, const void *k, void *q_out, void *k_out,
+                    uint32_t tokens, uint32_t seq, const int32_t *cu_seqlens, uint32_t nseq,
+                    uint32_t heads, uint32_t kv_heads, uint32_t dim, int in_dtype, int out_dtype,
+                    const uint16_t *q_norm_w, const uint16_t *k_norm_w, float eps, float theta,
+                    void *stream) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!q || !k || !q_out || !k_out || !q_norm_w || !k_norm_w)
+    return fail(c, TX_EINVAL, "null pointer");
+  if (!(dim == 32 || dim == 64 || dim == 128 || dim == 256))
+    return fail(c, TX_EINVAL, "head_dim 32, 64, 128 or 256");
+  if (!heads || !kv_heads) return fail(c, TX_EINVAL, "heads must be positive");
+  if (!cu_seqlens && !seq) return fail(c, TX_EINVAL, "seq must be positive");
+  if (cu_seqlens && !nseq) return fail(c, TX_EINVAL, "nseq must be positive");
+  if ((in_dtype != TX_F32 && in_dtype != TX_BF16) || (out_dtype != TX_F32 && out_dtype != TX_BF16))
+    return fail(c, TX_EINVAL, "bad dtype");
+  if (in_dtype != out_dtype && (q == q_out || k == k_out))
+    return fail(c, TX_EINVAL, "in-place prologue needs equal dtypes");
+  tx::PrologueProblem pp{};
+  pp.q = q; pp.k = k; pp.q_out = q_out; pp.k_out = k_out; pp.tokens = tokens; pp.seq = seq;
+  pp.cu_seqlens = cu_seqlens; pp.nseq = nseq; pp.heads = heads; pp.kv_heads = kv_heads;
+  pp.dim = dim; pp.in_dtype = in_dtype; pp.out_dtype = out_dtype; pp.q_w = q_norm_w;
+  pp.k_w = k_norm_w; pp.eps = eps; pp.theta = theta;
+  cudaSetDevice(c->device);
+  cudaError_t e = tx::launch_qk_norm_rope(pp, stream ? (cudaStream_t)stream : c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "prologue launch");
+  ++c->launches;
+  return TX_OK;
+}
+
+int tx_sync(void *ctx, void *stream) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  cudaSetDevice(c->device);
+  cudaError_t e = cudaStreamSynchronize(stream ? (cudaStream_t)stream : c->stream);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(c, e, "sync");
+  return check_status(c);
+}
+
+}  // extern "C"

@@ -1,0 +1,54 @@
+"""Sequence sharding across the GPUs of one node.
+
+Attention never mixes sequences (kernels.metal:86-91 indexes every load by its own
+batch row), so a batch splits into independent shards with no collective on the data
+path.  Sequences are assigned longest-processing-time first: sorted by attention cost
+(n(n+1)/2 causal, n^2 bidirectional) and each placed on the least-loaded rank.
+"""
+
+from __future__ import annotations
+
+import heapq
+
+import numpy as np
+from numpy.typing import NDArray
+
+
+def sequence_cost(lengths: NDArray, causal: bool) -> NDArray[np.int64]:
+    n = np.asarray(lengths, dtype=np.int64)
+    return n * (n + 1) // 2 if causal else n * n
+
+
+def shard_sequences(lengths: NDArray, world: int, causal: bool = True) -> list[NDArray[np.int64]]:
+    """Returns, per rank, the (sorted) indices of the sequences it owns."""
+    if world < 1:
+        raise ValueError("world must be positive")
+    cost = sequence_cost(lengths, causal)
+    order = np.argsort(-cost, kind="stable")
+    heap = [(0, r) for r in range(world)]
+    owned: list[list[int]] = [[] for _ in range(world)]
+    for i in order:
+        load, r = heapq.heappop(heap)
+        owned[r].append(int(i))
+        heapq.heappush(heap, (load + int(cost[i]), r))
+    return [np.array(sorted(o), dtype=np.int64) for o in owned]
+
+
+def pack(lengths: NDArray) -> NDArray[np.int32]:
+    """cu_seqlens for sequences laid end to end."""
+    n = np.asarray(lengths, dtype=np.int64)
+    cu = np.zeros(n.size + 1, dtype=np.int64)
+    cu[1:] = np.cumsum(n)
+    if cu[-1] >= 2**31:
+        raise ValueError("too many tokens for int32 offsets")
+    return cu.astype(np.int32)
+
+
+def gather_shard(tensor: NDArray, cu_seqlens: NDArray, owned: NDArray) -> tuple[NDArray,
+                                                                                 NDArray]:
+    """Rows of the owned sequences of a packed tensor, and their cu_seqlens."""
+    cu = np.asarray(cu_seqlens, dtype=np.int64)
+    pieces = [tensor[cu[i]:cu[i + 1]] for i in owned]
+    lengths = np.array([cu[i + 1] - cu[i] for i in owned], dtype=np.int64)
+    rows = np.concatenate(pieces, axis=0) if pieces else tensor[:0]
+    return rows, pack(lengths)

@@ -1,0 +1,49 @@
+"""The CPU oracle against the golden vectors recorded from the reference's own tests."""
+
+import numpy as np
+import pytest
+
+import oracle
+from golden_cases import compare, inputs_match, load_cases, regenerate
+
+CASES = load_cases()
+
+
+def run_oracle(case, inputs):
+    d = case.dispatch
+    if case.kernel.startswith("attention"):
+        return oracle.attention_padded(inputs["q"], inputs["k"], inputs["v"], inputs["lengths"],
+                                       not d.get("bidirectional", 0), d["scale"])
+    if case.kernel == "rope":
+        x = inputs["x"].reshape(-1, d["heads"], d["dim"])
+        pos = np.arange(x.shape[0]) % d["seq"]
+        return oracle.rope(x, pos, d["theta"]).reshape(inputs["x"].shape)
+    if case.kernel == "rms_norm":
+        x = inputs["x"].reshape(-1, d["cols"])
+        return oracle.rms_norm(x, inputs["w"], d["eps"]).reshape(inputs["x"].shape)
+    if case.kernel == "pool_project":
+        return oracle.pool_project(inputs["x"], inputs["lengths"], d["dim"],
+                                   bool(d.get("first_token", 0)))
+    raise KeyError(case.kernel)
+
+
+def test_fixture_covers_reference_grids():
+    tests = {c.test for c in CASES}
+    assert "test_tiled_attention_ragged_f64" in tests
+    ragged = [c for c in CASES if c.test == "test_tiled_attention_ragged_f64"]
+    assert len(ragged) == 44  # 2 dims x 2 directions x 11 (seq, lengths) rows
+    extreme = [c for c in CASES if c.test.startswith("test_tiled_attention_extreme")]
+    assert len(extreme) == 24
+    assert all(c.oracle_max_abs <= c.atol + c.rtol * 1e10 for c in CASES)
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: c.id)
+def test_oracle_matches_reference_expectations(case):
+    inputs = regenerate(case)
+    assert inputs_match(case, inputs), "regenerated inputs differ from the reference run"
+    result = run_oracle(case, inputs)
+    assert tuple(result.shape) == case.shape
+    compare(case, result)
+    # Whole-array moments recorded from the reference's expected array.
+    np.testing.assert_allclose(np.sum(result, dtype=np.float64), case.sum, rtol=1e-9,
+                               atol=1e-6 * max(1.0, abs(case.sum)))
