@@ -143,7 +143,9 @@ int tx_profile_read(void *ctx, double *seconds, uint32_t count);
  * `scale` multiplies q.k (the reference passes dim^-0.5).
  * in_dtype: TX_F32 or TX_BF16 for q, k, v.  out_dtype: TX_F32 or TX_BF16.
  * q_norm_w / k_norm_w: bf16 bit patterns [dim] (kernels.metal:53-63 reads its weight
- * as bf16); both NULL means no prologue.  eps/theta as in the reference Params.
+ * as bf16); a non-NULL weight applies RMSNorm + RoPE to that input first (NULL: the
+ * input is used as given, e.g. k already normalised by tx_qk_norm_rope).  eps/theta as
+ * in the reference Params.
  * Positions for RoPE: the padded index (kernels.metal:68) or the index within the
  * sequence (varlen).
  * lengths / cu_seqlens: device arrays read by the kernels.  lengths_host /
@@ -169,14 +171,18 @@ int tx_attention_varlen(void *ctx, const void *q, const void *k, const void *v,
 
 /* Standalone fused q/k prologue (qwen3.py:216-237 as one pass): RMSNorm with bf16
  * weights then split-half RoPE, reading q/k in `in_dtype` and writing bf16 or f32
- * (`out_dtype`) to q_out/k_out (which may alias q/k when the types match).
+ * (`out_dtype`) to q_out/k_out (which may alias q/k when the types match).  q (with
+ * q_out, q_norm_w) or k (with k_out, k_norm_w) may be NULL to transform only the other.
  * positions: padded layout when cu_seqlens is NULL (rows = batch*seq tokens,
- * position = token % seq), else index within each varlen sequence. */
+ * position = token % seq), else index within each varlen sequence.
+ * lengths (device, padded layout, may be NULL): tokens at positions >= their
+ * sequence's length are skipped and their output rows left unwritten -- the rows no
+ * attention reads when the output is k. */
 int tx_qk_norm_rope(void *ctx, const void *q, const void *k, void *q_out, void *k_out,
                     uint32_t tokens, uint32_t seq, const int32_t *cu_seqlens, uint32_t nseq,
-                    uint32_t heads, uint32_t kv_heads, uint32_t dim, int in_dtype,
-                    int out_dtype, const uint16_t *q_norm_w, const uint16_t *k_norm_w,
-                    float eps, float theta, void *stream);
+                    const uint32_t *lengths, uint32_t heads, uint32_t kv_heads, uint32_t dim,
+                    int in_dtype, int out_dtype, const uint16_t *q_norm_w,
+                    const uint16_t *k_norm_w, float eps, float theta, void *stream);
 
 /* Waits for all work queued on `stream` (NULL: context stream) and reports kernel
  * errors, including device-side wait timeouts, as a status code. */

@@ -67,8 +67,9 @@ def attention(
 
     Padded: q [B, L, H, d], k/v [B, L, Hkv, d], lengths [B].
     Packed: q [T, H, d], k/v [T, Hkv, d], cu_seqlens [nseq+1] (int32, cu[0] = 0).
-    q_norm_weight/k_norm_weight: uint16 bf16 bits [d]; when given, q and k are RMSNorm'd
-    and rotated (RoPE, positions = padded index or index within the sequence) first.
+    q_norm_weight/k_norm_weight: uint16 bf16 bits [d]; when given, that input is
+    RMSNorm'd and rotated (RoPE, positions = padded index or index within the sequence)
+    first.
     Returns float32 (or uint16 bf16 bits when out_dtype == "bf16") in q's layout,
     written into `out` when given (e.g. a page-locked array from host.pinned_empty).
     """
@@ -80,11 +81,10 @@ def attention(
     out_code = {"float32": native.TX_F32, "bf16": native.TX_BF16}.get(out_dtype)
     if out_code is None:
         raise InvalidInputError()
-    if (q_norm_weight is None) != (k_norm_weight is None):
-        raise InvalidInputError()
     qw = kw = None
     if q_norm_weight is not None:
         qw = _upload(rt, "q_norm_weight", np.asarray(q_norm_weight, dtype=np.uint16))
+    if k_norm_weight is not None:
         kw = _upload(rt, "k_norm_weight", np.asarray(k_norm_weight, dtype=np.uint16))
     out_np_dtype = np.float32 if out_code == native.TX_F32 else np.uint16
     if (lengths is None) == (cu_seqlens is None):

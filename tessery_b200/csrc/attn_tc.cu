@@ -1,31 +1,34 @@
 // Blackwell (sm_100a) tensor-core attention for head_dim 128, bf16 q/k/v, fp32 softmax
 // and accumulation: the Qwen3 causal GQA operator of qwen3.py:238-245 dispatched by
 // MetalRuntime._attention (metal.py:532-569), with the semantics of kernels.metal:78-103
-// (and of its tiled/tail variants :108-298).
+// (and of its tiled/tail variants :108-298).  Optionally fused in front: the q RMSNorm +
+// RoPE of qwen3.py:216-237 (kernels.metal:53-74), applied to each Q tile in shared memory.
 //
 // Work unit: (sequence, pair of query heads sharing one kv head, 128-row query tile).
-// The two query heads of a pair share every K/V tile, so each K/V tile is fetched from
-// HBM/L2 once per pair (GQA head sharing).  A persistent grid of one CTA per SM walks a
-// host-built, longest-first list of units.
+// The two query heads of a pair share every K/V tile, so each K/V tile is fetched once
+// per pair (GQA head sharing).  A persistent grid of one CTA per SM walks a host-built,
+// longest-first list of units.
 //
 // Warp roles (320 threads, one CTA per SM):
-//   warps 0-3  softmax for head slot 0 (thread t owns query row t of the tile)
-//   warps 4-7  softmax for head slot 1
-//   warp 8     TMA producer: Q tiles once per unit, then K_j, V_j through a 3-slot ring
+//   warps 0-3  head slot 0: q prologue on the Q tile, softmax, epilogue (thread t = row t)
+//   warps 4-7  head slot 1
+//   warp 8     TMA producer: Q_h tiles (each as soon as its last QK of the previous unit
+//              has run), then K_j, V_j through a 3-slot ring
 //   warp 9     TMEM allocator and single-thread tcgen05.mma issuer
 // Tensor memory (512 columns x 128 lanes, fp32):
-//   [0,128) S for slot 0, [128,256) S for slot 1, [256,384) O slot 0, [384,512) O slot 1.
-// Shared memory: Q0, Q1, 3 K/V slots and P0, P1, each a 128x128 bf16 tile stored as two
-// 128-row x 128-byte atoms in the 128-byte-swizzled layout that TMA writes and the UMMA
-// descriptors read; barriers after them.
+//   [0,128) S slot 0, [128,256) S slot 1, [256,384) O slot 0, [384,512) O slot 1.
+// Shared memory: Q0, Q1, 3 K/V slots, P0, P1: 128x128 bf16 tiles, each two 128-row x
+// 128-byte atoms in the 128-byte-swizzled layout that TMA writes and UMMA reads.  After
+// the last P.V of a unit, P_h is the staging buffer of the output tile, which leaves by
+// TMA bulk-tensor stores.
 //
-// Per key tile j the issuer runs  S_h = Q_h K_j^T  (M=128, N=128, K=128, bf16 -> f32 in
-// TMEM), the softmax warps turn S_h into P_h = exp2(S_h*scale*log2e - m) (bf16, shared
-// memory) and the issuer accumulates O_h += P_h V_j in TMEM.  Tiles above the causal
+// Per key tile j the issuer runs S_h = Q_h K_j^T (M=128, N=128, K=128, bf16 -> f32 in
+// TMEM); the softmax warps turn S_h into P_h = exp2(S_h*scale*log2e - m) (bf16, shared
+// memory); the issuer accumulates O_h += P_h V_j in TMEM.  Tiles above the causal
 // diagonal and beyond each sequence's length are never visited; the diagonal and the
 // last tile are masked per row.  The running maximum is updated lazily: O is rescaled
-// only when a tile's maximum exceeds the reference maximum by more than 8 (log2 units),
-// which keeps every probability below 2^8 and gives the same normalised result.
+// only when a tile maximum exceeds the reference maximum by more than 8 (log2 units),
+// so every probability stays below 2^8 and the normalised result is unchanged.
 //
 // Every wait is bounded (about a second); a wait that gives up records
 // TX_ETIMEOUT | site<<8 in the context status word, raises a CTA-wide abort flag, and
@@ -49,33 +52,39 @@ constexpr uint32_t kTileBytes = 2 * kAtomBytes;
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffKV = kOffQ + 2 * kTileBytes;
 constexpr uint32_t kOffP = kOffKV + kStages * kTileBytes;
-constexpr uint32_t kOffBar = kOffP + 2 * kTileBytes;
-constexpr uint32_t kBarBytes = 256;
-constexpr uint32_t kSmemBytes = kOffBar + kBarBytes + 1024;  // + base alignment slack
+constexpr uint32_t kOffMisc = kOffP + 2 * kTileBytes;
+constexpr uint32_t kMiscBytes = 768;
+constexpr uint32_t kSmemBytes = kOffMisc + kMiscBytes + 1024;  // + base alignment slack
 constexpr int kThreads = 320;
 constexpr int kTmaWarp = 8, kMmaWarp = 9;
 constexpr long long kWaitCycles = 2000000000ll;  // ~1 s at B200 clocks
 constexpr float kRescaleThreshold = 8.0f;        // log2 units
+constexpr uint32_t kStageBytes = 4096;           // one 32-row x 128-byte output box
 
-// Barrier slots (uint64 each) inside the barrier area.
+// Barrier slots (uint64 each) at the start of the misc area.
 enum : uint32_t {
-  kBarQFull = 0, kBarQEmpty = 1,
-  kBarKVFull = 2,                   // + slot (3)
-  kBarKVEmpty = kBarKVFull + 3,     // + slot (3)
-  kBarSFull = kBarKVEmpty + 3,      // + head slot (2)
-  kBarPFull = kBarSFull + 2,        // + head slot (2)
-  kBarODone = kBarPFull + 2,        // + head slot (2)
+  kBarQFull = 0,                      // + head slot: Q_h landed (TMA transaction count)
+  kBarQReady = kBarQFull + 2,         // + head slot: Q_h transformed (128 arrivals)
+  kBarQEmpty = kBarQReady + 2,        // + head slot: last QK_h of the unit ran
+  kBarKVFull = kBarQEmpty + 2,        // + ring slot
+  kBarKVEmpty = kBarKVFull + kStages,
+  kBarSFull = kBarKVEmpty + kStages,  // + head slot
+  kBarPFull = kBarSFull + 2,          // + head slot (128 arrivals)
+  kBarODone = kBarPFull + 2,          // + head slot
   kBarDrain = kBarODone + 2,
   kNumBars = kBarDrain + 1
 };
-constexpr uint32_t kOffTmemSlot = kNumBars * 8;      // uint32 TMEM base address
-constexpr uint32_t kOffAbort = kOffTmemSlot + 4;     // int abort flag
-static_assert(kOffAbort + 4 <= kBarBytes, "barrier area overflow");
+constexpr uint32_t kOffTmemSlot = kNumBars * 8;   // uint32 TMEM base address
+constexpr uint32_t kOffAbort = kOffTmemSlot + 4;  // int abort flag
+constexpr uint32_t kOffQw = 256;                  // bf16 q-norm weight [128]
+constexpr uint32_t kOffInvFreq = 512;             // float inverse frequencies [64]
+static_assert(kOffAbort + 4 <= kOffQw, "misc area overflow");
+static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 // Wait sites, reported in the status word for diagnosis.
 enum : int {
-  kSiteQEmpty = 1, kSiteKVEmpty = 2, kSiteQFull = 3, kSiteKVFull = 4, kSitePFull = 5,
-  kSiteSFull = 6, kSiteODone = 7, kSiteDrain = 8
+  kSiteQEmpty = 1, kSiteKVEmpty = 2, kSiteQReady = 3, kSiteKVFull = 4, kSitePFull = 5,
+  kSiteSFull = 6, kSiteODone = 7, kSiteQFull = 8
 };
 
 // ---- unit encoding --------------------------------------------------------------------
@@ -91,11 +100,13 @@ struct Params {
   const uint32_t *lengths;  // padded
   const int32_t *cu;        // varlen (NULL for padded)
   void *out;
-  uint32_t seq;             // padded L (rows per sequence); varlen: unused
+  uint32_t seq;             // padded L (rows per sequence)
   uint32_t heads, group;    // query heads; heads per kv head
   int causal, out_bf16;
   float scale_log2;
   int *status;
+  const uint16_t *q_norm_w;  // fused q prologue when non-NULL
+  float eps, theta;
 };
 
 struct Unit {
@@ -173,6 +184,13 @@ __device__ __noinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile 
   }
 }
 
+// Bounded wait without a status report (drains after an abort).
+__device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity) {
+  long long t0 = clock64();
+  while (!mbar_test(bar, parity) && clock64() - t0 < kWaitCycles) {
+  }
+}
+
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar,
                                             int x, int y, int z) {
   asm volatile(
@@ -180,6 +198,24 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
       : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t src, int x, int y,
+                                             int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -193,6 +229,21 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1.
@@ -271,37 +322,144 @@ __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// 2^x on the special-function unit; results below 2^-126 flush to zero (probabilities that
+// small are negligible against a row sum of at least 1).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// sin and cos of a float angle: Cody-Waite reduction by 2*pi (2*pi split into a float
+// head and a float tail) to [-pi, pi], then the hardware approximations, which are
+// accurate to about 2^-21 absolute on that interval.
+__device__ __forceinline__ void sincos_reduced(float angle, float *s, float *c) {
+  const float k = rintf(angle * 0.159154943091895336f);
+  float r = fmaf(k, -6.28318548202514648f, angle);
+  r = fmaf(k, 1.74845553e-07f, r);
+  __sincosf(r, s, c);
+}
+
+// In-place q RMSNorm + RoPE of row `r` of a swizzled 128x128 bf16 tile (thread r owns
+// the row).  Arithmetic order follows kernels.metal:53-74: x * inv * w, then the
+// split-half rotation of (element c, element c + 64) by angle pos * inv_freq[c].
+__device__ __forceinline__ void q_prologue_row(uint32_t tile, uint32_t r, uint32_t pos,
+                                               const uint16_t *w, const float *inv_freq,
+                                               float eps) {
+  const uint32_t row = tile + r * 128;
+  const uint32_t sw = r & 7;
+  uint4 v[16];
+#pragma unroll
+  for (int c = 0; c < 16; ++c)
+    v[c] = ld_shared_v4(row + (c >> 3) * kAtomBytes + (((c & 7) ^ sw) << 4));
+  float ssq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    const uint32_t wv[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float lo = __uint_as_float(wv[e] << 16), hi = __uint_as_float(wv[e] & 0xffff0000u);
+      ssq[e] = fmaf(lo, lo, ssq[e]);
+      ssq[e] = fmaf(hi, hi, ssq[e]);
+    }
+  }
+  const float ss = (ssq[0] + ssq[1]) + (ssq[2] + ssq[3]);
+  const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
+  const float fpos = (float)pos;
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {  // chunk g (elements 8g..8g+7) pairs with chunk g + 8
+    const uint32_t a4[4] = {v[g].x, v[g].y, v[g].z, v[g].w};
+    const uint32_t b4[4] = {v[g + 8].x, v[g + 8].y, v[g + 8].z, v[g + 8].w};
+    uint32_t lo_out[4], hi_out[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float ra[2], rb[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = 8 * g + 2 * e + h;
+        const float xa = __uint_as_float(h ? (a4[e] & 0xffff0000u) : (a4[e] << 16));
+        const float xb = __uint_as_float(h ? (b4[e] & 0xffff0000u) : (b4[e] << 16));
+        const float a = xa * inv * bf16_bits_to_f32(w[c]);
+        const float b = xb * inv * bf16_bits_to_f32(w[c + 64]);
+        float s, co;
+        sincos_reduced(fpos * inv_freq[c], &s, &co);
+        ra[h] = a * co - b * s;
+        rb[h] = a * s + b * co;
+      }
+      lo_out[e] = pack_bf16x2(ra[0], ra[1]);
+      hi_out[e] = pack_bf16x2(rb[0], rb[1]);
+    }
+    st_shared_v4(row + (((uint32_t)g ^ sw) << 4), lo_out[0], lo_out[1], lo_out[2], lo_out[3]);
+    st_shared_v4(row + kAtomBytes + (((uint32_t)g ^ sw) << 4), hi_out[0], hi_out[1], hi_out[2],
+                 hi_out[3]);
+  }
+}
+
+// exp2(x*sl - m) of one 32-key chunk of a row (0 for keys at or past `valid`), rounded to
+// bf16 pairs and stored into the row's slots (`prow` = shared address of row r of the
+// swizzled K-major P tile).  Returns the chunk's probability sum.
+__device__ __forceinline__ float emit_p(const uint32_t (&x)[32], int c, int valid, float sl,
+                                        float m, uint32_t prow, uint32_t r) {
+  float sum[4] = {0.f, 0.f, 0.f, 0.f};
+  uint32_t packed[16];
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    const int k0 = c * 32 + 2 * t;
+    float p0 = k0 < valid ? ex2(fmaf(__uint_as_float(x[2 * t]), sl, -m)) : 0.f;
+    float p1 = k0 + 1 < valid ? ex2(fmaf(__uint_as_float(x[2 * t + 1]), sl, -m)) : 0.f;
+    sum[t & 3] += p0 + p1;
+    packed[t] = pack_bf16x2(p0, p1);
+  }
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint32_t c8 = c * 4 + g;  // 8-key group 0..15
+    st_shared_v4(prow + (c8 >> 3) * kAtomBytes + (((c8 & 7) ^ (r & 7)) << 4), packed[4 * g],
+                 packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+  }
+  return (sum[0] + sum[1]) + (sum[2] + sum[3]);
+}
+
 // ---- the kernel -----------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_k,
-                   const __grid_constant__ CUtensorMap tm_v, const Params p) {
+                   const __grid_constant__ CUtensorMap tm_v,
+                   const __grid_constant__ CUtensorMap tm_o, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles.
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const uint32_t sbase = smem_addr(smem);
-  const uint32_t bars = sbase + kOffBar;
-  uint32_t *tmem_slot = (uint32_t *)(smem + kOffBar + kOffTmemSlot);
-  volatile int *abort_flag = (volatile int *)(smem + kOffBar + kOffAbort);
+  const uint32_t bars = sbase + kOffMisc;
+  uint8_t *misc = smem + kOffMisc;
+  uint32_t *tmem_slot = (uint32_t *)(misc + kOffTmemSlot);
+  volatile int *abort_flag = (volatile int *)(misc + kOffAbort);
+  uint16_t *qw_s = (uint16_t *)(misc + kOffQw);
+  float *invf_s = (float *)(misc + kOffInvFreq);
   auto bar = [&](uint32_t i) { return bars + 8u * i; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(kBarQFull), 1);
-    mbar_init(bar(kBarQEmpty), 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(kBarKVFull + s), 1);
-      mbar_init(bar(kBarKVEmpty + s), 1);
-    }
     for (int h = 0; h < 2; ++h) {
+      mbar_init(bar(kBarQFull + h), 1);
+      mbar_init(bar(kBarQReady + h), 128);
+      mbar_init(bar(kBarQEmpty + h), 1);
       mbar_init(bar(kBarSFull + h), 1);
       mbar_init(bar(kBarPFull + h), 128);
       mbar_init(bar(kBarODone + h), 1);
     }
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(kBarKVFull + s), 1);
+      mbar_init(bar(kBarKVEmpty + s), 1);
+    }
     mbar_init(bar(kBarDrain), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (p.q_norm_w) {
+    for (int i = threadIdx.x; i < 128; i += kThreads) qw_s[i] = p.q_norm_w[i];
+    for (int i = threadIdx.x; i < 64; i += kThreads)
+      invf_s[i] = (float)pow((double)p.theta, -2.0 * (double)i / 128.0);
   }
   if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -314,6 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
+    prefetch_tmap(&tm_o);
   }
   tc_fence_before();
   __syncthreads();
@@ -324,20 +483,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       uint32_t loads = 0, units_done = 0;
-      uint32_t armed[kStages] = {0, 0, 0};   // fills per slot (for the abort drain)
+      uint32_t armed[kStages] = {0, 0, 0};  // fills per slot (for the abort drain)
       bool ok = true;
       for (uint32_t ui = blockIdx.x; ok && ui < p.n_units; ui += gridDim.x) {
         Unit u = decode(p, p.units[ui]);
         if (!u.nt) continue;
-        if (units_done > 0 &&
-            !(ok = wait_phase(bar(kBarQEmpty), (units_done - 1) & 1, abort_flag, p.status,
-                              kSiteQEmpty)))
-          break;
-        mbar_expect_tx(bar(kBarQFull), 2 * kTileBytes);
-        for (int h = 0; h < 2; ++h)
+        for (int h = 0; h < 2 && ok; ++h) {
+          if (units_done > 0 &&
+              !(ok = wait_phase(bar(kBarQEmpty + h), (units_done - 1) & 1, abort_flag,
+                                p.status, kSiteQEmpty)))
+            break;
+          mbar_expect_tx(bar(kBarQFull + h), kTileBytes);
           for (int a = 0; a < 2; ++a)
-            tma_load_3d(sbase + kOffQ + h * kTileBytes + a * kAtomBytes, &tm_q, bar(kBarQFull),
-                        a * 64, (int)(u.head0 + h), (int)(u.tok0 + u.q0));
+            tma_load_3d(sbase + kOffQ + h * kTileBytes + a * kAtomBytes, &tm_q,
+                        bar(kBarQFull + h), a * 64, (int)(u.head0 + h), (int)(u.tok0 + u.q0));
+        }
+        if (!ok) break;
         ++units_done;
         for (uint32_t j = 0; ok && j < u.nt; ++j) {
           for (int which = 0; which < 2; ++which) {  // 0: K_j, 1: V_j
@@ -357,21 +518,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) {
-        // Drain: every armed fill completes by itself; wait for the latest of each slot
-        // and for the last Q fill so no copy lands in freed shared memory.
+        // Every armed fill completes by itself: wait for the latest of each slot and for
+        // the Q fills so that no copy lands in shared memory after the CTA exits.
         for (int s = 0; s < kStages; ++s)
-          if (armed[s]) {
-            long long t0 = clock64();
-            while (!mbar_test(bar(kBarKVFull + s), (armed[s] - 1) & 1) &&
-                   clock64() - t0 < kWaitCycles) {
-            }
-          }
-        if (units_done) {
-          long long t0 = clock64();
-          while (!mbar_test(bar(kBarQFull), (units_done - 1) & 1) &&
-                 clock64() - t0 < kWaitCycles) {
-          }
-        }
+          if (armed[s]) drain_phase(bar(kBarKVFull + s), (armed[s] - 1) & 1);
+        for (int h = 0; h < 2; ++h)
+          if (units_done) drain_phase(bar(kBarQFull + h), (units_done - 1) & 1);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -388,24 +540,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (uint32_t ui = blockIdx.x; ok && ui < p.n_units; ui += gridDim.x) {
         Unit u = decode(p, p.units[ui]);
         if (!u.nt) continue;
-        if (!(ok = wait_phase(bar(kBarQFull), units_done & 1, abort_flag, p.status,
-                              kSiteQFull)))
-          break;
-        ++units_done;
-        // K_0
+        // K_0 and both Q tiles, then S_h = Q_h K_0^T.
         uint32_t slotK = loads % kStages;
         if (!(ok = wait_phase(bar(kBarKVFull + slotK), (loads / kStages) & 1, abort_flag,
                               p.status, kSiteKVFull)))
           break;
         ++loads;
-        tc_fence_after();
-        for (int h = 0; h < 2; ++h) {
-          uint32_t kt = sbase + kOffKV + slotK * kTileBytes;
+        const uint32_t kt0 = sbase + kOffKV + slotK * kTileBytes;
+        for (int h = 0; h < 2 && ok; ++h) {
+          if (!(ok = wait_phase(bar(kBarQReady + h), units_done & 1, abort_flag, p.status,
+                                kSiteQReady)))
+            break;
+          tc_fence_after();
           for (int ks = 0; ks < 8; ++ks)
-            umma(tS[h], kmajor_desc(q_tile[h], ks), kmajor_desc(kt, ks), kIdescQK, ks > 0);
+            umma(tS[h], kmajor_desc(q_tile[h], ks), kmajor_desc(kt0, ks), kIdescQK, ks > 0);
           umma_commit(bar(kBarSFull + h));
+          if (u.nt == 1) umma_commit(bar(kBarQEmpty + h));
           issued = true;
         }
+        if (!ok) break;
+        ++units_done;
         umma_commit(bar(kBarKVEmpty + slotK));
         for (uint32_t j = 0; ok && j < u.nt; ++j) {
           uint32_t slotV = loads % kStages;
@@ -439,32 +593,33 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int ks = 0; ks < 8; ++ks)
                 umma(tS[h], kmajor_desc(q_tile[h], ks), kmajor_desc(kt, ks), kIdescQK, ks > 0);
               umma_commit(bar(kBarSFull + h));
+              if (j + 2 == u.nt) umma_commit(bar(kBarQEmpty + h));  // last QK_h of the unit
             }
           }
           if (!ok) break;
           if (more) umma_commit(bar(kBarKVEmpty + slotN));
           umma_commit(bar(kBarKVEmpty + slotV));
         }
-        if (ok) umma_commit(bar(kBarQEmpty));
       }
       if (issued) {
         // Wait until every MMA this thread issued has completed (normal exit and abort).
         umma_commit(bar(kBarDrain));
-        long long t0 = clock64();
-        while (!mbar_test(bar(kBarDrain), 0) && clock64() - t0 < kWaitCycles) {
-        }
+        drain_phase(bar(kBarDrain), 0);
       }
     }
     __syncwarp();
   } else {
-    // ---------------- softmax warpgroups ----------------
+    // ---------------- q prologue, softmax and epilogue (one warpgroup per head slot) ----
     const int hs = warp >> 2;                   // head slot
-    const uint32_t r = (warp & 3) * 32 + lane;  // tile row == TMEM lane
-    const uint32_t lane_base = ((uint32_t)(warp & 3) * 32u) << 16;
+    const uint32_t wq = (uint32_t)(warp & 3);   // warp within the warpgroup
+    const uint32_t r = wq * 32 + lane;          // tile row == TMEM lane
+    const uint32_t lane_base = (wq * 32u) << 16;
     const uint32_t tS = tmem + lane_base + hs * 128;
     const uint32_t tO = tmem + lane_base + 256 + hs * 128;
-    uint8_t *ptile = smem + kOffP + hs * kTileBytes;
-    uint32_t scount = 0, ocount = 0;
+    const uint32_t prow = sbase + kOffP + hs * kTileBytes + r * 128;  // row r of P_h
+    const uint32_t qtile = sbase + kOffQ + hs * kTileBytes;
+    const uint32_t stage = sbase + kOffP + hs * kTileBytes + wq * 2 * kStageBytes;
+    uint32_t qcount = 0, scount = 0, ocount = 0;
     bool ok = true;
     for (uint32_t ui = blockIdx.x; ui < p.n_units; ui += gridDim.x) {
       Unit u = decode(p, p.units[ui]);
@@ -487,6 +642,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
       if (!ok) break;
+      // Q tile: wait for the copy, apply the q prologue in place, hand it to the issuer.
+      ok = __all_sync(0xffffffffu, wait_phase(bar(kBarQFull + hs), qcount & 1, abort_flag,
+                                              p.status, kSiteQFull));
+      if (!ok) break;
+      ++qcount;
+      if (p.q_norm_w) {
+        q_prologue_row(qtile, r, qpos, qw_s, invf_s, p.eps);
+        fence_proxy_async();
+      }
+      mbar_arrive(bar(kBarQReady + hs));
+
       const uint32_t end = p.causal ? min(qpos + 1, u.n) : u.n;
       float m_ref = -INFINITY, l = 0.f;
       for (uint32_t j = 0; j < u.nt; ++j) {
@@ -496,109 +662,160 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++scount;
         tc_fence_after();
         const int valid = (int)min(max((int)end - (int)(j * kTile), 0), kTile);
-        // Pass 1: row maximum over the valid keys.
-        float mx = -INFINITY;
-        for (int c = 0; c < 4; ++c) {
-          uint32_t x[32];
-          tmem_ld32(tS + c * 32, x);
-          tmem_ld_wait();
+        // Row maximum over the valid keys: chunks 0-1, then 2-3 (kept for the exp pass).
+        uint32_t xa[32], xb[32];
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        tmem_ld32(tS + 0, xa);
+        tmem_ld32(tS + 32, xb);
+        tmem_ld_wait();
 #pragma unroll
-          for (int t = 0; t < 32; ++t)
-            if (c * 32 + t < valid) mx = fmaxf(mx, __uint_as_float(x[t]));
+        for (int t = 0; t < 32; ++t) {
+          if (t < valid) mq[t & 1] = fmaxf(mq[t & 1], __uint_as_float(xa[t]));
+          if (32 + t < valid) mq[2 + (t & 1)] = fmaxf(mq[2 + (t & 1)], __uint_as_float(xb[t]));
         }
+        uint32_t xc[32], xd[32];
+        tmem_ld32(tS + 64, xc);
+        tmem_ld32(tS + 96, xd);
+        tmem_ld_wait();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          if (64 + t < valid) mq[t & 1] = fmaxf(mq[t & 1], __uint_as_float(xc[t]));
+          if (96 + t < valid) mq[2 + (t & 1)] = fmaxf(mq[2 + (t & 1)], __uint_as_float(xd[t]));
+        }
+        const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
         const float mt = mx * p.scale_log2;
         if (j > 0) {
-          // P(j-1).V(j-1) must be complete before P and O are touched.
-          ok = __all_sync(0xffffffffu, wait_phase(bar(kBarODone + hs), ocount & 1, abort_flag,
-                                                  p.status, kSiteODone));
-          if (!ok) break;
+          // P(j-1).V(j-1), which reads P and accumulates into O, has completed: the issuer
+          // committed s_full(j) after it, and a commit tracks every earlier tcgen05 op of
+          // the issuing thread.  Its o_done phase is therefore complete; count it.
           ++ocount;
-          tc_fence_after();
           // Rescale decision is per row; TMEM access is warp-wide (.sync.aligned), so
           // the warp rescales when any of its rows needs it (others scale by 1).
           float corr = 1.0f;
           const bool need = mt > m_ref + kRescaleThreshold;
           if (need) {
-            corr = exp2f(m_ref - mt);
+            corr = ex2(m_ref - mt);
             l *= corr;
             m_ref = mt;
           }
           if (__any_sync(0xffffffffu, need)) {
             for (int c = 0; c < 4; ++c) {
-              uint32_t x[32];
-              tmem_ld32(tO + c * 32, x);
+              uint32_t o[32];
+              tmem_ld32(tO + c * 32, o);
               tmem_ld_wait();
 #pragma unroll
-              for (int t = 0; t < 32; ++t) x[t] = __float_as_uint(__uint_as_float(x[t]) * corr);
-              tmem_st32(tO + c * 32, x);
+              for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * corr);
+              tmem_st32(tO + c * 32, o);
             }
             tmem_st_wait();
           }
         } else {
           m_ref = mt;
         }
-        // Pass 2: probabilities -> bf16 -> P tile (128-byte swizzle, K-major).
-        for (int c = 0; c < 4; ++c) {
-          uint32_t x[32];
-          tmem_ld32(tS + c * 32, x);
-          tmem_ld_wait();
-          uint32_t packed[16];
-#pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            const int k0 = c * 32 + 2 * t;
-            float p0 = k0 < valid ? exp2f(__uint_as_float(x[2 * t]) * p.scale_log2 - m_ref) : 0.f;
-            float p1 =
-                k0 + 1 < valid ? exp2f(__uint_as_float(x[2 * t + 1]) * p.scale_log2 - m_ref) : 0.f;
-            l += p0 + p1;
-            packed[t] = pack_bf16x2(p0, p1);
-          }
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const uint32_t c8 = c * 4 + g;  // 8-key group 0..15
-            const uint32_t off = (c8 >> 3) * kAtomBytes + r * 128 + (((c8 & 7) ^ (r & 7)) << 4);
-            *(uint4 *)(ptile + off) =
-                make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
-          }
-        }
+        // Probabilities -> bf16 -> P tile: chunks 2-3 from registers while chunks 0-1 are
+        // loaded again from TMEM.
+        tmem_ld32(tS + 0, xa);
+        l += emit_p(xc, 2, valid, p.scale_log2, m_ref, prow, r);
+        tmem_ld32(tS + 32, xb);
+        l += emit_p(xd, 3, valid, p.scale_log2, m_ref, prow, r);
+        tmem_ld_wait();
+        l += emit_p(xa, 0, valid, p.scale_log2, m_ref, prow, r);
+        l += emit_p(xb, 1, valid, p.scale_log2, m_ref, prow, r);
         fence_proxy_async();
         tc_fence_before();
         mbar_arrive(bar(kBarPFull + hs));
       }
       if (!ok) break;
-      // Epilogue: wait for the last P.V, normalise, store.
+      // Epilogue: wait for the last P.V, normalise, store.  Warps whose 32 rows are all
+      // inside the sequence stage their rows (swizzled, in the now free P tile) and send
+      // them with TMA bulk-tensor stores; a warp at a ragged end stores row by row.
       ok = __all_sync(0xffffffffu, wait_phase(bar(kBarODone + hs), ocount & 1, abort_flag,
                                               p.status, kSiteODone));
       if (!ok) break;
       ++ocount;
       tc_fence_after();
       const float inv = 1.0f / l;
-      for (int c = 0; c < 4; ++c) {
-        uint32_t x[32];
-        tmem_ld32(tO + c * 32, x);
-        tmem_ld_wait();
-        if (!store) continue;
-        if (p.out_bf16) {
-          uint4 *o = (uint4 *)((uint16_t *)p.out + orow + c * 32);
+      const uint32_t wrow0 = u.q0 + wq * 32;
+      const bool bulk = wrow0 + 32 <= u.rows;
+      const uint32_t srow = stage + (uint32_t)lane * 128;
+      const uint32_t sw = (uint32_t)lane & 7;
+      if (!p.out_bf16) {
+        uint32_t ob[2][32];
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint32_t w[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              w[e] = pack_bf16x2(__uint_as_float(x[8 * g + 2 * e]) * inv,
-                                 __uint_as_float(x[8 * g + 2 * e + 1]) * inv);
-            o[g] = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int c = 0; c < 4; ++c) {
+          if ((c & 1) == 0) {  // two 32-column chunks per TMEM round trip
+            tmem_ld32(tO + c * 32, ob[0]);
+            tmem_ld32(tO + c * 32 + 32, ob[1]);
+            tmem_ld_wait();
           }
-        } else {
-          float4 *o = (float4 *)((float *)p.out + orow + c * 32);
+          uint32_t (&x)[32] = ob[c & 1];
 #pragma unroll
-          for (int g = 0; g < 8; ++g)
-            o[g] = make_float4(__uint_as_float(x[4 * g]) * inv, __uint_as_float(x[4 * g + 1]) * inv,
-                               __uint_as_float(x[4 * g + 2]) * inv,
-                               __uint_as_float(x[4 * g + 3]) * inv);
+          for (int t = 0; t < 32; ++t) x[t] = __float_as_uint(__uint_as_float(x[t]) * inv);
+          if (bulk) {
+            const uint32_t buf = (uint32_t)(c & 1) * kStageBytes;
+            if (c >= 2) {
+              if (lane == 0) bulk_wait_read<1>();
+              __syncwarp();
+            }
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+              st_shared_v4(srow + buf + (((uint32_t)g ^ sw) << 4), x[4 * g], x[4 * g + 1],
+                           x[4 * g + 2], x[4 * g + 3]);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&tm_o, stage + buf, c * 32, (int)head, (int)(u.tok0 + wrow0));
+              bulk_commit();
+            }
+          } else if (store) {
+            float4 *o = (float4 *)((float *)p.out + orow + c * 32);
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+              o[g] = make_float4(__uint_as_float(x[4 * g]), __uint_as_float(x[4 * g + 1]),
+                                 __uint_as_float(x[4 * g + 2]), __uint_as_float(x[4 * g + 3]));
+          }
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t w[32];
+          uint32_t xa[32], xb[32];
+          tmem_ld32(tO + c * 64, xa);
+          tmem_ld32(tO + c * 64 + 32, xb);
+          tmem_ld_wait();
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            w[t] = pack_bf16x2(__uint_as_float(xa[2 * t]) * inv, __uint_as_float(xa[2 * t + 1]) * inv);
+            w[16 + t] =
+                pack_bf16x2(__uint_as_float(xb[2 * t]) * inv, __uint_as_float(xb[2 * t + 1]) * inv);
+          }
+          if (bulk) {
+            const uint32_t buf = (uint32_t)c * kStageBytes;
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+              st_shared_v4(srow + buf + (((uint32_t)g ^ sw) << 4), w[4 * g], w[4 * g + 1],
+                           w[4 * g + 2], w[4 * g + 3]);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&tm_o, stage + buf, c * 64, (int)head, (int)(u.tok0 + wrow0));
+              bulk_commit();
+            }
+          } else if (store) {
+            uint4 *o = (uint4 *)((uint16_t *)p.out + orow + c * 64);
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+              o[g] = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+          }
         }
       }
+      // The staging area is the P tile of the next unit: its reads must be done.
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
       tc_fence_before();
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -695,17 +912,20 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 3-D map over a [rows, heads, 128] bf16 tensor; box = 128 rows x 1 head x 64 columns,
-// 128-byte swizzle, zero fill beyond the last row.
-bool make_map(CUtensorMap *map, const void *base, uint32_t rows, uint32_t heads) {
+// 3-D map over a [rows, heads, 128] tensor; a box is box_rows rows x 1 head x 128 bytes
+// of elements, in the 128-byte swizzle.
+bool make_map(CUtensorMap *map, const void *base, uint32_t rows, uint32_t heads, bool f32,
+              uint32_t box_rows) {
   auto fn = encode_fn();
   if (!fn) return false;
+  const cuuint64_t esz = f32 ? 4 : 2;
   cuuint64_t dims[3] = {128, heads, rows};
-  cuuint64_t strides[2] = {128 * 2, (cuuint64_t)heads * 128 * 2};
-  cuuint32_t box[3] = {64, 1, 128};
+  cuuint64_t strides[2] = {128 * esz, (cuuint64_t)heads * 128 * esz};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / esz), 1, box_rows};
   cuuint32_t elem[3] = {1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims,
-                  strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                  const_cast<void *>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -713,12 +933,15 @@ bool make_map(CUtensorMap *map, const void *base, uint32_t rows, uint32_t heads)
 }  // namespace
 
 cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uint32_t n_units,
-                                int num_sms, int *status, cudaStream_t stream) {
+                                int num_sms, int *status, const uint16_t *q_norm_w, float eps,
+                                float theta, cudaStream_t stream) {
   if (!n_units) return cudaSuccess;
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   const uint32_t rows = p.total;
-  if (!make_map(&mq, p.q, rows, p.heads) || !make_map(&mk, p.k, rows, p.kv_heads) ||
-      !make_map(&mv, p.v, rows, p.kv_heads))
+  if (!make_map(&mq, p.q, rows, p.heads, false, 128) ||
+      !make_map(&mk, p.k, rows, p.kv_heads, false, 128) ||
+      !make_map(&mv, p.v, rows, p.kv_heads, false, 128) ||
+      !make_map(&mo, p.out, rows, p.heads, p.out_dtype == 0, 32))
     return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(tc::attn_tc_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -737,8 +960,11 @@ cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uin
   prm.out_bf16 = p.out_dtype == 1;
   prm.scale_log2 = p.scale * 1.4426950408889634f;
   prm.status = status;
+  prm.q_norm_w = q_norm_w;
+  prm.eps = eps;
+  prm.theta = theta;
   uint32_t grid = std::min<uint32_t>(n_units, (uint32_t)num_sms);
-  tc::attn_tc_kernel<<<grid, tc::kThreads, tc::kSmemBytes, stream>>>(mq, mk, mv, prm);
+  tc::attn_tc_kernel<<<grid, tc::kThreads, tc::kSmemBytes, stream>>>(mq, mk, mv, mo, prm);
   return cudaGetLastError();
 }
 

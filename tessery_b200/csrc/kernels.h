@@ -31,6 +31,9 @@ cudaError_t launch_rope(float *x, uint32_t n, uint32_t heads, uint32_t seq, uint
 cudaError_t launch_attention_simt(const AttnProblem &p, cudaStream_t stream);
 
 // Fused q/k RMSNorm + RoPE prologue.  Rows: tokens*heads (q) and tokens*kv_heads (k).
+// q or k may be NULL to transform only the other one.  With `lengths` (padded layout),
+// tokens at positions >= their sequence's length are skipped (their rows are left
+// untouched): used for k, whose padded rows no attention reads.
 struct PrologueProblem {
   const void *q, *k;
   void *q_out, *k_out;
@@ -41,6 +44,7 @@ struct PrologueProblem {
   int in_dtype, out_dtype;
   const uint16_t *q_w, *k_w;
   float eps, theta;
+  const uint32_t *lengths;    // optional, padded layout only
 };
 cudaError_t launch_qk_norm_rope(const PrologueProblem &p, cudaStream_t stream);
 
@@ -51,8 +55,11 @@ cudaError_t launch_attention_d32(const AttnProblem &p, cudaStream_t stream);
 // `units` is a device work list (see attn_tc.cu for the encoding), `status` the
 // context's device status word.
 bool tc_attention_supported(const AttnProblem &p);
+// q_norm_w: bf16 q RMSNorm weight [128] applied with RoPE to each Q tile in the kernel
+// (NULL: q is used as given).
 cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uint32_t n_units,
-                                int num_sms, int *status, cudaStream_t stream);
+                                int num_sms, int *status, const uint16_t *q_norm_w, float eps,
+                                float theta, cudaStream_t stream);
 // Host-side work-list construction for launch_attention_tc.
 // Fills `units` (capacity >= tc_max_units) and returns the count.
 uint32_t tc_max_units(const AttnProblem &p);

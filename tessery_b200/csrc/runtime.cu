@@ -20,7 +20,7 @@
 
 namespace {
 
-constexpr uint32_t kAbiVersion = 1;
+constexpr uint32_t kAbiVersion = 2;
 
 struct Ctx;
 
@@ -157,9 +157,7 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
   if (p.in_dtype != TX_F32 && p.in_dtype != TX_BF16) return fail(c, TX_EINVAL, "bad in_dtype");
   if (p.out_dtype != TX_F32 && p.out_dtype != TX_BF16) return fail(c, TX_EINVAL, "bad out_dtype");
   if (!std::isfinite(p.scale)) return fail(c, TX_EINVAL, "scale must be finite");
-  if ((q_w == nullptr) != (k_w == nullptr))
-    return fail(c, TX_EINVAL, "q_norm_w and k_norm_w are given together");
-  const bool prologue = q_w != nullptr;
+  const bool prologue = q_w != nullptr || k_w != nullptr;
   if (prologue && !(p.dim == 32 || p.dim == 64 || p.dim == 128 || p.dim == 256))
     return fail(c, TX_EINVAL, "prologue supports head_dim 32, 64, 128, 256");
   if (prologue && !(eps >= 0.f && std::isfinite(eps) && std::isfinite(theta) && theta > 0.f))
@@ -197,27 +195,34 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
   if (uses_scratch && (e = scratch_acquire(c, stream)) != cudaSuccess)
     return cuda_fail(c, e, "scratch wait");
 
-  if (prologue) {
-    // Normalised q/k go to scratch in the attention kernel's input type.
-    const int mid = p.in_dtype;
+  // The tensor-core kernel applies the q prologue to each Q tile in shared memory; k
+  // (read by several query tiles) is normalised once into scratch, valid rows only.
+  const uint16_t *tc_q_w = tc_path ? q_w : nullptr;
+  const bool pro_q = q_w != nullptr && !tc_path, pro_k = k_w != nullptr;
+  if (pro_q || pro_k) {
+    const int mid = p.in_dtype;  // normalised q/k keep the attention kernel's input type
     const size_t esz = mid == TX_BF16 ? 2 : 4;
-    const size_t qn = (size_t)p.total * p.heads * p.dim, kn = (size_t)p.total * p.kv_heads * p.dim;
+    const size_t qn = pro_q ? (size_t)p.total * p.heads * p.dim : 0;
+    const size_t kn = pro_k ? (size_t)p.total * p.kv_heads * p.dim : 0;
     if ((e = ensure_qk_scratch(c, (qn + kn) * esz + 256)) != cudaSuccess)
       return cuda_fail(c, e, "scratch allocation");
     void *qs = c->qk_scratch;
     void *ks = (uint8_t *)c->qk_scratch + ((qn * esz + 255) & ~(size_t)255);
     tx::PrologueProblem pp{};
-    pp.q = p.q; pp.k = p.k; pp.q_out = qs; pp.k_out = ks;
-    pp.tokens = p.total; pp.seq = p.cu_seqlens ? p.seq : p.seq;
+    pp.q = pro_q ? p.q : nullptr;
+    pp.k = pro_k ? p.k : nullptr;
+    pp.q_out = qs; pp.k_out = ks;
+    pp.tokens = p.total; pp.seq = p.seq;
     pp.cu_seqlens = p.cu_seqlens; pp.nseq = p.batch;
     pp.heads = p.heads; pp.kv_heads = p.kv_heads; pp.dim = p.dim;
     pp.in_dtype = p.in_dtype; pp.out_dtype = mid;
     pp.q_w = q_w; pp.k_w = k_w; pp.eps = eps; pp.theta = theta;
+    pp.lengths = tc_path && !p.cu_seqlens ? p.lengths : nullptr;
     if ((e = tx::launch_qk_norm_rope(pp, stream)) != cudaSuccess)
       return cuda_fail(c, e, "prologue launch");
     ++c->launches;
-    p.q = qs;
-    p.k = ks;
+    if (pro_q) p.q = qs;
+    if (pro_k) p.k = ks;
   }
 
   if (tc_path) {
@@ -240,8 +245,8 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
         return cuda_fail(c, e, "work list upload");
       c->units_key = key;
     }
-    if ((e = tx::launch_attention_tc(p, c->units, c->units_count, c->sms, c->status, stream)) !=
-        cudaSuccess)
+    if ((e = tx::launch_attention_tc(p, c->units, c->units_count, c->sms, c->status, tc_q_w, eps,
+                                     theta, stream)) != cudaSuccess)
       return cuda_fail(c, e, "attention launch");
     c->last_kernel = "tc_bf16_d128";
     ++c->launches;
@@ -665,28 +670,30 @@ int tx_attention_varlen(void *ctx, const void *q, const void *k, const void *v,
 
 int tx_qk_norm_rope(void *ctx, const void *q, const void *k, void *q_out, void *k_out,
                     uint32_t tokens, uint32_t seq, const int32_t *cu_seqlens, uint32_t nseq,
-                    uint32_t heads, uint32_t kv_heads, uint32_t dim, int in_dtype, int out_dtype,
-                    const uint16_t *q_norm_w, const uint16_t *k_norm_w, float eps, float theta,
-                    void *stream) {
+                    const uint32_t *lengths, uint32_t heads, uint32_t kv_heads, uint32_t dim,
+                    int in_dtype, int out_dtype, const uint16_t *q_norm_w,
+                    const uint16_t *k_norm_w, float eps, float theta, void *stream) {
   Ctx *c = (Ctx *)ctx;
   if (!c) return TX_EINVAL;
   std::lock_guard<std::recursive_mutex> g(c->mu);
-  if (!q || !k || !q_out || !k_out || !q_norm_w || !k_norm_w)
+  if (!q && !k) return fail(c, TX_EINVAL, "q or k required");
+  if ((q && (!q_out || !q_norm_w)) || (k && (!k_out || !k_norm_w)))
     return fail(c, TX_EINVAL, "null pointer");
   if (!(dim == 32 || dim == 64 || dim == 128 || dim == 256))
     return fail(c, TX_EINVAL, "head_dim 32, 64, 128 or 256");
   if (!heads || !kv_heads) return fail(c, TX_EINVAL, "heads must be positive");
   if (!cu_seqlens && !seq) return fail(c, TX_EINVAL, "seq must be positive");
   if (cu_seqlens && !nseq) return fail(c, TX_EINVAL, "nseq must be positive");
+  if (cu_seqlens && lengths) return fail(c, TX_EINVAL, "lengths apply to the padded layout");
   if ((in_dtype != TX_F32 && in_dtype != TX_BF16) || (out_dtype != TX_F32 && out_dtype != TX_BF16))
     return fail(c, TX_EINVAL, "bad dtype");
-  if (in_dtype != out_dtype && (q == q_out || k == k_out))
+  if (in_dtype != out_dtype && ((q && q == q_out) || (k && k == k_out)))
     return fail(c, TX_EINVAL, "in-place prologue needs equal dtypes");
   tx::PrologueProblem pp{};
   pp.q = q; pp.k = k; pp.q_out = q_out; pp.k_out = k_out; pp.tokens = tokens; pp.seq = seq;
   pp.cu_seqlens = cu_seqlens; pp.nseq = nseq; pp.heads = heads; pp.kv_heads = kv_heads;
   pp.dim = dim; pp.in_dtype = in_dtype; pp.out_dtype = out_dtype; pp.q_w = q_norm_w;
-  pp.k_w = k_norm_w; pp.eps = eps; pp.theta = theta;
+  pp.k_w = k_norm_w; pp.eps = eps; pp.theta = theta; pp.lengths = lengths;
   cudaSetDevice(c->device);
   cudaError_t e = tx::launch_qk_norm_rope(pp, stream ? (cudaStream_t)stream : c->stream);
   if (e != cudaSuccess) return cuda_fail(c, e, "prologue launch");

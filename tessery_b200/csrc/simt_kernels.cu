@@ -158,14 +158,21 @@ cudaError_t launch_attention_simt(const AttnProblem &p, cudaStream_t stream) {
 // [E*l, E*l+E); lanes 0..15 hold the first half of the row, lanes 16..31 the second,
 // so each rotation pair (c, c+dim/2) sits in lanes l and l^16.  The rotation angles
 // depend only on the position, so they are computed once per token and reused for all
-// q and k heads.  Arithmetic per row follows rms_norm then rope exactly.
-template <int E, typename TI, typename TO>
-__device__ __forceinline__ void norm_rope_row(const TI *in, TO *out, const uint16_t *w,
-                                              const float *co, const float *si, uint32_t lane,
-                                              uint32_t dim, float eps) {
-  float x[E];
+// q and k heads.  Rows are processed in groups of kGroup whose loads are all issued
+// before any arithmetic, so a warp keeps several row loads in flight.  Arithmetic per
+// row follows rms_norm then rope exactly.
+constexpr int kGroup = 4;
+
+template <int E, typename TI>
+__device__ __forceinline__ void load_row(const TI *in, uint32_t lane, float (&x)[E]) {
 #pragma unroll
   for (int e = 0; e < E; ++e) x[e] = Elem<TI>::load(in, lane * E + e);
+}
+
+template <int E, typename TO>
+__device__ __forceinline__ void norm_rope_store(float (&x)[E], TO *out, const uint16_t *w,
+                                                const float *co, const float *si, uint32_t lane,
+                                                uint32_t dim, float eps) {
   float squares = 0.f;
 #pragma unroll
   for (int e = 0; e < E; ++e) squares += x[e] * x[e];
@@ -184,6 +191,23 @@ __device__ __forceinline__ void norm_rope_row(const TI *in, TO *out, const uint1
 }
 
 template <int E, typename TI, typename TO>
+__device__ __forceinline__ void norm_rope_heads(const TI *in, TO *out, uint32_t nheads,
+                                                const uint16_t *w, const float *co,
+                                                const float *si, uint32_t lane, uint32_t dim,
+                                                float eps) {
+  for (uint32_t h0 = 0; h0 < nheads; h0 += kGroup) {
+    float x[kGroup][E];
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g)
+      if (h0 + g < nheads) load_row<E, TI>(in + (size_t)(h0 + g) * dim, lane, x[g]);
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g)
+      if (h0 + g < nheads)
+        norm_rope_store<E, TO>(x[g], out + (size_t)(h0 + g) * dim, w, co, si, lane, dim, eps);
+  }
+}
+
+template <int E, typename TI, typename TO>
 __global__ void qk_norm_rope_kernel(PrologueProblem p) {
   uint32_t lane = threadIdx.x & 31;
   uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -194,20 +218,24 @@ __global__ void qk_norm_rope_kernel(PrologueProblem p) {
   for (int e = 0; e < E; ++e) inv_freq[e] = rope_inv_freq(p.theta, (lane % 16) * E + e, dim);
   for (uint32_t tok = warp; tok < p.tokens; tok += nwarps) {
     uint32_t pos;
-    if (p.cu_seqlens) pos = tok - (uint32_t)p.cu_seqlens[find_seq(p.cu_seqlens, p.nseq, tok)];
-    else pos = tok % p.seq;
+    if (p.cu_seqlens) {
+      pos = tok - (uint32_t)p.cu_seqlens[find_seq(p.cu_seqlens, p.nseq, tok)];
+    } else {
+      pos = tok % p.seq;
+      if (p.lengths && pos >= min(p.lengths[tok / p.seq], p.seq)) continue;
+    }
     float co[E], si[E];
 #pragma unroll
     for (int e = 0; e < E; ++e) sincosf((float)pos * inv_freq[e], &si[e], &co[e]);
-    for (uint32_t h = 0; h < p.heads; ++h) {
-      size_t row = ((size_t)tok * p.heads + h) * dim;
-      norm_rope_row<E, TI, TO>((const TI *)p.q + row, (TO *)p.q_out + row, p.q_w, co, si, lane,
-                               dim, p.eps);
+    if (p.q) {
+      size_t row = (size_t)tok * p.heads * dim;
+      norm_rope_heads<E, TI, TO>((const TI *)p.q + row, (TO *)p.q_out + row, p.heads, p.q_w, co,
+                                 si, lane, dim, p.eps);
     }
-    for (uint32_t h = 0; h < p.kv_heads; ++h) {
-      size_t row = ((size_t)tok * p.kv_heads + h) * dim;
-      norm_rope_row<E, TI, TO>((const TI *)p.k + row, (TO *)p.k_out + row, p.k_w, co, si, lane,
-                               dim, p.eps);
+    if (p.k) {
+      size_t row = (size_t)tok * p.kv_heads * dim;
+      norm_rope_heads<E, TI, TO>((const TI *)p.k + row, (TO *)p.k_out + row, p.kv_heads, p.k_w,
+                                 co, si, lane, dim, p.eps);
     }
   }
 }
@@ -229,7 +257,7 @@ static cudaError_t launch_prologue_e(const PrologueProblem &p, cudaStream_t stre
 }
 
 cudaError_t launch_qk_norm_rope(const PrologueProblem &p, cudaStream_t stream) {
-  if (!p.tokens) return cudaSuccess;
+  if (!p.tokens || (!p.q && !p.k)) return cudaSuccess;
   switch (p.dim) {
     case 32: return launch_prologue_e<1>(p, stream);
     case 64: return launch_prologue_e<2>(p, stream);

@@ -399,31 +399,33 @@ class CudaRuntime:
 
     def qk_norm_rope_device(
         self,
-        q: int,
-        k: int,
-        q_out: int,
-        k_out: int,
+        q: int | None,
+        k: int | None,
+        q_out: int | None,
+        k_out: int | None,
         *,
         tokens: int,
         seq: int,
         heads: int,
         kv_heads: int,
         dim: int,
-        q_norm_weight: int,
-        k_norm_weight: int,
+        q_norm_weight: int | None,
+        k_norm_weight: int | None,
         cu_seqlens: int | None = None,
         nseq: int = 0,
+        lengths: int | None = None,
         in_dtype: int = native.TX_BF16,
         out_dtype: int = native.TX_BF16,
         eps: float = 1e-6,
         theta: float = 1e6,
         stream: int | None = None,
     ) -> None:
-        """Queues the fused q/k RMSNorm + RoPE prologue (tx_qk_norm_rope)."""
+        """Queues the fused q/k RMSNorm + RoPE prologue (tx_qk_norm_rope); q or k may be
+        None.  `lengths` (padded layout) skips the rows past each sequence's length."""
         self._check_open()
         rc = self._lib.tx_qk_norm_rope(
-            self._pointer, q, k, q_out, k_out, tokens, seq, cu_seqlens, nseq, heads, kv_heads,
-            dim, in_dtype, out_dtype, q_norm_weight, k_norm_weight, eps, theta, stream,
+            self._pointer, q, k, q_out, k_out, tokens, seq, cu_seqlens, nseq, lengths, heads,
+            kv_heads, dim, in_dtype, out_dtype, q_norm_weight, k_norm_weight, eps, theta, stream,
         )
         _raise_for(rc)
 

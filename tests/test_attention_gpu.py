@@ -282,3 +282,33 @@ def test_prologue_matches_oracle(runtime):
 
 def test_typed_dtype_codes():
     assert (TX_F32, TX_BF16) == (0, 1)
+
+
+def test_composed_prologue_matches_one_call(runtime):
+    """k-only prologue over the valid rows (tx_qk_norm_rope with device lengths), then
+    attention with only the q weight, equals the one-call path bit for bit."""
+    from tessery_b200 import TX_BF16, TX_F32
+
+    w = workloads.qwen_padded(batch=4, seq=384, seed=26, lengths=np.array([384, 200, 1, 129]))
+    one_call = run_workload(runtime, w)
+    rt = runtime
+    bufs = {n: rt.buffer(a.nbytes, np.ascontiguousarray(a)) for n, a in
+            (("q", w.q), ("k", w.k), ("v", w.v), ("len", w.lengths.astype(np.uint32)),
+             ("qw", w.q_norm_weight), ("kw", w.k_norm_weight))}
+    kn = rt.buffer(w.k.nbytes)
+    out = rt.buffer(w.q.size * 4)
+    B, L, H, D = w.q.shape
+    rt.qk_norm_rope_device(None, bufs["k"].device_ptr, None, kn.device_ptr, tokens=B * L, seq=L,
+                           heads=H, kv_heads=8, dim=D, q_norm_weight=None,
+                           k_norm_weight=bufs["kw"].device_ptr, lengths=bufs["len"].device_ptr,
+                           in_dtype=TX_BF16, out_dtype=TX_BF16)
+    rt.attention_padded_device(bufs["q"].device_ptr, kn.device_ptr, bufs["v"].device_ptr,
+                               bufs["len"].device_ptr, out.device_ptr, batch=B, seq=L, heads=H,
+                               kv_heads=8, dim=D, in_dtype=TX_BF16, out_dtype=TX_F32,
+                               causal=True, lengths_host=w.lengths,
+                               q_norm_weight=bufs["qw"].device_ptr)
+    rt.sync()
+    got = rt.read(out, w.q.shape)
+    assert np.array_equal(got, one_call)
+    for b in list(bufs.values()) + [kn, out]:
+        b.close()
