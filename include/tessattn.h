@@ -184,6 +184,29 @@ int tx_qk_norm_rope(void *ctx, const void *q, const void *k, void *q_out, void *
                     int in_dtype, int out_dtype, const uint16_t *q_norm_w,
                     const uint16_t *k_norm_w, float eps, float theta, void *stream);
 
+/* Allocation-free variant of tx_attention_padded (no counterpart in the reference,
+ * whose Metal runtime always owns its buffers).  For callers that may not allocate
+ * device memory -- hosts that reserve all memory up front and treat a later
+ * cudaMalloc as an error, since it can fail under memory pressure and stall the
+ * device -- and that therefore cannot create a context either.  It takes no context.
+ * Path: the tensor-core kernel only (bf16 q/k/v on the current device, head_dim 128,
+ * an even number of query heads per kv head); q_norm_w (or NULL) applies the fused q
+ * RMSNorm + RoPE, while k must already be normalised (tx_qk_norm_rope).  Its only
+ * scratch, the work list, is a static device array of 16384 units (one unit = 128
+ * query rows of a head pair: batch * heads/2 * ceil(seq/128) units); larger problems
+ * are rejected with TX_EINVAL.  The first call on a device looks up that array's
+ * device address (with the device current) and should come before any stream
+ * capture.  All calls share the array and it keeps the last call's contents: calls
+ * whose work overlaps on the GPU race.  status: device int the kernel sets to
+ * TX_ETIMEOUT | site << 8 if a bounded wait gives up (zeroed by this call first), or
+ * NULL.  Returns TX_OK once queued on `stream` (NULL: the legacy default stream). */
+int tx_attention_padded_noalloc(const void *q, const void *k, const void *v,
+                                const uint32_t *lengths, const uint32_t *lengths_host,
+                                void *out, uint32_t batch, uint32_t seq, uint32_t heads,
+                                uint32_t kv_heads, int out_dtype, int causal, float scale,
+                                const uint16_t *q_norm_w, float eps, float theta, int *status,
+                                void *stream);
+
 /* Waits for all work queued on `stream` (NULL: context stream) and reports kernel
  * errors, including device-side wait timeouts, as a status code. */
 int tx_sync(void *ctx, void *stream);

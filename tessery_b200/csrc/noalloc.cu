@@ -1,0 +1,115 @@
+// tx_attention_padded_noalloc: the bf16 tensor-core attention without any device-memory
+// allocation, for callers that may not allocate.
+//
+// Who needs it: hosts that reserve all device memory up front (a serving process whose
+// memory is carved out of one arena at start-up, an embedded runtime with a fixed
+// memory budget) and treat any later allocation as an error, because cudaMalloc can
+// fail when memory is full or fragmented and cudaMalloc/cudaFree can stall the whole
+// device while they run.  Such callers cannot create a libtessattn context either
+// (tx_create allocates its status word), so this entry point takes no context.
+//
+// How: the only scratch the kernel needs besides its inputs and outputs is the work
+// list (one uint32 per unit of work).  It lives in the file-scope array below, which the
+// CUDA runtime places in device memory when the module is loaded; every GPU that loads
+// the library holds it until the process exits.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "../../include/tessattn.h"
+#include "kernels.h"
+
+namespace {
+
+// Capacity of the work list: units = batch * (heads / 2) * ceil(seq / 128).
+constexpr uint32_t kNoAllocMaxUnits = 16384;
+// Word 0: status word used when the caller passes no status pointer.  Words 64..: units.
+constexpr uint32_t kHeaderWords = 64;
+
+static __device__ __align__(256) uint32_t g_noalloc_scratch[kHeaderWords + kNoAllocMaxUnits];
+
+// Device address of g_noalloc_scratch per device, looked up once with that device
+// current.  In host code the array's name is only a host-side stand-in, not a device
+// address, so the kernel must be given the looked-up address.
+std::mutex g_noalloc_mu;
+uint32_t *g_noalloc_ptr[64] = {};
+int g_noalloc_sms[64] = {};
+uint32_t g_host_units[kNoAllocMaxUnits];  // host copy of the work list (under the mutex)
+
+// Longest-first unit list like tc_build_units, built without any allocation: units are
+// bucketed by cost (key tiles visited, 1..255) with a counting sort that keeps
+// generation order within a cost.
+uint32_t build_units_noalloc(const tx::AttnProblem &p, const uint32_t *lengths_host,
+                             uint32_t *units) {
+  const uint32_t tiles = (p.seq + 127) / 128, pairs = p.heads / 2;
+  uint32_t count[257] = {};
+  auto cost_of = [&](uint32_t s, uint32_t t) {
+    const uint32_t n = lengths_host[s] < p.seq ? lengths_host[s] : p.seq;
+    const uint32_t q0 = t * 128;
+    const uint32_t kend = p.causal ? (q0 + 128 < n ? q0 + 128 : n) : n;
+    return (kend + 127) / 128;
+  };
+  for (uint32_t s = 0; s < p.batch; ++s)
+    for (uint32_t t = 0; t < tiles; ++t) count[cost_of(s, t)] += pairs;
+  uint32_t start[257];
+  uint32_t acc = 0;
+  for (int c = 256; c >= 0; --c) {  // highest cost first
+    start[c] = acc;
+    acc += count[c];
+  }
+  for (uint32_t s = 0; s < p.batch; ++s)
+    for (uint32_t t = 0; t < tiles; ++t) {
+      const uint32_t c = cost_of(s, t);
+      for (uint32_t hp = 0; hp < pairs; ++hp) units[start[c]++] = (s << 14) | (hp << 8) | t;
+    }
+  return acc;
+}
+
+}  // namespace
+
+extern "C" int tx_attention_padded_noalloc(const void *q, const void *k, const void *v,
+                                           const uint32_t *lengths, const uint32_t *lengths_host,
+                                           void *out, uint32_t batch, uint32_t seq,
+                                           uint32_t heads, uint32_t kv_heads, int out_dtype,
+                                           int causal, float scale, const uint16_t *q_norm_w,
+                                           float eps, float theta, int *status, void *stream) {
+  if (!q || !k || !v || !lengths || !lengths_host || !out) return TX_EINVAL;
+  if (out_dtype != TX_F32 && out_dtype != TX_BF16) return TX_EINVAL;
+  if (!batch || !seq || !(scale > 0.f) || !(scale < 1e30f)) return TX_EINVAL;
+  if ((uint64_t)batch * seq > 0xffffffffull) return TX_EINVAL;
+  for (uint32_t b = 0; b < batch; ++b)
+    if (lengths_host[b] > seq) return TX_EINVAL;
+  tx::AttnProblem p{};
+  p.q = q; p.k = k; p.v = v; p.out = out; p.lengths = lengths; p.cu_seqlens = nullptr;
+  p.batch = batch; p.seq = seq; p.total = batch * seq; p.heads = heads; p.kv_heads = kv_heads;
+  p.dim = 128; p.in_dtype = TX_BF16; p.out_dtype = out_dtype; p.causal = causal ? 1 : 0;
+  p.scale = scale;
+  if (!tx::tc_attention_supported(p)) return TX_EINVAL;
+  if (tx::tc_max_units(p) > kNoAllocMaxUnits) return TX_EINVAL;  // beyond the static list
+
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return TX_ECUDA;
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) {
+    // One-time set-up for this device (the caller's current device).
+    void *ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return TX_ECUDA;
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+      return TX_ECUDA;
+    g_noalloc_sms[device] = sms;
+    g_noalloc_ptr[device] = (uint32_t *)ptr;
+  }
+  uint32_t *scratch = g_noalloc_ptr[device];
+  cudaStream_t s = (cudaStream_t)stream;
+  int *st = status ? status : (int *)scratch;
+  const uint32_t n = build_units_noalloc(p, lengths_host, g_host_units);
+  // The array keeps the previous call's contents: the status word must start at zero.
+  if (cudaMemsetAsync(st, 0, sizeof(int), s) != cudaSuccess) return TX_ECUDA;
+  if (n && cudaMemcpyAsync(scratch + kHeaderWords, g_host_units, n * sizeof(uint32_t),
+                           cudaMemcpyHostToDevice, s) != cudaSuccess)
+    return TX_ECUDA;
+  cudaError_t e = tx::launch_attention_tc(p, scratch + kHeaderWords, n, g_noalloc_sms[device],
+                                          st, q_norm_w, eps, theta, s);
+  return e == cudaSuccess ? TX_OK : TX_ECUDA;
+}

@@ -63,6 +63,11 @@ SIGNATURES: dict[str, tuple[list[Any], Any]] = {
         _i32,
     ),
     "tx_sync": ([_vp, _vp], _i32),
+    "tx_attention_padded_noalloc": (
+        [_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _i32, _i32, _f32, _vp, _f32,
+         _f32, _vp, _vp],
+        _i32,
+    ),
 }
 
 _lock = threading.Lock()

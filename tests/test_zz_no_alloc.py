@@ -1,0 +1,82 @@
+"""tx_attention_padded_noalloc, the allocation-free entry point (needs a B200).
+
+It serves callers that may not allocate device memory -- processes that reserve all
+memory up front and treat a later cudaMalloc as an error -- so it keeps its work list in
+a static device array instead of allocating.  This file is collected last so that a run
+stopping at the first failure has already run every other test.  It checks the entry
+point, called through the C ABI, against tx_attention_padded on the same inputs, on two
+calls in a row with different shapes (the shared static array keeps the previous call's
+contents), and checks that an oversized problem is rejected.
+"""
+
+import ctypes as ct
+
+import numpy as np
+import pytest
+
+from tessery_b200 import TX_BF16, TX_F32, native, workloads
+
+pytestmark = pytest.mark.gpu
+
+BF16_GATE = 2e-2  # the bf16-in / fp32-accumulate tolerance used by the other GPU tests
+
+
+def run_both(rt, w):
+    lib = native.load()
+    B, L, H, D = w.q.shape
+    kv = w.k.shape[2]
+    arrays = {"q": w.q, "k": w.k, "v": w.v, "len": w.lengths.astype(np.uint32),
+              "qw": w.q_norm_weight}
+    bufs = {n: rt.buffer(a.nbytes, np.ascontiguousarray(a)) for n, a in arrays.items()}
+    out_ref = rt.buffer(w.q.size * 4)
+    out_new = rt.buffer(w.q.size * 4)
+    status = rt.buffer(4, np.array([12345], np.int32))  # stale value: the call must zero it
+    lengths_host = np.ascontiguousarray(w.lengths, dtype=np.uint32)
+    try:
+        rt.attention_padded_device(
+            bufs["q"].device_ptr, bufs["k"].device_ptr, bufs["v"].device_ptr,
+            bufs["len"].device_ptr, out_ref.device_ptr, batch=B, seq=L, heads=H, kv_heads=kv,
+            dim=D, in_dtype=TX_BF16, out_dtype=TX_F32, causal=True, scale=w.scale,
+            lengths_host=lengths_host, q_norm_weight=bufs["qw"].device_ptr, eps=w.eps,
+            theta=w.theta)
+        rt.sync()
+        rc = lib.tx_attention_padded_noalloc(
+            bufs["q"].device_ptr, bufs["k"].device_ptr, bufs["v"].device_ptr,
+            bufs["len"].device_ptr, lengths_host.ctypes.data, out_new.device_ptr, B, L, H, kv,
+            TX_F32, 1, ct.c_float(w.scale), bufs["qw"].device_ptr, ct.c_float(w.eps),
+            ct.c_float(w.theta), status.device_ptr, None)
+        assert rc == native.TX_OK
+        ref = rt.read(out_ref, w.q.shape)
+        new = rt.read(out_new, w.q.shape)  # synchronous read after the default stream
+        st = rt.read(status, (1,), dtype=np.int32)
+        return ref, new, int(st[0])
+    finally:
+        for b in [*bufs.values(), out_ref, out_new, status]:
+            b.close()
+
+
+def test_noalloc_matches_existing_entry_point_twice(runtime):
+    first = workloads.qwen_padded(batch=5, seq=384, seed=61,
+                                  lengths=np.array([384, 1, 200, 129, 300]))
+    second = workloads.qwen_padded(batch=3, seq=256, seed=62, lengths=np.array([17, 256, 128]))
+    for w in (first, second):
+        ref, new, st = run_both(runtime, w)
+        assert st == 0
+        assert np.isfinite(new).all()
+        np.testing.assert_allclose(new, ref, atol=BF16_GATE, rtol=0)
+
+
+def test_noalloc_rejects_problems_beyond_the_static_work_list(runtime):
+    lib = native.load()
+    # 129 sequences x 8 head pairs x 16 tiles = 16512 units > 16384.
+    B, L = 129, 2048
+    lengths = np.full(B, 1, np.uint32)
+    dummy = runtime.buffer(256)
+    try:
+        p = dummy.device_ptr
+        rc = lib.tx_attention_padded_noalloc(p, p, p, p, lengths.ctypes.data, p, B, L, 16, 8,
+                                             TX_F32, 1, ct.c_float(128**-0.5), None,
+                                             ct.c_float(1e-6), ct.c_float(1e6), None, None)
+        assert rc == native.TX_EINVAL
+    finally:
+        dummy.close()
