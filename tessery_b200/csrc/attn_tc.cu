@@ -64,14 +64,15 @@ constexpr uint32_t kStageBytes = 4096;           // one 32-row x 128-byte output
 // Barrier slots (uint64 each) at the start of the misc area.
 enum : uint32_t {
   kBarQFull = 0,                      // + head slot: Q_h landed (TMA transaction count)
-  kBarQReady = kBarQFull + 2,         // + head slot: Q_h transformed (128 arrivals)
+  kBarQReady = kBarQFull + 2,         // + head slot: Q_h transformed (256 arrivals)
   kBarQEmpty = kBarQReady + 2,        // + head slot: last QK_h of the unit ran
   kBarKVFull = kBarQEmpty + 2,        // + ring slot
   kBarKVEmpty = kBarKVFull + kStages,
   kBarSFull = kBarKVEmpty + kStages,  // + head slot
   kBarPFull = kBarSFull + 2,          // + head slot (128 arrivals)
   kBarODone = kBarPFull + 2,          // + head slot
-  kBarDrain = kBarODone + 2,
+  kBarXform = kBarODone + 2,          // q prologue: both row norms read (256 arrivals)
+  kBarDrain = kBarXform + 1,
   kNumBars = kBarDrain + 1
 };
 constexpr uint32_t kOffTmemSlot = kNumBars * 8;   // uint32 TMEM base address
@@ -84,7 +85,7 @@ static_assert(kSmemBytes <= 232448, "shared memory budget");
 // Wait sites, reported in the status word for diagnosis.
 enum : int {
   kSiteQEmpty = 1, kSiteKVEmpty = 2, kSiteQReady = 3, kSiteKVFull = 4, kSitePFull = 5,
-  kSiteSFull = 6, kSiteODone = 7, kSiteQFull = 8
+  kSiteSFull = 6, kSiteODone = 7, kSiteQFull = 8, kSiteXform = 9
 };
 
 // ---- unit encoding --------------------------------------------------------------------
@@ -198,6 +199,13 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
       : "memory");
+}
+// L2 prefetch of one box (no shared memory, no completion tracking).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap *map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
 }
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t src, int x, int y,
                                              int z) {
@@ -340,58 +348,91 @@ __device__ __forceinline__ void sincos_reduced(float angle, float *s, float *c) 
   __sincosf(r, s, c);
 }
 
-// In-place q RMSNorm + RoPE of row `r` of a swizzled 128x128 bf16 tile (thread r owns
-// the row).  Arithmetic order follows kernels.metal:53-74: x * inv * w, then the
-// split-half rotation of (element c, element c + 64) by angle pos * inv_freq[c].
-__device__ __forceinline__ void q_prologue_row(uint32_t tile, uint32_t r, uint32_t pos,
-                                               const uint16_t *w, const float *inv_freq,
-                                               float eps) {
-  const uint32_t row = tile + r * 128;
-  const uint32_t sw = r & 7;
-  uint4 v[16];
+__device__ __forceinline__ uint32_t u4_at(const uint4 &v, int e) {
+  return e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w;
+}
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ void acc_squares(float (&ssq)[4], const uint4 &v) {
 #pragma unroll
-  for (int c = 0; c < 16; ++c)
-    v[c] = ld_shared_v4(row + (c >> 3) * kAtomBytes + (((c & 7) ^ sw) << 4));
-  float ssq[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int c = 0; c < 16; ++c) {
-    const uint32_t wv[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float lo = __uint_as_float(wv[e] << 16), hi = __uint_as_float(wv[e] & 0xffff0000u);
-      ssq[e] = fmaf(lo, lo, ssq[e]);
-      ssq[e] = fmaf(hi, hi, ssq[e]);
-    }
+  for (int e = 0; e < 4; ++e) {
+    const uint32_t x = u4_at(v, e);
+    ssq[e] = fmaf(bf16_lo(x), bf16_lo(x), ssq[e]);
+    ssq[e] = fmaf(bf16_hi(x), bf16_hi(x), ssq[e]);
   }
-  const float ss = (ssq[0] + ssq[1]) + (ssq[2] + ssq[3]);
-  const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
-  const float fpos = (float)pos;
+}
+
+// In-place q RMSNorm + RoPE of the two Q tiles (head slots 0 and 1) of a unit, shared
+// by both warpgroups: the thread owning row r in warpgroup `part` transforms row r of
+// both tiles for the rotation pairs c in [32*part, 32*part + 32), so each (position, c)
+// sine and cosine is evaluated once for the two heads.  Arithmetic per element follows
+// kernels.metal:53-74: x * inv * w, then the rotation of (element c, element c + 64) by
+// angle pos * inv_freq[c].  Every row norm reads the whole row, half of which the other
+// warpgroup rewrites, so the two passes are separated by a barrier of both warpgroups.
+// Pass 1 of the q prologue: inverse RMS of row r of both Q tiles.
+__device__ __forceinline__ void q_row_norms(uint32_t q_tiles, uint32_t r, float eps,
+                                            float (&inv)[2]) {
+  const uint32_t sw = r & 7;
 #pragma unroll
-  for (int g = 0; g < 8; ++g) {  // chunk g (elements 8g..8g+7) pairs with chunk g + 8
-    const uint32_t a4[4] = {v[g].x, v[g].y, v[g].z, v[g].w};
-    const uint32_t b4[4] = {v[g + 8].x, v[g + 8].y, v[g + 8].z, v[g + 8].w};
-    uint32_t lo_out[4], hi_out[4];
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t row = q_tiles + h * kTileBytes + r * 128;
+    float ssq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      acc_squares(ssq, ld_shared_v4(row + (c >> 3) * kAtomBytes + (((c & 7) ^ sw) << 4)));
+    inv[h] = 1.0f / sqrtf(((ssq[0] + ssq[1]) + (ssq[2] + ssq[3])) / 128.0f + eps);
+  }
+}
+
+// Pass 2: normalise and rotate this warpgroup's half of the rotation pairs of row r of
+// both tiles (run only after both warpgroups finished pass 1 on the tiles).
+__device__ __forceinline__ void q_rotate_pair(uint32_t q_tiles, uint32_t r, uint32_t pos,
+                                              int part, const uint16_t *w,
+                                              const float *inv_freq, const float (&inv)[2]) {
+  const uint32_t sw = r & 7;
+  const float fpos = (float)pos;
+#pragma unroll 1
+  for (int gg = 0; gg < 4; ++gg) {  // pass 2: own chunk groups, both heads at once
+    const uint32_t g = 4 * part + gg;
+    uint4 lo[2], hi[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t row = q_tiles + h * kTileBytes + r * 128;
+      lo[h] = ld_shared_v4(row + ((g ^ sw) << 4));
+      hi[h] = ld_shared_v4(row + kAtomBytes + ((g ^ sw) << 4));
+    }
+    uint32_t out_lo[2][4], out_hi[2][4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      float ra[2], rb[2];
+      float ra[2][2], rb[2][2];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int c = 8 * g + 2 * e + h;
-        const float xa = __uint_as_float(h ? (a4[e] & 0xffff0000u) : (a4[e] << 16));
-        const float xb = __uint_as_float(h ? (b4[e] & 0xffff0000u) : (b4[e] << 16));
-        const float a = xa * inv * bf16_bits_to_f32(w[c]);
-        const float b = xb * inv * bf16_bits_to_f32(w[c + 64]);
+      for (int hh = 0; hh < 2; ++hh) {  // element within the bf16 pair
+        const uint32_t c = 8 * g + 2 * e + hh;
         float s, co;
         sincos_reduced(fpos * inv_freq[c], &s, &co);
-        ra[h] = a * co - b * s;
-        rb[h] = a * s + b * co;
+        const float wa = bf16_bits_to_f32(w[c]), wb = bf16_bits_to_f32(w[c + 64]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t A = u4_at(lo[h], e), B = u4_at(hi[h], e);
+          const float a = (hh ? bf16_hi(A) : bf16_lo(A)) * inv[h] * wa;
+          const float b = (hh ? bf16_hi(B) : bf16_lo(B)) * inv[h] * wb;
+          ra[h][hh] = a * co - b * s;
+          rb[h][hh] = a * s + b * co;
+        }
       }
-      lo_out[e] = pack_bf16x2(ra[0], ra[1]);
-      hi_out[e] = pack_bf16x2(rb[0], rb[1]);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        out_lo[h][e] = pack_bf16x2(ra[h][0], ra[h][1]);
+        out_hi[h][e] = pack_bf16x2(rb[h][0], rb[h][1]);
+      }
     }
-    st_shared_v4(row + (((uint32_t)g ^ sw) << 4), lo_out[0], lo_out[1], lo_out[2], lo_out[3]);
-    st_shared_v4(row + kAtomBytes + (((uint32_t)g ^ sw) << 4), hi_out[0], hi_out[1], hi_out[2],
-                 hi_out[3]);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t row = q_tiles + h * kTileBytes + r * 128;
+      st_shared_v4(row + ((g ^ sw) << 4), out_lo[h][0], out_lo[h][1], out_lo[h][2], out_lo[h][3]);
+      st_shared_v4(row + kAtomBytes + ((g ^ sw) << 4), out_hi[h][0], out_hi[h][1], out_hi[h][2],
+                   out_hi[h][3]);
+    }
   }
 }
 
@@ -442,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int h = 0; h < 2; ++h) {
       mbar_init(bar(kBarQFull + h), 1);
-      mbar_init(bar(kBarQReady + h), 128);
+      mbar_init(bar(kBarQReady + h), 256);
       mbar_init(bar(kBarQEmpty + h), 1);
       mbar_init(bar(kBarSFull + h), 1);
       mbar_init(bar(kBarPFull + h), 128);
@@ -452,6 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(kBarKVFull + s), 1);
       mbar_init(bar(kBarKVEmpty + s), 1);
     }
+    mbar_init(bar(kBarXform), 256);
     mbar_init(bar(kBarDrain), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -500,6 +542,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         ++units_done;
+        // Warm L2 with the next unit's tiles so that its TMA loads hit L2.
+        for (uint32_t un = ui + gridDim.x; un < p.n_units; un += gridDim.x) {
+          const Unit v = decode(p, p.units[un]);
+          if (!v.nt) continue;
+          for (int h = 0; h < 2; ++h)
+            for (int a = 0; a < 2; ++a)
+              tma_prefetch_3d(&tm_q, a * 64, (int)(v.head0 + h), (int)(v.tok0 + v.q0));
+          for (uint32_t j = 0; j < v.nt; ++j)
+            for (int a = 0; a < 2; ++a) {
+              tma_prefetch_3d(&tm_k, a * 64, (int)v.kvh, (int)(v.tok0 + j * kTile));
+              tma_prefetch_3d(&tm_v, a * 64, (int)v.kvh, (int)(v.tok0 + j * kTile));
+            }
+          break;
+        }
         for (uint32_t j = 0; ok && j < u.nt; ++j) {
           for (int which = 0; which < 2; ++which) {  // 0: K_j, 1: V_j
             uint32_t slot = loads % kStages, round = loads / kStages;
@@ -617,10 +673,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tS = tmem + lane_base + hs * 128;
     const uint32_t tO = tmem + lane_base + 256 + hs * 128;
     const uint32_t prow = sbase + kOffP + hs * kTileBytes + r * 128;  // row r of P_h
-    const uint32_t qtile = sbase + kOffQ + hs * kTileBytes;
-    const uint32_t stage = sbase + kOffP + hs * kTileBytes + wq * 2 * kStageBytes;
+    // Output staging of this warp: the P rows it writes itself (rows 32*wq.. of each of
+    // the two atoms of P_h, 4 KB each), so only this warp's bulk stores read them.
+    const uint32_t stage[2] = {sbase + kOffP + hs * kTileBytes + wq * kStageBytes,
+                               sbase + kOffP + hs * kTileBytes + kAtomBytes + wq * kStageBytes};
     uint32_t qcount = 0, scount = 0, ocount = 0;
     bool ok = true;
+    // Q tiles of a unit: wait for both copies, apply the q prologue (both warpgroups,
+    // half the rotation pairs each), hand both tiles to the issuer.
+    uint32_t prepared = 0xffffffffu, xcount = 0;
+    auto prepare = [&](uint32_t index, const Unit &v) {
+      for (int h = 0; h < 2 && ok; ++h)
+        ok = __all_sync(0xffffffffu, wait_phase(bar(kBarQFull + h), qcount & 1, abort_flag,
+                                                p.status, kSiteQFull));
+      if (!ok) return;
+      ++qcount;
+      if (p.q_norm_w) {
+        float inv[2];
+        q_row_norms(sbase + kOffQ, r, p.eps, inv);
+        mbar_arrive(bar(kBarXform));
+        ok = __all_sync(0xffffffffu, wait_phase(bar(kBarXform), xcount & 1, abort_flag, p.status,
+                                                kSiteXform));
+        ++xcount;
+        if (!ok) return;
+        q_rotate_pair(sbase + kOffQ, r, v.q0 + r, hs, qw_s, invf_s, inv);
+        fence_proxy_async();
+      }
+      mbar_arrive(bar(kBarQReady + 0));
+      mbar_arrive(bar(kBarQReady + 1));
+      prepared = index;
+    };
     for (uint32_t ui = blockIdx.x; ui < p.n_units; ui += gridDim.x) {
       Unit u = decode(p, p.units[ui]);
       if (!u.live) continue;
@@ -642,16 +724,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
       if (!ok) break;
-      // Q tile: wait for the copy, apply the q prologue in place, hand it to the issuer.
-      ok = __all_sync(0xffffffffu, wait_phase(bar(kBarQFull + hs), qcount & 1, abort_flag,
-                                              p.status, kSiteQFull));
+      if (prepared != ui) prepare(ui, u);
       if (!ok) break;
-      ++qcount;
-      if (p.q_norm_w) {
-        q_prologue_row(qtile, r, qpos, qw_s, invf_s, p.eps);
-        fence_proxy_async();
-      }
-      mbar_arrive(bar(kBarQReady + hs));
 
       const uint32_t end = p.causal ? min(qpos + 1, u.n) : u.n;
       float m_ref = -INFINITY, l = 0.f;
@@ -712,6 +786,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           m_ref = mt;
         }
+        if (j == 0) {
+          // P_h was the previous unit's output staging: its bulk stores must have read it.
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+        }
         // Probabilities -> bf16 -> P tile: chunks 2-3 from registers while chunks 0-1 are
         // loaded again from TMEM.
         tmem_ld32(tS + 0, xa);
@@ -726,6 +805,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(bar(kBarPFull + hs));
       }
       if (!ok) break;
+      // Hand the next unit's Q tiles to the issuer before this unit's epilogue, so the
+      // tensor cores start on it while the output leaves.
+      for (uint32_t un = ui + gridDim.x; un < p.n_units; un += gridDim.x) {
+        const Unit v = decode(p, p.units[un]);
+        if (v.live && v.nt) {
+          prepare(un, v);
+          break;
+        }
+      }
+      if (!ok) break;
       // Epilogue: wait for the last P.V, normalise, store.  Warps whose 32 rows are all
       // inside the sequence stage their rows (swizzled, in the now free P tile) and send
       // them with TMA bulk-tensor stores; a warp at a ragged end stores row by row.
@@ -737,7 +826,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv = 1.0f / l;
       const uint32_t wrow0 = u.q0 + wq * 32;
       const bool bulk = wrow0 + 32 <= u.rows;
-      const uint32_t srow = stage + (uint32_t)lane * 128;
+      const uint32_t srow0 = (uint32_t)lane * 128;
       const uint32_t sw = (uint32_t)lane & 7;
       if (!p.out_bf16) {
         uint32_t ob[2][32];
@@ -752,19 +841,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int t = 0; t < 32; ++t) x[t] = __float_as_uint(__uint_as_float(x[t]) * inv);
           if (bulk) {
-            const uint32_t buf = (uint32_t)(c & 1) * kStageBytes;
+            const uint32_t buf = stage[c & 1];
             if (c >= 2) {
               if (lane == 0) bulk_wait_read<1>();
               __syncwarp();
             }
 #pragma unroll
             for (int g = 0; g < 8; ++g)
-              st_shared_v4(srow + buf + (((uint32_t)g ^ sw) << 4), x[4 * g], x[4 * g + 1],
+              st_shared_v4(buf + srow0 + (((uint32_t)g ^ sw) << 4), x[4 * g], x[4 * g + 1],
                            x[4 * g + 2], x[4 * g + 3]);
             fence_proxy_async();
             __syncwarp();
             if (lane == 0) {
-              tma_store_3d(&tm_o, stage + buf, c * 32, (int)head, (int)(u.tok0 + wrow0));
+              tma_store_3d(&tm_o, buf, c * 32, (int)head, (int)(u.tok0 + wrow0));
               bulk_commit();
             }
           } else if (store) {
@@ -790,15 +879,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 pack_bf16x2(__uint_as_float(xb[2 * t]) * inv, __uint_as_float(xb[2 * t + 1]) * inv);
           }
           if (bulk) {
-            const uint32_t buf = (uint32_t)c * kStageBytes;
+            const uint32_t buf = stage[c];
 #pragma unroll
             for (int g = 0; g < 8; ++g)
-              st_shared_v4(srow + buf + (((uint32_t)g ^ sw) << 4), w[4 * g], w[4 * g + 1],
+              st_shared_v4(buf + srow0 + (((uint32_t)g ^ sw) << 4), w[4 * g], w[4 * g + 1],
                            w[4 * g + 2], w[4 * g + 3]);
             fence_proxy_async();
             __syncwarp();
             if (lane == 0) {
-              tma_store_3d(&tm_o, stage + buf, c * 64, (int)head, (int)(u.tok0 + wrow0));
+              tma_store_3d(&tm_o, buf, c * 64, (int)head, (int)(u.tok0 + wrow0));
               bulk_commit();
             }
           } else if (store) {
@@ -809,9 +898,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // The staging area is the P tile of the next unit: its reads must be done.
-      if (lane == 0) bulk_wait_read<0>();
-      __syncwarp();
       tc_fence_before();
     }
     if (lane == 0) bulk_wait_all();

@@ -45,6 +45,7 @@ struct PrologueProblem {
   const uint16_t *q_w, *k_w;
   float eps, theta;
   const uint32_t *lengths;    // optional, padded layout only
+  float inv_freq[128];        // theta^(-2c/dim) per column c < dim/2 (set by the launcher)
 };
 cudaError_t launch_qk_norm_rope(const PrologueProblem &p, cudaStream_t stream);
 

@@ -5,6 +5,8 @@
 //                     general fallback: any head_dim <= 256, f32/bf16, padded/varlen
 //   qk_norm_rope   -- the q/k RMSNorm + RoPE sequence of qwen3.py:216-237 fused into
 //                     one pass that computes the rotation angles once per token.
+#include <cmath>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -215,7 +217,7 @@ __global__ void qk_norm_rope_kernel(PrologueProblem p) {
   const uint32_t dim = p.dim;
   float inv_freq[E];
 #pragma unroll
-  for (int e = 0; e < E; ++e) inv_freq[e] = rope_inv_freq(p.theta, (lane % 16) * E + e, dim);
+  for (int e = 0; e < E; ++e) inv_freq[e] = p.inv_freq[(lane % 16) * E + e];
   for (uint32_t tok = warp; tok < p.tokens; tok += nwarps) {
     uint32_t pos;
     if (p.cu_seqlens) {
@@ -256,8 +258,14 @@ static cudaError_t launch_prologue_e(const PrologueProblem &p, cudaStream_t stre
   return cudaGetLastError();
 }
 
-cudaError_t launch_qk_norm_rope(const PrologueProblem &p, cudaStream_t stream) {
-  if (!p.tokens || (!p.q && !p.k)) return cudaSuccess;
+cudaError_t launch_qk_norm_rope(const PrologueProblem &problem, cudaStream_t stream) {
+  if (!problem.tokens || (!problem.q && !problem.k)) return cudaSuccess;
+  if (problem.dim > 256) return cudaErrorInvalidValue;
+  // Inverse frequencies once per launch, in double and rounded once to float: the same
+  // value rope_inv_freq gives on the device (and the CPU oracle uses).
+  PrologueProblem p = problem;
+  for (uint32_t c = 0; c < p.dim / 2; ++c)
+    p.inv_freq[c] = (float)std::pow((double)p.theta, -2.0 * (double)c / (double)p.dim);
   switch (p.dim) {
     case 32: return launch_prologue_e<1>(p, stream);
     case 64: return launch_prologue_e<2>(p, stream);
