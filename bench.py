@@ -1,18 +1,34 @@
 #!/usr/bin/env python
 """Benchmark of the encoder-attention hot path on B200 (one process per GPU).
 
-Default workload (one step = one pass of the hot path over one batch):
-  Qwen3-Embedding-0.6B attention layer: 32 sequences per GPU,
-  right-padded to L=512, lengths ~ U[32, 512] (seeded), 16 query / 8 kv heads,
-  head_dim 128, causal, q/k RMSNorm (eps 1e-6, bf16 weights 1+N(0,0.02)) + RoPE
-  (theta 1e6), bf16 N(0,1) inputs, fp32 softmax/accumulation, fp32 output.
-  One step = the k prologue kernel (RMSNorm + RoPE of the valid k rows) + the tcgen05
-  attention kernel, which applies the q RMSNorm + RoPE to each Q tile in shared memory.
+One step = one pass of the hot path over one batch of synthetic input.  Workloads
+(--workload), each restating one of the benchmark configurations with seeded data:
 
-Multi-GPU (torchrun, N ranks): a global batch of 32*N sequences is split across ranks
-by sequence (longest-processing-time first); shards are independent, so there is no
-collective on the data path (torch.distributed is used only for the barrier and the
-max-over-ranks of the timings).  Per-GPU work is fixed as N grows: scaling "weak".
+  qwen_padded  (default) Qwen3-Embedding-0.6B attention layer: 32 sequences per GPU,
+               right-padded to L=512, lengths ~ U[32, 512], 16 query / 8 kv heads,
+               head_dim 128, causal, q/k RMSNorm (eps 1e-6, bf16 weights 1+N(0,0.02)) +
+               RoPE (theta 1e6), bf16 N(0,1) inputs, fp32 softmax/accumulation, fp32 out.
+               Step = the k prologue kernel (RMSNorm + RoPE of the valid k rows) + the
+               tcgen05 attention kernel, which applies the q RMSNorm + RoPE to each Q tile
+               in shared memory.  Weak scaling: 32*N sequences over N GPUs.
+  qwen_varlen  the same layer on 256 sequences packed by cu_seqlens (no padding), lengths
+               log-normal (median 96, sigma 0.8) clipped to [2, 512].  The 256 sequences
+               are split across the N GPUs: strong scaling.
+  bge          BGE-small attention block: batch 4, L=128, 12 heads x 32, bidirectional,
+               fp32 N(0,1)/sqrt(32), lengths ~ U[16, 128] (3 MB: a latency figure).
+  bge_scaled   the same distribution at batch 4096 per GPU (2.5 GB of contract bytes), the
+               bandwidth figure of the head_dim-32 kernel.
+  tails_qwen / tails_bge
+               short-sequence tails: 32 sequences of length U[2, 32], packed, bf16 N(0,1),
+               Qwen shape (with the q/k prologue) or BGE shape (bidirectional).
+  pool_qwen    the step after the last layer: final hidden states [32, 512, 1024] fp32 per
+               GPU, lengths ~ U[32, 512]; the final RMSNorm of the last valid token of
+               each sequence fused with last-token pooling and L2 normalisation
+               (metric: sequences/s; a latency figure, 32 rows of 4 KB).
+
+Multi-GPU (torchrun, N ranks): sequences are assigned to ranks longest-first; shards are
+independent, so there is no collective on the data path (torch.distributed is used only
+for the barrier and the max-over-ranks of the timings).
 
 Timing: W untimed warm-up steps, then K steps bracketed by barrier + synchronize; each
 step is timed with CUDA events on the launching stream and L2 is flushed (256 MiB
@@ -44,9 +60,11 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "attention tokens/s at Qwen3-0.6B shape & % of bf16 TC peak, 1/2/4/8 B200"
-SEQS_PER_GPU = 32
-SEQ_LEN = 512
-LENGTH_SEED = 2
+WORKLOADS = ("qwen_padded", "qwen_varlen", "bge", "bge_scaled", "tails_qwen", "tails_bge",
+             "pool_qwen")
+# FP32 FMA throughput of the SIMT cores: 148 SMs x 128 lanes x 2 flops x 1.965 GHz
+# (nominal; packed f32x2 FMA doubles it).  Used for the head_dim-32 compute floor.
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 
 
 def parse_args():
@@ -55,6 +73,9 @@ def parse_args():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=WORKLOADS, default="qwen_padded")
+    p.add_argument("--batch", type=int, default=4096,
+                   help="per-GPU batch of bge_scaled (smaller for profiler captures)")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--soak-seconds", type=float, default=1.5,
@@ -72,25 +93,71 @@ def measured_peaks() -> dict:
             "source": "fallback"}
 
 
-def profile_traffic() -> dict | None:
+def profile_traffic(workload: str) -> dict:
+    """DRAM bytes per launch from ncu captures (profiles/traffic.json), per workload."""
     path = ROOT / "profiles" / "traffic.json"
     if path.exists():
-        return json.loads(path.read_text())
-    return None
+        return json.loads(path.read_text()).get(workload, {})
+    return {}
 
 
-def global_lengths(world: int) -> np.ndarray:
-    rng = np.random.default_rng(LENGTH_SEED)
-    return rng.integers(32, SEQ_LEN + 1, size=SEQS_PER_GPU * world)
-
-
-def rank_workload(rank: int, world: int):
+# ---- workloads ----------------------------------------------------------------------------
+def make_workload(name: str, rank: int, world: int, scaled_batch: int = 4096):
     from tessery_b200 import shard_sequences, workloads
 
-    lengths = global_lengths(world)
-    owned = shard_sequences(lengths, world, causal=True)[rank]
-    return workloads.qwen_padded(batch=len(owned), seq=SEQ_LEN, seed=LENGTH_SEED + 1000 * rank,
-                                 lengths=lengths[owned])
+    if name == "qwen_padded":
+        lengths = np.random.default_rng(2).integers(32, 513, size=32 * world)
+        owned = shard_sequences(lengths, world, causal=True)[rank]
+        return workloads.qwen_padded(batch=len(owned), seq=512, seed=2 + 1000 * rank,
+                                     lengths=lengths[owned])
+    if name == "qwen_varlen":
+        lengths = workloads.varlen_lengths(256, 3)
+        owned = shard_sequences(lengths, world, causal=True)[rank]
+        return workloads.qwen_varlen(seed=3 + 1000 * rank, lengths=lengths[owned])
+    if name == "bge":
+        return workloads.bge(batch=4, seq=128, seed=1 + 1000 * rank)
+    if name == "bge_scaled":
+        return workloads.bge(batch=scaled_batch, seq=128, seed=1 + 1000 * rank)
+    if name == "tails_qwen":
+        return workloads.short_tails("qwen", batch=32, seed=4 + 1000 * rank)
+    if name == "tails_bge":
+        return workloads.short_tails("bge", batch=32, seed=4 + 1000 * rank)
+    raise ValueError(name)
+
+
+def scaling_of(name: str) -> str:
+    return "strong" if name == "qwen_varlen" else "weak"
+
+
+def metric_of(name: str) -> str:
+    if name == "qwen_padded":
+        return METRIC
+    shape = "BGE-small d32" if "bge" in name else "Qwen3-0.6B"
+    return f"attention tokens/s, {name} ({shape} shape)"
+
+
+def config_block(name: str, w, world: int) -> dict:
+    per_gpu = {"qwen_padded": 32, "bge": 4, "bge_scaled": w.batch, "tails_qwen": 32,
+               "tails_bge": 32}
+    glob = 256 if name == "qwen_varlen" else per_gpu[name] * world
+    cfg = {"workload": name, "global_batch": glob, "heads": w.heads, "kv_heads": w.kv_heads,
+           "head_dim": w.dim, "causal": w.causal, "layout": w.layout,
+           "input_dtype": w.in_dtype, "output_dtype": "f32",
+           "parallelism": f"sequence shards x{world} (longest first), no collective"}
+    if w.layout == "padded":
+        cfg["seq_len"] = w.seq
+    else:
+        cfg["max_len"] = w.seq
+    cfg["lengths"] = {"qwen_padded": "U[32,512] seed 2", "qwen_varlen":
+                      "lognormal(ln 96, 0.8) clip [2,512] seed 3", "bge": "U[16,128] seed 1",
+                      "bge_scaled": "U[16,128] seed 1", "tails_qwen": "U[2,32] seed 4",
+                      "tails_bge": "U[2,32] seed 4"}[name]
+    if w.q_norm_weight is not None:
+        cfg["prologue"] = "q/k RMSNorm eps 1e-6 + RoPE theta 1e6"
+    contract = w.q.nbytes + w.k.nbytes + w.v.nbytes + w.q.size * 4
+    cfg["l2"] = (f"flushed between timed steps (256 MiB write); contract bytes "
+                 f"{contract / 1e6:.1f} MB per GPU")
+    return cfg
 
 
 # ---- clocks ------------------------------------------------------------------------------
@@ -163,20 +230,36 @@ def physical_gpu(local_rank: int) -> int:
 
 # ---- CPU formula (reference arm and cpu_baseline) ------------------------------------------
 def cpu_formula(w, n_seqs: int):
-    """The reference's float32 NumPy formula (q/k RMSNorm + RoPE, then attention) on the
-    first n_seqs sequences of the workload; returns (seconds, valid tokens)."""
+    """The reference's float32 NumPy formula (q/k RMSNorm + RoPE when the workload has
+    them, then attention) on the first n_seqs sequences of the workload; returns
+    (seconds, valid tokens)."""
     import oracle
     from tessery_b200.workloads import from_bf16_bits
 
-    sel = slice(0, n_seqs)
-    q, k, v = (from_bf16_bits(a[sel]) for a in (w.q, w.k, w.v))
-    lengths = w.lengths[sel]
-    start = time.perf_counter()
-    pos = np.broadcast_to(np.arange(w.seq), (q.shape[0], w.seq))
-    qn, kn = oracle.qk_norm_rope(q, k, w.q_norm_weight, w.k_norm_weight, w.eps, w.theta, pos,
-                                 dtype=np.float32)
-    oracle.attention_padded(qn, kn, v, lengths, True, w.scale, dtype=np.float32)
-    return time.perf_counter() - start, int(np.minimum(lengths, w.seq).sum())
+    widen = from_bf16_bits if w.in_dtype == "bf16" else (lambda a: a)
+    n_seqs = min(n_seqs, w.batch)
+    if w.layout == "padded":
+        q, k, v = (widen(a[:n_seqs]) for a in (w.q, w.k, w.v))
+        lengths = w.lengths[:n_seqs]
+        tokens = int(np.minimum(lengths, w.seq).sum())
+        start = time.perf_counter()
+        if w.q_norm_weight is not None:
+            pos = np.broadcast_to(np.arange(w.seq), (q.shape[0], w.seq))
+            q, k = oracle.qk_norm_rope(q, k, w.q_norm_weight, w.k_norm_weight, w.eps, w.theta,
+                                       pos, dtype=np.float32)
+        oracle.attention_padded(q, k, v, lengths, w.causal, w.scale, dtype=np.float32)
+    else:
+        cu = w.cu_seqlens[: n_seqs + 1]
+        end = int(cu[-1])
+        q, k, v = (widen(a[:end]) for a in (w.q, w.k, w.v))
+        tokens = end
+        start = time.perf_counter()
+        if w.q_norm_weight is not None:
+            pos = np.concatenate([np.arange(cu[i + 1] - cu[i]) for i in range(n_seqs)])
+            q, k = oracle.qk_norm_rope(q, k, w.q_norm_weight, w.k_norm_weight, w.eps, w.theta,
+                                       pos, dtype=np.float32)
+        oracle.attention_varlen(q, k, v, cu, w.causal, w.scale, dtype=np.float32)
+    return time.perf_counter() - start, tokens
 
 
 def cpu_threads() -> int:
@@ -189,21 +272,6 @@ def cpu_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_baseline_run(w, target_seconds: float = 12.0) -> dict:
-    seconds, tokens = cpu_formula(w, 2)  # warm BLAS, estimate
-    per_seq = seconds / 2
-    n = int(max(2, min(w.batch, target_seconds / max(per_seq, 1e-6) / 2)))
-    times = []
-    for _ in range(2):
-        seconds, tokens = cpu_formula(w, n)
-        times.append(seconds)
-    sec = min(times)
-    return {"value": tokens / sec, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
-            "sample": f"first {n} of {w.batch} sequences of the workload (valid tokens {tokens}),"
-                      f" float32 NumPy, q/k prologue included, best of 2",
-            "cpu_model": cpu_model()}
-
-
 def cpu_model() -> str:
     try:
         for line in Path("/proc/cpuinfo").read_text().splitlines():
@@ -214,12 +282,25 @@ def cpu_model() -> str:
     return "unknown"
 
 
-def config_block(world: int) -> dict:
-    return {"workload": "qwen3_0.6b_attention_padded_b32_l512", "global_batch": SEQS_PER_GPU * world,
-            "seq_len": SEQ_LEN, "heads": 16, "kv_heads": 8, "head_dim": 128, "causal": True,
-            "prologue": "q/k RMSNorm eps 1e-6 + RoPE theta 1e6",
-            "lengths": "U[32,512] seeded", "parallelism": f"sequence shards x{world} (LPT), no collective",
-            "l2": "flushed between timed steps (256 MiB write); inputs 134 MB > L2"}
+def sample_size(w, target_seconds: float) -> int:
+    """Sequences of the workload that take about target_seconds through cpu_formula."""
+    n0 = min(2, w.batch)
+    seconds, _ = cpu_formula(w, n0)  # also warms BLAS
+    return int(max(1, min(w.batch, target_seconds / max(seconds / n0, 1e-6))))
+
+
+def cpu_baseline_run(w, target_seconds: float = 6.0) -> dict:
+    n = sample_size(w, target_seconds)
+    times = []
+    for _ in range(2):
+        seconds, tokens = cpu_formula(w, n)
+        times.append(seconds)
+    sec = min(times)
+    prologue = ", q/k prologue included" if w.q_norm_weight is not None else ""
+    return {"value": tokens / sec, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+            "sample": f"first {n} of {w.batch} sequences of the workload (valid tokens {tokens}),"
+                      f" float32 NumPy{prologue}, best of 2",
+            "cpu_model": cpu_model()}
 
 
 def run_reference(args):
@@ -227,10 +308,9 @@ def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    w = rank_workload(0, 1)
+    w = make_workload(args.workload, 0, world, args.batch)
     # Size each step so the run stays within a few minutes.
-    sec2, _ = cpu_formula(w, 2)
-    n = int(max(1, min(w.batch, 1.0 / max(sec2 / 2, 1e-6))))
+    n = sample_size(w, 1.0)
     for _ in range(args.warmup):
         cpu_formula(w, n)
     total, tokens = 0.0, 0
@@ -239,14 +319,16 @@ def run_reference(args):
         total += s
         tokens += t
     value = tokens / total
-    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": config_block(1), "impl": "reference",
+    line = {"metric": metric_of(args.workload), "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+            "scaling": scaling_of(args.workload), "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": config_block(args.workload, w, world),
+            "impl": "reference",
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu_threads(),
                              "kind": "port",
-                             "sample": f"first {n} of 32 sequences per step, float32 NumPy "
-                                       "restatement of the reference formula with q/k prologue",
+                             "sample": f"first {n} of {w.batch} sequences per step, float32 "
+                                       "NumPy restatement of the reference formula",
                              "cpu_model": cpu_model()},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -274,18 +356,31 @@ def run_ours(args):
     from tessery_b200.host import pinned_copy, pinned_empty
 
     rt = CudaRuntime(local)
-    w = rank_workload(rank, world)
-    B, L, H, KV, D = w.batch, w.seq, w.heads, w.kv_heads, w.dim
+    name = args.workload
+    w = make_workload(name, rank, world, args.batch)
+    H, KV, D = w.heads, w.kv_heads, w.dim
+    in_code = TX_BF16 if w.in_dtype == "bf16" else TX_F32
     dev = torch.device("cuda", local)
 
     def to_dev(a):
         return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
 
     q, k, v = to_dev(w.q), to_dev(w.k), to_dev(w.v)
-    lengths = to_dev(w.lengths.astype(np.uint32).view(np.int32))
-    qw, kw = to_dev(w.q_norm_weight), to_dev(w.k_norm_weight)
-    kn = torch.empty_like(k)
-    out = torch.empty((B, L, H, D), dtype=torch.float32, device=dev)
+    prologue = w.q_norm_weight is not None
+    if prologue:
+        qw, kw = to_dev(w.q_norm_weight), to_dev(w.k_norm_weight)
+        kn = torch.empty_like(k)
+    out = torch.empty(w.q.shape, dtype=torch.float32, device=dev)
+    if w.layout == "padded":
+        lengths = to_dev(w.lengths.astype(np.uint32).view(np.int32))
+        lengths_host = w.lengths.astype(np.uint32)
+        B, L = w.q.shape[:2]
+        tokens_in_layout = B * L
+    else:
+        cu = to_dev(w.cu_seqlens.astype(np.int32))
+        cu_host = w.cu_seqlens.astype(np.int32)
+        nseq, total = w.batch, int(cu_host[-1])
+        tokens_in_layout = total
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     # A dedicated stream: the legacy default stream has handle 0, which the library reads
     # as "use the context's own stream".
@@ -293,29 +388,50 @@ def run_ours(args):
     torch.cuda.set_stream(stream)
     sptr = stream.cuda_stream
     assert sptr != 0
-    lengths_host = w.lengths.astype(np.uint32)
+    marks = {"mid": None}
 
     def step():
-        # k: RMSNorm + RoPE of the valid rows into kn (bf16); q: fused into the attention
-        # kernel, which normalises and rotates each Q tile in shared memory.
-        rt.qk_norm_rope_device(None, k.data_ptr(), None, kn.data_ptr(), tokens=B * L, seq=L,
-                               heads=H, kv_heads=KV, dim=D, q_norm_weight=None,
-                               k_norm_weight=kw.data_ptr(), lengths=lengths.data_ptr(),
-                               in_dtype=TX_BF16, out_dtype=TX_BF16, eps=w.eps, theta=w.theta,
-                               stream=sptr)
-        mid.record(stream)
-        rt.attention_padded_device(q.data_ptr(), kn.data_ptr(), v.data_ptr(),
-                                   lengths.data_ptr(), out.data_ptr(), batch=B, seq=L, heads=H,
-                                   kv_heads=KV, dim=D, in_dtype=TX_BF16, out_dtype=TX_F32,
-                                   causal=True, scale=w.scale, lengths_host=lengths_host,
-                                   q_norm_weight=qw.data_ptr(), eps=w.eps, theta=w.theta,
-                                   stream=sptr)
+        k_in = k
+        if prologue:
+            # k: RMSNorm + RoPE of the valid rows into kn (bf16); q: fused into the
+            # attention kernel, which normalises and rotates each Q tile in shared memory.
+            if w.layout == "padded":
+                rt.qk_norm_rope_device(None, k.data_ptr(), None, kn.data_ptr(),
+                                       tokens=tokens_in_layout, seq=L, heads=H, kv_heads=KV,
+                                       dim=D, q_norm_weight=None, k_norm_weight=kw.data_ptr(),
+                                       lengths=lengths.data_ptr(), in_dtype=in_code,
+                                       out_dtype=in_code, eps=w.eps, theta=w.theta,
+                                       stream=sptr)
+            else:
+                rt.qk_norm_rope_device(None, k.data_ptr(), None, kn.data_ptr(),
+                                       tokens=tokens_in_layout, seq=w.seq, heads=H,
+                                       kv_heads=KV, dim=D, q_norm_weight=None,
+                                       k_norm_weight=kw.data_ptr(), cu_seqlens=cu.data_ptr(),
+                                       nseq=nseq, in_dtype=in_code, out_dtype=in_code,
+                                       eps=w.eps, theta=w.theta, stream=sptr)
+            k_in = kn
+        marks["mid"].record(stream)
+        extra = dict(q_norm_weight=qw.data_ptr(), eps=w.eps, theta=w.theta) if prologue else {}
+        if w.layout == "padded":
+            rt.attention_padded_device(q.data_ptr(), k_in.data_ptr(), v.data_ptr(),
+                                       lengths.data_ptr(), out.data_ptr(), batch=B, seq=L,
+                                       heads=H, kv_heads=KV, dim=D, in_dtype=in_code,
+                                       out_dtype=TX_F32, causal=w.causal, scale=w.scale,
+                                       lengths_host=lengths_host, stream=sptr, **extra)
+        else:
+            rt.attention_varlen_device(q.data_ptr(), k_in.data_ptr(), v.data_ptr(),
+                                       cu.data_ptr(), out.data_ptr(), nseq=nseq, total=total,
+                                       max_len=w.seq, heads=H, kv_heads=KV, dim=D,
+                                       in_dtype=in_code, out_dtype=TX_F32, causal=w.causal,
+                                       scale=w.scale, cu_seqlens_host=cu_host, stream=sptr,
+                                       **extra)
 
-    mid = torch.cuda.Event(enable_timing=True)
+    marks["mid"] = torch.cuda.Event(enable_timing=True)
     for _ in range(max(args.warmup, 3)):
         flush.zero_()
         step()
     torch.cuda.synchronize()
+    kernel = rt.last_kernel()
 
     # Clock sampler: soak loop of the same step, then the timed region.
     sampler = ClockSampler(physical_gpu(local))
@@ -323,6 +439,7 @@ def run_ours(args):
     t_end = time.perf_counter() + args.soak_seconds
     while time.perf_counter() < t_end:
         for _ in range(20):
+            flush.zero_()
             step()
         torch.cuda.synchronize()
 
@@ -337,7 +454,7 @@ def run_ours(args):
     for i in range(args.steps):
         flush.zero_()
         starts[i].record(stream)
-        mid = mids[i]
+        marks["mid"] = mids[i]
         step()
         ends[i].record(stream)
     torch.cuda.synchronize()
@@ -368,13 +485,19 @@ def run_ours(args):
 
     # e2e through the public NumPy API with page-locked host buffers.
     hq, hk, hv = pinned_copy(w.q), pinned_copy(w.k), pinned_copy(w.v)
-    hl = pinned_copy(w.lengths.astype(np.uint32))
-    hqw, hkw = pinned_copy(w.q_norm_weight), pinned_copy(w.k_norm_weight)
     hout = pinned_empty(w.q.shape, np.float32)
+    if w.layout == "padded":
+        hsel = {"lengths": pinned_copy(w.lengths.astype(np.uint32))}
+    else:
+        hsel = {"cu_seqlens": pinned_copy(w.cu_seqlens.astype(np.int32))}
+    hpro = {}
+    if prologue:
+        hpro = {"q_norm_weight": pinned_copy(w.q_norm_weight),
+                "k_norm_weight": pinned_copy(w.k_norm_weight), "eps": w.eps, "theta": w.theta}
 
     def e2e_step():
-        return attention(hq, hk, hv, lengths=hl, causal=True, q_norm_weight=hqw,
-                         k_norm_weight=hkw, eps=w.eps, theta=w.theta, runtime=rt, out=hout)
+        return attention(hq, hk, hv, causal=w.causal, scale=w.scale, runtime=rt, out=hout,
+                         **hsel, **hpro)
 
     e2e_step()
     if dist:
@@ -383,68 +506,285 @@ def run_ours(args):
     for _ in range(args.e2e_steps):
         result = e2e_step()
     e2e_s = time.perf_counter() - t0
-    assert np.isfinite(result[0, : int(w.lengths[0])]).all()
+    first = int(w.seq_lengths[0])
+    check = result[0, :first] if w.layout == "padded" else result[:first]
+    assert np.isfinite(check).all()
     e2e_stats = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(e2e_stats, op=dist.ReduceOp.MAX)
     e2e_tokens_all = tokens_all / args.steps * args.e2e_steps
     e2e_value = e2e_tokens_all / float(e2e_stats[0])
-    h2d = hq.nbytes + hk.nbytes + hv.nbytes + hl.nbytes + hqw.nbytes + hkw.nbytes
+    h2d = hq.nbytes + hk.nbytes + hv.nbytes + sum(
+        a.nbytes for a in [*hsel.values(), *[x for x in hpro.values()
+                                             if isinstance(x, np.ndarray)]])
     d2h = result.nbytes
 
-    peaks = measured_peaks()
-    att_mean = statistics.mean(att_ms) * 1e-3
-    pro_mean = statistics.mean(pro_ms) * 1e-3
-    traffic = profile_traffic()
-    valid = w.valid_tokens()
-    kv_valid_bytes = valid * KV * D * 2  # one of k or v, valid rows, bf16
-    # Contract I/O of the attention launch: every q row (padded rows are outputs too),
-    # the valid k/v rows, the fp32 output of every row.
-    att_bytes = w.q.nbytes + 2 * kv_valid_bytes + out.numel() * 4 + w.q_norm_weight.nbytes
-    t_hbm = att_bytes / (peaks["hbm_gbs"] * 1e9)
-    t_tc = flops / (peaks["bf16_tflops"] * 1e12)
-    tensor = {"achieved": flops / att_mean / 1e12, "peak": peaks["bf16_tflops"],
-              "unit": "TFLOP/s", "frac": flops / att_mean / 1e12 / peaks["bf16_tflops"],
-              "algorithmic_flops_per_launch": flops}
-    hbm = {"achieved": att_bytes / att_mean / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-           "frac": att_bytes / att_mean / 1e9 / peaks["hbm_gbs"],
-           "algorithmic_bytes_per_launch": att_bytes}
-    bound = "hbm" if t_hbm >= t_tc else "tensor"
-    main = hbm if bound == "hbm" else tensor
-    roof = {"bound": bound, "kernel": "attn_tc_kernel", "achieved": main["achieved"],
-            "peak": main["peak"], "unit": main["unit"], "frac": main["frac"],
-            "peak_source": f"{peaks['source']} (kernel timed alone: burst figures)",
-            "traffic": traffic.get("attn_tc_kernel_bytes_per_launch") if traffic else None,
-            "hbm": hbm, "tensor": tensor,
-            "floor_us": {"hbm": 1e6 * t_hbm, "tensor": 1e6 * t_tc}}
-    pro_bytes = 2 * kv_valid_bytes + w.k_norm_weight.nbytes
-    prologue_roof = {"bound": "hbm", "kernel": "qk_norm_rope_kernel (k rows)",
-                     "achieved": pro_bytes / pro_mean / 1e9, "peak": peaks["hbm_gbs"],
-                     "unit": "GB/s", "frac": pro_bytes / pro_mean / 1e9 / peaks["hbm_gbs"],
-                     "algorithmic_bytes_per_launch": pro_bytes,
-                     "traffic": traffic.get("qk_norm_rope_bytes_per_launch") if traffic else None}
-    achieved = tensor["achieved"]
+    roof, prologue_roof = rooflines(w, name, kernel, statistics.mean(att_ms) * 1e-3,
+                                    statistics.mean(pro_ms) * 1e-3 if prologue else None)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_run(w)
 
     if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        peaks = measured_peaks()
+        line = {"metric": metric_of(name), "value": value, "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": 1e3 * total_max / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic (seeded N(0,1) bf16 q/k/v, lengths U[32,512])",
-                "config": config_block(world), "roofline": roof, "prologue_roofline": prologue_roof,
-                "attention_ms": 1e3 * att_mean, "prologue_ms": 1e3 * pro_mean,
-                "useful_tflops_attention": achieved,
+                "scaling": scaling_of(name), "vs_baseline": None, "dtype": w.in_dtype,
+                "data": f"synthetic (seeded, {w.in_dtype} inputs; lengths "
+                        f"{config_block(name, w, world)['lengths']})",
+                "config": config_block(name, w, world), "roofline": roof,
+                "attention_ms": statistics.mean(att_ms),
+                "useful_tflops_attention": flops / (statistics.mean(att_ms) * 1e-3) / 1e12,
                 "tc_frac_of_dense_peak_incl_prologue": flops / (total_s / args.steps) / 1e12
                 / peaks["bf16_tflops"],
-                "cpu_baseline": cpu,
+                "route": kernel, "cpu_baseline": cpu,
                 "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
                         "path": "tessery_b200.attention (NumPy in/out, pinned host buffers)"},
                 "gpu_launches": launches, "wall_s_timed_region": wall, "clocks": clocks}
+        if prologue_roof:
+            line["prologue_roofline"] = prologue_roof
+            line["prologue_ms"] = statistics.mean(pro_ms)
+        print(json.dumps(line), flush=True)
+    rt.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+def rooflines(w, name: str, kernel: str, att_s: float, pro_s: float | None):
+    """Roofline of the attention launch and, when present, of the k prologue launch.
+
+    Algorithmic bytes of the attention launch (contract I/O): every q row (padded rows
+    produce outputs too), the valid k and v rows, the fp32 output of every q row, the q
+    norm weight when the q prologue is fused.  FLOPs: 4 * head_dim * heads per useful
+    (query, key) pair of valid query rows.
+    """
+    peaks = measured_peaks()
+    traffic = profile_traffic(name)
+    esz = 2 if w.in_dtype == "bf16" else 4
+    valid = w.valid_tokens()
+    kv_valid_bytes = valid * w.kv_heads * w.dim * esz  # one of k or v
+    fused_w = w.q_norm_weight.nbytes if w.q_norm_weight is not None else 0
+    att_bytes = w.q.nbytes + 2 * kv_valid_bytes + w.q.size * 4 + fused_w
+    flops = w.useful_flops()
+    t_hbm = att_bytes / (peaks["hbm_gbs"] * 1e9)
+    hbm = {"achieved": att_bytes / att_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+           "frac": att_bytes / att_s / 1e9 / peaks["hbm_gbs"],
+           "algorithmic_bytes_per_launch": att_bytes}
+    kname = {"tc_bf16_d128": "attn_tc_kernel", "d32": "attention_d32_kernel",
+             "simt": "attention_simt_kernel"}.get(kernel, kernel)
+    if kernel == "tc_bf16_d128":
+        t_c = flops / (peaks["bf16_tflops"] * 1e12)
+        comp = {"achieved": flops / att_s / 1e12, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": flops / att_s / 1e12 / peaks["bf16_tflops"],
+                "algorithmic_flops_per_launch": flops}
+        comp_bound, comp_key = "tensor", "tensor"
+    else:
+        t_c = flops / (FP32_NOMINAL_TFLOPS * 1e12)
+        comp = {"achieved": flops / att_s / 1e12, "peak": FP32_NOMINAL_TFLOPS,
+                "unit": "TFLOP/s", "frac": flops / att_s / 1e12 / FP32_NOMINAL_TFLOPS,
+                "algorithmic_flops_per_launch": flops,
+                "peak_source": "nominal FP32 FMA, 148 SMs x 128 lanes x 2 x 1.965 GHz"}
+        comp_bound, comp_key = "fp32", "fp32"
+    main = hbm if t_hbm >= t_c or comp_bound == "fp32" else comp
+    bound = "hbm" if main is hbm else comp_bound
+    roof = {"bound": bound, "kernel": kname, "achieved": main["achieved"],
+            "peak": main["peak"], "unit": main["unit"], "frac": main["frac"],
+            "peak_source": f"{peaks['source']} (kernel timed alone: burst figures)",
+            "traffic": traffic.get(kname), "hbm": hbm, comp_key: comp,
+            "floor_us": {"hbm": 1e6 * t_hbm, comp_key: 1e6 * t_c},
+            "launch_us": 1e6 * att_s}
+    pro = None
+    if pro_s is not None:
+        pro_bytes = 2 * kv_valid_bytes + w.k_norm_weight.nbytes
+        pro = {"bound": "hbm", "kernel": "qk_norm_rope_kernel (k rows)",
+               "achieved": pro_bytes / pro_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+               "frac": pro_bytes / pro_s / 1e9 / peaks["hbm_gbs"],
+               "algorithmic_bytes_per_launch": pro_bytes,
+               "traffic": traffic.get("qk_norm_rope_kernel"), "launch_us": 1e6 * pro_s}
+    return roof, pro
+
+
+# ---- pooling (the step after the last layer) --------------------------------------------
+def pool_workload(rank: int):
+    from tessery_b200.workloads import to_bf16_bits
+
+    rng = np.random.default_rng(5 + 1000 * rank)
+    b, seq, cols = 32, 512, 1024
+    lengths = rng.integers(32, seq + 1, size=b).astype(np.uint32)
+    x = rng.standard_normal(size=(b, seq, cols), dtype=np.float32)
+    w = to_bf16_bits(1.0 + 0.02 * rng.standard_normal(cols).astype(np.float32))
+    return x, lengths, w
+
+
+def pool_config(world: int) -> dict:
+    return {"workload": "pool_qwen", "global_batch": 32 * world, "seq_len": 512, "cols": 1024,
+            "dim": 1024, "pooling": "last token", "final_norm": "RMSNorm eps 1e-6 fused",
+            "lengths": "U[32,512] seed 5", "input_dtype": "f32",
+            "parallelism": f"sequence shards x{world}, no collective",
+            "l2": "flushed between timed steps (256 MiB write)"}
+
+
+def pool_cpu(x, lengths, w, n: int):
+    """The reference's order: rms_norm over every token (qwen3.py:281), then
+    pool_project (kernels.metal:339-349), float32 NumPy; returns seconds."""
+    import oracle
+
+    start = time.perf_counter()
+    normed = oracle.rms_norm(x[:n], w, 1e-6, dtype=np.float32)
+    oracle.pool_project(normed, lengths[:n], x.shape[2], False, dtype=np.float32)
+    return time.perf_counter() - start
+
+
+def run_pool_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    x, lengths, w = pool_workload(0)
+    n = x.shape[0]
+    for _ in range(args.warmup):
+        pool_cpu(x, lengths, w, n)
+    total = sum(pool_cpu(x, lengths, w, n) for _ in range(args.steps))
+    value = n * args.steps / total
+    line = {"metric": "pooled embeddings/s (final RMSNorm + last-token pool + L2)",
+            "value": value, "unit": "sequences/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": pool_config(1), "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": "sequences/s", "cores": cpu_threads(),
+                             "kind": "port",
+                             "sample": f"all {n} sequences per step: rms_norm of every token "
+                                       "then pool_project, float32 NumPy",
+                             "cpu_model": cpu_model()},
+            "e2e": {"value": value, "unit": "sequences/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_pool(args):
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    from tessery_b200 import CudaRuntime, pool_project
+    from tessery_b200.host import pinned_copy, pinned_empty
+
+    rt = CudaRuntime(local)
+    x, lengths, w = pool_workload(rank)
+    b, seq, cols = x.shape
+    dev = torch.device("cuda", local)
+    xd = torch.from_numpy(x).to(dev)
+    ld = torch.from_numpy(lengths.view(np.int32)).to(dev)
+    wd = torch.from_numpy(w.view(np.int16)).to(dev)
+    out = torch.empty((b, cols), dtype=torch.float32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    sptr = stream.cuda_stream
+    assert sptr != 0
+
+    def step():
+        rt.pool_project_device(xd.data_ptr(), out.data_ptr(), batch=b, cols=cols, dim=cols,
+                               seq=seq, lengths=ld.data_ptr(), norm_weight=wd.data_ptr(),
+                               eps=1e-6, stream=sptr)
+
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(physical_gpu(local))
+    sampler.start()
+    t_end = time.perf_counter() + args.soak_seconds
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            flush.zero_()
+            step()
+        torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = rt.launch_count()
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    launches = rt.launch_count() - launches0
+    clocks = sampler.stop()
+    rt.sync(sptr)
+    ms = [s.elapsed_time(e) for s, e in zip(starts, ends, strict=True)]
+    total_s = sum(ms) * 1e-3
+    stats = torch.tensor([total_s], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    value = b * world * args.steps / float(stats[0])
+
+    hx, hl, hw = pinned_copy(x), pinned_copy(lengths), pinned_copy(w)
+    hout = pinned_empty((b, cols), np.float32)
+
+    def e2e_step():
+        return pool_project(hx, lengths=hl, norm_weight=hw, eps=1e-6, runtime=rt, out=hout)
+
+    e2e_step()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        result = e2e_step()
+    e2e = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
+    assert np.isfinite(result).all()
+    e2e_value = b * world * args.e2e_steps / float(e2e[0])
+
+    peaks = measured_peaks()
+    mean_s = statistics.mean(ms) * 1e-3
+    nbytes = b * cols * 4 + w.nbytes + b * 4 + b * cols * 4  # picked rows, weight, lengths, out
+    roof = {"bound": "hbm", "kernel": "pool_project_kernel",
+            "achieved": nbytes / mean_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": nbytes / mean_s / 1e9 / peaks["hbm_gbs"],
+            "algorithmic_bytes_per_launch": nbytes, "launch_us": 1e6 * mean_s,
+            "peak_source": f"{peaks['source']} (kernel timed alone: burst figures)",
+            "traffic": profile_traffic("pool_qwen").get("pool_project_kernel"),
+            "note": "latency-bound: 32 rows of 4 KB per launch"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        times = [pool_cpu(x, lengths, w, b) for _ in range(3)]
+        cpu = {"value": b / min(times), "unit": "sequences/s", "cores": cpu_threads(),
+               "kind": "port", "sample": f"all {b} sequences: rms_norm of every token then "
+                                        "pool_project, float32 NumPy, best of 3",
+               "cpu_model": cpu_model()}
+    if rank == 0:
+        line = {"metric": "pooled embeddings/s (final RMSNorm + last-token pool + L2)",
+                "value": value, "unit": "sequences/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": 1e3 * float(stats[0]) / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic (seeded N(0,1) fp32 hidden states)",
+                "config": pool_config(world), "roofline": roof, "route": "pool_project",
+                "cpu_baseline": cpu,
+                "e2e": {"value": e2e_value, "unit": "sequences/s",
+                        "h2d_bytes_per_step": hx.nbytes + hl.nbytes + hw.nbytes,
+                        "d2h_bytes_per_step": result.nbytes, "steps": args.e2e_steps,
+                        "path": "tessery_b200.pool_project (NumPy in/out, pinned host buffers)"},
+                "gpu_launches": launches, "clocks": clocks}
         print(json.dumps(line), flush=True)
     rt.close()
     if dist:
@@ -453,6 +793,9 @@ def run_ours(args):
 
 def main():
     args = parse_args()
+    if args.workload == "pool_qwen":
+        run_pool_reference(args) if args.impl == "reference" else run_pool(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

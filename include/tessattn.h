@@ -184,6 +184,23 @@ int tx_qk_norm_rope(void *ctx, const void *q, const void *k, void *q_out, void *
                     int in_dtype, int out_dtype, const uint16_t *q_norm_w,
                     const uint16_t *k_norm_w, float eps, float theta, void *stream);
 
+/* Embedding pooling after the last layer (replaces the "pool_project" dispatch,
+ * kernels.metal:339-349, and, with norm_w, the final rms_norm before it,
+ * qwen3.py:281-290).  For each sequence b, takes one row of x -- the last valid token
+ * (first_token = 0, Qwen3 last-token pooling) or the first (first_token = 1, BERT CLS,
+ * bert.py:236-244) -- optionally RMS-normalises it over all `cols` columns with the bf16
+ * weight norm_w (eps; x * rsqrt(mean(x^2) + eps) * w, as kernels.metal:53-63), and
+ * writes its first `dim` columns divided by their L2 norm to out[b, 0:dim] (fp32).
+ * x: in_dtype (TX_F32 or TX_BF16), padded [batch, seq, cols] with `lengths` (device
+ * u32[batch]), or packed [total, cols] with `cu_seqlens` (device i32[batch+1]; exactly
+ * one of the two is non-NULL; seq is ignored for packed).  A sequence without a valid
+ * row (length 0, length > seq, empty packed range) gets a NaN row.  dim <= cols.
+ * stream: a cudaStream_t, or NULL for the context's stream. */
+int tx_pool_project(void *ctx, const void *x, int in_dtype, const uint32_t *lengths,
+                    const int32_t *cu_seqlens, float *out, uint32_t batch, uint32_t seq,
+                    uint32_t cols, uint32_t dim, int first_token, const uint16_t *norm_w,
+                    float eps, void *stream);
+
 /* Allocation-free variant of tx_attention_padded (no counterpart in the reference,
  * whose Metal runtime always owns its buffers).  For callers that may not allocate
  * device memory -- hosts that reserve all memory up front and treat a later

@@ -20,6 +20,7 @@ from .attention import (  # noqa: F401
     bf16_bits_to_f32,
     bf16_round,
     pool_project,
+    pool_project_packed,
     qk_norm_rope,
     rms_norm,
     rope,

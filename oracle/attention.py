@@ -182,3 +182,14 @@ def pool_project(x, lengths, dim: int, first_token: bool, dtype=np.float64):
     rows = np.zeros(b_, dtype=np.int64) if first_token else np.asarray(lengths, np.int64) - 1
     picked = x[np.arange(b_), rows, :dim]
     return picked / np.sqrt(np.sum(picked * picked, axis=-1, keepdims=True))
+
+
+def pool_project_packed(x, cu_seqlens, dim: int, first_token: bool, dtype=np.float64):
+    """pool_project (kernels.metal:339-349) on packed rows: sequence b spans rows
+    cu[b]..cu[b+1]-1 of x [total, cols]; its last row (or first, first_token) is picked
+    and its first `dim` columns L2-normalised."""
+    x = np.asarray(x, dtype=dtype)
+    cu = np.asarray(cu_seqlens, dtype=np.int64)
+    rows = cu[:-1] if first_token else cu[1:] - 1
+    picked = x[rows, :dim]
+    return picked / np.sqrt(np.sum(picked * picked, axis=-1, keepdims=True))

@@ -4,7 +4,7 @@ Host side: NumPy in, NumPy out, no PyTorch dependency, a thin ctypes binding of
 libtessattn.so (hand-written CUDA for sm_100a).  See include/tessattn.h for the C ABI.
 """
 
-from .attention import attention, default_runtime, qk_norm_rope
+from .attention import attention, default_runtime, pool_project, qk_norm_rope
 from .batching import pack_rows, unpack_rows, varlen_batches
 from .errors import (
     ClosedError,
@@ -36,6 +36,7 @@ __all__ = [
     "gather_shard",
     "pack",
     "pack_rows",
+    "pool_project",
     "qk_norm_rope",
     "shard_sequences",
     "unpack_rows",

@@ -183,3 +183,71 @@ def qk_norm_rope(
     rt._lib.tx_read(qo.pointer, qr.ctypes.data, qr.nbytes)
     rt._lib.tx_read(ko.pointer, kr.ctypes.data, kr.nbytes)
     return qr, kr
+
+
+def pool_project(
+    x: NDArray,
+    *,
+    dim: int | None = None,
+    lengths: NDArray | None = None,
+    cu_seqlens: NDArray | None = None,
+    first_token: bool = False,
+    norm_weight: NDArray | None = None,
+    eps: float = 1e-6,
+    runtime: CudaRuntime | None = None,
+    out: NDArray | None = None,
+) -> NDArray:
+    """Embeddings from final hidden states (kernels.metal:339-349, with the final
+    rms_norm of qwen3.py:281-290 fused when norm_weight is given).
+
+    x: float32 or bf16 bits, padded [B, seq, cols] with lengths [B], or packed
+    [total, cols] with cu_seqlens [B+1].  Row per sequence: the last valid token, or the
+    first when first_token (BERT CLS).  norm_weight: bf16 bits [cols].  Returns
+    float32 [B, dim] (dim defaults to cols), each row of unit L2 norm.
+    """
+    rt = runtime or default_runtime()
+    x = np.ascontiguousarray(x)
+    code = _dtype_code(x)
+    if (lengths is None) == (cu_seqlens is None):
+        raise InvalidInputError()
+    if lengths is not None:
+        if x.ndim != 3:
+            raise InvalidInputError()
+        batch, seq, cols = x.shape
+        sel = np.ascontiguousarray(lengths, dtype=np.uint32)
+        if sel.shape != (batch,):
+            raise InvalidInputError()
+    else:
+        if x.ndim != 2:
+            raise InvalidInputError()
+        seq, cols = 0, x.shape[1]
+        sel = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+        if sel.ndim != 1 or sel.size < 2 or int(sel[0]) != 0 or int(sel[-1]) > x.shape[0] \
+                or np.any(np.diff(sel) < 0):
+            raise InvalidInputError()
+        batch = sel.size - 1
+    dim = cols if dim is None else int(dim)
+    if not 0 < dim <= cols:
+        raise InvalidInputError()
+    xp = _upload(rt, "pool_x", x)
+    sp = _upload(rt, "pool_sel", sel)
+    wp = None
+    if norm_weight is not None:
+        w = np.ascontiguousarray(norm_weight, dtype=np.uint16)
+        if w.shape != (cols,):
+            raise InvalidInputError()
+        wp = _upload(rt, "pool_norm_weight", w)
+    dev_out = rt.workspace("pool_out", batch * dim * 4)
+    rt.pool_project_device(
+        xp, dev_out.device_ptr, batch=batch, cols=cols, dim=dim, seq=seq,
+        lengths=sp if lengths is not None else None,
+        cu_seqlens=sp if cu_seqlens is not None else None, first_token=first_token,
+        norm_weight=wp, eps=eps, in_dtype=code,
+    )
+    rt.sync()
+    if out is None:
+        out = np.empty((batch, dim), dtype=np.float32)
+    elif out.shape != (batch, dim) or out.dtype != np.float32 or not out.flags.c_contiguous:
+        raise InvalidInputError()
+    _raise_for(rt._lib.tx_read(dev_out.pointer, out.ctypes.data, out.nbytes))
+    return out

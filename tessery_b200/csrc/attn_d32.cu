@@ -1,4 +1,4 @@
-// fp32 attention for head_dim 32 (BERT/BGE-small shapes: 12 heads x 32, bidirectional,
+// Attention for head_dim 32, fp32 arithmetic on fp32 or bf16 inputs (BERT/BGE-small shapes: 12 heads x 32, bidirectional,
 // key-padding mask by length), the operator of bert.py:196-204 dispatched through
 // MetalRuntime._attention (metal.py:532-569).
 //
@@ -34,11 +34,28 @@ __device__ __forceinline__ uint32_t d32_find_seq(const int32_t *cu, uint32_t nse
   return lo;
 }
 
+// Eight consecutive elements (16-byte aligned for f32 pairs of float4, 16-byte for bf16)
+// as floats.
+__device__ __forceinline__ void load8(const float *p, float (&x)[8]) {
+  const float4 a = ((const float4 *)p)[0], b = ((const float4 *)p)[1];
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+__device__ __forceinline__ void load8(const uint16_t *p, float (&x)[8]) {
+  const uint4 a = *(const uint4 *)p;
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = __uint_as_float(w[i] << 16);
+    x[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+template <typename TI, typename TO>
 __global__ void __launch_bounds__(kRows) attention_d32_kernel(AttnProblem p) {
   __shared__ __align__(16) float ks[kChunk * kD];
   __shared__ __align__(16) float vs[kChunk * kD];
-  const float *q = (const float *)p.q, *k = (const float *)p.k, *v = (const float *)p.v;
-  float *out = (float *)p.out;
+  const TI *q = (const TI *)p.q, *k = (const TI *)p.k, *v = (const TI *)p.v;
+  TO *out = (TO *)p.out;
   const uint32_t qblock = blockIdx.x, head = blockIdx.y, seqi = blockIdx.z;
   const uint32_t kvhead = head / (p.heads / p.kv_heads);
   const uint32_t tid = threadIdx.x;
@@ -65,11 +82,13 @@ __global__ void __launch_bounds__(kRows) attention_d32_kernel(AttnProblem p) {
 
   float qr[kD], acc[kD];
   if (active) {
-    const float4 *qp = (const float4 *)(q + ((base + pos) * p.heads + head) * kD);
+    const TI *qp = q + ((base + pos) * p.heads + head) * kD;
 #pragma unroll
-    for (int i = 0; i < kD / 4; ++i) {
-      float4 t = qp[i];
-      qr[4 * i] = t.x; qr[4 * i + 1] = t.y; qr[4 * i + 2] = t.z; qr[4 * i + 3] = t.w;
+    for (int i = 0; i < kD / 8; ++i) {
+      float t[8];
+      load8(qp + 8 * i, t);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) qr[8 * i + e] = t[e];
     }
   } else {
 #pragma unroll
@@ -86,12 +105,19 @@ __global__ void __launch_bounds__(kRows) attention_d32_kernel(AttnProblem p) {
   for (uint32_t c0 = 0; c0 < kend; c0 += kChunk) {
     const uint32_t cn = min(kChunk, kend - c0);
     __syncthreads();  // previous chunk fully consumed
-    // Stage K and V rows [c0, c0+cn): 8 float4 per row, coalesced.
-    for (uint32_t i = tid; i < cn * (kD / 4); i += kRows) {
-      uint32_t r = i / (kD / 4), c4 = i % (kD / 4);
-      uint64_t row = ((base + c0 + r) * p.kv_heads + kvhead) * kD;
-      ((float4 *)ks)[i] = ((const float4 *)(k + row))[c4];
-      ((float4 *)vs)[i] = ((const float4 *)(v + row))[c4];
+    // Stage K and V rows [c0, c0+cn) as fp32: 4 groups of 8 elements per row
+    // (128-bit loads for bf16, 2 x 128-bit for f32), consecutive threads on consecutive
+    // groups so the row reads coalesce.
+    for (uint32_t i = tid; i < cn * (kD / 8); i += kRows) {
+      uint32_t r = i / (kD / 8), c8 = i % (kD / 8);
+      uint64_t row = ((base + c0 + r) * p.kv_heads + kvhead) * kD + c8 * 8;
+      float t[8];
+      load8(k + row, t);
+      ((float4 *)ks)[2 * i] = make_float4(t[0], t[1], t[2], t[3]);
+      ((float4 *)ks)[2 * i + 1] = make_float4(t[4], t[5], t[6], t[7]);
+      load8(v + row, t);
+      ((float4 *)vs)[2 * i] = make_float4(t[0], t[1], t[2], t[3]);
+      ((float4 *)vs)[2 * i + 1] = make_float4(t[4], t[5], t[6], t[7]);
     }
     __syncthreads();
     if (wend <= c0) continue;
@@ -141,22 +167,38 @@ __global__ void __launch_bounds__(kRows) attention_d32_kernel(AttnProblem p) {
   }
   if (active) {
     float inv = 1.0f / l;
-    float4 *op = (float4 *)(out + ((base + pos) * p.heads + head) * kD);
+    TO *op = out + ((base + pos) * p.heads + head) * kD;
+    if constexpr (sizeof(TO) == 4) {
 #pragma unroll
-    for (int i = 0; i < kD / 4; ++i)
-      op[i] = make_float4(acc[4 * i] * inv, acc[4 * i + 1] * inv, acc[4 * i + 2] * inv,
-                          acc[4 * i + 3] * inv);
+      for (int i = 0; i < kD / 4; ++i)
+        ((float4 *)op)[i] = make_float4(acc[4 * i] * inv, acc[4 * i + 1] * inv,
+                                        acc[4 * i + 2] * inv, acc[4 * i + 3] * inv);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kD / 8; ++i)
+        ((uint4 *)op)[i] = make_uint4(pack_bf16x2(acc[8 * i] * inv, acc[8 * i + 1] * inv),
+                                      pack_bf16x2(acc[8 * i + 2] * inv, acc[8 * i + 3] * inv),
+                                      pack_bf16x2(acc[8 * i + 4] * inv, acc[8 * i + 5] * inv),
+                                      pack_bf16x2(acc[8 * i + 6] * inv, acc[8 * i + 7] * inv));
+    }
   }
 }
 
 cudaError_t launch_attention_d32(const AttnProblem &p, cudaStream_t stream) {
-  if (p.dim != kD || p.in_dtype != 0 || p.out_dtype != 0) return cudaErrorInvalidValue;
+  if (p.dim != kD) return cudaErrorInvalidValue;
   if (!p.batch || !p.heads) return cudaSuccess;
   uint32_t qblocks = (p.seq + kRows - 1) / kRows;
   if (!qblocks) return cudaSuccess;
   if (p.batch > 65535u || p.heads > 65535u) return cudaErrorInvalidValue;
   dim3 grid(qblocks, p.heads, p.batch);
-  attention_d32_kernel<<<grid, kRows, 0, stream>>>(p);
+  if (p.in_dtype == 0 && p.out_dtype == 0)
+    attention_d32_kernel<float, float><<<grid, kRows, 0, stream>>>(p);
+  else if (p.in_dtype == 0)
+    attention_d32_kernel<float, uint16_t><<<grid, kRows, 0, stream>>>(p);
+  else if (p.out_dtype == 0)
+    attention_d32_kernel<uint16_t, float><<<grid, kRows, 0, stream>>>(p);
+  else
+    attention_d32_kernel<uint16_t, uint16_t><<<grid, kRows, 0, stream>>>(p);
   return cudaGetLastError();
 }
 

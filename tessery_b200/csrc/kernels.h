@@ -49,6 +49,22 @@ struct PrologueProblem {
 };
 cudaError_t launch_qk_norm_rope(const PrologueProblem &p, cudaStream_t stream);
 
+// Embedding pooling: one row per sequence (last valid or first token), optional
+// RMSNorm with a bf16 weight over all cols, L2 normalisation of the first dim columns.
+struct PoolProblem {
+  const void *x;                // padded [batch, seq, cols] or packed [total, cols]
+  int in_dtype;                 // 0 f32, 1 bf16
+  const uint32_t *lengths;      // padded layout
+  const int32_t *cu_seqlens;    // packed layout (exactly one of lengths / cu_seqlens)
+  float *out;                   // [batch, dim]
+  uint32_t batch, seq, cols, dim;
+  int first_token;
+  const uint16_t *norm_w;       // bf16 [cols] or nullptr
+  float eps;
+  bool vector_ok;               // set by the launcher
+};
+cudaError_t launch_pool_project(const PoolProblem &p, cudaStream_t stream);
+
 // Bandwidth-oriented fp32 kernel for head_dim 32 (BERT/BGE shapes).
 cudaError_t launch_attention_d32(const AttnProblem &p, cudaStream_t stream);
 

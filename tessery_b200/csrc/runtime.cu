@@ -20,7 +20,7 @@
 
 namespace {
 
-constexpr uint32_t kAbiVersion = 2;
+constexpr uint32_t kAbiVersion = 3;
 
 struct Ctx;
 
@@ -185,7 +185,7 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
     return fail(c, TX_EINVAL, "problem too large");
 
   const bool tc_path = p.in_dtype == TX_BF16 && p.scale > 0.f && tx::tc_attention_supported(p);
-  const bool d32_path = !tc_path && p.in_dtype == TX_F32 && p.out_dtype == TX_F32 && p.dim == 32 &&
+  const bool d32_path = !tc_path && p.dim == 32 &&
                         p.batch <= 65535u && p.heads <= 65535u &&
                         (uintptr_t)p.q % 16 == 0 && (uintptr_t)p.k % 16 == 0 &&
                         (uintptr_t)p.v % 16 == 0 && (uintptr_t)p.out % 16 == 0;
@@ -253,7 +253,7 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
   } else if (d32_path) {
     if ((e = tx::launch_attention_d32(p, stream)) != cudaSuccess)
       return cuda_fail(c, e, "attention launch");
-    c->last_kernel = "d32_f32";
+    c->last_kernel = "d32";
     ++c->launches;
   } else {
     if ((e = tx::launch_attention_simt(p, stream)) != cudaSuccess)
@@ -539,6 +539,25 @@ int tx_dispatch(void *ctx, const char *name, void **buffers, uint32_t count, con
     int rc = run_attention(c, p, nullptr, nullptr, nullptr, nullptr, 0.f, 0.f, c->stream);
     prof_end(c);
     if (rc) return rc;
+  } else if (n == "pool_project") {
+    // buffers [x, lengths, out]; one 32-thread group per sequence (kernels.metal:339-349)
+    if (count != 3 || threads % 32 || !pr.seq || !pr.cols || !pr.dim || pr.dim > pr.cols)
+      return fail(c, TX_EINVAL, "pool_project: bad arguments");
+    uint64_t batch = threads / 32;
+    if (batch * pr.seq * pr.cols * 4 > b[0]->size || batch * 4 > b[1]->size ||
+        batch * pr.dim * 4 > b[2]->size)
+      return fail(c, TX_EINVAL, "pool_project: buffer too small");
+    tx::PoolProblem pp{};
+    pp.x = b[0]->dev; pp.in_dtype = TX_F32; pp.lengths = (const uint32_t *)b[1]->dev;
+    pp.out = (float *)b[2]->dev; pp.batch = (uint32_t)batch; pp.seq = pr.seq;
+    pp.cols = pr.cols; pp.dim = pr.dim; pp.first_token = pr.u1 ? 1 : 0;
+    prof_begin(c);
+    e = tx::launch_pool_project(pp, c->stream);
+    if (e == cudaSuccess) {
+      ++c->launches;
+      c->last_kernel = "pool_project";
+    }
+    prof_end(c);
   } else if (n == "qk_norm_rope") {
     // buffers: q, k (f32, in place), q_norm weight, k_norm weight (bf16); n = tokens
     if (count != 4 || !pr.heads || !pr.kv_heads || !pr.seq)
@@ -697,6 +716,32 @@ int tx_qk_norm_rope(void *ctx, const void *q, const void *k, void *q_out, void *
   cudaSetDevice(c->device);
   cudaError_t e = tx::launch_qk_norm_rope(pp, stream ? (cudaStream_t)stream : c->stream);
   if (e != cudaSuccess) return cuda_fail(c, e, "prologue launch");
+  ++c->launches;
+  return TX_OK;
+}
+
+int tx_pool_project(void *ctx, const void *x, int in_dtype, const uint32_t *lengths,
+                    const int32_t *cu_seqlens, float *out, uint32_t batch, uint32_t seq,
+                    uint32_t cols, uint32_t dim, int first_token, const uint16_t *norm_w,
+                    float eps, void *stream) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!x || !out) return fail(c, TX_EINVAL, "null pointer");
+  if (!lengths == !cu_seqlens) return fail(c, TX_EINVAL, "exactly one of lengths, cu_seqlens");
+  if (in_dtype != TX_F32 && in_dtype != TX_BF16) return fail(c, TX_EINVAL, "bad dtype");
+  if (!dim || dim > cols) return fail(c, TX_EINVAL, "need 0 < dim <= cols");
+  if (lengths && !seq) return fail(c, TX_EINVAL, "seq must be positive");
+  if (!(eps >= 0.f)) return fail(c, TX_EINVAL, "eps must be >= 0");
+  if (!batch) return TX_OK;
+  tx::PoolProblem p{};
+  p.x = x; p.in_dtype = in_dtype; p.lengths = lengths; p.cu_seqlens = cu_seqlens; p.out = out;
+  p.batch = batch; p.seq = seq; p.cols = cols; p.dim = dim; p.first_token = first_token ? 1 : 0;
+  p.norm_w = norm_w; p.eps = eps;
+  cudaSetDevice(c->device);
+  cudaError_t e = tx::launch_pool_project(p, stream ? (cudaStream_t)stream : c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "pool launch");
+  c->last_kernel = "pool_project";
   ++c->launches;
   return TX_OK;
 }

@@ -16,7 +16,7 @@ from typing import Any
 
 from .errors import NativeBuildError
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 LIBRARY_NAME = "libtessattn.so"
 
 TX_OK, TX_EINVAL, TX_ECUDA, TX_ETIMEOUT = 0, 1, 2, 3
@@ -60,6 +60,10 @@ SIGNATURES: dict[str, tuple[list[Any], Any]] = {
     "tx_qk_norm_rope": (
         [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _vp, _u32, _vp, _u32, _u32, _u32, _i32, _i32, _vp,
          _vp, _f32, _f32, _vp],
+        _i32,
+    ),
+    "tx_pool_project": (
+        [_vp, _vp, _i32, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _i32, _vp, _f32, _vp],
         _i32,
     ),
     "tx_sync": ([_vp, _vp], _i32),

@@ -123,7 +123,7 @@ class CudaRuntime:
         return int(self._lib.tx_device_sms(self._pointer))
 
     def last_kernel(self) -> str:
-        """Route of the last attention call: "tc_bf16_d128", "simt" or "d32_f32"."""
+        """Route of the last attention call: "tc_bf16_d128", "simt" or "d32" (or "pool_project")."""
         raw = self._lib.tx_last_kernel(self._pointer)
         return raw.decode() if raw else ""
 
@@ -426,6 +426,34 @@ class CudaRuntime:
         rc = self._lib.tx_qk_norm_rope(
             self._pointer, q, k, q_out, k_out, tokens, seq, cu_seqlens, nseq, lengths, heads,
             kv_heads, dim, in_dtype, out_dtype, q_norm_weight, k_norm_weight, eps, theta, stream,
+        )
+        _raise_for(rc)
+
+    def pool_project_device(
+        self,
+        x: int,
+        out: int,
+        *,
+        batch: int,
+        cols: int,
+        dim: int,
+        seq: int = 0,
+        lengths: int | None = None,
+        cu_seqlens: int | None = None,
+        first_token: bool = False,
+        norm_weight: int | None = None,
+        eps: float = 1e-6,
+        in_dtype: int = native.TX_F32,
+        stream: int | None = None,
+    ) -> None:
+        """Queues embedding pooling on device pointers (tx_pool_project): one row per
+        sequence (last valid token, or the first with first_token), RMSNorm with
+        norm_weight when given, L2 normalisation of the first `dim` columns into
+        out [batch, dim] fp32."""
+        self._check_open()
+        rc = self._lib.tx_pool_project(
+            self._pointer, x, in_dtype, lengths, cu_seqlens, out, batch, seq, cols, dim,
+            int(bool(first_token)), norm_weight, eps, stream,
         )
         _raise_for(rc)
 

@@ -64,7 +64,7 @@ def test_reference_golden_case(runtime, case):
 
 def test_attention_route_follows_head_dim(runtime):
     rng = np.random.default_rng(5)
-    for dim, route in ((32, "d32_f32"), (64, "simt"), (128, "simt")):
+    for dim, route in ((32, "d32"), (64, "simt"), (128, "simt")):
         q = rng.normal(size=(2, 40, 4, dim)).astype(np.float32)
         k = rng.normal(size=(2, 40, 2, dim)).astype(np.float32)
         v = rng.normal(size=k.shape).astype(np.float32)
@@ -89,7 +89,7 @@ def test_bge_d32_fp32_matches_oracle(runtime, batch, seq):
     w.lengths[0] = 1
     w.lengths[-1] = seq
     got = attention(w.q, w.k, w.v, lengths=w.lengths, causal=False, runtime=runtime)
-    assert runtime.last_kernel() == "d32_f32"
+    assert runtime.last_kernel() == "d32"
     want = oracle.attention_padded(w.q, w.k, w.v, w.lengths, False, w.scale)
     np.testing.assert_allclose(got, want, atol=F32_ATOL, rtol=F32_RTOL)
     assert np.max(np.abs(got - want)) <= 1e-4
@@ -105,7 +105,7 @@ def test_bge_d32_causal_and_varlen(runtime):
                for _ in range(3)]
     for causal in (False, True):
         got = attention(q, k, v, cu_seqlens=cu, causal=causal, runtime=runtime)
-        assert runtime.last_kernel() == "d32_f32"
+        assert runtime.last_kernel() == "d32"
         want = oracle.attention_varlen(q, k, v, cu, causal, 32**-0.5)
         np.testing.assert_allclose(got, want, atol=F32_ATOL, rtol=F32_RTOL)
 
@@ -177,11 +177,32 @@ def test_qwen_varlen_bf16_tensor_core(runtime, nseq, seed):
 
 
 def test_short_tails_both_shapes(runtime):
-    for kind in ("qwen", "bge"):
+    for kind, route in (("qwen", "tc_bf16_d128"), ("bge", "d32")):
         w = workloads.short_tails(kind, batch=32, seed=41)
         got = run_workload(runtime, w)
+        assert runtime.last_kernel() == route
         want = qwen_oracle(w)
         assert np.max(np.abs(got - want)) <= BF16_GATE, kind
+
+
+@pytest.mark.parametrize("out_dtype", ["float32", "bf16"])
+def test_bge_d32_bf16_inputs(runtime, out_dtype):
+    """bf16 inputs on the head_dim-32 kernel: rows are widened to fp32 as they are staged,
+    so against the oracle on the same (bf16-valued) inputs only fp32 rounding remains for
+    fp32 output; bf16 output adds one rounding of the result."""
+    w = workloads.bge(batch=3, seq=200, seed=13, min_len=1)
+    w.lengths[:] = [1, 200, 77]
+    q, k, v = (to_bf16_bits(a) for a in (w.q, w.k, w.v))
+    got = attention(q, k, v, lengths=w.lengths, causal=False, out_dtype=out_dtype,
+                    runtime=runtime)
+    assert runtime.last_kernel() == "d32"
+    want = oracle.attention_padded(*(from_bf16_bits(a) for a in (q, k, v)), w.lengths, False,
+                                   w.scale)
+    if out_dtype == "bf16":
+        got = from_bf16_bits(got)
+        np.testing.assert_allclose(got, want, atol=1e-2, rtol=1e-2)
+    else:
+        np.testing.assert_allclose(got, want, atol=F32_ATOL, rtol=F32_RTOL)
 
 
 def test_bidirectional_bf16_tensor_core(runtime):

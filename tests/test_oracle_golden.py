@@ -47,3 +47,16 @@ def test_oracle_matches_reference_expectations(case):
     # Whole-array moments recorded from the reference's expected array.
     np.testing.assert_allclose(np.sum(result, dtype=np.float64), case.sum, rtol=1e-9,
                                atol=1e-6 * max(1.0, abs(case.sum)))
+
+
+def test_packed_pool_matches_padded_pool():
+    """The packed-row pooling restatement picks the same rows as the padded one."""
+    rng = np.random.default_rng(9)
+    x = rng.normal(size=(4, 10, 48))
+    lengths = np.array([1, 10, 4, 7])
+    cu = np.zeros(5, np.int64)
+    cu[1:] = np.cumsum(lengths)
+    packed = np.concatenate([x[b, :n] for b, n in enumerate(lengths)])
+    for first in (False, True):
+        np.testing.assert_array_equal(oracle.pool_project_packed(packed, cu, 40, first),
+                                      oracle.pool_project(x, lengths, 40, first))
