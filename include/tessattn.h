@@ -207,11 +207,12 @@ int tx_pool_project(void *ctx, const void *x, int in_dtype, const uint32_t *leng
  * cudaMalloc as an error, since it can fail under memory pressure and stall the
  * device -- and that therefore cannot create a context either.  It takes no context.
  * Path: the tensor-core kernel only (bf16 q/k/v on the current device, head_dim 128,
- * an even number of query heads per kv head); q_norm_w (or NULL) applies the fused q
- * RMSNorm + RoPE, while k must already be normalised (tx_qk_norm_rope).  Its only
- * scratch, the work list, is a static device array of 16384 units (one unit = 128
- * query rows of a head pair: batch * heads/2 * ceil(seq/128) units); larger problems
- * are rejected with TX_EINVAL.  The first call on a device looks up that array's
+ * at most 64 query heads); q_norm_w (or NULL) applies the fused q RMSNorm + RoPE, while
+ * k must already be normalised (tx_qk_norm_rope).  Its only scratch, the work list, is
+ * a static device array of 32768 units (one unit = 128 query rows of a pair of query
+ * heads, or of one head when the query heads per kv head are odd:
+ * batch * heads/2 (or heads) * ceil(seq/128) units); larger problems are rejected with
+ * TX_EINVAL before any pointer is used.  The first call on a device looks up that array's
  * device address (with the device current) and should come before any stream
  * capture.  All calls share the array and it keeps the last call's contents: calls
  * whose work overlaps on the GPU race.  status: device int the kernel sets to

@@ -4,31 +4,40 @@
 // (and of its tiled/tail variants :108-298).  Optionally fused in front: the q RMSNorm +
 // RoPE of qwen3.py:216-237 (kernels.metal:53-74), applied to each Q tile in shared memory.
 //
-// Work unit: (sequence, pair of query heads sharing one kv head, 128-row query tile).
-// The two query heads of a pair share every K/V tile, so each K/V tile is fetched once
-// per pair (GQA head sharing).  A persistent grid of one CTA per SM walks a host-built,
-// longest-first list of units.
+// Work unit: (sequence, pair of query heads sharing one kv head, 128-row query tile);
+// when the query heads per kv head are odd, a unit holds one head.  The heads of a unit
+// share every K/V tile (GQA head sharing).  A persistent grid of one CTA per SM walks a
+// host-built, longest-first list of units.
 //
-// Warp roles (320 threads, one CTA per SM):
-//   warps 0-3  head slot 0: q prologue on the Q tile, softmax, epilogue (thread t = row t)
-//   warps 4-7  head slot 1
-//   warp 8     TMA producer: Q_h tiles (each as soon as its last QK of the previous unit
-//              has run), then K_j, V_j through a 3-slot ring
-//   warp 9     TMEM allocator and single-thread tcgen05.mma issuer
-// Tensor memory (512 columns x 128 lanes, fp32):
-//   [0,128) S slot 0, [128,256) S slot 1, [256,384) O slot 0, [384,512) O slot 1.
-// Shared memory: Q0, Q1, 3 K/V slots, P0, P1: 128x128 bf16 tiles, each two 128-row x
-// 128-byte atoms in the 128-byte-swizzled layout that TMA writes and UMMA reads.  After
-// the last P.V of a unit, P_h is the staging buffer of the output tile, which leaves by
-// TMA bulk-tensor stores.
+// Warp roles (448 threads, one CTA per SM), specialised so that each serial per-unit
+// step runs beside the others instead of in front of them:
+//   warps 0-3   softmax of head slot 0 (thread t = query row t)
+//   warps 4-7   softmax of head slot 1
+//   warps 8-11  epilogue of each unit (O from tensor memory, scaled, staged swizzled in
+//               the unit's Q buffer, sent by TMA bulk-tensor stores), then the Q tiles of
+//               the unit two ahead: TMA load into the buffer just freed, q prologue
+//   warp 12     TMA producer: K and V tiles of 64 keys through a 5-slot ring
+//   warp 13     TMEM allocator and single-thread tcgen05.mma issuer
+// Tensor memory (512 columns x 128 lanes, fp32), per head slot h at column 256h:
+//   [0,64) S slot 0, [64,128) S slot 1, [128,256) O.
+// P (bf16) is written over the first 32 columns of its S slot and read from there by
+// P.V as the tensor-memory A operand, so P needs no shared memory and is double
+// buffered with S.  Shared memory: two unit buffers of Q tiles (2 x 128x128 bf16 each,
+// so the next unit's Q is loaded and transformed while this one runs; a finished unit's
+// buffer stages its output), 5 ring slots (64x128 bf16: K or V), all in the
+// 128-byte-swizzled layout that TMA and UMMA use (a 128-byte row holds 64 bf16 or 32
+// fp32).
 //
-// Per key tile j the issuer runs S_h = Q_h K_j^T (M=128, N=128, K=128, bf16 -> f32 in
-// TMEM); the softmax warps turn S_h into P_h = exp2(S_h*scale*log2e - m) (bf16, shared
-// memory); the issuer accumulates O_h += P_h V_j in TMEM.  Tiles above the causal
-// diagonal and beyond each sequence's length are never visited; the diagonal and the
-// last tile are masked per row.  The running maximum is updated lazily: O is rescaled
-// only when a tile maximum exceeds the reference maximum by more than 8 (log2 units),
-// so every probability stays below 2^8 and the normalised result is unchanged.
+// Key tile j of a unit: the issuer runs S_h = Q_h K_j^T (M=128, N=64, K=128) into S
+// slot j%2 of head h, so a tile's scores are computed while the softmax warps work on the
+// previous one; the softmax warps turn S_h into P_h = exp2(S_h*scale*log2e - m); the
+// issuer accumulates O_h += P_h V_j (M=128, N=128, K=64).  Q.K^T of tile j+2 is issued
+// after P.V of tile j, which read the slot it overwrites (tcgen05.mma of one thread run
+// in order).  Tiles above the causal diagonal and beyond each sequence's length are
+// never visited; the diagonal and the last tile are masked per row.  The running
+// maximum is updated lazily: O is rescaled only when a tile maximum exceeds the
+// reference maximum by more than 8 (log2 units), so every probability stays below 2^8
+// and the normalised result is unchanged.
 //
 // Every wait is bounded (about a second); a wait that gives up records
 // TX_ETIMEOUT | site<<8 in the context status word, raises a CTA-wide abort flag, and
@@ -37,7 +46,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
-#include <vector>
+#include <cmath>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -45,54 +54,65 @@
 namespace tx {
 namespace tc {
 
-constexpr int kTile = 128;                     // query rows, keys and head_dim per tile
-constexpr int kStages = 3;                     // K/V ring slots
-constexpr uint32_t kAtomBytes = 128 * 128;     // 128 rows x 64 bf16 (one swizzle column)
-constexpr uint32_t kTileBytes = 2 * kAtomBytes;
-constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffKV = kOffQ + 2 * kTileBytes;
-constexpr uint32_t kOffP = kOffKV + kStages * kTileBytes;
-constexpr uint32_t kOffMisc = kOffP + 2 * kTileBytes;
-constexpr uint32_t kMiscBytes = 768;
+constexpr int kQRows = 128;                     // query rows per tile (TMEM lanes)
+constexpr int kKeys = 64;                       // keys per K/V tile
+constexpr int kStages = 5;                      // K/V ring slots
+constexpr uint32_t kQAtom = 128 * 128;          // 128 rows x 64 bf16
+constexpr uint32_t kQBytes = 2 * kQAtom;         // one head's Q tile
+constexpr uint32_t kQBufBytes = 2 * kQBytes;     // a unit's Q tiles (two head slots)
+constexpr uint32_t kKVAtom = kKeys * 128;       // 64 keys x 64 bf16
+constexpr uint32_t kKVBytes = 2 * kKVAtom;
+constexpr uint32_t kStageChunk = 128 * 128;     // staging: 128 rows x 128 bytes per chunk
+constexpr uint32_t kWarpBox = 32 * 128;         // one warp's 32 rows of a chunk
+constexpr uint32_t kOffQ = 0;                   // two unit buffers of Q tiles
+constexpr uint32_t kOffKV = kOffQ + 2 * kQBufBytes;
+constexpr uint32_t kOffMisc = kOffKV + kStages * kKVBytes;
+static_assert(4 * kStageChunk == kQBufBytes, "an O tile (fp32) stages in a Q buffer");
+constexpr uint32_t kMiscBytes = 3072;
 constexpr uint32_t kSmemBytes = kOffMisc + kMiscBytes + 1024;  // + base alignment slack
-constexpr int kThreads = 320;
-constexpr int kTmaWarp = 8, kMmaWarp = 9;
+constexpr int kThreads = 448;
+constexpr int kAuxWarp0 = 8, kTmaWarp = 12, kMmaWarp = 13;
+constexpr uint32_t kTmemCols = 512;
 constexpr long long kWaitCycles = 2000000000ll;  // ~1 s at B200 clocks
 constexpr float kRescaleThreshold = 8.0f;        // log2 units
-constexpr uint32_t kStageBytes = 4096;           // one 32-row x 128-byte output box
 
-// Barrier slots (uint64 each) at the start of the misc area.
+// Barrier slots (uint64 each) at the start of the misc area.  "h" = head slot,
+// "s" = S slot.
 enum : uint32_t {
-  kBarQFull = 0,                      // + head slot: Q_h landed (TMA transaction count)
-  kBarQReady = kBarQFull + 2,         // + head slot: Q_h transformed (256 arrivals)
-  kBarQEmpty = kBarQReady + 2,        // + head slot: last QK_h of the unit ran
-  kBarKVFull = kBarQEmpty + 2,        // + ring slot
+  kBarQFull = 0,                      // + Q buffer: the unit's Q tiles landed (TMA bytes)
+  kBarQReady = kBarQFull + 2,         // + Q buffer: Q tiles transformed (128 arrivals)
+  kBarStageFree = kBarQReady + 2,     // epilogue stores have read the staging (128 arrivals)
+  kBarKVFull = kBarStageFree + 1,     // + ring slot
   kBarKVEmpty = kBarKVFull + kStages,
-  kBarSFull = kBarKVEmpty + kStages,  // + head slot
-  kBarPFull = kBarSFull + 2,          // + head slot (128 arrivals)
-  kBarODone = kBarPFull + 2,          // + head slot
-  kBarXform = kBarODone + 2,          // q prologue: both row norms read (256 arrivals)
-  kBarDrain = kBarXform + 1,
+  kBarSFull = kBarKVEmpty + kStages,  // + 2h + s
+  kBarPFull = kBarSFull + 4,          // + 2h + s: P written in that S slot (128 arrivals)
+  kBarPVDone = kBarPFull + 4,         // + 2h + s: P.V from that S slot ran
+  kBarLReady = kBarPVDone + 4,        // + 2h + unit parity: row sums published (128 arrivals)
+  kBarOFree = kBarLReady + 4,         // + h: O_h read out (128 arrivals)
+  kBarDrain = kBarOFree + 2,
   kNumBars = kBarDrain + 1
 };
 constexpr uint32_t kOffTmemSlot = kNumBars * 8;   // uint32 TMEM base address
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;  // int abort flag
-constexpr uint32_t kOffQw = 256;                  // bf16 q-norm weight [128]
-constexpr uint32_t kOffInvFreq = 512;             // float inverse frequencies [64]
+constexpr uint32_t kOffQw = 512;                  // bf16 q-norm weight [128]
+constexpr uint32_t kOffInvFreq = 768;             // float inverse frequencies [64]
+constexpr uint32_t kOffRowSum = 1024;             // float [head slot][unit parity][128]
 static_assert(kOffAbort + 4 <= kOffQw, "misc area overflow");
+static_assert(kOffRowSum + 2 * 2 * 128 * 4 <= kMiscBytes, "misc area overflow");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 // Wait sites, reported in the status word for diagnosis.
 enum : int {
   kSiteQEmpty = 1, kSiteKVEmpty = 2, kSiteQReady = 3, kSiteKVFull = 4, kSitePFull = 5,
-  kSiteSFull = 6, kSiteODone = 7, kSiteQFull = 8, kSiteXform = 9
+  kSiteSFull = 6, kSitePVDone = 7, kSiteQFull = 8, kSiteLReady = 9, kSiteOFree = 10,
+  kSiteStageFree = 11
 };
 
 // ---- unit encoding --------------------------------------------------------------------
-// bits 0..7 query tile, 8..13 head pair, 14..31 sequence.
-__host__ __device__ __forceinline__ uint32_t encode_unit(uint32_t seq, uint32_t pair,
+// bits 0..7 query tile, 8..13 head pair (or head), 14..31 sequence.
+__host__ __device__ __forceinline__ uint32_t encode_unit(uint32_t seq, uint32_t idx,
                                                          uint32_t tile) {
-  return (seq << 14) | (pair << 8) | tile;
+  return (seq << 14) | (idx << 8) | tile;
 }
 
 struct Params {
@@ -102,12 +122,14 @@ struct Params {
   const int32_t *cu;        // varlen (NULL for padded)
   void *out;
   uint32_t seq;             // padded L (rows per sequence)
-  uint32_t heads, group;    // query heads; heads per kv head
+  uint32_t heads, group;    // query heads; query heads per kv head
+  uint32_t nh;              // heads per unit: 2 (pairs) or 1
   int causal, out_bf16;
   float scale_log2;
   int *status;
   const uint16_t *q_norm_w;  // fused q prologue when non-NULL
-  float eps, theta;
+  float eps;
+  float inv_freq[64];        // RoPE theta^(-2c/128), c < 64
 };
 
 struct Unit {
@@ -115,7 +137,7 @@ struct Unit {
   uint32_t q0;     // first query position of the tile
   uint32_t rows;   // rows of this sequence present in the layout
   uint32_t n;      // valid keys
-  uint32_t head0;  // first query head of the pair
+  uint32_t head0;  // first query head of the unit
   uint32_t kvh;
   uint32_t nt;     // key tiles to visit
   bool live;       // the tile holds rows to write
@@ -123,7 +145,7 @@ struct Unit {
 
 __device__ __forceinline__ Unit decode(const Params &p, uint32_t code) {
   Unit u;
-  uint32_t s = code >> 14, pair = (code >> 8) & 63u, t = code & 255u;
+  uint32_t s = code >> 14, idx = (code >> 8) & 63u, t = code & 255u;
   if (p.cu) {
     int32_t a = p.cu[s], b = p.cu[s + 1];
     u.tok0 = (uint32_t)a;
@@ -134,12 +156,12 @@ __device__ __forceinline__ Unit decode(const Params &p, uint32_t code) {
     u.n = min(p.lengths[s], p.seq);
     u.rows = p.seq;
   }
-  u.q0 = t * kTile;
-  u.head0 = 2 * pair;
+  u.q0 = t * kQRows;
+  u.head0 = idx * p.nh;
   u.kvh = u.head0 / p.group;
   u.live = u.q0 < u.rows;
-  uint32_t kend = p.causal ? min(u.q0 + kTile, u.n) : u.n;
-  u.nt = u.live ? (kend + kTile - 1) / kTile : 0u;
+  uint32_t kend = p.causal ? min(u.q0 + kQRows, u.n) : u.n;
+  u.nt = u.live ? (kend + kKeys - 1) / kKeys : 0u;
   return u;
 }
 
@@ -169,8 +191,12 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Phase parities of small per-slot counters kept as bits of one register (an array
+// indexed by a run-time slot would live in local memory).
+__device__ __forceinline__ uint32_t bit(uint32_t word, uint32_t i) { return (word >> i) & 1u; }
+
 // Bounded wait for the phase with parity `parity` of barrier `bar`.
-__device__ __noinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+__device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int *abort_flag,
                                         int *status, int site) {
   if (mbar_test(bar, parity)) return true;
   long long t0 = clock64();
@@ -199,13 +225,6 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
       : "memory");
-}
-// L2 prefetch of one box (no shared memory, no completion tracking).
-__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap *map, int x, int y, int z) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global [%0, {%1, %2, %3}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y), "r"(z)
-               : "memory");
 }
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t src, int x, int y,
                                              int z) {
@@ -264,22 +283,24 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr, uint32_t lbo, uint
   d |= (uint64_t)2 << 61;
   return d;
 }
-// K-major operand (rows = M or N, 64 bf16 of K per 128-byte row; 8-row groups 1024 B
-// apart).  Step `ks` (16 elements of K) of a 128-wide K: atom ks/4, 32 B per step.
-__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile, int ks) {
-  return sw128_desc(tile + (ks >> 2) * kAtomBytes + (ks & 3) * 32, 16, 1024);
+// K-major operand: rows (M or N) of 64 bf16 of K per 128-byte row, 8-row groups 1024 B
+// apart, one atom per 64 columns of K (`atom` bytes apart).  Step `ks` (16 elements of
+// K): atom ks/4, 32 bytes per step inside the swizzled row.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile, int ks, uint32_t atom) {
+  return sw128_desc(tile + (ks >> 2) * atom + (ks & 3) * 32, 16, 1024);
 }
 // MN-major operand (V as B of P.V: N = head_dim contiguous, K = keys).  The two 64-wide
-// N halves are the two atoms (16 KB apart, leading byte offset); 8-key groups are
-// 1024 B apart (stride byte offset); step `ks` covers keys 16ks..16ks+15.
+// N halves are the two atoms (leading byte offset = atom size); 8-key groups are 1024 B
+// apart (stride byte offset); step `ks` covers keys 16ks..16ks+15.
 __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile, int ks) {
-  return sw128_desc(tile + ks * 2048, kAtomBytes, 1024);
+  return sw128_desc(tile + ks * 2048, kKVAtom, 1024);
 }
 
-// Instruction descriptor: kind::f16, A=B=bf16, D=f32, M=128, N=128.
-constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) |
-                              ((128u >> 4) << 24);
-constexpr uint32_t kIdescPV = kIdescQK | (1u << 16);  // B is MN-major
+// Instruction descriptors, kind::f16 with A=B=bf16, D=f32: bit 4 D format, bits 7 and 10
+// A/B formats, bit 16 B MN-major, N>>3 at bit 17, M>>4 at bit 24.
+constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 4) << 24);
+constexpr uint32_t kIdescQK = kIdescBase | ((uint32_t)(kKeys >> 3) << 17);    // N = 64
+constexpr uint32_t kIdescPV = kIdescBase | (1u << 16) | ((128u >> 3) << 17);  // N = 128
 
 __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
                                      uint32_t accumulate) {
@@ -288,6 +309,16 @@ __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, ui
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D (+)= A B with A read from tensor memory (lane = row, two bf16 of K per column).
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -321,6 +352,24 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
       "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
       "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
       : "memory");
 }
 __device__ __forceinline__ void tmem_ld_wait() {
@@ -362,110 +411,89 @@ __device__ __forceinline__ void acc_squares(float (&ssq)[4], const uint4 &v) {
   }
 }
 
-// In-place q RMSNorm + RoPE of the two Q tiles (head slots 0 and 1) of a unit, shared
-// by both warpgroups: the thread owning row r in warpgroup `part` transforms row r of
-// both tiles for the rotation pairs c in [32*part, 32*part + 32), so each (position, c)
-// sine and cosine is evaluated once for the two heads.  Arithmetic per element follows
-// kernels.metal:53-74: x * inv * w, then the rotation of (element c, element c + 64) by
-// angle pos * inv_freq[c].  Every row norm reads the whole row, half of which the other
-// warpgroup rewrites, so the two passes are separated by a barrier of both warpgroups.
-// Pass 1 of the q prologue: inverse RMS of row r of both Q tiles.
-__device__ __forceinline__ void q_row_norms(uint32_t q_tiles, uint32_t r, float eps,
-                                            float (&inv)[2]) {
+// In-place q RMSNorm + RoPE of row r of the unit's Q tiles (nh of them; thread r owns
+// row r of every tile).  Each (position, column) sine and cosine is evaluated once for
+// the heads of the unit.  Arithmetic per element follows kernels.metal:53-74:
+// x * inv * w, then the rotation of (element c, element c + 64) by pos * inv_freq[c].
+__device__ __forceinline__ void q_transform_rows(uint32_t q_tiles, uint32_t r, uint32_t pos,
+                                                 uint32_t nh, const uint16_t *w,
+                                                 const float *inv_freq, float eps) {
   const uint32_t sw = r & 7;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const uint32_t row = q_tiles + h * kTileBytes + r * 128;
+  float inv[2] = {0.f, 0.f};
+  for (uint32_t h = 0; h < nh; ++h) {
+    const uint32_t row = q_tiles + h * kQBytes + r * 128;
     float ssq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int c = 0; c < 16; ++c)
-      acc_squares(ssq, ld_shared_v4(row + (c >> 3) * kAtomBytes + (((c & 7) ^ sw) << 4)));
+      acc_squares(ssq, ld_shared_v4(row + (c >> 3) * kQAtom + (((c & 7) ^ sw) << 4)));
     inv[h] = 1.0f / sqrtf(((ssq[0] + ssq[1]) + (ssq[2] + ssq[3])) / 128.0f + eps);
   }
-}
-
-// Pass 2: normalise and rotate this warpgroup's half of the rotation pairs of row r of
-// both tiles (run only after both warpgroups finished pass 1 on the tiles).
-__device__ __forceinline__ void q_rotate_pair(uint32_t q_tiles, uint32_t r, uint32_t pos,
-                                              int part, const uint16_t *w,
-                                              const float *inv_freq, const float (&inv)[2]) {
-  const uint32_t sw = r & 7;
   const float fpos = (float)pos;
 #pragma unroll 1
-  for (int gg = 0; gg < 4; ++gg) {  // pass 2: own chunk groups, both heads at once
-    const uint32_t g = 4 * part + gg;
-    uint4 lo[2], hi[2];
+  for (int g = 0; g < 8; ++g) {  // 16-byte chunk g: columns 8g..8g+7 and 64+8g..
+    float co[8], si[8], wa[8], wb[8];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint32_t row = q_tiles + h * kTileBytes + r * 128;
-      lo[h] = ld_shared_v4(row + ((g ^ sw) << 4));
-      hi[h] = ld_shared_v4(row + kAtomBytes + ((g ^ sw) << 4));
+    for (int e = 0; e < 8; ++e) {
+      const int c = 8 * g + e;
+      sincos_reduced(fpos * inv_freq[c], &si[e], &co[e]);
+      wa[e] = bf16_bits_to_f32(w[c]);
+      wb[e] = bf16_bits_to_f32(w[c + 64]);
     }
-    uint32_t out_lo[2][4], out_hi[2][4];
+    for (uint32_t h = 0; h < nh; ++h) {
+      const uint32_t row = q_tiles + h * kQBytes + r * 128;
+      const uint4 lo = ld_shared_v4(row + ((g ^ sw) << 4));
+      const uint4 hi = ld_shared_v4(row + kQAtom + ((g ^ sw) << 4));
+      uint32_t out_lo[4], out_hi[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float ra[2][2], rb[2][2];
+      for (int e = 0; e < 4; ++e) {
+        float ra[2], rb[2];
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {  // element within the bf16 pair
-        const uint32_t c = 8 * g + 2 * e + hh;
-        float s, co;
-        sincos_reduced(fpos * inv_freq[c], &s, &co);
-        const float wa = bf16_bits_to_f32(w[c]), wb = bf16_bits_to_f32(w[c + 64]);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t A = u4_at(lo[h], e), B = u4_at(hi[h], e);
-          const float a = (hh ? bf16_hi(A) : bf16_lo(A)) * inv[h] * wa;
-          const float b = (hh ? bf16_hi(B) : bf16_lo(B)) * inv[h] * wb;
-          ra[h][hh] = a * co - b * s;
-          rb[h][hh] = a * s + b * co;
+        for (int hh = 0; hh < 2; ++hh) {
+          const int k = 2 * e + hh;
+          const uint32_t A = u4_at(lo, e), B = u4_at(hi, e);
+          const float a = (hh ? bf16_hi(A) : bf16_lo(A)) * inv[h] * wa[k];
+          const float b = (hh ? bf16_hi(B) : bf16_lo(B)) * inv[h] * wb[k];
+          ra[hh] = a * co[k] - b * si[k];
+          rb[hh] = a * si[k] + b * co[k];
         }
+        out_lo[e] = pack_bf16x2(ra[0], ra[1]);
+        out_hi[e] = pack_bf16x2(rb[0], rb[1]);
       }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        out_lo[h][e] = pack_bf16x2(ra[h][0], ra[h][1]);
-        out_hi[h][e] = pack_bf16x2(rb[h][0], rb[h][1]);
-      }
-    }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint32_t row = q_tiles + h * kTileBytes + r * 128;
-      st_shared_v4(row + ((g ^ sw) << 4), out_lo[h][0], out_lo[h][1], out_lo[h][2], out_lo[h][3]);
-      st_shared_v4(row + kAtomBytes + ((g ^ sw) << 4), out_hi[h][0], out_hi[h][1], out_hi[h][2],
-                   out_hi[h][3]);
+      st_shared_v4(row + ((g ^ sw) << 4), out_lo[0], out_lo[1], out_lo[2], out_lo[3]);
+      st_shared_v4(row + kQAtom + ((g ^ sw) << 4), out_hi[0], out_hi[1], out_hi[2], out_hi[3]);
     }
   }
 }
 
-// exp2(x*sl - m) of one 32-key chunk of a row (0 for keys at or past `valid`), rounded to
-// bf16 pairs and stored into the row's slots (`prow` = shared address of row r of the
-// swizzled K-major P tile).  Returns the chunk's probability sum.
-__device__ __forceinline__ float emit_p(const uint32_t (&x)[32], int c, int valid, float sl,
-                                        float m, uint32_t prow, uint32_t r) {
+// exp2(x*sl - m) of one 32-key chunk of a row (0 for keys at or past `valid` when
+// kMasked), as 16 bf16 pairs; returns the chunk's sum.
+template <bool kMasked>
+__device__ __forceinline__ float exp_chunk(const uint32_t (&x)[32], int c, int valid, float sl,
+                                           float m, uint32_t (&packed)[16]) {
   float sum[4] = {0.f, 0.f, 0.f, 0.f};
-  uint32_t packed[16];
 #pragma unroll
   for (int t = 0; t < 16; ++t) {
     const int k0 = c * 32 + 2 * t;
-    float p0 = k0 < valid ? ex2(fmaf(__uint_as_float(x[2 * t]), sl, -m)) : 0.f;
-    float p1 = k0 + 1 < valid ? ex2(fmaf(__uint_as_float(x[2 * t + 1]), sl, -m)) : 0.f;
+    float p0 = ex2(fmaf(__uint_as_float(x[2 * t]), sl, -m));
+    float p1 = ex2(fmaf(__uint_as_float(x[2 * t + 1]), sl, -m));
+    if (kMasked) {
+      p0 = k0 < valid ? p0 : 0.f;
+      p1 = k0 + 1 < valid ? p1 : 0.f;
+    }
     sum[t & 3] += p0 + p1;
     packed[t] = pack_bf16x2(p0, p1);
-  }
-#pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    const uint32_t c8 = c * 4 + g;  // 8-key group 0..15
-    st_shared_v4(prow + (c8 >> 3) * kAtomBytes + (((c8 & 7) ^ (r & 7)) << 4), packed[4 * g],
-                 packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
   }
   return (sum[0] + sum[1]) + (sum[2] + sum[3]);
 }
 
 // ---- the kernel -----------------------------------------------------------------------
+// 128 registers per thread: 14 warps put 4 warps on some SM sub-partition, whose 16K
+// registers then allow 128 each.
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v,
-                   const __grid_constant__ CUtensorMap tm_o, const Params p) {
+                   const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles.
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -476,37 +504,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int *abort_flag = (volatile int *)(misc + kOffAbort);
   uint16_t *qw_s = (uint16_t *)(misc + kOffQw);
   float *invf_s = (float *)(misc + kOffInvFreq);
+  float *rowsum_s = (float *)(misc + kOffRowSum);
   auto bar = [&](uint32_t i) { return bars + 8u * i; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t nh = p.nh;
 
   if (threadIdx.x == 0) {
     for (int h = 0; h < 2; ++h) {
       mbar_init(bar(kBarQFull + h), 1);
-      mbar_init(bar(kBarQReady + h), 256);
-      mbar_init(bar(kBarQEmpty + h), 1);
-      mbar_init(bar(kBarSFull + h), 1);
-      mbar_init(bar(kBarPFull + h), 128);
-      mbar_init(bar(kBarODone + h), 1);
+      mbar_init(bar(kBarQReady + h), 128);
+      mbar_init(bar(kBarOFree + h), 128);
+      for (int s = 0; s < 2; ++s) {
+        mbar_init(bar(kBarSFull + 2 * h + s), 1);
+        mbar_init(bar(kBarPFull + 2 * h + s), 128);
+        mbar_init(bar(kBarLReady + 2 * h + s), 128);
+        mbar_init(bar(kBarPVDone + 2 * h + s), 1);
+      }
     }
+    mbar_init(bar(kBarStageFree), 128);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(kBarKVFull + s), 1);
       mbar_init(bar(kBarKVEmpty + s), 1);
     }
-    mbar_init(bar(kBarXform), 256);
     mbar_init(bar(kBarDrain), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (p.q_norm_w) {
     for (int i = threadIdx.x; i < 128; i += kThreads) qw_s[i] = p.q_norm_w[i];
-    for (int i = threadIdx.x; i < 64; i += kThreads)
-      invf_s[i] = (float)pow((double)p.theta, -2.0 * (double)i / 128.0);
+    for (int i = threadIdx.x; i < 64; i += kThreads) invf_s[i] = p.inv_freq[i];
   }
   if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_addr(tmem_slot)),
-                 "r"(512)
+                 "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -523,138 +555,137 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kTmaWarp) {
     // ---------------- TMA producer ----------------
+    // Load order per unit: K_0, K_1, then V_j, K_{j+2} for j = 0.. -- the order in which
+    // the issuer consumes them.
     if (lane == 0) {
-      uint32_t loads = 0, units_done = 0;
-      uint32_t armed[kStages] = {0, 0, 0};  // fills per slot (for the abort drain)
+      uint32_t loads = 0;
+      // Per ring slot: bit s = parity of its fills so far, bit 8+s = slot ever filled
+      // (for the abort drain).
+      uint32_t armed = 0;
       bool ok = true;
+      auto load_kv = [&](const CUtensorMap *map, const Unit &u, uint32_t j) {
+        const uint32_t slot = loads % kStages, round = loads / kStages;
+        if (round > 0 && !(ok = wait_phase(bar(kBarKVEmpty + slot), (round - 1) & 1,
+                                           abort_flag, p.status, kSiteKVEmpty)))
+          return;
+        const uint32_t dst = sbase + kOffKV + slot * kKVBytes;
+        mbar_expect_tx(bar(kBarKVFull + slot), kKVBytes);
+        for (int a = 0; a < 2; ++a)
+          tma_load_3d(dst + a * kKVAtom, map, bar(kBarKVFull + slot), a * 64, (int)u.kvh,
+                      (int)(u.tok0 + j * kKeys));
+        armed ^= 1u << slot;
+        armed |= 1u << (8 + slot);
+        ++loads;
+      };
       for (uint32_t ui = blockIdx.x; ok && ui < p.n_units; ui += gridDim.x) {
-        Unit u = decode(p, p.units[ui]);
+        const Unit u = decode(p, p.units[ui]);
         if (!u.nt) continue;
-        for (int h = 0; h < 2 && ok; ++h) {
-          if (units_done > 0 &&
-              !(ok = wait_phase(bar(kBarQEmpty + h), (units_done - 1) & 1, abort_flag,
-                                p.status, kSiteQEmpty)))
-            break;
-          mbar_expect_tx(bar(kBarQFull + h), kTileBytes);
-          for (int a = 0; a < 2; ++a)
-            tma_load_3d(sbase + kOffQ + h * kTileBytes + a * kAtomBytes, &tm_q,
-                        bar(kBarQFull + h), a * 64, (int)(u.head0 + h), (int)(u.tok0 + u.q0));
-        }
-        if (!ok) break;
-        ++units_done;
-        // Warm L2 with the next unit's tiles so that its TMA loads hit L2.
-        for (uint32_t un = ui + gridDim.x; un < p.n_units; un += gridDim.x) {
-          const Unit v = decode(p, p.units[un]);
-          if (!v.nt) continue;
-          for (int h = 0; h < 2; ++h)
-            for (int a = 0; a < 2; ++a)
-              tma_prefetch_3d(&tm_q, a * 64, (int)(v.head0 + h), (int)(v.tok0 + v.q0));
-          for (uint32_t j = 0; j < v.nt; ++j)
-            for (int a = 0; a < 2; ++a) {
-              tma_prefetch_3d(&tm_k, a * 64, (int)v.kvh, (int)(v.tok0 + j * kTile));
-              tma_prefetch_3d(&tm_v, a * 64, (int)v.kvh, (int)(v.tok0 + j * kTile));
-            }
-          break;
-        }
+        load_kv(&tm_k, u, 0);
+        if (ok && u.nt > 1) load_kv(&tm_k, u, 1);
         for (uint32_t j = 0; ok && j < u.nt; ++j) {
-          for (int which = 0; which < 2; ++which) {  // 0: K_j, 1: V_j
-            uint32_t slot = loads % kStages, round = loads / kStages;
-            if (round > 0 && !(ok = wait_phase(bar(kBarKVEmpty + slot), (round - 1) & 1,
-                                               abort_flag, p.status, kSiteKVEmpty)))
-              break;
-            uint32_t dst = sbase + kOffKV + slot * kTileBytes;
-            mbar_expect_tx(bar(kBarKVFull + slot), kTileBytes);
-            const CUtensorMap *map = which ? &tm_v : &tm_k;
-            for (int a = 0; a < 2; ++a)
-              tma_load_3d(dst + a * kAtomBytes, map, bar(kBarKVFull + slot), a * 64,
-                          (int)u.kvh, (int)(u.tok0 + j * kTile));
-            ++armed[slot];
-            ++loads;
-          }
+          load_kv(&tm_v, u, j);
+          if (ok && j + 2 < u.nt) load_kv(&tm_k, u, j + 2);
         }
       }
       if (!ok) {
-        // Every armed fill completes by itself: wait for the latest of each slot and for
-        // the Q fills so that no copy lands in shared memory after the CTA exits.
+        // Every armed fill completes by itself: wait for the latest of each slot so that
+        // no copy lands in shared memory after the CTA exits.
         for (int s = 0; s < kStages; ++s)
-          if (armed[s]) drain_phase(bar(kBarKVFull + s), (armed[s] - 1) & 1);
-        for (int h = 0; h < 2; ++h)
-          if (units_done) drain_phase(bar(kBarQFull + h), (units_done - 1) & 1);
+          if (bit(armed, 8 + s)) drain_phase(bar(kBarKVFull + s), bit(armed, s) ^ 1u);
       }
     }
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       uint32_t loads = 0, units_done = 0;
-      uint32_t pcount[2] = {0, 0};  // p_full completions consumed per head slot
-      bool ok = true;
-      const uint32_t tS[2] = {tmem + 0, tmem + 128};
-      const uint32_t tO[2] = {tmem + 256, tmem + 384};
-      const uint32_t q_tile[2] = {sbase + kOffQ, sbase + kOffQ + kTileBytes};
-      const uint32_t p_tile[2] = {sbase + kOffP, sbase + kOffP + kTileBytes};
-      bool issued = false;
-      for (uint32_t ui = blockIdx.x; ok && ui < p.n_units; ui += gridDim.x) {
-        Unit u = decode(p, p.units[ui]);
-        if (!u.nt) continue;
-        // K_0 and both Q tiles, then S_h = Q_h K_0^T.
-        uint32_t slotK = loads % kStages;
-        if (!(ok = wait_phase(bar(kBarKVFull + slotK), (loads / kStages) & 1, abort_flag,
+      uint32_t pbits = 0, obits = 0;  // parities: P-full per (head, S slot), O-free per head
+      bool ok = true, issued = false;
+      auto tS = [&](uint32_t h, uint32_t s) { return tmem + h * 256 + s * kKeys; };
+      auto tO = [&](uint32_t h) { return tmem + h * 256 + 2 * kKeys; };
+      uint32_t qbuf = 0;  // Q buffer of the current unit
+      // The next ring slot holding a K tile: wait for it, return its slot.
+      auto take_k = [&](uint32_t *slot) -> bool {
+        *slot = loads % kStages;
+        if (!(ok = wait_phase(bar(kBarKVFull + *slot), (loads / kStages) & 1, abort_flag,
                               p.status, kSiteKVFull)))
-          break;
+          return false;
         ++loads;
-        const uint32_t kt0 = sbase + kOffKV + slotK * kTileBytes;
-        for (int h = 0; h < 2 && ok; ++h) {
-          if (!(ok = wait_phase(bar(kBarQReady + h), units_done & 1, abort_flag, p.status,
-                                kSiteQReady)))
-            break;
-          tc_fence_after();
-          for (int ks = 0; ks < 8; ++ks)
-            umma(tS[h], kmajor_desc(q_tile[h], ks), kmajor_desc(kt0, ks), kIdescQK, ks > 0);
-          umma_commit(bar(kBarSFull + h));
-          if (u.nt == 1) umma_commit(bar(kBarQEmpty + h));
-          issued = true;
-        }
-        if (!ok) break;
+        tc_fence_after();
+        return true;
+      };
+      // S_h(slot_s) = Q_h K^T from ring slot `slot` (K-major, 64 keys x 128).  Descriptors
+      // of step 0; step ks adds its byte offset / 16 to the start-address field (addresses
+      // stay below 256 KB, so the field never carries).
+      auto qk_head = [&](uint32_t h, uint32_t slot_s, uint32_t slot) {
+        const uint64_t kd = kmajor_desc(sbase + kOffKV + slot * kKVBytes, 0, kKVAtom);
+        const uint64_t qd = kmajor_desc(sbase + kOffQ + qbuf * kQBufBytes + h * kQBytes, 0, kQAtom);
+        const uint32_t d = tS(h, slot_s);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma(d, qd + (uint64_t)((ks >> 2) * (kQAtom >> 4) + (ks & 3) * 2),
+               kd + (uint64_t)((ks >> 2) * (kKVAtom >> 4) + (ks & 3) * 2), kIdescQK, ks > 0);
+        umma_commit(bar(kBarSFull + 2 * h + slot_s));
+        issued = true;
+      };
+      for (uint32_t ui = blockIdx.x; ok && ui < p.n_units; ui += gridDim.x) {
+        const Unit u = decode(p, p.units[ui]);
+        if (!u.nt) continue;
+        // Work unit k uses Q buffer k % 2 (fill k / 2 of that buffer).
+        qbuf = units_done & 1;
+        if (!(ok = wait_phase(bar(kBarQReady + qbuf), (units_done >> 1) & 1, abort_flag,
+                              p.status, kSiteQReady)))
+          break;
         ++units_done;
-        umma_commit(bar(kBarKVEmpty + slotK));
+        tc_fence_after();
+        for (uint32_t j0 = 0; ok && j0 < 2 && j0 < u.nt; ++j0) {
+          uint32_t ks;
+          if (!take_k(&ks)) break;
+          for (uint32_t h = 0; h < nh; ++h) qk_head(h, j0, ks);
+          umma_commit(bar(kBarKVEmpty + ks));
+        }
         for (uint32_t j = 0; ok && j < u.nt; ++j) {
-          uint32_t slotV = loads % kStages;
+          const uint32_t slotV = loads % kStages;
           if (!(ok = wait_phase(bar(kBarKVFull + slotV), (loads / kStages) & 1, abort_flag,
                                 p.status, kSiteKVFull)))
             break;
           ++loads;
-          const uint32_t vt = sbase + kOffKV + slotV * kTileBytes;
-          const bool more = j + 1 < u.nt;
-          uint32_t slotN = 0, kt = 0;
-          for (int h = 0; h < 2 && ok; ++h) {
-            if (!(ok = wait_phase(bar(kBarPFull + h), pcount[h] & 1, abort_flag, p.status,
+          const uint32_t vt = sbase + kOffKV + slotV * kKVBytes;
+          const bool more = j + 2 < u.nt;
+          uint32_t slotK = 0;
+          // Per head: P.V of this tile, then at once that head's Q.K^T of tile j+2 into the
+          // S slot P.V has just read, so neither head waits for the other's softmax.
+          for (uint32_t h = 0; h < nh && ok; ++h) {
+            // One barrier per S slot: the softmax warps may finish the next tile before this
+            // wait, but not the one after (its S needs this P.V first).
+            const uint32_t pb = 2 * h + (j & 1);
+            if (!(ok = wait_phase(bar(kBarPFull + pb), bit(pbits, pb), abort_flag, p.status,
                                   kSitePFull)))
               break;
-            ++pcount[h];
+            pbits ^= 1u << pb;
+            if (j == 0 && units_done > 1) {
+              // O_h still holds the previous unit until the epilogue has read it.
+              if (!(ok = wait_phase(bar(kBarOFree + h), bit(obits, h), abort_flag, p.status,
+                                    kSiteOFree)))
+                break;
+              obits ^= 1u << h;
+            }
             tc_fence_after();
-            for (int ks = 0; ks < 8; ++ks)
-              umma(tO[h], kmajor_desc(p_tile[h], ks), mnmajor_desc(vt, ks), kIdescPV,
-                   (j > 0 || ks > 0) ? 1u : 0u);
-            umma_commit(bar(kBarODone + h));
+            const uint32_t pt = tS(h, j & 1);  // P: first 32 columns of the S slot
+            const uint32_t d = tO(h);
+            const uint64_t vd = mnmajor_desc(vt, 0);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              umma_ts(d, pt + ks * 8, vd + (uint64_t)(ks * (2048 >> 4)), kIdescPV,
+                      (j > 0 || ks > 0) ? 1u : 0u);
+            umma_commit(bar(kBarPVDone + 2 * h + (j & 1)));
             if (more) {
-              if (h == 0) {
-                slotN = loads % kStages;
-                if (!(ok = wait_phase(bar(kBarKVFull + slotN), (loads / kStages) & 1,
-                                      abort_flag, p.status, kSiteKVFull)))
-                  break;
-                ++loads;
-                tc_fence_after();
-                kt = sbase + kOffKV + slotN * kTileBytes;
-              }
-              for (int ks = 0; ks < 8; ++ks)
-                umma(tS[h], kmajor_desc(q_tile[h], ks), kmajor_desc(kt, ks), kIdescQK, ks > 0);
-              umma_commit(bar(kBarSFull + h));
-              if (j + 2 == u.nt) umma_commit(bar(kBarQEmpty + h));  // last QK_h of the unit
+              if (h == 0 && !take_k(&slotK)) break;
+              qk_head(h, j & 1, slotK);
             }
           }
           if (!ok) break;
-          if (more) umma_commit(bar(kBarKVEmpty + slotN));
           umma_commit(bar(kBarKVEmpty + slotV));
+          if (more) umma_commit(bar(kBarKVEmpty + slotK));
         }
       }
       if (issued) {
@@ -664,107 +695,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else {
-    // ---------------- q prologue, softmax and epilogue (one warpgroup per head slot) ----
-    const int hs = warp >> 2;                   // head slot
-    const uint32_t wq = (uint32_t)(warp & 3);   // warp within the warpgroup
-    const uint32_t r = wq * 32 + lane;          // tile row == TMEM lane
+  } else if (warp < kAuxWarp0) {
+    // ---------------- softmax (thread = query row of head slot h) ----------------------
+    const uint32_t h = (uint32_t)warp >> 2;
+    const uint32_t wq = (uint32_t)warp & 3;
+    const uint32_t r = wq * 32 + lane;  // tile row == TMEM lane
     const uint32_t lane_base = (wq * 32u) << 16;
-    const uint32_t tS = tmem + lane_base + hs * 128;
-    const uint32_t tO = tmem + lane_base + 256 + hs * 128;
-    const uint32_t prow = sbase + kOffP + hs * kTileBytes + r * 128;  // row r of P_h
-    // Output staging of this warp: the P rows it writes itself (rows 32*wq.. of each of
-    // the two atoms of P_h, 4 KB each), so only this warp's bulk stores read them.
-    const uint32_t stage[2] = {sbase + kOffP + hs * kTileBytes + wq * kStageBytes,
-                               sbase + kOffP + hs * kTileBytes + kAtomBytes + wq * kStageBytes};
-    uint32_t qcount = 0, scount = 0, ocount = 0;
+    const uint32_t tS0 = tmem + lane_base + h * 256;  // S slot s at tS0 + s * kKeys
+    const uint32_t tO = tmem + lane_base + h * 256 + 2 * kKeys;
+    // Parities per S slot: bits 0-1 S-full waits, bits 2-3 P.V issued from the slot.
+    uint32_t sbits = 0, units_seen = 0;
     bool ok = true;
-    // Q tiles of a unit: wait for both copies, apply the q prologue (both warpgroups,
-    // half the rotation pairs each), hand both tiles to the issuer.
-    uint32_t prepared = 0xffffffffu, xcount = 0;
-    auto prepare = [&](uint32_t index, const Unit &v) {
-      for (int h = 0; h < 2 && ok; ++h)
-        ok = __all_sync(0xffffffffu, wait_phase(bar(kBarQFull + h), qcount & 1, abort_flag,
-                                                p.status, kSiteQFull));
-      if (!ok) return;
-      ++qcount;
-      if (p.q_norm_w) {
-        float inv[2];
-        q_row_norms(sbase + kOffQ, r, p.eps, inv);
-        mbar_arrive(bar(kBarXform));
-        ok = __all_sync(0xffffffffu, wait_phase(bar(kBarXform), xcount & 1, abort_flag, p.status,
-                                                kSiteXform));
-        ++xcount;
-        if (!ok) return;
-        q_rotate_pair(sbase + kOffQ, r, v.q0 + r, hs, qw_s, invf_s, inv);
-        fence_proxy_async();
-      }
-      mbar_arrive(bar(kBarQReady + 0));
-      mbar_arrive(bar(kBarQReady + 1));
-      prepared = index;
-    };
-    for (uint32_t ui = blockIdx.x; ui < p.n_units; ui += gridDim.x) {
-      Unit u = decode(p, p.units[ui]);
-      if (!u.live) continue;
-      const uint32_t head = u.head0 + hs;
+    for (uint32_t ui = blockIdx.x; ok && h < nh && ui < p.n_units; ui += gridDim.x) {
+      const Unit u = decode(p, p.units[ui]);
+      if (!u.nt) continue;
       const uint32_t qpos = u.q0 + r;
-      const bool store = qpos < u.rows;
-      const size_t orow = ((size_t)(u.tok0 + qpos) * p.heads + head) * kTile;
-      if (!u.nt) {
-        // Zero valid keys: 0/0, as the reference's running sums give.
-        if (store) {
-          if (p.out_bf16) {
-            uint16_t *o = (uint16_t *)p.out + orow;
-            for (int c = 0; c < kTile; ++c) o[c] = 0x7fc0u;
-          } else {
-            float *o = (float *)p.out + orow;
-            for (int c = 0; c < kTile; ++c) o[c] = __int_as_float(0x7fc00000);
-          }
-        }
-        continue;
-      }
-      if (!ok) break;
-      if (prepared != ui) prepare(ui, u);
-      if (!ok) break;
-
       const uint32_t end = p.causal ? min(qpos + 1, u.n) : u.n;
       float m_ref = -INFINITY, l = 0.f;
       for (uint32_t j = 0; j < u.nt; ++j) {
-        ok = __all_sync(0xffffffffu, wait_phase(bar(kBarSFull + hs), scount & 1, abort_flag,
-                                                p.status, kSiteSFull));
+        const uint32_t s = j & 1;
+        ok = __all_sync(0xffffffffu, wait_phase(bar(kBarSFull + 2 * h + s), bit(sbits, s),
+                                                abort_flag, p.status, kSiteSFull));
         if (!ok) break;
-        ++scount;
+        sbits ^= 1u << s;
         tc_fence_after();
-        const int valid = (int)min(max((int)end - (int)(j * kTile), 0), kTile);
-        // Row maximum over the valid keys: chunks 0-1, then 2-3 (kept for the exp pass).
+        const int valid = (int)min(max((int)end - (int)(j * kKeys), 0), kKeys);
         uint32_t xa[32], xb[32];
+        tmem_ld32(tS0 + s * kKeys, xa);
+        tmem_ld32(tS0 + s * kKeys + 32, xb);
+        tmem_ld_wait();
         float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        tmem_ld32(tS + 0, xa);
-        tmem_ld32(tS + 32, xb);
-        tmem_ld_wait();
+        if (valid >= kKeys) {
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          if (t < valid) mq[t & 1] = fmaxf(mq[t & 1], __uint_as_float(xa[t]));
-          if (32 + t < valid) mq[2 + (t & 1)] = fmaxf(mq[2 + (t & 1)], __uint_as_float(xb[t]));
-        }
-        uint32_t xc[32], xd[32];
-        tmem_ld32(tS + 64, xc);
-        tmem_ld32(tS + 96, xd);
-        tmem_ld_wait();
+          for (int t = 0; t < 32; ++t) {
+            mq[t & 1] = fmaxf(mq[t & 1], __uint_as_float(xa[t]));
+            mq[2 + (t & 1)] = fmaxf(mq[2 + (t & 1)], __uint_as_float(xb[t]));
+          }
+        } else {
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          if (64 + t < valid) mq[t & 1] = fmaxf(mq[t & 1], __uint_as_float(xc[t]));
-          if (96 + t < valid) mq[2 + (t & 1)] = fmaxf(mq[2 + (t & 1)], __uint_as_float(xd[t]));
+          for (int t = 0; t < 32; ++t) {
+            if (t < valid) mq[t & 1] = fmaxf(mq[t & 1], __uint_as_float(xa[t]));
+            if (32 + t < valid) mq[2 + (t & 1)] = fmaxf(mq[2 + (t & 1)], __uint_as_float(xb[t]));
+          }
         }
-        const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-        const float mt = mx * p.scale_log2;
+        const float mt = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * p.scale_log2;
         if (j > 0) {
-          // P(j-1).V(j-1), which reads P and accumulates into O, has completed: the issuer
-          // committed s_full(j) after it, and a commit tracks every earlier tcgen05 op of
-          // the issuing thread.  Its o_done phase is therefore complete; count it.
-          ++ocount;
           // Rescale decision is per row; TMEM access is warp-wide (.sync.aligned), so
-          // the warp rescales when any of its rows needs it (others scale by 1).
+          // the warp rescales when any of its rows needs it (others scale by 1), after
+          // P.V of the previous tile has run.
           float corr = 1.0f;
           const bool need = mt > m_ref + kRescaleThreshold;
           if (need) {
@@ -773,142 +751,265 @@ __global__ void __launch_bounds__(kThreads, 1)
             m_ref = mt;
           }
           if (__any_sync(0xffffffffu, need)) {
-            for (int c = 0; c < 4; ++c) {
-              uint32_t o[32];
-              tmem_ld32(tO + c * 32, o);
+            const uint32_t ps = (j - 1) & 1;
+            ok = __all_sync(0xffffffffu,
+                            wait_phase(bar(kBarPVDone + 2 * h + ps), bit(sbits, 2 + ps) ^ 1u,
+                                       abort_flag, p.status, kSitePVDone));
+            if (!ok) break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < 8; ++c) {  // 16 columns at a time: S stays in registers
+              uint32_t o[16];
+              tmem_ld16(tO + c * 16, o);
               tmem_ld_wait();
 #pragma unroll
-              for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * corr);
-              tmem_st32(tO + c * 32, o);
+              for (int t = 0; t < 16; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * corr);
+              tmem_st16(tO + c * 16, o);
             }
             tmem_st_wait();
           }
         } else {
           m_ref = mt;
         }
-        if (j == 0) {
-          // P_h was the previous unit's output staging: its bulk stores must have read it.
-          if (lane == 0) bulk_wait_read<0>();
+        // P = exp2(S*scale*log2e - m) as bf16 pairs over the first 32 columns of the slot
+        // (keys 0-31 in columns 0-15, keys 32-63 in columns 16-31).
+        {
+          uint32_t packed[16];
+          if (valid >= kKeys) l += exp_chunk<false>(xa, 0, valid, p.scale_log2, m_ref, packed);
+          else l += exp_chunk<true>(xa, 0, valid, p.scale_log2, m_ref, packed);
+          tmem_st16(tS0 + s * kKeys, packed);
+          if (valid >= kKeys) l += exp_chunk<false>(xb, 1, valid, p.scale_log2, m_ref, packed);
+          else l += exp_chunk<true>(xb, 1, valid, p.scale_log2, m_ref, packed);
+          tmem_st16(tS0 + s * kKeys + 16, packed);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar(kBarPFull + 2 * h + s));
+        sbits ^= 1u << (2 + s);
+      }
+      if (!ok) break;
+      // Row sum of the unit for the epilogue warps.
+      rowsum_s[(h * 2 + (units_seen & 1)) * 128 + r] = l;
+      mbar_arrive(bar(kBarLReady + 2 * h + (units_seen & 1)));
+      ++units_seen;
+    }
+  } else {
+    // ---------------- epilogue and q prologue (thread = row of every head slot) --------
+    const uint32_t wq = (uint32_t)warp & 3;
+    const uint32_t r = wq * 32 + lane;
+    const uint32_t lane_base = (wq * 32u) << 16;
+    const bool leader = threadIdx.x == kAuxWarp0 * 32;  // issues the Q loads
+    // Per head h: bits 2h..2h+1 = units whose row sums were taken (mod 4);
+    // bits 4+2h+s = parity of the P.V count of S slot s.
+    uint32_t lbits = 0;
+    // Leader, per Q buffer b: bit b = parity of its fills, bit 2+b = ever filled.
+    uint32_t qarmed = 0;
+    bool ok = true;
+    const uint32_t srow = (uint32_t)lane * 128, sw = (uint32_t)lane & 7;
+    // The next unit at or after index `from` that has work (nt > 0).
+    auto next_work = [&](uint32_t from) -> uint32_t {
+      for (uint32_t ui = from; ui < p.n_units; ui += gridDim.x)
+        if (decode(p, p.units[ui]).nt) return ui;
+      return p.n_units;
+    };
+    // Leader: TMA load of the Q tiles of unit `ui` into buffer b.
+    auto load_q = [&](uint32_t ui, uint32_t b) {
+      const Unit v = decode(p, p.units[ui]);
+      mbar_expect_tx(bar(kBarQFull + b), nh * kQBytes);
+      for (uint32_t h = 0; h < nh; ++h)
+        for (int a = 0; a < 2; ++a)
+          tma_load_3d(sbase + kOffQ + b * kQBufBytes + h * kQBytes + a * kQAtom, &tm_q,
+                      bar(kBarQFull + b), a * 64, (int)(v.head0 + h), (int)(v.tok0 + v.q0));
+      qarmed ^= 1u << b;
+      qarmed |= 1u << (2 + b);
+    };
+    // Wait for fill `phase` of buffer b, apply the q prologue, hand the tiles to the issuer.
+    auto prepare = [&](uint32_t ui, uint32_t b, uint32_t phase) {
+      ok = __all_sync(0xffffffffu, wait_phase(bar(kBarQFull + b), phase & 1, abort_flag,
+                                              p.status, kSiteQFull));
+      if (!ok) return;
+      if (p.q_norm_w) {
+        const Unit v = decode(p, p.units[ui]);
+        q_transform_rows(sbase + kOffQ + b * kQBufBytes, r, v.q0 + r, nh, qw_s, invf_s, p.eps);
+        fence_proxy_async();
+      }
+      mbar_arrive(bar(kBarQReady + b));
+    };
+    // Epilogue of unit v: per head, wait for its row sums and last P.V, read O out of
+    // tensor memory (then release it to the next unit), normalise, store.  Warps whose 32
+    // rows all lie inside the sequence stage them in the unit's Q buffer (free once every
+    // Q.K^T of the unit has run, which the row sums imply) and send TMA bulk-tensor
+    // stores; a warp at a ragged end stores row by row.
+    auto epilogue = [&](const Unit &v, uint32_t stage) {
+      const uint32_t qpos = v.q0 + r;
+      const bool store = qpos < v.rows;
+      const uint32_t wrow0 = v.q0 + wq * 32;
+      const bool bulk = wrow0 + 32 <= v.rows;
+      for (uint32_t h = 0; h < nh && ok; ++h) {
+        // One barrier per unit parity: while this warpgroup works on head 0, the softmax
+        // warps of head 1 may finish this unit and the next one, but not a third.
+        const uint32_t lc = (lbits >> (2 * h)) & 3u;  // unit count mod 4 for this head
+        ok = __all_sync(0xffffffffu,
+                        wait_phase(bar(kBarLReady + 2 * h + (lc & 1)), (lc >> 1) & 1,
+                                   abort_flag, p.status, kSiteLReady));
+        if (!ok) break;
+        const float l = rowsum_s[(h * 2 + (lc & 1)) * 128 + r];
+        lbits = (lbits & ~(3u << (2 * h))) | (((lc + 1) & 3u) << (2 * h));
+        lbits ^= (((v.nt + 1) / 2) & 1u) << (4 + 2 * h);
+        lbits ^= ((v.nt / 2) & 1u) << (5 + 2 * h);
+        const uint32_t ls = (v.nt - 1) & 1;
+        ok = __all_sync(0xffffffffu, wait_phase(bar(kBarPVDone + 2 * h + ls),
+                                                bit(lbits, 4 + 2 * h + ls) ^ 1u, abort_flag,
+                                                p.status, kSitePVDone));
+        if (!ok) break;
+        tc_fence_after();
+        const float inv = 1.0f / l;
+        const uint32_t tO = tmem + lane_base + h * 256 + 2 * kKeys;
+        const uint32_t head = v.head0 + h;
+        const size_t orow = ((size_t)(v.tok0 + qpos) * p.heads + head) * 128;
+        // This warp's stores of the previous head must have read the staging rows.
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+        if (!p.out_bf16) {
+#pragma unroll 1
+          for (int c = 0; c < 4; c += 2) {
+            uint32_t xa[32], xb[32];
+            tmem_ld32(tO + c * 32, xa);
+            tmem_ld32(tO + c * 32 + 32, xb);
+            tmem_ld_wait();
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+              xa[t] = __float_as_uint(__uint_as_float(xa[t]) * inv);
+              xb[t] = __float_as_uint(__uint_as_float(xb[t]) * inv);
+            }
+            if (bulk) {
+              const uint32_t b0 = stage + c * kStageChunk + wq * kWarpBox + srow;
+#pragma unroll
+              for (int g = 0; g < 8; ++g) {
+                st_shared_v4(b0 + (((uint32_t)g ^ sw) << 4), xa[4 * g], xa[4 * g + 1],
+                             xa[4 * g + 2], xa[4 * g + 3]);
+                st_shared_v4(b0 + kStageChunk + (((uint32_t)g ^ sw) << 4), xb[4 * g],
+                             xb[4 * g + 1], xb[4 * g + 2], xb[4 * g + 3]);
+              }
+            } else if (store) {
+              float4 *o = (float4 *)((float *)p.out + orow + c * 32);
+#pragma unroll
+              for (int g = 0; g < 8; ++g) {
+                o[g] = make_float4(__uint_as_float(xa[4 * g]), __uint_as_float(xa[4 * g + 1]),
+                                   __uint_as_float(xa[4 * g + 2]), __uint_as_float(xa[4 * g + 3]));
+                o[8 + g] = make_float4(__uint_as_float(xb[4 * g]), __uint_as_float(xb[4 * g + 1]),
+                                       __uint_as_float(xb[4 * g + 2]),
+                                       __uint_as_float(xb[4 * g + 3]));
+              }
+            }
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {  // 32 columns (64 bytes of bf16) at a time
+            uint32_t x[32], w[16];
+            tmem_ld32(tO + c * 32, x);
+            tmem_ld_wait();
+#pragma unroll
+            for (int t = 0; t < 16; ++t)
+              w[t] = pack_bf16x2(__uint_as_float(x[2 * t]) * inv,
+                                 __uint_as_float(x[2 * t + 1]) * inv);
+            if (bulk) {
+              // Columns 32c.. are 16-byte units 4(c&1).. of the 128-byte row of chunk c/2.
+              const uint32_t b0 = stage + (c >> 1) * kStageChunk + wq * kWarpBox + srow;
+#pragma unroll
+              for (int g = 0; g < 4; ++g)
+                st_shared_v4(b0 + (((uint32_t)(4 * (c & 1) + g) ^ sw) << 4), w[4 * g],
+                             w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+            } else if (store) {
+              uint4 *o = (uint4 *)((uint16_t *)p.out + orow + c * 32);
+#pragma unroll
+              for (int g = 0; g < 4; ++g)
+                o[g] = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+            }
+          }
+        }
+        // O_h has been read: the next unit's first P.V may overwrite it.
+        tc_fence_before();
+        mbar_arrive(bar(kBarOFree + h));
+        if (bulk) {
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            const int nchunks = p.out_bf16 ? 2 : 4, width = p.out_bf16 ? 64 : 32;
+            for (int c = 0; c < nchunks; ++c)
+              tma_store_3d(&tm_o, stage + c * kStageChunk + wq * kWarpBox, c * width, (int)head,
+                           (int)(v.tok0 + wrow0));
+            bulk_commit();
+          }
           __syncwarp();
         }
-        // Probabilities -> bf16 -> P tile: chunks 2-3 from registers while chunks 0-1 are
-        // loaded again from TMEM.
-        tmem_ld32(tS + 0, xa);
-        l += emit_p(xc, 2, valid, p.scale_log2, m_ref, prow, r);
-        tmem_ld32(tS + 32, xb);
-        l += emit_p(xd, 3, valid, p.scale_log2, m_ref, prow, r);
-        tmem_ld_wait();
-        l += emit_p(xa, 0, valid, p.scale_log2, m_ref, prow, r);
-        l += emit_p(xb, 1, valid, p.scale_log2, m_ref, prow, r);
-        fence_proxy_async();
-        tc_fence_before();
-        mbar_arrive(bar(kBarPFull + hs));
       }
-      if (!ok) break;
-      // Hand the next unit's Q tiles to the issuer before this unit's epilogue, so the
-      // tensor cores start on it while the output leaves.
-      for (uint32_t un = ui + gridDim.x; un < p.n_units; un += gridDim.x) {
-        const Unit v = decode(p, p.units[un]);
-        if (v.live && v.nt) {
-          prepare(un, v);
-          break;
-        }
-      }
-      if (!ok) break;
-      // Epilogue: wait for the last P.V, normalise, store.  Warps whose 32 rows are all
-      // inside the sequence stage their rows (swizzled, in the now free P tile) and send
-      // them with TMA bulk-tensor stores; a warp at a ragged end stores row by row.
-      ok = __all_sync(0xffffffffu, wait_phase(bar(kBarODone + hs), ocount & 1, abort_flag,
-                                              p.status, kSiteODone));
-      if (!ok) break;
-      ++ocount;
-      tc_fence_after();
-      const float inv = 1.0f / l;
-      const uint32_t wrow0 = u.q0 + wq * 32;
-      const bool bulk = wrow0 + 32 <= u.rows;
-      const uint32_t srow0 = (uint32_t)lane * 128;
-      const uint32_t sw = (uint32_t)lane & 7;
-      if (!p.out_bf16) {
-        uint32_t ob[2][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if ((c & 1) == 0) {  // two 32-column chunks per TMEM round trip
-            tmem_ld32(tO + c * 32, ob[0]);
-            tmem_ld32(tO + c * 32 + 32, ob[1]);
-            tmem_ld_wait();
-          }
-          uint32_t (&x)[32] = ob[c & 1];
-#pragma unroll
-          for (int t = 0; t < 32; ++t) x[t] = __float_as_uint(__uint_as_float(x[t]) * inv);
-          if (bulk) {
-            const uint32_t buf = stage[c & 1];
-            if (c >= 2) {
-              if (lane == 0) bulk_wait_read<1>();
-              __syncwarp();
+    };
+
+    // Q tiles of the first two work units, then per work unit k: its epilogue, and the Q
+    // tiles of work unit k+2 into the buffer the epilogue has just drained.
+    const uint32_t first = next_work(blockIdx.x);
+    uint32_t next = first < p.n_units ? next_work(first + gridDim.x) : p.n_units;
+    if (leader) {
+      if (first < p.n_units) load_q(first, 0);
+      if (next < p.n_units) load_q(next, 1);
+    }
+    if (first < p.n_units) prepare(first, 0, 0);
+    if (ok && next < p.n_units) prepare(next, 1, 0);
+    uint32_t k = 0;  // work units done
+    for (uint32_t ui = blockIdx.x; ok && ui < p.n_units; ui += gridDim.x) {
+      const Unit u = decode(p, p.units[ui]);
+      if (!u.live) continue;
+      if (!u.nt) {
+        // Zero valid keys: 0/0, as the reference's running sums give.
+        const uint32_t qpos = u.q0 + r;
+        if (qpos < u.rows) {
+          for (uint32_t h = 0; h < nh; ++h) {
+            const size_t orow = ((size_t)(u.tok0 + qpos) * p.heads + u.head0 + h) * 128;
+            if (p.out_bf16) {
+              uint16_t *o = (uint16_t *)p.out + orow;
+              for (int c = 0; c < 128; ++c) o[c] = 0x7fc0u;
+            } else {
+              float *o = (float *)p.out + orow;
+              for (int c = 0; c < 128; ++c) o[c] = __int_as_float(0x7fc00000);
             }
-#pragma unroll
-            for (int g = 0; g < 8; ++g)
-              st_shared_v4(buf + srow0 + (((uint32_t)g ^ sw) << 4), x[4 * g], x[4 * g + 1],
-                           x[4 * g + 2], x[4 * g + 3]);
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_3d(&tm_o, buf, c * 32, (int)head, (int)(u.tok0 + wrow0));
-              bulk_commit();
-            }
-          } else if (store) {
-            float4 *o = (float4 *)((float *)p.out + orow + c * 32);
-#pragma unroll
-            for (int g = 0; g < 8; ++g)
-              o[g] = make_float4(__uint_as_float(x[4 * g]), __uint_as_float(x[4 * g + 1]),
-                                 __uint_as_float(x[4 * g + 2]), __uint_as_float(x[4 * g + 3]));
           }
         }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t w[32];
-          uint32_t xa[32], xb[32];
-          tmem_ld32(tO + c * 64, xa);
-          tmem_ld32(tO + c * 64 + 32, xb);
-          tmem_ld_wait();
-#pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            w[t] = pack_bf16x2(__uint_as_float(xa[2 * t]) * inv, __uint_as_float(xa[2 * t + 1]) * inv);
-            w[16 + t] =
-                pack_bf16x2(__uint_as_float(xb[2 * t]) * inv, __uint_as_float(xb[2 * t + 1]) * inv);
-          }
-          if (bulk) {
-            const uint32_t buf = stage[c];
-#pragma unroll
-            for (int g = 0; g < 8; ++g)
-              st_shared_v4(buf + srow0 + (((uint32_t)g ^ sw) << 4), w[4 * g], w[4 * g + 1],
-                           w[4 * g + 2], w[4 * g + 3]);
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_3d(&tm_o, buf, c * 64, (int)head, (int)(u.tok0 + wrow0));
-              bulk_commit();
-            }
-          } else if (store) {
-            uint4 *o = (uint4 *)((uint16_t *)p.out + orow + c * 64);
-#pragma unroll
-            for (int g = 0; g < 8; ++g)
-              o[g] = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
-          }
-        }
+        continue;
       }
-      tc_fence_before();
+      const uint32_t b = k & 1;
+      epilogue(u, sbase + kOffQ + b * kQBufBytes);
+      if (!ok) break;
+      const uint32_t ahead = next < p.n_units ? next_work(next + gridDim.x) : p.n_units;
+      // Buffer b is free once this warpgroup's stores have read it.
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+      mbar_arrive(bar(kBarStageFree));
+      if (ahead < p.n_units) {
+        if (leader) {
+          if (wait_phase(bar(kBarStageFree), k & 1, abort_flag, p.status, kSiteStageFree))
+            load_q(ahead, b);
+        }
+        prepare(ahead, b, (k + 2) >> 1);
+      }
+      next = ahead;
+      ++k;
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
+    if (!ok && leader) {
+      // No Q fill may land in shared memory after the CTA exits.
+      for (int b2 = 0; b2 < 2; ++b2)
+        if (bit(qarmed, 2 + b2)) drain_phase(bar(kBarQFull + b2), bit(qarmed, b2) ^ 1u);
+    }
   }
 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == kMmaWarp) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
                  : "memory");
   }
 }
@@ -920,9 +1021,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 bool tc_attention_supported(const AttnProblem &p) {
   if (p.dim != 128 || p.in_dtype != 1) return false;
   if (!p.kv_heads || p.heads % p.kv_heads) return false;
-  uint32_t group = p.heads / p.kv_heads;
-  if (group % 2) return false;            // head pairs must share one kv head
-  if (p.heads / 2 > 64) return false;     // pair index has 6 bits
+  if (p.heads > 64) return false;                   // head (pair) index has 6 bits
   if ((uint64_t)p.seq > 255u * 128u) return false;  // tile index has 8 bits
   if (p.batch >= (1u << 18)) return false;
   if ((uintptr_t)p.q % 16 || (uintptr_t)p.k % 16 || (uintptr_t)p.v % 16 || (uintptr_t)p.out % 16)
@@ -930,22 +1029,30 @@ bool tc_attention_supported(const AttnProblem &p) {
   return true;
 }
 
+namespace {
+// Query heads per unit: pairs when the heads per kv head are even (both heads of a
+// pair read the same K/V), else one.
+uint32_t heads_per_unit(const AttnProblem &p) {
+  return (p.heads / p.kv_heads) % 2 == 0 ? 2u : 1u;
+}
+}  // namespace
+
 uint32_t tc_max_units(const AttnProblem &p) {
-  uint32_t tiles = (p.seq + tc::kTile - 1) / tc::kTile;
-  return p.batch * (p.heads / 2) * tiles;
+  uint32_t tiles = (p.seq + tc::kQRows - 1) / tc::kQRows;
+  return p.batch * (p.heads / heads_per_unit(p)) * tiles;
 }
 
-// Longest-first list of units.  Cost of a unit = key tiles it visits (host lengths
-// known) or, without host lengths, its query-tile index (later tiles of a causal
-// sequence visit more key tiles).
+// Longest-first list of units, built without allocating: a counting sort on the cost of
+// a unit (key tiles it visits, 0..510), stable, so the units of one (sequence, query
+// tile) -- whose heads share K/V tiles through their kv head -- stay adjacent.  Without
+// host lengths the cost is an estimate from the query-tile index (later tiles of a
+// causal sequence visit more key tiles).
 uint32_t tc_build_units(const AttnProblem &p, const uint32_t *lengths_host, const int32_t *cu_host,
                         uint32_t *units) {
-  const uint32_t tiles = (p.seq + tc::kTile - 1) / tc::kTile;
-  const uint32_t pairs = p.heads / 2;
-  struct Item { uint32_t cost, code; };
-  std::vector<Item> items;
-  items.reserve((size_t)p.batch * pairs * tiles);
-  for (uint32_t s = 0; s < p.batch; ++s) {
+  constexpr uint32_t kMaxCost = 511;
+  const uint32_t tiles = (p.seq + tc::kQRows - 1) / tc::kQRows;
+  const uint32_t per_tile = p.heads / heads_per_unit(p);
+  auto cost_of = [&](uint32_t s, uint32_t t, uint32_t *rows_out) -> uint32_t {
     uint32_t n, rows;
     bool known = false;
     if (p.cu_seqlens) {
@@ -962,23 +1069,35 @@ uint32_t tc_build_units(const AttnProblem &p, const uint32_t *lengths_host, cons
       n = lengths_host ? std::min(lengths_host[s], p.seq) : p.seq;
       known = lengths_host != nullptr;
     }
+    *rows_out = rows;
+    const uint32_t q0 = t * tc::kQRows;
+    uint32_t kend;
+    if (known) kend = p.causal ? std::min(q0 + (uint32_t)tc::kQRows, n) : n;
+    else kend = p.causal ? std::min(q0 + (uint32_t)tc::kQRows, p.seq) : p.seq;
+    return std::min((kend + tc::kKeys - 1) / tc::kKeys, kMaxCost);
+  };
+  uint32_t count[kMaxCost + 1] = {};
+  for (uint32_t s = 0; s < p.batch; ++s)
     for (uint32_t t = 0; t < tiles; ++t) {
-      uint32_t q0 = t * tc::kTile;
-      if (q0 >= rows) break;
-      uint32_t cost;
-      if (known) {
-        uint32_t kend = p.causal ? std::min(q0 + (uint32_t)tc::kTile, n) : n;
-        cost = (kend + tc::kTile - 1) / tc::kTile;
-      } else {
-        cost = p.causal ? t + 1 : tiles;
-      }
-      for (uint32_t hp = 0; hp < pairs; ++hp) items.push_back({cost, tc::encode_unit(s, hp, t)});
+      uint32_t rows;
+      const uint32_t c = cost_of(s, t, &rows);
+      if (t * tc::kQRows >= rows) break;
+      count[c] += per_tile;
     }
+  uint32_t start[kMaxCost + 1];
+  uint32_t total = 0;
+  for (int c = (int)kMaxCost; c >= 0; --c) {  // highest cost first
+    start[c] = total;
+    total += count[c];
   }
-  std::stable_sort(items.begin(), items.end(),
-                   [](const Item &a, const Item &b) { return a.cost > b.cost; });
-  for (size_t i = 0; i < items.size(); ++i) units[i] = items[i].code;
-  return (uint32_t)items.size();
+  for (uint32_t s = 0; s < p.batch; ++s)
+    for (uint32_t t = 0; t < tiles; ++t) {
+      uint32_t rows;
+      const uint32_t c = cost_of(s, t, &rows);
+      if (t * tc::kQRows >= rows) break;
+      for (uint32_t i = 0; i < per_tile; ++i) units[start[c]++] = tc::encode_unit(s, i, t);
+    }
+  return total;
 }
 
 namespace {
@@ -998,8 +1117,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 3-D map over a [rows, heads, 128] tensor; a box is box_rows rows x 1 head x 128 bytes
-// of elements, in the 128-byte swizzle.
+// 3-D map over a [rows, heads, 128] tensor of bf16 (or fp32); a box is box_rows rows x
+// 1 head x 128 bytes of elements, in the 128-byte swizzle.
 bool make_map(CUtensorMap *map, const void *base, uint32_t rows, uint32_t heads, bool f32,
               uint32_t box_rows) {
   auto fn = encode_fn();
@@ -1024,9 +1143,9 @@ cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uin
   if (!n_units) return cudaSuccess;
   CUtensorMap mq, mk, mv, mo;
   const uint32_t rows = p.total;
-  if (!make_map(&mq, p.q, rows, p.heads, false, 128) ||
-      !make_map(&mk, p.k, rows, p.kv_heads, false, 128) ||
-      !make_map(&mv, p.v, rows, p.kv_heads, false, 128) ||
+  if (!make_map(&mq, p.q, rows, p.heads, false, tc::kQRows) ||
+      !make_map(&mk, p.k, rows, p.kv_heads, false, tc::kKeys) ||
+      !make_map(&mv, p.v, rows, p.kv_heads, false, tc::kKeys) ||
       !make_map(&mo, p.out, rows, p.heads, p.out_dtype == 0, 32))
     return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(tc::attn_tc_kernel,
@@ -1042,13 +1161,15 @@ cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uin
   prm.seq = p.seq;
   prm.heads = p.heads;
   prm.group = p.heads / p.kv_heads;
+  prm.nh = heads_per_unit(p);
   prm.causal = p.causal;
   prm.out_bf16 = p.out_dtype == 1;
   prm.scale_log2 = p.scale * 1.4426950408889634f;
   prm.status = status;
   prm.q_norm_w = q_norm_w;
   prm.eps = eps;
-  prm.theta = theta;
+  for (int i = 0; i < 64; ++i)
+    prm.inv_freq[i] = (float)std::pow((double)theta, -2.0 * (double)i / 128.0);
   uint32_t grid = std::min<uint32_t>(n_units, (uint32_t)num_sms);
   tc::attn_tc_kernel<<<grid, tc::kThreads, tc::kSmemBytes, stream>>>(mq, mk, mv, mo, prm);
   return cudaGetLastError();

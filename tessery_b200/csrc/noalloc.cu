@@ -21,8 +21,9 @@
 
 namespace {
 
-// Capacity of the work list: units = batch * (heads / 2) * ceil(seq / 128).
-constexpr uint32_t kNoAllocMaxUnits = 16384;
+// Capacity of the work list: units = batch * heads/2 * ceil(seq / 128) (heads, not
+// pairs, when the query heads per kv head are odd).
+constexpr uint32_t kNoAllocMaxUnits = 32768;
 // Word 0: status word used when the caller passes no status pointer.  Words 64..: units.
 constexpr uint32_t kHeaderWords = 64;
 
@@ -35,35 +36,6 @@ std::mutex g_noalloc_mu;
 uint32_t *g_noalloc_ptr[64] = {};
 int g_noalloc_sms[64] = {};
 uint32_t g_host_units[kNoAllocMaxUnits];  // host copy of the work list (under the mutex)
-
-// Longest-first unit list like tc_build_units, built without any allocation: units are
-// bucketed by cost (key tiles visited, 1..255) with a counting sort that keeps
-// generation order within a cost.
-uint32_t build_units_noalloc(const tx::AttnProblem &p, const uint32_t *lengths_host,
-                             uint32_t *units) {
-  const uint32_t tiles = (p.seq + 127) / 128, pairs = p.heads / 2;
-  uint32_t count[257] = {};
-  auto cost_of = [&](uint32_t s, uint32_t t) {
-    const uint32_t n = lengths_host[s] < p.seq ? lengths_host[s] : p.seq;
-    const uint32_t q0 = t * 128;
-    const uint32_t kend = p.causal ? (q0 + 128 < n ? q0 + 128 : n) : n;
-    return (kend + 127) / 128;
-  };
-  for (uint32_t s = 0; s < p.batch; ++s)
-    for (uint32_t t = 0; t < tiles; ++t) count[cost_of(s, t)] += pairs;
-  uint32_t start[257];
-  uint32_t acc = 0;
-  for (int c = 256; c >= 0; --c) {  // highest cost first
-    start[c] = acc;
-    acc += count[c];
-  }
-  for (uint32_t s = 0; s < p.batch; ++s)
-    for (uint32_t t = 0; t < tiles; ++t) {
-      const uint32_t c = cost_of(s, t);
-      for (uint32_t hp = 0; hp < pairs; ++hp) units[start[c]++] = (s << 14) | (hp << 8) | t;
-    }
-  return acc;
-}
 
 }  // namespace
 
@@ -103,7 +75,8 @@ extern "C" int tx_attention_padded_noalloc(const void *q, const void *k, const v
   uint32_t *scratch = g_noalloc_ptr[device];
   cudaStream_t s = (cudaStream_t)stream;
   int *st = status ? status : (int *)scratch;
-  const uint32_t n = build_units_noalloc(p, lengths_host, g_host_units);
+  // tc_build_units sorts with fixed-size arrays on the stack: no allocation.
+  const uint32_t n = tx::tc_build_units(p, lengths_host, nullptr, g_host_units);
   // The array keeps the previous call's contents: the status word must start at zero.
   if (cudaMemsetAsync(st, 0, sizeof(int), s) != cudaSuccess) return TX_ECUDA;
   if (n && cudaMemcpyAsync(scratch + kHeaderWords, g_host_units, n * sizeof(uint32_t),

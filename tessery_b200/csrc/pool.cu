@@ -9,10 +9,11 @@
 //                  form normalises just those rows, with the same per-row arithmetic.
 //   CLS pooling    bert.py:236-244 (first_token = 1, no norm).
 //
-// One warp per sequence; the row is read with 128-bit loads when it is 16-byte aligned
-// (cols a multiple of 4 for fp32, 8 for bf16), scalar loads otherwise.  A sequence with
-// no valid row (length 0, length > seq, or an empty packed range) gets a NaN row: the
-// reference would read outside the sequence there.
+// One warp per sequence.  Rows of up to 1024 columns that are 16-byte aligned (cols a
+// multiple of 4 for fp32, 8 for bf16) are loaded whole into registers with vector loads,
+// so a row costs one memory round trip; other rows are walked in strided passes.  A
+// sequence with no valid row (length 0, length > seq, or an empty packed range) gets a
+// NaN row: the reference would read outside the sequence there.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -43,6 +44,8 @@ __device__ __forceinline__ float normed(float x, float inv, const uint16_t *w, u
   return w ? x * inv * bf16_bits_to_f32(w[c]) : x;
 }
 
+constexpr int kHeld = 8;  // float4 groups per lane held in registers: rows up to 1024 cols
+
 template <typename TI>
 __global__ void __launch_bounds__(128) pool_project_kernel(PoolProblem p) {
   const uint32_t b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -65,6 +68,54 @@ __global__ void __launch_bounds__(128) pool_project_kernel(PoolProblem p) {
   const TI *x = (const TI *)p.x + (uint64_t)row * p.cols;
   const bool vec = p.vector_ok;
   const uint16_t *w = p.norm_w;
+
+  if (vec && p.cols <= 128 * kHeld) {
+    // The whole row in registers: every load is issued before the first use, so the row
+    // costs one memory round trip.
+    float v[kHeld][4];
+#pragma unroll
+    for (int i = 0; i < kHeld; ++i) {
+      const uint32_t c = 4 * lane + 128 * i;
+      if (c < p.cols) load4(x, c, v[i]);
+      else v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.f;
+    }
+    float inv = 1.f;
+    if (w) {
+      float sq = 0.f;
+#pragma unroll
+      for (int i = 0; i < kHeld; ++i)
+        sq += v[i][0] * v[i][0] + v[i][1] * v[i][1] + v[i][2] * v[i][2] + v[i][3] * v[i][3];
+      inv = 1.0f / sqrtf(warp_sum(sq) / (float)p.cols + p.eps);
+#pragma unroll
+      for (int i = 0; i < kHeld; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t c = 4 * lane + 128 * i + e;
+          v[i][e] = c < p.cols ? normed(v[i][e], inv, w, c) : 0.f;
+        }
+    }
+    float sq = 0.f;
+#pragma unroll
+    for (int i = 0; i < kHeld; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (4 * lane + 128 * i + e < p.dim) sq += v[i][e] * v[i][e];
+    const float scale = 1.0f / sqrtf(warp_sum(sq));
+    const bool out_vec = p.dim % 4 == 0 && ((uintptr_t)p.out & 15) == 0;
+#pragma unroll
+    for (int i = 0; i < kHeld; ++i) {
+      const uint32_t c = 4 * lane + 128 * i;
+      if (out_vec && c + 4 <= p.dim) {
+        *(float4 *)(out + c) = make_float4(v[i][0] * scale, v[i][1] * scale, v[i][2] * scale,
+                                           v[i][3] * scale);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (c + e < p.dim) out[c + e] = v[i][e] * scale;
+      }
+    }
+    return;
+  }
 
   // RMS of the whole row (only when the final norm is fused).
   float inv = 1.f;

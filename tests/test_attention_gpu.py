@@ -218,19 +218,36 @@ def test_extreme_logits_bf16_tensor_core(runtime):
     the bf16 tensor-core path."""
     for case in [c for c in CASES if c.test.startswith("test_tiled_attention_extreme")]:
         inp = regenerate(case)
-        # 2 heads / 2 kv heads in the reference; tensor-core head pairs share a kv head,
-        # so run 4 query heads over the same 2 kv heads.
-        q2 = np.concatenate([inp["q"], inp["q"]], axis=2)
         k, v = inp["k"], inp["v"]
         causal = not case.dispatch["bidirectional"]
-        got = attention(to_bf16_bits(q2), to_bf16_bits(k), to_bf16_bits(v),
-                        lengths=inp["lengths"], causal=causal, runtime=runtime)
+        # The reference's 2 heads / 2 kv heads, and 4 query heads over the same 2 kv heads
+        # (GQA group 2).
+        for q2 in (inp["q"], np.concatenate([inp["q"], inp["q"]], axis=2)):
+            got = attention(to_bf16_bits(q2), to_bf16_bits(k), to_bf16_bits(v),
+                            lengths=inp["lengths"], causal=causal, runtime=runtime)
+            assert runtime.last_kernel() == "tc_bf16_d128"
+            want = oracle.attention_padded(q2, from_bf16_bits(to_bf16_bits(k)),
+                                           from_bf16_bits(to_bf16_bits(v)), inp["lengths"],
+                                           causal, 128**-0.5)
+            # No overflow at +-1131 logits, and the masked 1e10 values never leak.
+            assert np.max(np.abs(got - want)) <= BF16_GATE, case.id
+
+
+@pytest.mark.parametrize("heads,kv_heads", [(6, 2), (3, 3), (16, 1)])
+def test_tensor_core_any_gqa_group(runtime, heads, kv_heads):
+    """Query heads per kv head of 3 (odd), 1 (MHA) and 16 on the tensor-core kernel."""
+    rng = np.random.default_rng(heads * 10 + kv_heads)
+    lengths = np.array([1, 130, 64, 200], np.uint32)
+    B, L, D = 4, 200, 128
+    q = to_bf16_bits(rng.normal(size=(B, L, heads, D)).astype(np.float32))
+    k = to_bf16_bits(rng.normal(size=(B, L, kv_heads, D)).astype(np.float32))
+    v = to_bf16_bits(rng.normal(size=(B, L, kv_heads, D)).astype(np.float32))
+    for causal in (True, False):
+        got = attention(q, k, v, lengths=lengths, causal=causal, runtime=runtime)
         assert runtime.last_kernel() == "tc_bf16_d128"
-        want = oracle.attention_padded(q2, from_bf16_bits(to_bf16_bits(k)),
-                                       from_bf16_bits(to_bf16_bits(v)), inp["lengths"], causal,
-                                       128**-0.5)
-        # No overflow at +-1131 logits, and the masked 1e10 values never leak.
-        assert np.max(np.abs(got - want)) <= BF16_GATE, case.id
+        want = oracle.attention_padded(from_bf16_bits(q), from_bf16_bits(k), from_bf16_bits(v),
+                                       lengths, causal, D**-0.5)
+        assert np.max(np.abs(got - want)) <= BF16_GATE
 
 
 def test_full_size_qwen_properties(runtime):
