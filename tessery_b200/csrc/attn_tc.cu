@@ -13,31 +13,35 @@
 // step runs beside the others instead of in front of them:
 //   warps 0-3   softmax of head slot 0 (thread t = query row t)
 //   warps 4-7   softmax of head slot 1
-//   warps 8-11  epilogue of each unit (O from tensor memory, scaled, staged swizzled in
-//               the unit's Q buffer, sent by TMA bulk-tensor stores), then the Q tiles of
-//               the unit two ahead: TMA load into the buffer just freed, q prologue
-//   warp 12     TMA producer: K and V tiles of 64 keys through a 5-slot ring
+//   warps 8-11  per work unit k: the q prologue of unit k+1 (RMSNorm + RoPE of its Q
+//               tiles in shared memory, as soon as they land), then the epilogue of unit
+//               k (O from tensor memory, scaled, staged swizzled in a per-warp ring of
+//               32-row chunks, sent by TMA bulk-tensor stores)
+//   warp 12     TMA producer: Q tiles of the unit two ahead (into the buffer whose last
+//               Q.K^T has run), K and V tiles of 128 keys through a 2-slot ring, and L2
+//               prefetches of the next units' tiles
 //   warp 13     TMEM allocator and single-thread tcgen05.mma issuer
 // Tensor memory (512 columns x 128 lanes, fp32), per head slot h at column 256h:
-//   [0,64) S slot 0, [64,128) S slot 1, [128,256) O.
-// P (bf16) is written over the first 32 columns of its S slot and read from there by
-// P.V as the tensor-memory A operand, so P needs no shared memory and is double
-// buffered with S.  Shared memory: two unit buffers of Q tiles (2 x 128x128 bf16 each,
-// so the next unit's Q is loaded and transformed while this one runs; a finished unit's
-// buffer stages its output), 5 ring slots (64x128 bf16: K or V), all in the
-// 128-byte-swizzled layout that TMA and UMMA use (a 128-byte row holds 64 bf16 or 32
-// fp32).
+//   [0,128) S_h, [128,256) O_h.
+// P_h (bf16) is written over the first 64 columns of S_h and read from there by P.V as
+// the tensor-memory A operand, so P needs no shared memory.  Shared memory: two unit
+// buffers of Q tiles (2 x 128x128 bf16 each, so the next unit's Q is loaded and
+// transformed while this one runs), 2 ring slots (128x128 bf16: K or V), and 2 output
+// staging chunks per epilogue warp (32 rows x 128 bytes), all in the 128-byte-swizzled
+// layout that TMA and UMMA use (a 128-byte row holds 64 bf16 or 32 fp32).
 //
-// Key tile j of a unit: the issuer runs S_h = Q_h K_j^T (M=128, N=64, K=128) into S
-// slot j%2 of head h, so a tile's scores are computed while the softmax warps work on the
-// previous one; the softmax warps turn S_h into P_h = exp2(S_h*scale*log2e - m); the
-// issuer accumulates O_h += P_h V_j (M=128, N=128, K=64).  Q.K^T of tile j+2 is issued
-// after P.V of tile j, which read the slot it overwrites (tcgen05.mma of one thread run
-// in order).  Tiles above the causal diagonal and beyond each sequence's length are
-// never visited; the diagonal and the last tile are masked per row.  The running
-// maximum is updated lazily: O is rescaled only when a tile maximum exceeds the
-// reference maximum by more than 8 (log2 units), so every probability stays below 2^8
-// and the normalised result is unchanged.
+// Key tile j of a unit (every MMA is M=128 x N=128 x K=16, issued 8 at a time): the
+// issuer runs S_h = Q_h K_j^T; the softmax warps of head h take the row maximum of S_h
+// (first pass over tensor memory) and write P_h = exp2(S_h*scale*log2e - m) (second
+// pass); the issuer runs O_h += P_h V_j and at once
+// S_h = Q_h K_{j+1}^T.  Both heads alternate, so one head's softmax overlaps the other
+// head's products.  Because S_h of tile j+1 is committed after P_h.V of tile j, a
+// softmax warp that sees S_h full also knows that O_h holds every earlier tile.  Tiles
+// above the causal diagonal and beyond each sequence's length are never visited; the
+// diagonal and the last tile are masked per row.  The running maximum is updated
+// lazily: O is rescaled only when a tile maximum exceeds the reference maximum by more
+// than 8 (log2 units), so every probability stays below 2^8 and the normalised result
+// is unchanged.
 //
 // Every wait is bounded (about a second); a wait that gives up records
 // TX_ETIMEOUT | site<<8 in the context status word, raises a CTA-wide abort flag, and
@@ -55,39 +59,41 @@ namespace tx {
 namespace tc {
 
 constexpr int kQRows = 128;                     // query rows per tile (TMEM lanes)
-constexpr int kKeys = 64;                       // keys per K/V tile
-constexpr int kStages = 5;                      // K/V ring slots
+constexpr int kKeys = 128;                      // keys per K/V tile
+constexpr int kStages = 2;                      // K/V ring slots
 constexpr uint32_t kQAtom = 128 * 128;          // 128 rows x 64 bf16
 constexpr uint32_t kQBytes = 2 * kQAtom;         // one head's Q tile
 constexpr uint32_t kQBufBytes = 2 * kQBytes;     // a unit's Q tiles (two head slots)
-constexpr uint32_t kKVAtom = kKeys * 128;       // 64 keys x 64 bf16
+constexpr uint32_t kKVAtom = kKeys * 128;       // 128 keys x 64 bf16
 constexpr uint32_t kKVBytes = 2 * kKVAtom;
-constexpr uint32_t kStageChunk = 128 * 128;     // staging: 128 rows x 128 bytes per chunk
-constexpr uint32_t kWarpBox = 32 * 128;         // one warp's 32 rows of a chunk
+constexpr uint32_t kChunkBytes = 32 * 128;      // output staging: 32 rows x 128 bytes
+constexpr uint32_t kStageSlots = 2;             // staging chunks per epilogue warp
 constexpr uint32_t kOffQ = 0;                   // two unit buffers of Q tiles
 constexpr uint32_t kOffKV = kOffQ + 2 * kQBufBytes;
-constexpr uint32_t kOffMisc = kOffKV + kStages * kKVBytes;
-static_assert(4 * kStageChunk == kQBufBytes, "an O tile (fp32) stages in a Q buffer");
+constexpr uint32_t kOffStage = kOffKV + kStages * kKVBytes;
+constexpr uint32_t kOffMisc = kOffStage + 4 * kStageSlots * kChunkBytes;
 constexpr uint32_t kMiscBytes = 3072;
-constexpr uint32_t kSmemBytes = kOffMisc + kMiscBytes + 1024;  // + base alignment slack
+// The whole per-CTA budget; the dynamic shared-memory window must start 1024-byte
+// aligned (the swizzled tiles need it), which the kernel checks.
+constexpr uint32_t kSmemBytes = kOffMisc + kMiscBytes;
 constexpr int kThreads = 448;
-constexpr int kAuxWarp0 = 8, kTmaWarp = 12, kMmaWarp = 13;
+constexpr int kEpiWarp0 = 8, kTmaWarp = 12, kMmaWarp = 13;
 constexpr uint32_t kTmemCols = 512;
 constexpr long long kWaitCycles = 2000000000ll;  // ~1 s at B200 clocks
 constexpr float kRescaleThreshold = 8.0f;        // log2 units
 
 // Barrier slots (uint64 each) at the start of the misc area.  "h" = head slot,
-// "s" = S slot.
+// "b" = Q buffer.
 enum : uint32_t {
-  kBarQFull = 0,                      // + Q buffer: the unit's Q tiles landed (TMA bytes)
-  kBarQReady = kBarQFull + 2,         // + Q buffer: Q tiles transformed (128 arrivals)
-  kBarStageFree = kBarQReady + 2,     // epilogue stores have read the staging (128 arrivals)
-  kBarKVFull = kBarStageFree + 1,     // + ring slot
+  kBarQFull = 0,                      // + b: the unit's Q tiles landed (TMA bytes)
+  kBarQReady = kBarQFull + 2,         // + b: Q tiles transformed (128 per head slot)
+  kBarQEmpty = kBarQReady + 2,        // + b: every Q.K^T reading the buffer ran (commit)
+  kBarKVFull = kBarQEmpty + 2,        // + ring slot
   kBarKVEmpty = kBarKVFull + kStages,
-  kBarSFull = kBarKVEmpty + kStages,  // + 2h + s
-  kBarPFull = kBarSFull + 4,          // + 2h + s: P written in that S slot (128 arrivals)
-  kBarPVDone = kBarPFull + 4,         // + 2h + s: P.V from that S slot ran
-  kBarLReady = kBarPVDone + 4,        // + 2h + unit parity: row sums published (128 arrivals)
+  kBarSFull = kBarKVEmpty + kStages,  // + h: S_h of the next key tile (commit)
+  kBarPFull = kBarSFull + 2,          // + h: P_h written over S_h (128 arrivals)
+  kBarPVDone = kBarPFull + 2,         // + h: P_h.V ran (commit)
+  kBarLReady = kBarPVDone + 2,        // + 2h + unit parity: row sums published (128 arrivals)
   kBarOFree = kBarLReady + 4,         // + h: O_h read out (128 arrivals)
   kBarDrain = kBarOFree + 2,
   kNumBars = kBarDrain + 1
@@ -100,12 +106,12 @@ constexpr uint32_t kOffRowSum = 1024;             // float [head slot][unit pari
 static_assert(kOffAbort + 4 <= kOffQw, "misc area overflow");
 static_assert(kOffRowSum + 2 * 2 * 128 * 4 <= kMiscBytes, "misc area overflow");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
+static_assert(kOffKV % 1024 == 0 && kOffStage % 1024 == 0, "swizzled tiles need 1024 B alignment");
 
 // Wait sites, reported in the status word for diagnosis.
 enum : int {
   kSiteQEmpty = 1, kSiteKVEmpty = 2, kSiteQReady = 3, kSiteKVFull = 4, kSitePFull = 5,
-  kSiteSFull = 6, kSitePVDone = 7, kSiteQFull = 8, kSiteLReady = 9, kSiteOFree = 10,
-  kSiteStageFree = 11
+  kSiteSFull = 6, kSitePVDone = 7, kSiteQFull = 8, kSiteLReady = 9, kSiteOFree = 10
 };
 
 // ---- unit encoding --------------------------------------------------------------------
@@ -129,6 +135,8 @@ struct Params {
   int *status;
   const uint16_t *q_norm_w;  // fused q prologue when non-NULL
   float eps;
+  const float4 *rope;        // cosine/sine table of the positions (NULL: computed)
+  uint32_t rope_rows;        // positions in the table
   float inv_freq[64];        // RoPE theta^(-2c/128), c < 64
 };
 
@@ -163,6 +171,13 @@ __device__ __forceinline__ Unit decode(const Params &p, uint32_t code) {
   uint32_t kend = p.causal ? min(u.q0 + kQRows, u.n) : u.n;
   u.nt = u.live ? (kend + kKeys - 1) / kKeys : 0u;
   return u;
+}
+
+// The next unit at or after index `from` (stepping by the grid) that visits key tiles.
+__device__ __forceinline__ uint32_t next_work(const Params &p, uint32_t from) {
+  for (uint32_t ui = from; ui < p.n_units; ui += gridDim.x)
+    if (decode(p, p.units[ui]).nt) return ui;
+  return p.n_units;
 }
 
 // ---- PTX wrappers ---------------------------------------------------------------------
@@ -244,6 +259,13 @@ __device__ __forceinline__ void bulk_wait_read() {
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
+// Brings one box of a tensor into L2 (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap *map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -299,7 +321,7 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile, int ks) {
 // Instruction descriptors, kind::f16 with A=B=bf16, D=f32: bit 4 D format, bits 7 and 10
 // A/B formats, bit 16 B MN-major, N>>3 at bit 17, M>>4 at bit 24.
 constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 4) << 24);
-constexpr uint32_t kIdescQK = kIdescBase | ((uint32_t)(kKeys >> 3) << 17);    // N = 64
+constexpr uint32_t kIdescQK = kIdescBase | ((uint32_t)(kKeys >> 3) << 17);    // N = kKeys
 constexpr uint32_t kIdescPV = kIdescBase | (1u << 16) | ((128u >> 3) << 17);  // N = 128
 
 __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
@@ -411,57 +433,73 @@ __device__ __forceinline__ void acc_squares(float (&ssq)[4], const uint4 &v) {
   }
 }
 
-// In-place q RMSNorm + RoPE of row r of the unit's Q tiles (nh of them; thread r owns
-// row r of every tile).  Each (position, column) sine and cosine is evaluated once for
-// the heads of the unit.  Arithmetic per element follows kernels.metal:53-74:
-// x * inv * w, then the rotation of (element c, element c + 64) by pos * inv_freq[c].
-__device__ __forceinline__ void q_transform_rows(uint32_t q_tiles, uint32_t r, uint32_t pos,
-                                                 uint32_t nh, const uint16_t *w,
-                                                 const float *inv_freq, float eps) {
+// In-place q RMSNorm + RoPE of row r of one head's Q tile (`q_tile`: 128 rows x 128
+// bf16, two 64-column atoms, 128-byte swizzle).  Arithmetic per element follows
+// kernels.metal:53-74: x * inv * w, then the rotation of (element c, element c + 64)
+// by pos * inv_freq[c].  `w_s` is the shared-memory address of the bf16 weights.  The
+// cosines and sines come from `rope` when given (float4 {cos c, sin c, cos c+1,
+// sin c+1} for column group g = c/8 at rope[(g * rope_rows + pos) * 4 + (c%8)/2], so a
+// warp's 32 consecutive positions read 2 KB contiguously); otherwise they are
+// evaluated here.
+__device__ __forceinline__ void q_transform_row(uint32_t q_tile, uint32_t r, uint32_t pos,
+                                                uint32_t w_s, const float *inv_freq, float eps,
+                                                const float4 *rope, uint32_t rope_rows) {
   const uint32_t sw = r & 7;
-  float inv[2] = {0.f, 0.f};
-  for (uint32_t h = 0; h < nh; ++h) {
-    const uint32_t row = q_tiles + h * kQBytes + r * 128;
-    float ssq[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint32_t row = q_tile + r * 128;
+  const float4 *trow = rope ? rope + (size_t)pos * 4 : nullptr;
+  const size_t gstride = (size_t)rope_rows * 4;
+  float4 nxt[4];
+  if (trow) {
 #pragma unroll
-    for (int c = 0; c < 16; ++c)
-      acc_squares(ssq, ld_shared_v4(row + (c >> 3) * kQAtom + (((c & 7) ^ sw) << 4)));
-    inv[h] = 1.0f / sqrtf(((ssq[0] + ssq[1]) + (ssq[2] + ssq[3])) / 128.0f + eps);
+    for (int i = 0; i < 4; ++i) nxt[i] = __ldg(trow + i);
   }
+  float ssq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int c = 0; c < 16; ++c)
+    acc_squares(ssq, ld_shared_v4(row + (c >> 3) * kQAtom + (((c & 7) ^ sw) << 4)));
+  const float inv = 1.0f / sqrtf(((ssq[0] + ssq[1]) + (ssq[2] + ssq[3])) / 128.0f + eps);
   const float fpos = (float)pos;
 #pragma unroll 1
   for (int g = 0; g < 8; ++g) {  // 16-byte chunk g: columns 8g..8g+7 and 64+8g..
-    float co[8], si[8], wa[8], wb[8];
+    float co[8], si[8];
+    if (trow) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int c = 8 * g + e;
-      sincos_reduced(fpos * inv_freq[c], &si[e], &co[e]);
-      wa[e] = bf16_bits_to_f32(w[c]);
-      wb[e] = bf16_bits_to_f32(w[c + 64]);
-    }
-    for (uint32_t h = 0; h < nh; ++h) {
-      const uint32_t row = q_tiles + h * kQBytes + r * 128;
-      const uint4 lo = ld_shared_v4(row + ((g ^ sw) << 4));
-      const uint4 hi = ld_shared_v4(row + kQAtom + ((g ^ sw) << 4));
-      uint32_t out_lo[4], out_hi[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float ra[2], rb[2];
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int k = 2 * e + hh;
-          const uint32_t A = u4_at(lo, e), B = u4_at(hi, e);
-          const float a = (hh ? bf16_hi(A) : bf16_lo(A)) * inv[h] * wa[k];
-          const float b = (hh ? bf16_hi(B) : bf16_lo(B)) * inv[h] * wb[k];
-          ra[hh] = a * co[k] - b * si[k];
-          rb[hh] = a * si[k] + b * co[k];
-        }
-        out_lo[e] = pack_bf16x2(ra[0], ra[1]);
-        out_hi[e] = pack_bf16x2(rb[0], rb[1]);
+      for (int i = 0; i < 4; ++i) {
+        co[2 * i] = nxt[i].x;
+        si[2 * i] = nxt[i].y;
+        co[2 * i + 1] = nxt[i].z;
+        si[2 * i + 1] = nxt[i].w;
       }
-      st_shared_v4(row + ((g ^ sw) << 4), out_lo[0], out_lo[1], out_lo[2], out_lo[3]);
-      st_shared_v4(row + kQAtom + ((g ^ sw) << 4), out_hi[0], out_hi[1], out_hi[2], out_hi[3]);
+      if (g < 7) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) nxt[i] = __ldg(trow + (g + 1) * gstride + i);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sincos_reduced(fpos * inv_freq[8 * g + e], &si[e], &co[e]);
     }
+    const uint4 wa = ld_shared_v4(w_s + 16 * g), wb = ld_shared_v4(w_s + 128 + 16 * g);
+    const uint4 lo = ld_shared_v4(row + ((g ^ sw) << 4));
+    const uint4 hi = ld_shared_v4(row + kQAtom + ((g ^ sw) << 4));
+    uint32_t out_lo[4], out_hi[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float ra[2], rb[2];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int k = 2 * e + hh;
+        const uint32_t A = u4_at(lo, e), B = u4_at(hi, e);
+        const uint32_t WA = u4_at(wa, e), WB = u4_at(wb, e);
+        const float a = (hh ? bf16_hi(A) : bf16_lo(A)) * inv * (hh ? bf16_hi(WA) : bf16_lo(WA));
+        const float b = (hh ? bf16_hi(B) : bf16_lo(B)) * inv * (hh ? bf16_hi(WB) : bf16_lo(WB));
+        ra[hh] = a * co[k] - b * si[k];
+        rb[hh] = a * si[k] + b * co[k];
+      }
+      out_lo[e] = pack_bf16x2(ra[0], ra[1]);
+      out_hi[e] = pack_bf16x2(rb[0], rb[1]);
+    }
+    st_shared_v4(row + ((g ^ sw) << 4), out_lo[0], out_lo[1], out_lo[2], out_lo[3]);
+    st_shared_v4(row + kQAtom + ((g ^ sw) << 4), out_hi[0], out_hi[1], out_hi[2], out_hi[3]);
   }
 }
 
@@ -494,10 +532,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v,
                    const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  // 1024-byte alignment for the swizzled tiles.
-  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_addr(smem);
+  if (sbase & 1023u) {  // the swizzled tiles need a 1024-byte aligned window
+    if (threadIdx.x == 0) report_status(p.status, kStatusBadArg);
+    return;
+  }
   const uint32_t bars = sbase + kOffMisc;
   uint8_t *misc = smem + kOffMisc;
   uint32_t *tmem_slot = (uint32_t *)(misc + kOffTmemSlot);
@@ -514,15 +554,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int h = 0; h < 2; ++h) {
       mbar_init(bar(kBarQFull + h), 1);
       mbar_init(bar(kBarQReady + h), 128);
+      mbar_init(bar(kBarQEmpty + h), 1);
+      mbar_init(bar(kBarSFull + h), 1);
+      mbar_init(bar(kBarPFull + h), 128);
+      mbar_init(bar(kBarPVDone + h), 1);
       mbar_init(bar(kBarOFree + h), 128);
-      for (int s = 0; s < 2; ++s) {
-        mbar_init(bar(kBarSFull + 2 * h + s), 1);
-        mbar_init(bar(kBarPFull + 2 * h + s), 128);
-        mbar_init(bar(kBarLReady + 2 * h + s), 128);
-        mbar_init(bar(kBarPVDone + 2 * h + s), 1);
-      }
+      for (int s = 0; s < 2; ++s) mbar_init(bar(kBarLReady + 2 * h + s), 128);
     }
-    mbar_init(bar(kBarStageFree), 128);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(kBarKVFull + s), 1);
       mbar_init(bar(kBarKVEmpty + s), 1);
@@ -555,16 +593,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kTmaWarp) {
     // ---------------- TMA producer ----------------
-    // Load order per unit: K_0, K_1, then V_j, K_{j+2} for j = 0.. -- the order in which
-    // the issuer consumes them.
+    // Q tiles of the first two work units, then per work unit k: its K/V tiles in the
+    // order the issuer consumes them (K_0, then V_j, K_{j+1} for j = 0..), and the Q tiles
+    // of work unit k+2 into buffer k%2 once the last Q.K^T of unit k has run.
     if (lane == 0) {
       uint32_t loads = 0;
-      // Per ring slot: bit s = parity of its fills so far, bit 8+s = slot ever filled
-      // (for the abort drain).
+      // Per ring slot: bit s = parity of its fills so far, bit 8+s = slot ever filled;
+      // per Q buffer b: bit 16+b = parity of its fills, bit 18+b = ever filled (for the
+      // abort drain).
       uint32_t armed = 0;
       bool ok = true;
       auto load_kv = [&](const CUtensorMap *map, const Unit &u, uint32_t j) {
-        const uint32_t slot = loads % kStages, round = loads / kStages;
+        const uint32_t slot = loads & (kStages - 1), round = loads / kStages;
         if (round > 0 && !(ok = wait_phase(bar(kBarKVEmpty + slot), (round - 1) & 1,
                                            abort_flag, p.status, kSiteKVEmpty)))
           return;
@@ -577,35 +617,75 @@ __global__ void __launch_bounds__(kThreads, 1)
         armed |= 1u << (8 + slot);
         ++loads;
       };
-      for (uint32_t ui = blockIdx.x; ok && ui < p.n_units; ui += gridDim.x) {
-        const Unit u = decode(p, p.units[ui]);
-        if (!u.nt) continue;
+      auto load_q = [&](uint32_t ui, uint32_t b) {
+        const Unit v = decode(p, p.units[ui]);
+        mbar_expect_tx(bar(kBarQFull + b), nh * kQBytes);
+        for (uint32_t h = 0; h < nh; ++h)
+          for (int a = 0; a < 2; ++a)
+            tma_load_3d(sbase + kOffQ + b * kQBufBytes + h * kQBytes + a * kQAtom, &tm_q,
+                        bar(kBarQFull + b), a * 64, (int)(v.head0 + h), (int)(v.tok0 + v.q0));
+        armed ^= 1u << (16 + b);
+        armed |= 1u << (18 + b);
+      };
+      // L2 prefetch of a unit's Q tiles (and, with kv, of its K/V tiles).
+      auto prefetch_unit = [&](uint32_t ui, bool kv) {
+        const Unit v = decode(p, p.units[ui]);
+        for (uint32_t h = 0; h < nh; ++h)
+          for (int a = 0; a < 2; ++a)
+            tma_prefetch_3d(&tm_q, a * 64, (int)(v.head0 + h), (int)(v.tok0 + v.q0));
+        if (kv)
+          for (uint32_t j = 0; j < v.nt; ++j)
+            for (int a = 0; a < 2; ++a) {
+              tma_prefetch_3d(&tm_k, a * 64, (int)v.kvh, (int)(v.tok0 + j * kKeys));
+              tma_prefetch_3d(&tm_v, a * 64, (int)v.kvh, (int)(v.tok0 + j * kKeys));
+            }
+      };
+      uint32_t cur = next_work(p, blockIdx.x);
+      uint32_t nxt = cur < p.n_units ? next_work(p, cur + gridDim.x) : p.n_units;
+      if (cur < p.n_units) load_q(cur, 0);
+      if (nxt < p.n_units) load_q(nxt, 1);
+      for (uint32_t k = 0; ok && cur < p.n_units; ++k) {
+        const Unit u = decode(p, p.units[cur]);
+        const uint32_t ahead = nxt < p.n_units ? next_work(p, nxt + gridDim.x) : p.n_units;
+        if (ahead < p.n_units) prefetch_unit(ahead, false);
+        if (nxt < p.n_units) prefetch_unit(nxt, true);
         load_kv(&tm_k, u, 0);
-        if (ok && u.nt > 1) load_kv(&tm_k, u, 1);
         for (uint32_t j = 0; ok && j < u.nt; ++j) {
           load_kv(&tm_v, u, j);
-          if (ok && j + 2 < u.nt) load_kv(&tm_k, u, j + 2);
+          if (ok && j + 1 < u.nt) load_kv(&tm_k, u, j + 1);
         }
+        if (ok && ahead < p.n_units) {
+          const uint32_t b = k & 1;
+          if ((ok = wait_phase(bar(kBarQEmpty + b), (k >> 1) & 1, abort_flag, p.status,
+                               kSiteQEmpty)))
+            load_q(ahead, b);
+        }
+        cur = nxt;
+        nxt = ahead;
       }
       if (!ok) {
-        // Every armed fill completes by itself: wait for the latest of each slot so that
-        // no copy lands in shared memory after the CTA exits.
+        // Every armed fill completes by itself: wait for the latest of each slot and Q
+        // buffer so that no copy lands in shared memory after the CTA exits.
         for (int s = 0; s < kStages; ++s)
           if (bit(armed, 8 + s)) drain_phase(bar(kBarKVFull + s), bit(armed, s) ^ 1u);
+        for (int b = 0; b < 2; ++b)
+          if (bit(armed, 18 + b)) drain_phase(bar(kBarQFull + b), bit(armed, 16 + b) ^ 1u);
       }
     }
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
+    // Per work unit: S_h = Q_h K_0^T for both heads; then per key tile j: for each head,
+    // O_h (+)= P_h V_j and at once S_h = Q_h K_{j+1}^T into the columns P_h.V has just
+    // read (tcgen05.mma of one thread run in order), so one head's softmax overlaps the
+    // other head's products.
     if (lane == 0) {
       uint32_t loads = 0, units_done = 0;
-      uint32_t pbits = 0, obits = 0;  // parities: P-full per (head, S slot), O-free per head
+      uint32_t pbits = 0, obits = 0;  // parities: P-full per head, O-free per head
       bool ok = true, issued = false;
-      auto tS = [&](uint32_t h, uint32_t s) { return tmem + h * 256 + s * kKeys; };
-      auto tO = [&](uint32_t h) { return tmem + h * 256 + 2 * kKeys; };
       uint32_t qbuf = 0;  // Q buffer of the current unit
-      // The next ring slot holding a K tile: wait for it, return its slot.
-      auto take_k = [&](uint32_t *slot) -> bool {
-        *slot = loads % kStages;
+      // The next ring slot (a K or V tile, in load order): wait for it.
+      auto take = [&](uint32_t *slot) -> bool {
+        *slot = loads & (kStages - 1);
         if (!(ok = wait_phase(bar(kBarKVFull + *slot), (loads / kStages) & 1, abort_flag,
                               p.status, kSiteKVFull)))
           return false;
@@ -613,19 +693,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         return true;
       };
-      // S_h(slot_s) = Q_h K^T from ring slot `slot` (K-major, 64 keys x 128).  Descriptors
-      // of step 0; step ks adds its byte offset / 16 to the start-address field (addresses
-      // stay below 256 KB, so the field never carries).
-      auto qk_head = [&](uint32_t h, uint32_t slot_s, uint32_t slot) {
+      // S_h = Q_h K^T (M=128, N=128 keys, K=128) from the K tile in ring slot `slot`.
+      // Descriptors of step 0; step ks adds its byte offset / 16 to the start-address
+      // field (addresses stay below 256 KB, so the field never carries).
+      auto qk_head = [&](uint32_t h, uint32_t slot) {
         const uint64_t kd = kmajor_desc(sbase + kOffKV + slot * kKVBytes, 0, kKVAtom);
-        const uint64_t qd = kmajor_desc(sbase + kOffQ + qbuf * kQBufBytes + h * kQBytes, 0, kQAtom);
-        const uint32_t d = tS(h, slot_s);
+        const uint64_t qd =
+            kmajor_desc(sbase + kOffQ + qbuf * kQBufBytes + h * kQBytes, 0, kQAtom);
+        const uint32_t d = tmem + h * 256;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
           umma(d, qd + (uint64_t)((ks >> 2) * (kQAtom >> 4) + (ks & 3) * 2),
                kd + (uint64_t)((ks >> 2) * (kKVAtom >> 4) + (ks & 3) * 2), kIdescQK, ks > 0);
-        umma_commit(bar(kBarSFull + 2 * h + slot_s));
+        umma_commit(bar(kBarSFull + h));
         issued = true;
+      };
+      // O_h (+)= P_h V with P_h (bf16, 128 keys) in the first 64 columns of S_h.
+      auto pv_head = [&](uint32_t h, uint32_t slot, uint32_t acc) {
+        const uint64_t vd = mnmajor_desc(sbase + kOffKV + slot * kKVBytes, 0);
+        const uint32_t pt = tmem + h * 256, d = tmem + h * 256 + 128;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma_ts(d, pt + ks * 8, vd + (uint64_t)(ks * (2048 >> 4)), kIdescPV,
+                  (acc || ks > 0) ? 1u : 0u);
+        umma_commit(bar(kBarPVDone + h));
       };
       for (uint32_t ui = blockIdx.x; ok && ui < p.n_units; ui += gridDim.x) {
         const Unit u = decode(p, p.units[ui]);
@@ -637,31 +728,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         ++units_done;
         tc_fence_after();
-        for (uint32_t j0 = 0; ok && j0 < 2 && j0 < u.nt; ++j0) {
-          uint32_t ks;
-          if (!take_k(&ks)) break;
-          for (uint32_t h = 0; h < nh; ++h) qk_head(h, j0, ks);
-          umma_commit(bar(kBarKVEmpty + ks));
-        }
+        uint32_t slotK;
+        if (!take(&slotK)) break;
+        for (uint32_t h = 0; h < nh; ++h) qk_head(h, slotK);
+        umma_commit(bar(kBarKVEmpty + slotK));
+        if (u.nt == 1) umma_commit(bar(kBarQEmpty + qbuf));  // the unit's last Q.K^T
         for (uint32_t j = 0; ok && j < u.nt; ++j) {
-          const uint32_t slotV = loads % kStages;
-          if (!(ok = wait_phase(bar(kBarKVFull + slotV), (loads / kStages) & 1, abort_flag,
-                                p.status, kSiteKVFull)))
-            break;
-          ++loads;
-          const uint32_t vt = sbase + kOffKV + slotV * kKVBytes;
-          const bool more = j + 2 < u.nt;
-          uint32_t slotK = 0;
-          // Per head: P.V of this tile, then at once that head's Q.K^T of tile j+2 into the
-          // S slot P.V has just read, so neither head waits for the other's softmax.
+          uint32_t slotV;
+          if (!take(&slotV)) break;
+          const bool more = j + 1 < u.nt;
           for (uint32_t h = 0; h < nh && ok; ++h) {
-            // One barrier per S slot: the softmax warps may finish the next tile before this
-            // wait, but not the one after (its S needs this P.V first).
-            const uint32_t pb = 2 * h + (j & 1);
-            if (!(ok = wait_phase(bar(kBarPFull + pb), bit(pbits, pb), abort_flag, p.status,
+            if (!(ok = wait_phase(bar(kBarPFull + h), bit(pbits, h), abort_flag, p.status,
                                   kSitePFull)))
               break;
-            pbits ^= 1u << pb;
+            pbits ^= 1u << h;
             if (j == 0 && units_done > 1) {
               // O_h still holds the previous unit until the epilogue has read it.
               if (!(ok = wait_phase(bar(kBarOFree + h), bit(obits, h), abort_flag, p.status,
@@ -670,22 +750,18 @@ __global__ void __launch_bounds__(kThreads, 1)
               obits ^= 1u << h;
             }
             tc_fence_after();
-            const uint32_t pt = tS(h, j & 1);  // P: first 32 columns of the S slot
-            const uint32_t d = tO(h);
-            const uint64_t vd = mnmajor_desc(vt, 0);
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-              umma_ts(d, pt + ks * 8, vd + (uint64_t)(ks * (2048 >> 4)), kIdescPV,
-                      (j > 0 || ks > 0) ? 1u : 0u);
-            umma_commit(bar(kBarPVDone + 2 * h + (j & 1)));
+            pv_head(h, slotV, j > 0);
             if (more) {
-              if (h == 0 && !take_k(&slotK)) break;
-              qk_head(h, j & 1, slotK);
+              if (h == 0 && !take(&slotK)) break;
+              qk_head(h, slotK);
             }
           }
           if (!ok) break;
           umma_commit(bar(kBarKVEmpty + slotV));
-          if (more) umma_commit(bar(kBarKVEmpty + slotK));
+          if (more) {
+            umma_commit(bar(kBarKVEmpty + slotK));
+            if (j + 2 == u.nt) umma_commit(bar(kBarQEmpty + qbuf));  // Q.K^T of the last tile
+          }
         }
       }
       if (issued) {
@@ -695,16 +771,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp < kAuxWarp0) {
+  } else if (warp < kEpiWarp0) {
     // ---------------- softmax (thread = query row of head slot h) ----------------------
     const uint32_t h = (uint32_t)warp >> 2;
     const uint32_t wq = (uint32_t)warp & 3;
     const uint32_t r = wq * 32 + lane;  // tile row == TMEM lane
     const uint32_t lane_base = (wq * 32u) << 16;
-    const uint32_t tS0 = tmem + lane_base + h * 256;  // S slot s at tS0 + s * kKeys
-    const uint32_t tO = tmem + lane_base + h * 256 + 2 * kKeys;
-    // Parities per S slot: bits 0-1 S-full waits, bits 2-3 P.V issued from the slot.
-    uint32_t sbits = 0, units_seen = 0;
+    const uint32_t tS = tmem + lane_base + h * 256;
+    const uint32_t tO = tS + 128;
+    uint32_t tiles = 0, units_seen = 0;  // key tiles and work units processed
     bool ok = true;
     for (uint32_t ui = blockIdx.x; ok && h < nh && ui < p.n_units; ui += gridDim.x) {
       const Unit u = decode(p, p.units[ui]);
@@ -712,37 +787,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t qpos = u.q0 + r;
       const uint32_t end = p.causal ? min(qpos + 1, u.n) : u.n;
       float m_ref = -INFINITY, l = 0.f;
-      for (uint32_t j = 0; j < u.nt; ++j) {
-        const uint32_t s = j & 1;
-        ok = __all_sync(0xffffffffu, wait_phase(bar(kBarSFull + 2 * h + s), bit(sbits, s),
-                                                abort_flag, p.status, kSiteSFull));
+      for (uint32_t j = 0; j < u.nt; ++j, ++tiles) {
+        ok = __all_sync(0xffffffffu, wait_phase(bar(kBarSFull + h), tiles & 1, abort_flag,
+                                                p.status, kSiteSFull));
         if (!ok) break;
-        sbits ^= 1u << s;
         tc_fence_after();
         const int valid = (int)min(max((int)end - (int)(j * kKeys), 0), kKeys);
-        uint32_t xa[32], xb[32];
-        tmem_ld32(tS0 + s * kKeys, xa);
-        tmem_ld32(tS0 + s * kKeys + 32, xb);
-        tmem_ld_wait();
+        // Pass 1: the tile's row maximum (64 columns in registers at a time).
         float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        if (valid >= kKeys) {
 #pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            mq[t & 1] = fmaxf(mq[t & 1], __uint_as_float(xa[t]));
-            mq[2 + (t & 1)] = fmaxf(mq[2 + (t & 1)], __uint_as_float(xb[t]));
-          }
-        } else {
+        for (int half = 0; half < 2; ++half) {
+          uint32_t xa[32], xb[32];
+          tmem_ld32(tS + half * 64, xa);
+          tmem_ld32(tS + half * 64 + 32, xb);
+          tmem_ld_wait();
+          if (valid >= kKeys) {
 #pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            if (t < valid) mq[t & 1] = fmaxf(mq[t & 1], __uint_as_float(xa[t]));
-            if (32 + t < valid) mq[2 + (t & 1)] = fmaxf(mq[2 + (t & 1)], __uint_as_float(xb[t]));
+            for (int t = 0; t < 32; ++t) {
+              mq[t & 1] = fmaxf(mq[t & 1], __uint_as_float(xa[t]));
+              mq[2 + (t & 1)] = fmaxf(mq[2 + (t & 1)], __uint_as_float(xb[t]));
+            }
+          } else {
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+              if (half * 64 + t < valid) mq[t & 1] = fmaxf(mq[t & 1], __uint_as_float(xa[t]));
+              if (half * 64 + 32 + t < valid)
+                mq[2 + (t & 1)] = fmaxf(mq[2 + (t & 1)], __uint_as_float(xb[t]));
+            }
           }
         }
         const float mt = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * p.scale_log2;
         if (j > 0) {
-          // Rescale decision is per row; TMEM access is warp-wide (.sync.aligned), so
-          // the warp rescales when any of its rows needs it (others scale by 1), after
-          // P.V of the previous tile has run.
+          // Rescale decision is per row; TMEM access is warp-wide (.sync.aligned), so the
+          // warp rescales when any of its rows needs it (others scale by 1).  S of this
+          // tile was committed after P.V of the previous one, so O_h is complete.
           float corr = 1.0f;
           const bool need = mt > m_ref + kRescaleThreshold;
           if (need) {
@@ -751,14 +829,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             m_ref = mt;
           }
           if (__any_sync(0xffffffffu, need)) {
-            const uint32_t ps = (j - 1) & 1;
-            ok = __all_sync(0xffffffffu,
-                            wait_phase(bar(kBarPVDone + 2 * h + ps), bit(sbits, 2 + ps) ^ 1u,
-                                       abort_flag, p.status, kSitePVDone));
-            if (!ok) break;
-            tc_fence_after();
 #pragma unroll 1
-            for (int c = 0; c < 8; ++c) {  // 16 columns at a time: S stays in registers
+            for (int c = 0; c < 8; ++c) {  // 16 columns at a time
               uint32_t o[16];
               tmem_ld16(tO + c * 16, o);
               tmem_ld_wait();
@@ -771,21 +843,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           m_ref = mt;
         }
-        // P = exp2(S*scale*log2e - m) as bf16 pairs over the first 32 columns of the slot
-        // (keys 0-31 in columns 0-15, keys 32-63 in columns 16-31).
-        {
-          uint32_t packed[16];
-          if (valid >= kKeys) l += exp_chunk<false>(xa, 0, valid, p.scale_log2, m_ref, packed);
-          else l += exp_chunk<true>(xa, 0, valid, p.scale_log2, m_ref, packed);
-          tmem_st16(tS0 + s * kKeys, packed);
-          if (valid >= kKeys) l += exp_chunk<false>(xb, 1, valid, p.scale_log2, m_ref, packed);
-          else l += exp_chunk<true>(xb, 1, valid, p.scale_log2, m_ref, packed);
-          tmem_st16(tS0 + s * kKeys + 16, packed);
+        // Pass 2: P = exp2(S*scale*log2e - m) as bf16 pairs over the first 64 columns
+        // (keys 32c..32c+31 in columns 16c..16c+15; each chunk is read before the chunk
+        // it overlaps is written).
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t x[32], packed[16];
+          tmem_ld32(tS + c * 32, x);
+          tmem_ld_wait();
+          if (valid >= kKeys) l += exp_chunk<false>(x, c, valid, p.scale_log2, m_ref, packed);
+          else l += exp_chunk<true>(x, c, valid, p.scale_log2, m_ref, packed);
+          tmem_st16(tS + c * 16, packed);
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(bar(kBarPFull + 2 * h + s));
-        sbits ^= 1u << (2 + s);
+        mbar_arrive(bar(kBarPFull + h));
       }
       if (!ok) break;
       // Row sum of the unit for the epilogue warps.
@@ -794,168 +866,141 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++units_seen;
     }
   } else {
-    // ---------------- epilogue and q prologue (thread = row of every head slot) --------
+    // ---------------- q prologue and epilogue (thread = row of every head slot) --------
     const uint32_t wq = (uint32_t)warp & 3;
     const uint32_t r = wq * 32 + lane;
     const uint32_t lane_base = (wq * 32u) << 16;
-    const bool leader = threadIdx.x == kAuxWarp0 * 32;  // issues the Q loads
-    // Per head h: bits 2h..2h+1 = units whose row sums were taken (mod 4);
-    // bits 4+2h+s = parity of the P.V count of S slot s.
-    uint32_t lbits = 0;
-    // Leader, per Q buffer b: bit b = parity of its fills, bit 2+b = ever filled.
-    uint32_t qarmed = 0;
+    uint32_t lcount = 0;  // work units whose row sums were taken
+    uint32_t tiles = 0;   // key tiles of the work units finished so far
+    uint32_t chunks = 0;  // staging chunks this warp has sent (slot = chunks % 2)
     bool ok = true;
     const uint32_t srow = (uint32_t)lane * 128, sw = (uint32_t)lane & 7;
-    // The next unit at or after index `from` that has work (nt > 0).
-    auto next_work = [&](uint32_t from) -> uint32_t {
-      for (uint32_t ui = from; ui < p.n_units; ui += gridDim.x)
-        if (decode(p, p.units[ui]).nt) return ui;
-      return p.n_units;
-    };
-    // Leader: TMA load of the Q tiles of unit `ui` into buffer b.
-    auto load_q = [&](uint32_t ui, uint32_t b) {
-      const Unit v = decode(p, p.units[ui]);
-      mbar_expect_tx(bar(kBarQFull + b), nh * kQBytes);
-      for (uint32_t h = 0; h < nh; ++h)
-        for (int a = 0; a < 2; ++a)
-          tma_load_3d(sbase + kOffQ + b * kQBufBytes + h * kQBytes + a * kQAtom, &tm_q,
-                      bar(kBarQFull + b), a * 64, (int)(v.head0 + h), (int)(v.tok0 + v.q0));
-      qarmed ^= 1u << b;
-      qarmed |= 1u << (2 + b);
-    };
-    // Wait for fill `phase` of buffer b, apply the q prologue, hand the tiles to the issuer.
+    const uint32_t stage0 = sbase + kOffStage + wq * kStageSlots * kChunkBytes;
+    // Wait for fill `phase` of buffer b, apply the q prologue to each head's tile, hand
+    // the tiles to the issuer.
     auto prepare = [&](uint32_t ui, uint32_t b, uint32_t phase) {
       ok = __all_sync(0xffffffffu, wait_phase(bar(kBarQFull + b), phase & 1, abort_flag,
                                               p.status, kSiteQFull));
       if (!ok) return;
       if (p.q_norm_w) {
         const Unit v = decode(p, p.units[ui]);
-        q_transform_rows(sbase + kOffQ + b * kQBufBytes, r, v.q0 + r, nh, qw_s, invf_s, p.eps);
+        for (uint32_t h = 0; h < nh; ++h)
+          q_transform_row(sbase + kOffQ + b * kQBufBytes + h * kQBytes, r, v.q0 + r,
+                          smem_addr(qw_s), invf_s, p.eps, p.rope, p.rope_rows);
         fence_proxy_async();
       }
       mbar_arrive(bar(kBarQReady + b));
     };
+    // The staging slot for this warp's next chunk, once the store that last read it is done.
+    auto take_slot = [&]() -> uint32_t {
+      if (lane == 0) bulk_wait_read<kStageSlots - 1>();
+      __syncwarp();
+      return stage0 + (chunks++ % kStageSlots) * kChunkBytes;
+    };
+    // Sends this warp's staged 32 rows (chunk at `slot`) to columns [x, ..) of `head`.
+    auto send = [&](uint32_t slot, int x, uint32_t head, uint32_t row0) {
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_3d(&tm_o, slot, x, (int)head, (int)row0);
+        bulk_commit();
+      }
+    };
     // Epilogue of unit v: per head, wait for its row sums and last P.V, read O out of
-    // tensor memory (then release it to the next unit), normalise, store.  Warps whose 32
-    // rows all lie inside the sequence stage them in the unit's Q buffer (free once every
-    // Q.K^T of the unit has run, which the row sums imply) and send TMA bulk-tensor
-    // stores; a warp at a ragged end stores row by row.
-    auto epilogue = [&](const Unit &v, uint32_t stage) {
+    // tensor memory 32 columns at a time (after the last read O is released to the next
+    // unit), normalise, store.  Warps whose 32 rows all lie inside the sequence stage
+    // each 32-row chunk in their ring and send it with a TMA bulk-tensor store; a warp at
+    // a ragged end stores row by row.
+    auto epilogue = [&](const Unit &v) {
       const uint32_t qpos = v.q0 + r;
       const bool store = qpos < v.rows;
       const uint32_t wrow0 = v.q0 + wq * 32;
       const bool bulk = wrow0 + 32 <= v.rows;
+      const uint32_t last_pv = tiles + v.nt - 1;  // index of the unit's last P.V per head
       for (uint32_t h = 0; h < nh && ok; ++h) {
-        // One barrier per unit parity: while this warpgroup works on head 0, the softmax
-        // warps of head 1 may finish this unit and the next one, but not a third.
-        const uint32_t lc = (lbits >> (2 * h)) & 3u;  // unit count mod 4 for this head
+        // Row sums: one barrier per unit parity (the softmax warps of a head cannot run
+        // two units ahead of this epilogue: their next-but-one unit needs O_h freed).
         ok = __all_sync(0xffffffffu,
-                        wait_phase(bar(kBarLReady + 2 * h + (lc & 1)), (lc >> 1) & 1,
+                        wait_phase(bar(kBarLReady + 2 * h + (lcount & 1)), (lcount >> 1) & 1,
                                    abort_flag, p.status, kSiteLReady));
         if (!ok) break;
-        const float l = rowsum_s[(h * 2 + (lc & 1)) * 128 + r];
-        lbits = (lbits & ~(3u << (2 * h))) | (((lc + 1) & 3u) << (2 * h));
-        lbits ^= (((v.nt + 1) / 2) & 1u) << (4 + 2 * h);
-        lbits ^= ((v.nt / 2) & 1u) << (5 + 2 * h);
-        const uint32_t ls = (v.nt - 1) & 1;
-        ok = __all_sync(0xffffffffu, wait_phase(bar(kBarPVDone + 2 * h + ls),
-                                                bit(lbits, 4 + 2 * h + ls) ^ 1u, abort_flag,
+        const float l = rowsum_s[(h * 2 + (lcount & 1)) * 128 + r];
+        ok = __all_sync(0xffffffffu, wait_phase(bar(kBarPVDone + h), last_pv & 1, abort_flag,
                                                 p.status, kSitePVDone));
         if (!ok) break;
         tc_fence_after();
         const float inv = 1.0f / l;
-        const uint32_t tO = tmem + lane_base + h * 256 + 2 * kKeys;
+        const uint32_t tO = tmem + lane_base + h * 256 + 128;
         const uint32_t head = v.head0 + h;
         const size_t orow = ((size_t)(v.tok0 + qpos) * p.heads + head) * 128;
-        // This warp's stores of the previous head must have read the staging rows.
-        if (lane == 0) bulk_wait_read<0>();
-        __syncwarp();
         if (!p.out_bf16) {
 #pragma unroll 1
-          for (int c = 0; c < 4; c += 2) {
-            uint32_t xa[32], xb[32];
-            tmem_ld32(tO + c * 32, xa);
-            tmem_ld32(tO + c * 32 + 32, xb);
+          for (int c = 0; c < 4; ++c) {  // 32 fp32 columns = one 128-byte staging row
+            uint32_t x[32];
+            tmem_ld32(tO + c * 32, x);
             tmem_ld_wait();
-#pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              xa[t] = __float_as_uint(__uint_as_float(xa[t]) * inv);
-              xb[t] = __float_as_uint(__uint_as_float(xb[t]) * inv);
+            if (c == 3) {
+              tc_fence_before();
+              mbar_arrive(bar(kBarOFree + h));
             }
-            if (bulk) {
-              const uint32_t b0 = stage + c * kStageChunk + wq * kWarpBox + srow;
 #pragma unroll
-              for (int g = 0; g < 8; ++g) {
-                st_shared_v4(b0 + (((uint32_t)g ^ sw) << 4), xa[4 * g], xa[4 * g + 1],
-                             xa[4 * g + 2], xa[4 * g + 3]);
-                st_shared_v4(b0 + kStageChunk + (((uint32_t)g ^ sw) << 4), xb[4 * g],
-                             xb[4 * g + 1], xb[4 * g + 2], xb[4 * g + 3]);
-              }
+            for (int t = 0; t < 32; ++t) x[t] = __float_as_uint(__uint_as_float(x[t]) * inv);
+            if (bulk) {
+              const uint32_t slot = take_slot();
+#pragma unroll
+              for (int g = 0; g < 8; ++g)
+                st_shared_v4(slot + srow + (((uint32_t)g ^ sw) << 4), x[4 * g], x[4 * g + 1],
+                             x[4 * g + 2], x[4 * g + 3]);
+              send(slot, c * 32, head, v.tok0 + wrow0);
             } else if (store) {
               float4 *o = (float4 *)((float *)p.out + orow + c * 32);
 #pragma unroll
-              for (int g = 0; g < 8; ++g) {
-                o[g] = make_float4(__uint_as_float(xa[4 * g]), __uint_as_float(xa[4 * g + 1]),
-                                   __uint_as_float(xa[4 * g + 2]), __uint_as_float(xa[4 * g + 3]));
-                o[8 + g] = make_float4(__uint_as_float(xb[4 * g]), __uint_as_float(xb[4 * g + 1]),
-                                       __uint_as_float(xb[4 * g + 2]),
-                                       __uint_as_float(xb[4 * g + 3]));
-              }
+              for (int g = 0; g < 8; ++g)
+                o[g] = make_float4(__uint_as_float(x[4 * g]), __uint_as_float(x[4 * g + 1]),
+                                   __uint_as_float(x[4 * g + 2]), __uint_as_float(x[4 * g + 3]));
             }
           }
         } else {
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {  // 32 columns (64 bytes of bf16) at a time
-            uint32_t x[32], w[16];
-            tmem_ld32(tO + c * 32, x);
-            tmem_ld_wait();
+          for (int c = 0; c < 2; ++c) {  // 64 bf16 columns = one 128-byte staging row
+            const uint32_t slot = bulk ? take_slot() : 0u;
+#pragma unroll 1
+            for (int half = 0; half < 2; ++half) {  // 32 columns = 4 16-byte units
+              uint32_t x[32], w[16];
+              tmem_ld32(tO + c * 64 + half * 32, x);
+              tmem_ld_wait();
+              if (c == 1 && half == 1) {
+                tc_fence_before();
+                mbar_arrive(bar(kBarOFree + h));
+              }
 #pragma unroll
-            for (int t = 0; t < 16; ++t)
-              w[t] = pack_bf16x2(__uint_as_float(x[2 * t]) * inv,
-                                 __uint_as_float(x[2 * t + 1]) * inv);
-            if (bulk) {
-              // Columns 32c.. are 16-byte units 4(c&1).. of the 128-byte row of chunk c/2.
-              const uint32_t b0 = stage + (c >> 1) * kStageChunk + wq * kWarpBox + srow;
+              for (int t = 0; t < 16; ++t)
+                w[t] = pack_bf16x2(__uint_as_float(x[2 * t]) * inv,
+                                   __uint_as_float(x[2 * t + 1]) * inv);
+              if (bulk) {
 #pragma unroll
-              for (int g = 0; g < 4; ++g)
-                st_shared_v4(b0 + (((uint32_t)(4 * (c & 1) + g) ^ sw) << 4), w[4 * g],
-                             w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
-            } else if (store) {
-              uint4 *o = (uint4 *)((uint16_t *)p.out + orow + c * 32);
+                for (int g = 0; g < 4; ++g)
+                  st_shared_v4(slot + srow + (((uint32_t)(4 * half + g) ^ sw) << 4), w[4 * g],
+                               w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+              } else if (store) {
+                uint4 *o = (uint4 *)((uint16_t *)p.out + orow + c * 64 + half * 32);
 #pragma unroll
-              for (int g = 0; g < 4; ++g)
-                o[g] = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+                for (int g = 0; g < 4; ++g)
+                  o[g] = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+              }
             }
+            if (bulk) send(slot, c * 64, head, v.tok0 + wrow0);
           }
-        }
-        // O_h has been read: the next unit's first P.V may overwrite it.
-        tc_fence_before();
-        mbar_arrive(bar(kBarOFree + h));
-        if (bulk) {
-          fence_proxy_async();
-          __syncwarp();
-          if (lane == 0) {
-            const int nchunks = p.out_bf16 ? 2 : 4, width = p.out_bf16 ? 64 : 32;
-            for (int c = 0; c < nchunks; ++c)
-              tma_store_3d(&tm_o, stage + c * kStageChunk + wq * kWarpBox, c * width, (int)head,
-                           (int)(v.tok0 + wrow0));
-            bulk_commit();
-          }
-          __syncwarp();
         }
       }
+      ++lcount;
+      tiles += v.nt;
     };
-
-    // Q tiles of the first two work units, then per work unit k: its epilogue, and the Q
-    // tiles of work unit k+2 into the buffer the epilogue has just drained.
-    const uint32_t first = next_work(blockIdx.x);
-    uint32_t next = first < p.n_units ? next_work(first + gridDim.x) : p.n_units;
-    if (leader) {
-      if (first < p.n_units) load_q(first, 0);
-      if (next < p.n_units) load_q(next, 1);
-    }
-    if (first < p.n_units) prepare(first, 0, 0);
-    if (ok && next < p.n_units) prepare(next, 1, 0);
+    // The q prologue of work unit 0, then per work unit k: the q prologue of work unit
+    // k+1 (whose tiles the producer loaded while unit k-1 ran), then the epilogue of k.
+    uint32_t next = next_work(p, blockIdx.x);
+    if (next < p.n_units) prepare(next, 0, 0);
+    next = next < p.n_units ? next_work(p, next + gridDim.x) : p.n_units;
     uint32_t k = 0;  // work units done
     for (uint32_t ui = blockIdx.x; ok && ui < p.n_units; ui += gridDim.x) {
       const Unit u = decode(p, p.units[ui]);
@@ -977,31 +1022,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         continue;
       }
-      const uint32_t b = k & 1;
-      epilogue(u, sbase + kOffQ + b * kQBufBytes);
-      if (!ok) break;
-      const uint32_t ahead = next < p.n_units ? next_work(next + gridDim.x) : p.n_units;
-      // Buffer b is free once this warpgroup's stores have read it.
-      if (lane == 0) bulk_wait_read<0>();
-      __syncwarp();
-      mbar_arrive(bar(kBarStageFree));
-      if (ahead < p.n_units) {
-        if (leader) {
-          if (wait_phase(bar(kBarStageFree), k & 1, abort_flag, p.status, kSiteStageFree))
-            load_q(ahead, b);
-        }
-        prepare(ahead, b, (k + 2) >> 1);
+      if (next < p.n_units) {
+        prepare(next, (k + 1) & 1, (k + 1) >> 1);
+        if (!ok) break;
+        next = next_work(p, next + gridDim.x);
       }
-      next = ahead;
+      epilogue(u);
       ++k;
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
-    if (!ok && leader) {
-      // No Q fill may land in shared memory after the CTA exits.
-      for (int b2 = 0; b2 < 2; ++b2)
-        if (bit(qarmed, 2 + b2)) drain_phase(bar(kBarQFull + b2), bit(qarmed, b2) ^ 1u);
-    }
   }
 
   tc_fence_before();
@@ -1137,9 +1167,25 @@ bool make_map(CUtensorMap *map, const void *base, uint32_t rows, uint32_t heads,
 
 }  // namespace
 
+uint32_t tc_rope_rows(uint32_t seq) { return (seq + tc::kQRows - 1) / tc::kQRows * tc::kQRows; }
+
+void tc_rope_table(float theta, uint32_t rows, float *table) {
+  for (uint32_t g = 0; g < 8; ++g)
+    for (uint32_t pos = 0; pos < rows; ++pos)
+      for (uint32_t e = 0; e < 8; ++e) {
+        const uint32_t c = 8 * g + e;
+        const float inv_freq = (float)std::pow((double)theta, -2.0 * (double)c / 128.0);
+        const float angle = (float)pos * inv_freq;  // the float product, as the kernels form it
+        float *t = table + ((size_t)(g * rows + pos) * 8 + e) * 2;
+        t[0] = (float)std::cos((double)angle);
+        t[1] = (float)std::sin((double)angle);
+      }
+}
+
 cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uint32_t n_units,
                                 int num_sms, int *status, const uint16_t *q_norm_w, float eps,
-                                float theta, cudaStream_t stream) {
+                                float theta, const float *rope, uint32_t rope_rows,
+                                cudaStream_t stream) {
   if (!n_units) return cudaSuccess;
   CUtensorMap mq, mk, mv, mo;
   const uint32_t rows = p.total;
@@ -1168,6 +1214,8 @@ cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uin
   prm.status = status;
   prm.q_norm_w = q_norm_w;
   prm.eps = eps;
+  prm.rope = reinterpret_cast<const float4 *>(rope);
+  prm.rope_rows = rope_rows;
   for (int i = 0; i < 64; ++i)
     prm.inv_freq[i] = (float)std::pow((double)theta, -2.0 * (double)i / 128.0);
   uint32_t grid = std::min<uint32_t>(n_units, (uint32_t)num_sms);
