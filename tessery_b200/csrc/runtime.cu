@@ -220,6 +220,16 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
   if (uses_scratch && (e = scratch_acquire(c, stream)) != cudaSuccess)
     return cuda_fail(c, e, "scratch wait");
 
+  // RoPE table of the tensor-core kernel's fused q prologue.
+  const float *rope = nullptr;
+  uint32_t rope_rows = 0;
+  if (tc_path && q_w) {
+    if ((e = ensure_rope(c, theta, tx::tc_rope_rows(p.seq))) != cudaSuccess)
+      return cuda_fail(c, e, "rope table");
+    rope = c->rope;
+    rope_rows = c->rope_rows;
+  }
+
   // The tensor-core kernel applies the q prologue to each Q tile in shared memory; k
   // (read by several query tiles) is normalised once into scratch, valid rows only.
   const uint16_t *tc_q_w = tc_path ? q_w : nullptr;
@@ -270,16 +280,9 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
         return cuda_fail(c, e, "work list upload");
       c->units_key = key;
     }
-    const float *rope = nullptr;
-    uint32_t rope_rows = 0;
-    if (tc_q_w) {
-      if ((e = ensure_rope(c, theta, tx::tc_rope_rows(p.seq))) != cudaSuccess)
-        return cuda_fail(c, e, "rope table");
-      rope = c->rope;
-      rope_rows = c->rope_rows;
-    }
     if ((e = tx::launch_attention_tc(p, c->units, c->units_count, c->sms, c->status, tc_q_w, eps,
-                                     theta, rope, rope_rows, stream)) != cudaSuccess)
+                                     theta, tc_q_w ? rope : nullptr, tc_q_w ? rope_rows : 0,
+                                     stream)) != cudaSuccess)
       return cuda_fail(c, e, "attention launch");
     c->last_kernel = "tc_bf16_d128";
     ++c->launches;
@@ -748,6 +751,7 @@ int tx_qk_norm_rope(void *ctx, const void *q, const void *k, void *q_out, void *
   pp.dim = dim; pp.in_dtype = in_dtype; pp.out_dtype = out_dtype; pp.q_w = q_norm_w;
   pp.k_w = k_norm_w; pp.eps = eps; pp.theta = theta; pp.lengths = lengths;
   cudaSetDevice(c->device);
+
   cudaError_t e = tx::launch_qk_norm_rope(pp, stream ? (cudaStream_t)stream : c->stream);
   if (e != cudaSuccess) return cuda_fail(c, e, "prologue launch");
   ++c->launches;

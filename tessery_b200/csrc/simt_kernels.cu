@@ -258,6 +258,190 @@ static cudaError_t launch_prologue_e(const PrologueProblem &p, cudaStream_t stre
   return cudaGetLastError();
 }
 
+// ---- bf16 head_dim-128 prologue, written for bandwidth -------------------------------
+// One pass over the rows of one tensor (q or k).  A block of 4 warps covers 16
+// consecutive tokens (padded layout: 16 positions of one sequence, blockIdx.y = the
+// sequence, so its length is read once and blocks past it exit); each warp takes 4
+// tokens and loads the next token's rows while it transforms the current one.  Within a
+// token, each half-warp owns one 256-byte row (one head) per load, lane l%16 holding the
+// 16 bytes of columns 8(l%16)..8(l%16)+7, so every load and store moves 512 contiguous
+// bytes per warp.  The rotation partner of column c (c < 64) is column c + 64, held by
+// lane l^8: the lanes swap their raw bf16 words and each computes its own output of
+// kernels.metal:53-74 (a = x_c * inv * w_c, b = x_{c+64} * inv * w_{c+64}; a*cos - b*sin
+// for the first half, a*sin + b*cos for the second), regrouped as
+// inv * (own * (w_own * cos) -/+ partner * (w_partner * sin)) so that the per-token
+// products are shared by all heads.  The angle is the float product pos * inv_freq[c];
+// its sine and cosine come from a Cody-Waite reduction by 2*pi and the hardware
+// approximations (about 2^-21 absolute error).
+constexpr int kRowTokensPerWarp = 4;
+
+struct RowPass {
+  const uint16_t *in;
+  uint16_t *out;
+  const uint16_t *w;
+  uint32_t nheads;
+  uint32_t tokens, seq;
+  const int32_t *cu;
+  uint32_t nseq;
+  const uint32_t *lengths;
+  float eps;
+  float inv_freq[64];
+};
+
+__device__ __forceinline__ void bf16x8_unpack(const uint4 &v, float (&f)[8]) {
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const uint32_t w = e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w;
+    f[2 * e] = __uint_as_float(w << 16);
+    f[2 * e + 1] = __uint_as_float(w & 0xffff0000u);
+  }
+}
+
+__device__ __forceinline__ void sincos_2pi_reduced(float angle, float *s, float *c) {
+  const float k = rintf(angle * 0.159154943091895336f);
+  float r = fmaf(k, -6.28318548202514648f, angle);
+  r = fmaf(k, 1.74845553e-07f, r);
+  __sincosf(r, s, c);
+}
+
+template <int NP>  // row pairs per token: ceil(nheads / 2)
+__global__ void __launch_bounds__(128) norm_rope_rows_bf16_kernel(RowPass p) {
+  __shared__ int32_t cu_s[1025];
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t l16 = lane & 15, half = lane >> 4, g = l16 & 7;
+  const bool first = l16 < 8;
+  // Tokens of this warp: [t0, t0 + n) of one sequence (padded) or of the packed rows.
+  uint32_t t0, n, pos0 = 0, seq_start = 0;
+  if (p.cu) {
+    const bool cu_shared = p.nseq < 1025;
+    if (cu_shared)
+      for (uint32_t i = threadIdx.x; i <= p.nseq; i += blockDim.x) cu_s[i] = p.cu[i];
+    __syncthreads();
+    t0 = (blockIdx.x * 4 + warp) * kRowTokensPerWarp;
+    if (t0 >= p.tokens) return;
+    n = min((uint32_t)kRowTokensPerWarp, p.tokens - t0);
+    (void)cu_shared;
+  } else {
+    const uint32_t b = blockIdx.y;
+    const uint32_t len = p.lengths ? min(p.lengths[b], p.seq) : p.seq;
+    pos0 = (blockIdx.x * 4 + warp) * kRowTokensPerWarp;
+    if (pos0 >= len) return;
+    n = min((uint32_t)kRowTokensPerWarp, len - pos0);
+    t0 = b * p.seq + pos0;
+  }
+  // Weights of this lane's columns and of its partner's (bf16 pairs, unpacked per use).
+  const uint4 wo = __ldg(reinterpret_cast<const uint4 *>(p.w) + l16);
+  const uint4 wp = __ldg(reinterpret_cast<const uint4 *>(p.w) + (l16 ^ 8));
+  float wof[8], wpf[8];
+  bf16x8_unpack(wo, wof);
+  bf16x8_unpack(wp, wpf);
+  auto position = [&](uint32_t i) -> uint32_t {
+    if (!p.cu) return pos0 + i;
+    const uint32_t tok = t0 + i;
+    uint32_t lo = 0, hi = p.nseq;
+    if (p.nseq < 1025) {
+      while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if ((uint32_t)cu_s[mid] <= tok) lo = mid; else hi = mid;
+      }
+      return tok - (uint32_t)cu_s[lo];
+    }
+    return tok - (uint32_t)p.cu[find_seq(p.cu, p.nseq, tok)];
+  };
+  auto load = [&](uint32_t i, uint4 (&x)[NP]) {
+    const uint16_t *row = p.in + (size_t)(t0 + i) * p.nheads * 128;
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+      const uint32_t head = 2 * j + half;
+      x[j] = head < p.nheads ? __ldg(reinterpret_cast<const uint4 *>(row + (size_t)head * 128) + l16)
+                             : make_uint4(0, 0, 0, 0);
+    }
+  };
+  uint4 xa[NP], xb[NP];
+  load(0, xa);
+#pragma unroll 1
+  for (uint32_t i = 0; i < n; ++i) {
+    uint4(&x)[NP] = (i & 1) ? xb : xa;
+    uint4(&nx)[NP] = (i & 1) ? xa : xb;
+    if (i + 1 < n) load(i + 1, nx);
+    const float fpos = (float)position(i);
+    float c1[8], c2[8];  // w_own * cos and -/+ w_partner * sin
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float sn, cs;
+      sincos_2pi_reduced(fpos * p.inv_freq[8 * g + e], &sn, &cs);
+      c1[e] = wof[e] * cs;
+      c2[e] = first ? -(wpf[e] * sn) : wpf[e] * sn;
+    }
+    uint16_t *orow = p.out + (size_t)(t0 + i) * p.nheads * 128;
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+      const uint32_t head = 2 * j + half;
+      float a[8], b[8];
+      bf16x8_unpack(x[j], a);
+      uint4 px;
+      px.x = __shfl_xor_sync(0xffffffffu, x[j].x, 8);
+      px.y = __shfl_xor_sync(0xffffffffu, x[j].y, 8);
+      px.z = __shfl_xor_sync(0xffffffffu, x[j].z, 8);
+      px.w = __shfl_xor_sync(0xffffffffu, x[j].w, 8);
+      bf16x8_unpack(px, b);
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(a[e], a[e], ss);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 8);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      const float inv = 1.0f / sqrtf(ss / 128.0f + p.eps);
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        o[e] = pack_bf16x2(inv * fmaf(b[2 * e], c2[2 * e], a[2 * e] * c1[2 * e]),
+                           inv * fmaf(b[2 * e + 1], c2[2 * e + 1], a[2 * e + 1] * c1[2 * e + 1]));
+      if (head < p.nheads)
+        reinterpret_cast<uint4 *>(orow + (size_t)head * 128)[l16] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+template <int NP>
+static cudaError_t launch_rows(const RowPass &rp, const PrologueProblem &p, cudaStream_t stream) {
+  dim3 grid;
+  if (rp.cu) {
+    grid = dim3((rp.tokens + 15) / 16, 1, 1);
+  } else {
+    if (p.tokens % p.seq) return cudaErrorInvalidValue;
+    grid = dim3((rp.seq + 15) / 16, rp.tokens / rp.seq, 1);
+    if (grid.y > 65535u) return cudaErrorInvalidValue;
+  }
+  norm_rope_rows_bf16_kernel<NP><<<grid, 128, 0, stream>>>(rp);
+  return cudaGetLastError();
+}
+
+static cudaError_t launch_rows_pass(const void *in, void *out, const uint16_t *w, uint32_t nheads,
+                                    const PrologueProblem &p, cudaStream_t stream) {
+  RowPass rp{};
+  rp.in = (const uint16_t *)in;
+  rp.out = (uint16_t *)out;
+  rp.w = w;
+  rp.nheads = nheads;
+  rp.tokens = p.tokens;
+  rp.seq = p.seq;
+  rp.cu = p.cu_seqlens;
+  rp.nseq = p.nseq;
+  rp.lengths = p.lengths;
+  rp.eps = p.eps;
+  for (int c = 0; c < 64; ++c) rp.inv_freq[c] = p.inv_freq[c];
+  switch ((nheads + 1) / 2) {
+    case 1: return launch_rows<1>(rp, p, stream);
+    case 2: return launch_rows<2>(rp, p, stream);
+    case 3: return launch_rows<3>(rp, p, stream);
+    case 4: return launch_rows<4>(rp, p, stream);
+    case 5: case 6: return launch_rows<6>(rp, p, stream);
+    default: return launch_rows<8>(rp, p, stream);
+  }
+}
+
 cudaError_t launch_qk_norm_rope(const PrologueProblem &problem, cudaStream_t stream) {
   if (!problem.tokens || (!problem.q && !problem.k)) return cudaSuccess;
   if (problem.dim > 256) return cudaErrorInvalidValue;
@@ -266,6 +450,19 @@ cudaError_t launch_qk_norm_rope(const PrologueProblem &problem, cudaStream_t str
   PrologueProblem p = problem;
   for (uint32_t c = 0; c < p.dim / 2; ++c)
     p.inv_freq[c] = (float)std::pow((double)p.theta, -2.0 * (double)c / (double)p.dim);
+  // bf16 head_dim 128 with up to 16 heads: one bandwidth-oriented pass per tensor.
+  const bool fast = p.dim == 128 && p.in_dtype == 1 && p.out_dtype == 1 &&
+                    (!p.q || (p.heads <= 16 && (uintptr_t)p.q % 16 == 0 &&
+                              (uintptr_t)p.q_out % 16 == 0 && (uintptr_t)p.q_w % 16 == 0)) &&
+                    (!p.k || (p.kv_heads <= 16 && (uintptr_t)p.k % 16 == 0 &&
+                              (uintptr_t)p.k_out % 16 == 0 && (uintptr_t)p.k_w % 16 == 0)) &&
+                    (p.cu_seqlens || (p.seq && p.tokens % p.seq == 0 && p.tokens / p.seq <= 65535u));
+  if (fast) {
+    cudaError_t e = cudaSuccess;
+    if (p.q) e = launch_rows_pass(p.q, p.q_out, p.q_w, p.heads, p, stream);
+    if (e == cudaSuccess && p.k) e = launch_rows_pass(p.k, p.k_out, p.k_w, p.kv_heads, p, stream);
+    return e;
+  }
   switch (p.dim) {
     case 32: return launch_prologue_e<1>(p, stream);
     case 64: return launch_prologue_e<2>(p, stream);
