@@ -9,25 +9,26 @@
 // share every K/V tile (GQA head sharing).  A persistent grid of one CTA per SM walks a
 // host-built, longest-first list of units.
 //
-// Warp roles (448 threads, one CTA per SM), specialised so that each serial per-unit
+// Warp roles (576 threads, one CTA per SM), specialised so that each serial per-unit
 // step runs beside the others instead of in front of them:
 //   warps 0-3   softmax of head slot 0 (thread t = query row t)
 //   warps 4-7   softmax of head slot 1
-//   warps 8-11  per work unit k: the q prologue of unit k+1 (RMSNorm + RoPE of its Q
-//               tiles in shared memory, as soon as they land), then the epilogue of unit
-//               k (O from tensor memory, scaled, staged swizzled in a per-warp ring of
-//               32-row chunks, sent by TMA bulk-tensor stores)
-//   warp 12     TMA producer: Q tiles of the unit two ahead (into the buffer whose last
+//   warps 8-11  per work unit k, for head slot 0: the q prologue of unit k+1 (RMSNorm +
+//               RoPE of its Q tile in shared memory, as soon as it lands), then the
+//               epilogue of unit k (O from tensor memory, scaled, staged swizzled in a
+//               per-warp 32-row chunk, sent by TMA bulk-tensor stores)
+//   warps 12-15 the same for head slot 1
+//   warp 16     TMA producer: Q tiles of the unit two ahead (into the buffer whose last
 //               Q.K^T has run), K and V tiles of 128 keys through a 2-slot ring, and L2
 //               prefetches of the next units' tiles
-//   warp 13     TMEM allocator and single-thread tcgen05.mma issuer
+//   warp 17     TMEM allocator and single-thread tcgen05.mma issuer
 // Tensor memory (512 columns x 128 lanes, fp32), per head slot h at column 256h:
 //   [0,128) S_h, [128,256) O_h.
 // P_h (bf16) is written over the first 64 columns of S_h and read from there by P.V as
 // the tensor-memory A operand, so P needs no shared memory.  Shared memory: two unit
 // buffers of Q tiles (2 x 128x128 bf16 each, so the next unit's Q is loaded and
-// transformed while this one runs), 2 ring slots (128x128 bf16: K or V), and 2 output
-// staging chunks per epilogue warp (32 rows x 128 bytes), all in the 128-byte-swizzled
+// transformed while this one runs), 2 ring slots (128x128 bf16: K or V), and one output
+// staging chunk per epilogue warp (32 rows x 128 bytes), all in the 128-byte-swizzled
 // layout that TMA and UMMA use (a 128-byte row holds 64 bf16 or 32 fp32).
 //
 // Key tile j of a unit (every MMA is M=128 x N=128 x K=16, issued 8 at a time): the
@@ -67,17 +68,17 @@ constexpr uint32_t kQBufBytes = 2 * kQBytes;     // a unit's Q tiles (two head s
 constexpr uint32_t kKVAtom = kKeys * 128;       // 128 keys x 64 bf16
 constexpr uint32_t kKVBytes = 2 * kKVAtom;
 constexpr uint32_t kChunkBytes = 32 * 128;      // output staging: 32 rows x 128 bytes
-constexpr uint32_t kStageSlots = 2;             // staging chunks per epilogue warp
+constexpr uint32_t kStageSlots = 1;             // staging chunks per epilogue warp
 constexpr uint32_t kOffQ = 0;                   // two unit buffers of Q tiles
 constexpr uint32_t kOffKV = kOffQ + 2 * kQBufBytes;
 constexpr uint32_t kOffStage = kOffKV + kStages * kKVBytes;
-constexpr uint32_t kOffMisc = kOffStage + 4 * kStageSlots * kChunkBytes;
+constexpr uint32_t kOffMisc = kOffStage + 8 * kStageSlots * kChunkBytes;
 constexpr uint32_t kMiscBytes = 3072;
 // The whole per-CTA budget; the dynamic shared-memory window must start 1024-byte
 // aligned (the swizzled tiles need it), which the kernel checks.
 constexpr uint32_t kSmemBytes = kOffMisc + kMiscBytes;
-constexpr int kThreads = 448;
-constexpr int kEpiWarp0 = 8, kTmaWarp = 12, kMmaWarp = 13;
+constexpr int kThreads = 576;
+constexpr int kEpiWarp0 = 8, kTmaWarp = 16, kMmaWarp = 17;
 constexpr uint32_t kTmemCols = 512;
 constexpr long long kWaitCycles = 2000000000ll;  // ~1 s at B200 clocks
 constexpr float kRescaleThreshold = 8.0f;        // log2 units
@@ -135,8 +136,6 @@ struct Params {
   int *status;
   const uint16_t *q_norm_w;  // fused q prologue when non-NULL
   float eps;
-  const float4 *rope;        // cosine/sine table of the positions (NULL: computed)
-  uint32_t rope_rows;        // positions in the table
   float inv_freq[64];        // RoPE theta^(-2c/128), c < 64
 };
 
@@ -436,23 +435,11 @@ __device__ __forceinline__ void acc_squares(float (&ssq)[4], const uint4 &v) {
 // In-place q RMSNorm + RoPE of row r of one head's Q tile (`q_tile`: 128 rows x 128
 // bf16, two 64-column atoms, 128-byte swizzle).  Arithmetic per element follows
 // kernels.metal:53-74: x * inv * w, then the rotation of (element c, element c + 64)
-// by pos * inv_freq[c].  `w_s` is the shared-memory address of the bf16 weights.  The
-// cosines and sines come from `rope` when given (float4 {cos c, sin c, cos c+1,
-// sin c+1} for column group g = c/8 at rope[(g * rope_rows + pos) * 4 + (c%8)/2], so a
-// warp's 32 consecutive positions read 2 KB contiguously); otherwise they are
-// evaluated here.
+// by pos * inv_freq[c].  `w_s` is the shared-memory address of the bf16 weights.
 __device__ __forceinline__ void q_transform_row(uint32_t q_tile, uint32_t r, uint32_t pos,
-                                                uint32_t w_s, const float *inv_freq, float eps,
-                                                const float4 *rope, uint32_t rope_rows) {
+                                                uint32_t w_s, const float *inv_freq, float eps) {
   const uint32_t sw = r & 7;
   const uint32_t row = q_tile + r * 128;
-  const float4 *trow = rope ? rope + (size_t)pos * 4 : nullptr;
-  const size_t gstride = (size_t)rope_rows * 4;
-  float4 nxt[4];
-  if (trow) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) nxt[i] = __ldg(trow + i);
-  }
   float ssq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int c = 0; c < 16; ++c)
@@ -462,22 +449,8 @@ __device__ __forceinline__ void q_transform_row(uint32_t q_tile, uint32_t r, uin
 #pragma unroll 1
   for (int g = 0; g < 8; ++g) {  // 16-byte chunk g: columns 8g..8g+7 and 64+8g..
     float co[8], si[8];
-    if (trow) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        co[2 * i] = nxt[i].x;
-        si[2 * i] = nxt[i].y;
-        co[2 * i + 1] = nxt[i].z;
-        si[2 * i + 1] = nxt[i].w;
-      }
-      if (g < 7) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) nxt[i] = __ldg(trow + (g + 1) * gstride + i);
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) sincos_reduced(fpos * inv_freq[8 * g + e], &si[e], &co[e]);
-    }
+    for (int e = 0; e < 8; ++e) sincos_reduced(fpos * inv_freq[8 * g + e], &si[e], &co[e]);
     const uint4 wa = ld_shared_v4(w_s + 16 * g), wb = ld_shared_v4(w_s + 128 + 16 * g);
     const uint4 lo = ld_shared_v4(row + ((g ^ sw) << 4));
     const uint4 hi = ld_shared_v4(row + kQAtom + ((g ^ sw) << 4));
@@ -525,8 +498,8 @@ __device__ __forceinline__ float exp_chunk(const uint32_t (&x)[32], int c, int v
 }
 
 // ---- the kernel -----------------------------------------------------------------------
-// 128 registers per thread: 14 warps put 4 warps on some SM sub-partition, whose 16K
-// registers then allow 128 each.
+// 96 registers per thread: 18 warps put 5 warps on some SM sub-partition, whose 16K
+// registers then allow 102 each.
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_k,
@@ -553,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int h = 0; h < 2; ++h) {
       mbar_init(bar(kBarQFull + h), 1);
-      mbar_init(bar(kBarQReady + h), 128);
+      mbar_init(bar(kBarQReady + h), 128 * nh);
       mbar_init(bar(kBarQEmpty + h), 1);
       mbar_init(bar(kBarSFull + h), 1);
       mbar_init(bar(kBarPFull + h), 128);
@@ -866,27 +839,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++units_seen;
     }
   } else {
-    // ---------------- q prologue and epilogue (thread = row of every head slot) --------
+    // ---------------- q prologue and epilogue (warpgroup h: head slot h; thread = row) -
+    const uint32_t h = (uint32_t)(warp - kEpiWarp0) >> 2;
     const uint32_t wq = (uint32_t)warp & 3;
     const uint32_t r = wq * 32 + lane;
     const uint32_t lane_base = (wq * 32u) << 16;
     uint32_t lcount = 0;  // work units whose row sums were taken
     uint32_t tiles = 0;   // key tiles of the work units finished so far
-    uint32_t chunks = 0;  // staging chunks this warp has sent (slot = chunks % 2)
+    uint32_t chunks = 0;  // staging chunks this warp has sent
     bool ok = true;
     const uint32_t srow = (uint32_t)lane * 128, sw = (uint32_t)lane & 7;
-    const uint32_t stage0 = sbase + kOffStage + wq * kStageSlots * kChunkBytes;
-    // Wait for fill `phase` of buffer b, apply the q prologue to each head's tile, hand
-    // the tiles to the issuer.
+    const uint32_t stage0 = sbase + kOffStage + (h * 4 + wq) * kStageSlots * kChunkBytes;
+    // Wait for fill `phase` of buffer b, apply the q prologue to this head's tile, hand
+    // it to the issuer (which waits for every head slot).
     auto prepare = [&](uint32_t ui, uint32_t b, uint32_t phase) {
       ok = __all_sync(0xffffffffu, wait_phase(bar(kBarQFull + b), phase & 1, abort_flag,
                                               p.status, kSiteQFull));
       if (!ok) return;
       if (p.q_norm_w) {
         const Unit v = decode(p, p.units[ui]);
-        for (uint32_t h = 0; h < nh; ++h)
-          q_transform_row(sbase + kOffQ + b * kQBufBytes + h * kQBytes, r, v.q0 + r,
-                          smem_addr(qw_s), invf_s, p.eps, p.rope, p.rope_rows);
+        q_transform_row(sbase + kOffQ + b * kQBufBytes + h * kQBytes, r, v.q0 + r,
+                        smem_addr(qw_s), invf_s, p.eps);
         fence_proxy_async();
       }
       mbar_arrive(bar(kBarQReady + b));
@@ -906,10 +879,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         bulk_commit();
       }
     };
-    // Epilogue of unit v: per head, wait for its row sums and last P.V, read O out of
+    // Epilogue of unit v for head slot h: wait for its row sums and last P.V, read O out of
     // tensor memory 32 columns at a time (after the last read O is released to the next
     // unit), normalise, store.  Warps whose 32 rows all lie inside the sequence stage
-    // each 32-row chunk in their ring and send it with a TMA bulk-tensor store; a warp at
+    // each 32-row chunk in shared memory and send it with a TMA bulk-tensor store; a warp at
     // a ragged end stores row by row.
     auto epilogue = [&](const Unit &v) {
       const uint32_t qpos = v.q0 + r;
@@ -917,17 +890,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t wrow0 = v.q0 + wq * 32;
       const bool bulk = wrow0 + 32 <= v.rows;
       const uint32_t last_pv = tiles + v.nt - 1;  // index of the unit's last P.V per head
-      for (uint32_t h = 0; h < nh && ok; ++h) {
+      {
         // Row sums: one barrier per unit parity (the softmax warps of a head cannot run
         // two units ahead of this epilogue: their next-but-one unit needs O_h freed).
         ok = __all_sync(0xffffffffu,
                         wait_phase(bar(kBarLReady + 2 * h + (lcount & 1)), (lcount >> 1) & 1,
                                    abort_flag, p.status, kSiteLReady));
-        if (!ok) break;
+        if (!ok) return;
         const float l = rowsum_s[(h * 2 + (lcount & 1)) * 128 + r];
         ok = __all_sync(0xffffffffu, wait_phase(bar(kBarPVDone + h), last_pv & 1, abort_flag,
                                                 p.status, kSitePVDone));
-        if (!ok) break;
+        if (!ok) return;
         tc_fence_after();
         const float inv = 1.0f / l;
         const uint32_t tO = tmem + lane_base + h * 256 + 128;
@@ -998,26 +971,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // The q prologue of work unit 0, then per work unit k: the q prologue of work unit
     // k+1 (whose tiles the producer loaded while unit k-1 ran), then the epilogue of k.
-    uint32_t next = next_work(p, blockIdx.x);
+    uint32_t next = h < nh ? next_work(p, blockIdx.x) : p.n_units;
     if (next < p.n_units) prepare(next, 0, 0);
     next = next < p.n_units ? next_work(p, next + gridDim.x) : p.n_units;
     uint32_t k = 0;  // work units done
-    for (uint32_t ui = blockIdx.x; ok && ui < p.n_units; ui += gridDim.x) {
+    for (uint32_t ui = blockIdx.x; ok && h < nh && ui < p.n_units; ui += gridDim.x) {
       const Unit u = decode(p, p.units[ui]);
       if (!u.live) continue;
       if (!u.nt) {
         // Zero valid keys: 0/0, as the reference's running sums give.
         const uint32_t qpos = u.q0 + r;
         if (qpos < u.rows) {
-          for (uint32_t h = 0; h < nh; ++h) {
-            const size_t orow = ((size_t)(u.tok0 + qpos) * p.heads + u.head0 + h) * 128;
-            if (p.out_bf16) {
-              uint16_t *o = (uint16_t *)p.out + orow;
-              for (int c = 0; c < 128; ++c) o[c] = 0x7fc0u;
-            } else {
-              float *o = (float *)p.out + orow;
-              for (int c = 0; c < 128; ++c) o[c] = __int_as_float(0x7fc00000);
-            }
+          const size_t orow = ((size_t)(u.tok0 + qpos) * p.heads + u.head0 + h) * 128;
+          if (p.out_bf16) {
+            uint16_t *o = (uint16_t *)p.out + orow;
+            for (int c = 0; c < 128; ++c) o[c] = 0x7fc0u;
+          } else {
+            float *o = (float *)p.out + orow;
+            for (int c = 0; c < 128; ++c) o[c] = __int_as_float(0x7fc00000);
           }
         }
         continue;
@@ -1167,25 +1138,9 @@ bool make_map(CUtensorMap *map, const void *base, uint32_t rows, uint32_t heads,
 
 }  // namespace
 
-uint32_t tc_rope_rows(uint32_t seq) { return (seq + tc::kQRows - 1) / tc::kQRows * tc::kQRows; }
-
-void tc_rope_table(float theta, uint32_t rows, float *table) {
-  for (uint32_t g = 0; g < 8; ++g)
-    for (uint32_t pos = 0; pos < rows; ++pos)
-      for (uint32_t e = 0; e < 8; ++e) {
-        const uint32_t c = 8 * g + e;
-        const float inv_freq = (float)std::pow((double)theta, -2.0 * (double)c / 128.0);
-        const float angle = (float)pos * inv_freq;  // the float product, as the kernels form it
-        float *t = table + ((size_t)(g * rows + pos) * 8 + e) * 2;
-        t[0] = (float)std::cos((double)angle);
-        t[1] = (float)std::sin((double)angle);
-      }
-}
-
 cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uint32_t n_units,
                                 int num_sms, int *status, const uint16_t *q_norm_w, float eps,
-                                float theta, const float *rope, uint32_t rope_rows,
-                                cudaStream_t stream) {
+                                float theta, cudaStream_t stream) {
   if (!n_units) return cudaSuccess;
   CUtensorMap mq, mk, mv, mo;
   const uint32_t rows = p.total;
@@ -1214,8 +1169,6 @@ cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uin
   prm.status = status;
   prm.q_norm_w = q_norm_w;
   prm.eps = eps;
-  prm.rope = reinterpret_cast<const float4 *>(rope);
-  prm.rope_rows = rope_rows;
   for (int i = 0; i < 64; ++i)
     prm.inv_freq[i] = (float)std::pow((double)theta, -2.0 * (double)i / 128.0);
   uint32_t grid = std::min<uint32_t>(n_units, (uint32_t)num_sms);

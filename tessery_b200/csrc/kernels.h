@@ -74,18 +74,9 @@ cudaError_t launch_attention_d32(const AttnProblem &p, cudaStream_t stream);
 bool tc_attention_supported(const AttnProblem &p);
 // q_norm_w: bf16 q RMSNorm weight [128] applied with RoPE to each Q tile in the kernel
 // (NULL: q is used as given).
-// rope: optional cosine/sine table of tc_rope_rows(seq) positions built by tc_rope_table
-// (NULL: the kernel evaluates them).
 cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uint32_t n_units,
                                 int num_sms, int *status, const uint16_t *q_norm_w, float eps,
-                                float theta, const float *rope, uint32_t rope_rows,
-                                cudaStream_t stream);
-// Positions the RoPE table of a problem with `seq` rows must cover (whole query tiles).
-uint32_t tc_rope_rows(uint32_t seq);
-// Host-side RoPE table for head_dim 128: 128 floats per position (cos and sin of
-// float(pos) * theta^(-2c/128) for c < 64, each rounded once from double), grouped by
-// eight columns: floats [(g * rows + pos) * 16, +16) hold columns 8g..8g+7 as (cos, sin).
-void tc_rope_table(float theta, uint32_t rows, float *table);
+                                float theta, cudaStream_t stream);
 // Host-side work-list construction for launch_attention_tc.
 // Fills `units` (capacity >= tc_max_units) and returns the count.
 uint32_t tc_max_units(const AttnProblem &p);

@@ -83,6 +83,6 @@ extern "C" int tx_attention_padded_noalloc(const void *q, const void *k, const v
                            cudaMemcpyHostToDevice, s) != cudaSuccess)
     return TX_ECUDA;
   cudaError_t e = tx::launch_attention_tc(p, scratch + kHeaderWords, n, g_noalloc_sms[device],
-                                          st, q_norm_w, eps, theta, nullptr, 0, s);
+                                          st, q_norm_w, eps, theta, s);
   return e == cudaSuccess ? TX_OK : TX_ECUDA;
 }

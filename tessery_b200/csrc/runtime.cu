@@ -56,9 +56,6 @@ struct Ctx {
   std::vector<uint32_t> units_host;
   uint64_t units_key = 0;
   uint32_t units_count = 0;
-  float *rope = nullptr;               // RoPE cosine/sine table of the tensor-core kernel
-  uint32_t rope_rows = 0;
-  float rope_theta = 0.f;
   cudaEvent_t scratch_done = nullptr;  // last launch that read scratch
   std::set<Buf *> buffers;
   const char *last_kernel = "";
@@ -112,27 +109,6 @@ cudaError_t ensure_units(Ctx *c, size_t count) {
   e = cudaMalloc(&c->units, count * sizeof(uint32_t));
   if (e != cudaSuccess) return e;
   c->units_cap = count;
-  return cudaSuccess;
-}
-
-// The RoPE table for `theta` covering `rows` positions (built on the host, uploaded once
-// and kept while later calls fit in it).
-cudaError_t ensure_rope(Ctx *c, float theta, uint32_t rows) {
-  if (c->rope && c->rope_theta == theta && c->rope_rows >= rows) return cudaSuccess;
-  rows = std::max(rows, c->rope_theta == theta ? c->rope_rows : 0u);
-  std::vector<float> host((size_t)rows * 128);
-  tx::tc_rope_table(theta, rows, host.data());
-  cudaError_t e = cudaDeviceSynchronize();
-  if (e != cudaSuccess) return e;
-  if (c->rope) cudaFree(c->rope);
-  c->rope = nullptr;
-  c->rope_rows = 0;
-  if ((e = cudaMalloc(&c->rope, host.size() * sizeof(float))) != cudaSuccess) return e;
-  if ((e = cudaMemcpy(c->rope, host.data(), host.size() * sizeof(float),
-                      cudaMemcpyHostToDevice)) != cudaSuccess)
-    return e;
-  c->rope_rows = rows;
-  c->rope_theta = theta;
   return cudaSuccess;
 }
 
@@ -220,16 +196,6 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
   if (uses_scratch && (e = scratch_acquire(c, stream)) != cudaSuccess)
     return cuda_fail(c, e, "scratch wait");
 
-  // RoPE table of the tensor-core kernel's fused q prologue.
-  const float *rope = nullptr;
-  uint32_t rope_rows = 0;
-  if (tc_path && q_w) {
-    if ((e = ensure_rope(c, theta, tx::tc_rope_rows(p.seq))) != cudaSuccess)
-      return cuda_fail(c, e, "rope table");
-    rope = c->rope;
-    rope_rows = c->rope_rows;
-  }
-
   // The tensor-core kernel applies the q prologue to each Q tile in shared memory; k
   // (read by several query tiles) is normalised once into scratch, valid rows only.
   const uint16_t *tc_q_w = tc_path ? q_w : nullptr;
@@ -281,8 +247,7 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
       c->units_key = key;
     }
     if ((e = tx::launch_attention_tc(p, c->units, c->units_count, c->sms, c->status, tc_q_w, eps,
-                                     theta, tc_q_w ? rope : nullptr, tc_q_w ? rope_rows : 0,
-                                     stream)) != cudaSuccess)
+                                     theta, stream)) != cudaSuccess)
       return cuda_fail(c, e, "attention launch");
     c->last_kernel = "tc_bf16_d128";
     ++c->launches;
@@ -381,7 +346,6 @@ void tx_destroy(void *ctx) {
     }
     c->buffers.clear();
     if (c->qk_scratch) cudaFree(c->qk_scratch);
-    if (c->rope) cudaFree(c->rope);
     if (c->units) cudaFree(c->units);
     if (c->status) cudaFree(c->status);
     for (cudaEvent_t ev : c->prof_events) cudaEventDestroy(ev);
