@@ -408,6 +408,43 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Packed pairs of floats (Blackwell f32x2 arithmetic: two lanes per instruction, each
+// rounded as the scalar instruction would round it).
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_bits(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// The two bf16 of a word as a float pair (lo first).
+__device__ __forceinline__ uint64_t bf16x2_f2(uint32_t w) {
+  return f2_bits(w << 16, w & 0xffff0000u);
+}
+
 // sin and cos of a float angle: Cody-Waite reduction by 2*pi (2*pi split into a float
 // head and a float tail) to [-pi, pi], then the hardware approximations, which are
 // accurate to about 2^-21 absolute on that interval.
@@ -445,6 +482,7 @@ __device__ __forceinline__ void q_transform_row(uint32_t q_tile, uint32_t r, uin
   for (int c = 0; c < 16; ++c)
     acc_squares(ssq, ld_shared_v4(row + (c >> 3) * kQAtom + (((c & 7) ^ sw) << 4)));
   const float inv = 1.0f / sqrtf(((ssq[0] + ssq[1]) + (ssq[2] + ssq[3])) / 128.0f + eps);
+  const uint64_t inv2 = f2(inv, inv);
   const float fpos = (float)pos;
 #pragma unroll 1
   for (int g = 0; g < 8; ++g) {  // 16-byte chunk g: columns 8g..8g+7 and 64+8g..
@@ -456,20 +494,15 @@ __device__ __forceinline__ void q_transform_row(uint32_t q_tile, uint32_t r, uin
     const uint4 hi = ld_shared_v4(row + kQAtom + ((g ^ sw) << 4));
     uint32_t out_lo[4], out_hi[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float ra[2], rb[2];
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int k = 2 * e + hh;
-        const uint32_t A = u4_at(lo, e), B = u4_at(hi, e);
-        const uint32_t WA = u4_at(wa, e), WB = u4_at(wb, e);
-        const float a = (hh ? bf16_hi(A) : bf16_lo(A)) * inv * (hh ? bf16_hi(WA) : bf16_lo(WA));
-        const float b = (hh ? bf16_hi(B) : bf16_lo(B)) * inv * (hh ? bf16_hi(WB) : bf16_lo(WB));
-        ra[hh] = a * co[k] - b * si[k];
-        rb[hh] = a * si[k] + b * co[k];
-      }
-      out_lo[e] = pack_bf16x2(ra[0], ra[1]);
-      out_hi[e] = pack_bf16x2(rb[0], rb[1]);
+    for (int e = 0; e < 4; ++e) {  // columns c = 8g+2e, c+1 and their partners c+64, c+65
+      const uint64_t a = mul2(mul2(bf16x2_f2(u4_at(lo, e)), inv2), bf16x2_f2(u4_at(wa, e)));
+      const uint64_t b = mul2(mul2(bf16x2_f2(u4_at(hi, e)), inv2), bf16x2_f2(u4_at(wb, e)));
+      const uint64_t cs = f2(co[2 * e], co[2 * e + 1]), sn = f2(si[2 * e], si[2 * e + 1]);
+      const uint64_t nsn = f2(-si[2 * e], -si[2 * e + 1]);
+      const float2 ra = f2_unpack(fma2(a, cs, mul2(b, nsn)));  // a*cos - b*sin
+      const float2 rb = f2_unpack(fma2(a, sn, mul2(b, cs)));   // a*sin + b*cos
+      out_lo[e] = pack_bf16x2(ra.x, ra.y);
+      out_hi[e] = pack_bf16x2(rb.x, rb.y);
     }
     st_shared_v4(row + ((g ^ sw) << 4), out_lo[0], out_lo[1], out_lo[2], out_lo[3]);
     st_shared_v4(row + kQAtom + ((g ^ sw) << 4), out_hi[0], out_hi[1], out_hi[2], out_hi[3]);
@@ -481,20 +514,22 @@ __device__ __forceinline__ void q_transform_row(uint32_t q_tile, uint32_t r, uin
 template <bool kMasked>
 __device__ __forceinline__ float exp_chunk(const uint32_t (&x)[32], int c, int valid, float sl,
                                            float m, uint32_t (&packed)[16]) {
-  float sum[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint64_t sl2 = f2(sl, sl), nm2 = f2(-m, -m);
+  uint64_t sum[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
 #pragma unroll
   for (int t = 0; t < 16; ++t) {
     const int k0 = c * 32 + 2 * t;
-    float p0 = ex2(fmaf(__uint_as_float(x[2 * t]), sl, -m));
-    float p1 = ex2(fmaf(__uint_as_float(x[2 * t + 1]), sl, -m));
+    const float2 z = f2_unpack(fma2(f2_bits(x[2 * t], x[2 * t + 1]), sl2, nm2));
+    float p0 = ex2(z.x), p1 = ex2(z.y);
     if (kMasked) {
       p0 = k0 < valid ? p0 : 0.f;
       p1 = k0 + 1 < valid ? p1 : 0.f;
     }
-    sum[t & 3] += p0 + p1;
+    sum[t & 1] = add2(sum[t & 1], f2(p0, p1));
     packed[t] = pack_bf16x2(p0, p1);
   }
-  return (sum[0] + sum[1]) + (sum[2] + sum[3]);
+  const float2 s0 = f2_unpack(sum[0]), s1 = f2_unpack(sum[1]);
+  return (s0.x + s1.x) + (s0.y + s1.y);
 }
 
 // ---- the kernel -----------------------------------------------------------------------
