@@ -599,11 +599,11 @@ def rooflines(w, name: str, kernel: str, att_s: float, pro_s: float | None):
     pro = None
     if pro_s is not None:
         pro_bytes = 2 * kv_valid_bytes + w.k_norm_weight.nbytes
-        pro = {"bound": "hbm", "kernel": "qk_norm_rope_kernel (k rows)",
+        pro = {"bound": "hbm", "kernel": "norm_rope_rows_bf16_kernel (k rows)",
                "achieved": pro_bytes / pro_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                "frac": pro_bytes / pro_s / 1e9 / peaks["hbm_gbs"],
                "algorithmic_bytes_per_launch": pro_bytes,
-               "traffic": traffic.get("qk_norm_rope_kernel"), "launch_us": 1e6 * pro_s}
+               "traffic": traffic.get("norm_rope_rows_bf16_kernel"), "launch_us": 1e6 * pro_s}
     return roof, pro
 
 
