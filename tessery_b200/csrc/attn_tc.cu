@@ -652,6 +652,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t nxt = cur < p.n_units ? next_work(p, cur + gridDim.x) : p.n_units;
       if (cur < p.n_units) load_q(cur, 0);
       if (nxt < p.n_units) load_q(nxt, 1);
+      // K may be written by the kernel launched just before this one (the k prologue):
+      // with a programmatic dependent launch this grid starts while that one drains, so
+      // wait for it before the first K load.  Q and V are the caller's inputs.
+      asm volatile("griddepcontrol.wait;" ::: "memory");
       for (uint32_t k = 0; ok && cur < p.n_units; ++k) {
         const Unit u = decode(p, p.units[cur]);
         const uint32_t ahead = nxt < p.n_units ? next_work(p, nxt + gridDim.x) : p.n_units;
@@ -1207,7 +1211,21 @@ cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uin
   for (int i = 0; i < 64; ++i)
     prm.inv_freq[i] = (float)std::pow((double)theta, -2.0 * (double)i / 128.0);
   uint32_t grid = std::min<uint32_t>(n_units, (uint32_t)num_sms);
-  tc::attn_tc_kernel<<<grid, tc::kThreads, tc::kSmemBytes, stream>>>(mq, mk, mv, mo, prm);
+  // Programmatic dependent launch: the CTAs may start (barrier set-up, tensor-memory
+  // allocation, Q loads and the q prologue) while the previous kernel on the stream
+  // finishes; the producer waits for it before reading K (griddepcontrol.wait).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(tc::kThreads);
+  cfg.dynamicSmemBytes = tc::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, tc::attn_tc_kernel, mq, mk, mv, mo, prm);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

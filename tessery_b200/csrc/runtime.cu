@@ -196,6 +196,32 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
   if (uses_scratch && (e = scratch_acquire(c, stream)) != cudaSuccess)
     return cuda_fail(c, e, "scratch wait");
 
+  // Work list of the tensor-core kernel, uploaded before the prologue launch: the
+  // attention kernel is launched as a programmatic dependent of the prologue and may
+  // start while the prologue runs, so everything it reads besides k must already be in
+  // place in stream order.
+  if (tc_path) {
+    uint32_t cap = tx::tc_max_units(p);
+    uint64_t key = 1469598103934665603ull;
+    uint32_t hdr[8] = {p.batch, p.seq, p.heads, p.kv_heads, (uint32_t)p.causal,
+                       p.cu_seqlens ? 1u : 0u, lengths_host || cu_host ? 1u : 0u, p.total};
+    key = fnv1a(key, hdr, sizeof hdr);
+    if (lengths_host) key = fnv1a(key, lengths_host, sizeof(uint32_t) * p.batch);
+    if (cu_host) key = fnv1a(key, cu_host, sizeof(int32_t) * (p.batch + 1));
+    if (key != c->units_key) {
+      if ((e = ensure_units(c, cap)) != cudaSuccess) return cuda_fail(c, e, "work list allocation");
+      c->units_host.resize(cap);
+      c->units_count = tx::tc_build_units(p, lengths_host, cu_host, c->units_host.data());
+      // Pageable source: the call returns once the data is staged, so the host vector
+      // can be rebuilt by the next call.
+      if (c->units_count &&
+          (e = cudaMemcpyAsync(c->units, c->units_host.data(), c->units_count * sizeof(uint32_t),
+                               cudaMemcpyHostToDevice, stream)) != cudaSuccess)
+        return cuda_fail(c, e, "work list upload");
+      c->units_key = key;
+    }
+  }
+
   // The tensor-core kernel applies the q prologue to each Q tile in shared memory; k
   // (read by several query tiles) is normalised once into scratch, valid rows only.
   const uint16_t *tc_q_w = tc_path ? q_w : nullptr;
@@ -227,25 +253,6 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
   }
 
   if (tc_path) {
-    uint32_t cap = tx::tc_max_units(p);
-    uint64_t key = 1469598103934665603ull;
-    uint32_t hdr[8] = {p.batch, p.seq, p.heads, p.kv_heads, (uint32_t)p.causal,
-                       p.cu_seqlens ? 1u : 0u, lengths_host || cu_host ? 1u : 0u, p.total};
-    key = fnv1a(key, hdr, sizeof hdr);
-    if (lengths_host) key = fnv1a(key, lengths_host, sizeof(uint32_t) * p.batch);
-    if (cu_host) key = fnv1a(key, cu_host, sizeof(int32_t) * (p.batch + 1));
-    if (key != c->units_key) {
-      if ((e = ensure_units(c, cap)) != cudaSuccess) return cuda_fail(c, e, "work list allocation");
-      c->units_host.resize(cap);
-      c->units_count = tx::tc_build_units(p, lengths_host, cu_host, c->units_host.data());
-      // Pageable source: the call returns once the data is staged, so the host vector
-      // can be rebuilt by the next call.
-      if (c->units_count &&
-          (e = cudaMemcpyAsync(c->units, c->units_host.data(), c->units_count * sizeof(uint32_t),
-                               cudaMemcpyHostToDevice, stream)) != cudaSuccess)
-        return cuda_fail(c, e, "work list upload");
-      c->units_key = key;
-    }
     if ((e = tx::launch_attention_tc(p, c->units, c->units_count, c->sms, c->status, tc_q_w, eps,
                                      theta, stream)) != cudaSuccess)
       return cuda_fail(c, e, "attention launch");

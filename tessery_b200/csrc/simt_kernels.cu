@@ -306,6 +306,9 @@ __device__ __forceinline__ void sincos_2pi_reduced(float angle, float *s, float 
 
 template <int NP>  // row pairs per token: ceil(nheads / 2)
 __global__ void __launch_bounds__(128) norm_rope_rows_bf16_kernel(RowPass p) {
+  // The attention kernel that follows may be launched early (programmatic dependent
+  // launch); it waits for this grid's completion before it reads what this one writes.
+  asm volatile("griddepcontrol.launch_dependents;");
   __shared__ int32_t cu_s[1025];
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t l16 = lane & 15, half = lane >> 4, g = l16 & 7;
