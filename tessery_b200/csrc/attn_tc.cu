@@ -6,8 +6,9 @@
 //
 // Work unit: (sequence, pair of query heads sharing one kv head, 128-row query tile);
 // when the query heads per kv head are odd, a unit holds one head.  The heads of a unit
-// share every K/V tile (GQA head sharing).  A persistent grid of one CTA per SM walks a
-// host-built, longest-first list of units.
+// share every K/V tile (GQA head sharing).  A persistent grid of one CTA per SM; each
+// CTA runs its own contiguous part of a host-built work list (units assigned longest
+// first to the least-loaded CTA).
 //
 // Warp roles (576 threads, one CTA per SM), specialised so that each serial per-unit
 // step runs beside the others instead of in front of them:
@@ -123,7 +124,8 @@ __host__ __device__ __forceinline__ uint32_t encode_unit(uint32_t seq, uint32_t 
 }
 
 struct Params {
-  const uint32_t *units;
+  const uint32_t *units;    // work units, grouped by CTA
+  const uint32_t *offsets;  // CTA c runs units [offsets[c], offsets[c+1])
   uint32_t n_units;
   const uint32_t *lengths;  // padded
   const int32_t *cu;        // varlen (NULL for padded)
@@ -172,9 +174,11 @@ __device__ __forceinline__ Unit decode(const Params &p, uint32_t code) {
   return u;
 }
 
-// The next unit at or after index `from` (stepping by the grid) that visits key tiles.
+// The next unit of this CTA at or after index `from` that visits key tiles (n_units when
+// there is none).
 __device__ __forceinline__ uint32_t next_work(const Params &p, uint32_t from) {
-  for (uint32_t ui = from; ui < p.n_units; ui += gridDim.x)
+  const uint32_t end = p.offsets[blockIdx.x + 1];
+  for (uint32_t ui = from; ui < end; ++ui)
     if (decode(p, p.units[ui]).nt) return ui;
   return p.n_units;
 }
@@ -648,8 +652,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_prefetch_3d(&tm_v, a * 64, (int)v.kvh, (int)(v.tok0 + j * kKeys));
             }
       };
-      uint32_t cur = next_work(p, blockIdx.x);
-      uint32_t nxt = cur < p.n_units ? next_work(p, cur + gridDim.x) : p.n_units;
+      uint32_t cur = next_work(p, p.offsets[blockIdx.x]);
+      uint32_t nxt = cur < p.n_units ? next_work(p, cur + 1) : p.n_units;
       if (cur < p.n_units) load_q(cur, 0);
       if (nxt < p.n_units) load_q(nxt, 1);
       // K may be written by the kernel launched just before this one (the k prologue):
@@ -658,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("griddepcontrol.wait;" ::: "memory");
       for (uint32_t k = 0; ok && cur < p.n_units; ++k) {
         const Unit u = decode(p, p.units[cur]);
-        const uint32_t ahead = nxt < p.n_units ? next_work(p, nxt + gridDim.x) : p.n_units;
+        const uint32_t ahead = nxt < p.n_units ? next_work(p, nxt + 1) : p.n_units;
         if (ahead < p.n_units) prefetch_unit(ahead, false);
         if (nxt < p.n_units) prefetch_unit(nxt, true);
         load_kv(&tm_k, u, 0);
@@ -730,7 +734,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   (acc || ks > 0) ? 1u : 0u);
         umma_commit(bar(kBarPVDone + h));
       };
-      for (uint32_t ui = blockIdx.x; ok && ui < p.n_units; ui += gridDim.x) {
+      for (uint32_t ui = p.offsets[blockIdx.x]; ok && ui < p.offsets[blockIdx.x + 1]; ++ui) {
         const Unit u = decode(p, p.units[ui]);
         if (!u.nt) continue;
         // Work unit k uses Q buffer k % 2 (fill k / 2 of that buffer).
@@ -793,7 +797,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tO = tS + 128;
     uint32_t tiles = 0, units_seen = 0;  // key tiles and work units processed
     bool ok = true;
-    for (uint32_t ui = blockIdx.x; ok && h < nh && ui < p.n_units; ui += gridDim.x) {
+    for (uint32_t ui = p.offsets[blockIdx.x]; ok && h < nh && ui < p.offsets[blockIdx.x + 1];
+         ++ui) {
       const Unit u = decode(p, p.units[ui]);
       if (!u.nt) continue;
       const uint32_t qpos = u.q0 + r;
@@ -1010,11 +1015,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // The q prologue of work unit 0, then per work unit k: the q prologue of work unit
     // k+1 (whose tiles the producer loaded while unit k-1 ran), then the epilogue of k.
-    uint32_t next = h < nh ? next_work(p, blockIdx.x) : p.n_units;
+    uint32_t next = h < nh ? next_work(p, p.offsets[blockIdx.x]) : p.n_units;
     if (next < p.n_units) prepare(next, 0, 0);
-    next = next < p.n_units ? next_work(p, next + gridDim.x) : p.n_units;
+    next = next < p.n_units ? next_work(p, next + 1) : p.n_units;
     uint32_t k = 0;  // work units done
-    for (uint32_t ui = blockIdx.x; ok && h < nh && ui < p.n_units; ui += gridDim.x) {
+    for (uint32_t ui = p.offsets[blockIdx.x]; ok && h < nh && ui < p.offsets[blockIdx.x + 1];
+         ++ui) {
       const Unit u = decode(p, p.units[ui]);
       if (!u.live) continue;
       if (!u.nt) {
@@ -1035,7 +1041,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (next < p.n_units) {
         prepare(next, (k + 1) & 1, (k + 1) >> 1);
         if (!ok) break;
-        next = next_work(p, next + gridDim.x);
+        next = next_work(p, next + 1);
       }
       epilogue(u);
       ++k;
@@ -1082,61 +1088,141 @@ uint32_t tc_max_units(const AttnProblem &p) {
   return p.batch * (p.heads / heads_per_unit(p)) * tiles;
 }
 
-// Longest-first list of units, built without allocating: a counting sort on the cost of
-// a unit (key tiles it visits, 0..510), stable, so the units of one (sequence, query
-// tile) -- whose heads share K/V tiles through their kv head -- stay adjacent.  Without
-// host lengths the cost is an estimate from the query-tile index (later tiles of a
-// causal sequence visit more key tiles).
+uint32_t tc_grid(uint32_t n_units, int num_sms) {
+  return std::min<uint32_t>(n_units, (uint32_t)std::max(num_sms, 1));
+}
+
+uint32_t tc_work_words(const AttnProblem &p, int num_sms) {
+  return tc_max_units(p) + (uint32_t)std::max(num_sms, 1) + 1;
+}
+
+namespace {
+
+// Key tiles a unit (sequence s, query tile t) visits, 0..511.  Without host lengths the
+// cost is an estimate from the query-tile index (later tiles of a causal sequence visit
+// more key tiles).
+uint32_t unit_tiles(const AttnProblem &p, const uint32_t *lengths_host, const int32_t *cu_host,
+                    uint32_t s, uint32_t t, uint32_t *rows_out) {
+  uint32_t n, rows;
+  bool known = false;
+  if (p.cu_seqlens) {
+    if (cu_host) {
+      int32_t a = cu_host[s], b = cu_host[s + 1];
+      n = b > a ? (uint32_t)(b - a) : 0u;
+      rows = n;
+      known = true;
+    } else {
+      n = rows = p.seq;
+    }
+  } else {
+    rows = p.seq;
+    n = lengths_host ? std::min(lengths_host[s], p.seq) : p.seq;
+    known = lengths_host != nullptr;
+  }
+  *rows_out = rows;
+  const uint32_t q0 = t * tc::kQRows;
+  uint32_t kend;
+  if (known) kend = p.causal ? std::min(q0 + (uint32_t)tc::kQRows, n) : n;
+  else kend = p.causal ? std::min(q0 + (uint32_t)tc::kQRows, p.seq) : p.seq;
+  return std::min((kend + tc::kKeys - 1) / tc::kKeys, 511u);
+}
+
+// Relative cost of a unit for the load balance: about 9k cycles per key tile and 4.5k
+// per unit (loading and transforming its Q tiles, the epilogue), measured on B200.
+uint32_t unit_cost(uint32_t tiles) { return 2 * tiles + 1; }
+
+// Min-heap of (load << 16 | cta) keys over the CTAs (grid <= 65535).
+struct LoadHeap {
+  uint64_t *h;
+  uint32_t n;
+  void push_all(uint32_t grid) {
+    n = grid;
+    for (uint32_t c = 0; c < grid; ++c) h[c] = c;  // load 0, ordered by CTA
+  }
+  // Adds `cost` to the least-loaded CTA and returns it.
+  uint32_t take(uint32_t cost) {
+    const uint32_t cta = (uint32_t)(h[0] & 0xffffu);
+    h[0] += (uint64_t)cost << 16;
+    for (uint32_t i = 0;;) {  // sift down
+      uint32_t l = 2 * i + 1, r = l + 1, m = i;
+      if (l < n && h[l] < h[m]) m = l;
+      if (r < n && h[r] < h[m]) m = r;
+      if (m == i) break;
+      std::swap(h[i], h[m]);
+      i = m;
+    }
+    return cta;
+  }
+};
+
+}  // namespace
+
+// The work list, built without allocating: the units sorted by cost, longest first (a
+// counting sort on the key tiles, stable, so the units of one (sequence, query tile) --
+// whose heads share K/V tiles through their kv head -- stay adjacent), then assigned in
+// that order to the least-loaded CTA (longest-processing-time scheduling) and written
+// grouped by CTA, followed by the grid+1 offsets of the groups.
 uint32_t tc_build_units(const AttnProblem &p, const uint32_t *lengths_host, const int32_t *cu_host,
-                        uint32_t *units) {
-  constexpr uint32_t kMaxCost = 511;
+                        int num_sms, uint32_t *sorted, uint32_t *work) {
+  constexpr uint32_t kMaxTiles = 511;
   const uint32_t tiles = (p.seq + tc::kQRows - 1) / tc::kQRows;
   const uint32_t per_tile = p.heads / heads_per_unit(p);
-  auto cost_of = [&](uint32_t s, uint32_t t, uint32_t *rows_out) -> uint32_t {
-    uint32_t n, rows;
-    bool known = false;
-    if (p.cu_seqlens) {
-      if (cu_host) {
-        int32_t a = cu_host[s], b = cu_host[s + 1];
-        n = b > a ? (uint32_t)(b - a) : 0u;
-        rows = n;
-        known = true;
-      } else {
-        n = rows = p.seq;
-      }
-    } else {
-      rows = p.seq;
-      n = lengths_host ? std::min(lengths_host[s], p.seq) : p.seq;
-      known = lengths_host != nullptr;
-    }
-    *rows_out = rows;
-    const uint32_t q0 = t * tc::kQRows;
-    uint32_t kend;
-    if (known) kend = p.causal ? std::min(q0 + (uint32_t)tc::kQRows, n) : n;
-    else kend = p.causal ? std::min(q0 + (uint32_t)tc::kQRows, p.seq) : p.seq;
-    return std::min((kend + tc::kKeys - 1) / tc::kKeys, kMaxCost);
-  };
-  uint32_t count[kMaxCost + 1] = {};
+  uint32_t count[kMaxTiles + 1] = {};
   for (uint32_t s = 0; s < p.batch; ++s)
     for (uint32_t t = 0; t < tiles; ++t) {
       uint32_t rows;
-      const uint32_t c = cost_of(s, t, &rows);
+      const uint32_t c = unit_tiles(p, lengths_host, cu_host, s, t, &rows);
       if (t * tc::kQRows >= rows) break;
       count[c] += per_tile;
     }
-  uint32_t start[kMaxCost + 1];
+  uint32_t start[kMaxTiles + 1];
   uint32_t total = 0;
-  for (int c = (int)kMaxCost; c >= 0; --c) {  // highest cost first
+  for (int c = (int)kMaxTiles; c >= 0; --c) {  // highest cost first
     start[c] = total;
     total += count[c];
   }
   for (uint32_t s = 0; s < p.batch; ++s)
     for (uint32_t t = 0; t < tiles; ++t) {
       uint32_t rows;
-      const uint32_t c = cost_of(s, t, &rows);
+      const uint32_t c = unit_tiles(p, lengths_host, cu_host, s, t, &rows);
       if (t * tc::kQRows >= rows) break;
-      for (uint32_t i = 0; i < per_tile; ++i) units[start[c]++] = tc::encode_unit(s, i, t);
+      for (uint32_t i = 0; i < per_tile; ++i) sorted[start[c]++] = tc::encode_unit(s, i, t);
     }
+  const uint32_t grid = tc_grid(total, num_sms);
+  uint32_t *offsets = work + total;
+  if (!total) {
+    offsets[0] = 0;
+    return 0;
+  }
+  // Two identical greedy passes: the first counts each CTA's units, the second places
+  // them (no per-unit assignment array needed).
+  uint64_t heap_mem[1024];
+  uint32_t cursor[1024];
+  const uint32_t g = std::min<uint32_t>(grid, 1024u);
+  LoadHeap heap{heap_mem, 0};
+  for (int pass = 0; pass < 2; ++pass) {
+    heap.push_all(g);
+    if (pass == 0)
+      for (uint32_t c = 0; c < g; ++c) cursor[c] = 0;
+    for (uint32_t i = 0; i < total; ++i) {
+      const uint32_t code = sorted[i];
+      uint32_t rows;
+      const uint32_t cost =
+          unit_cost(unit_tiles(p, lengths_host, cu_host, code >> 14, code & 255u, &rows));
+      const uint32_t cta = heap.take(cost);
+      if (pass == 0) ++cursor[cta];
+      else work[cursor[cta]++] = code;
+    }
+    if (pass == 0) {
+      uint32_t acc = 0;
+      for (uint32_t c = 0; c < g; ++c) {
+        offsets[c] = acc;
+        acc += cursor[c];
+        cursor[c] = offsets[c];
+      }
+      offsets[g] = acc;
+    }
+  }
   return total;
 }
 
@@ -1194,6 +1280,7 @@ cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uin
   if (e != cudaSuccess) return e;
   tc::Params prm;
   prm.units = units;
+  prm.offsets = units + n_units;
   prm.n_units = n_units;
   prm.lengths = p.lengths;
   prm.cu = p.cu_seqlens;
@@ -1210,7 +1297,7 @@ cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uin
   prm.eps = eps;
   for (int i = 0; i < 64; ++i)
     prm.inv_freq[i] = (float)std::pow((double)theta, -2.0 * (double)i / 128.0);
-  uint32_t grid = std::min<uint32_t>(n_units, (uint32_t)num_sms);
+  const uint32_t grid = std::min(tc_grid(n_units, num_sms), 1024u);
   // Programmatic dependent launch: the CTAs may start (barrier set-up, tensor-memory
   // allocation, Q loads and the q prologue) while the previous kernel on the stream
   // finishes; the producer waits for it before reading K (griddepcontrol.wait).

@@ -77,10 +77,14 @@ bool tc_attention_supported(const AttnProblem &p);
 cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uint32_t n_units,
                                 int num_sms, int *status, const uint16_t *q_norm_w, float eps,
                                 float theta, cudaStream_t stream);
-// Host-side work-list construction for launch_attention_tc.
-// Fills `units` (capacity >= tc_max_units) and returns the count.
+// Host-side work-list construction for launch_attention_tc (same num_sms for both).
+// `sorted` is host scratch of tc_max_units words; `work` (tc_work_words words) receives
+// the n units grouped by CTA followed by grid+1 offsets; returns n.  The launcher takes
+// `work` (on the device) and n.
 uint32_t tc_max_units(const AttnProblem &p);
+uint32_t tc_work_words(const AttnProblem &p, int num_sms);
+uint32_t tc_grid(uint32_t n_units, int num_sms);
 uint32_t tc_build_units(const AttnProblem &p, const uint32_t *lengths_host,
-                        const int32_t *cu_host, uint32_t *units);
+                        const int32_t *cu_host, int num_sms, uint32_t *sorted, uint32_t *work);
 
 }  // namespace tx

@@ -24,10 +24,14 @@ namespace {
 // Capacity of the work list: units = batch * heads/2 * ceil(seq / 128) (heads, not
 // pairs, when the query heads per kv head are odd).
 constexpr uint32_t kNoAllocMaxUnits = 32768;
-// Word 0: status word used when the caller passes no status pointer.  Words 64..: units.
+// The work list also holds one offset per CTA of the grid, plus one.
+constexpr uint32_t kNoAllocMaxOffsets = 1025;
+// Word 0: status word used when the caller passes no status pointer.  Words 64..: the
+// work list (units grouped by CTA, then the offsets).
 constexpr uint32_t kHeaderWords = 64;
 
-static __device__ __align__(256) uint32_t g_noalloc_scratch[kHeaderWords + kNoAllocMaxUnits];
+static __device__ __align__(256) uint32_t
+    g_noalloc_scratch[kHeaderWords + kNoAllocMaxUnits + kNoAllocMaxOffsets];
 
 // Device address of g_noalloc_scratch per device, looked up once with that device
 // current.  In host code the array's name is only a host-side stand-in, not a device
@@ -35,7 +39,9 @@ static __device__ __align__(256) uint32_t g_noalloc_scratch[kHeaderWords + kNoAl
 std::mutex g_noalloc_mu;
 uint32_t *g_noalloc_ptr[64] = {};
 int g_noalloc_sms[64] = {};
-uint32_t g_host_units[kNoAllocMaxUnits];  // host copy of the work list (under the mutex)
+// Host work space for building the work list (under the mutex).
+uint32_t g_host_sorted[kNoAllocMaxUnits];
+uint32_t g_host_work[kNoAllocMaxUnits + kNoAllocMaxOffsets];
 
 }  // namespace
 
@@ -75,14 +81,18 @@ extern "C" int tx_attention_padded_noalloc(const void *q, const void *k, const v
   uint32_t *scratch = g_noalloc_ptr[device];
   cudaStream_t s = (cudaStream_t)stream;
   int *st = status ? status : (int *)scratch;
-  // tc_build_units sorts with fixed-size arrays on the stack: no allocation.
-  const uint32_t n = tx::tc_build_units(p, lengths_host, nullptr, g_host_units);
+  const int sms = g_noalloc_sms[device];
+  if (sms < 1 || tx::tc_grid(tx::tc_max_units(p), sms) + 1 > kNoAllocMaxOffsets) return TX_EINVAL;
+  // tc_build_units sorts and balances with fixed-size arrays on the stack and the static
+  // host arrays above: no allocation.
+  const uint32_t n = tx::tc_build_units(p, lengths_host, nullptr, sms, g_host_sorted, g_host_work);
+  const uint32_t words = n + tx::tc_grid(n, sms) + 1;
   // The array keeps the previous call's contents: the status word must start at zero.
   if (cudaMemsetAsync(st, 0, sizeof(int), s) != cudaSuccess) return TX_ECUDA;
-  if (n && cudaMemcpyAsync(scratch + kHeaderWords, g_host_units, n * sizeof(uint32_t),
+  if (n && cudaMemcpyAsync(scratch + kHeaderWords, g_host_work, words * sizeof(uint32_t),
                            cudaMemcpyHostToDevice, s) != cudaSuccess)
     return TX_ECUDA;
-  cudaError_t e = tx::launch_attention_tc(p, scratch + kHeaderWords, n, g_noalloc_sms[device],
-                                          st, q_norm_w, eps, theta, s);
+  cudaError_t e = tx::launch_attention_tc(p, scratch + kHeaderWords, n, sms, st, q_norm_w, eps,
+                                          theta, s);
   return e == cudaSuccess ? TX_OK : TX_ECUDA;
 }

@@ -201,7 +201,7 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
   // start while the prologue runs, so everything it reads besides k must already be in
   // place in stream order.
   if (tc_path) {
-    uint32_t cap = tx::tc_max_units(p);
+    const uint32_t cap = tx::tc_max_units(p), words = tx::tc_work_words(p, c->sms);
     uint64_t key = 1469598103934665603ull;
     uint32_t hdr[8] = {p.batch, p.seq, p.heads, p.kv_heads, (uint32_t)p.causal,
                        p.cu_seqlens ? 1u : 0u, lengths_host || cu_host ? 1u : 0u, p.total};
@@ -209,13 +209,16 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
     if (lengths_host) key = fnv1a(key, lengths_host, sizeof(uint32_t) * p.batch);
     if (cu_host) key = fnv1a(key, cu_host, sizeof(int32_t) * (p.batch + 1));
     if (key != c->units_key) {
-      if ((e = ensure_units(c, cap)) != cudaSuccess) return cuda_fail(c, e, "work list allocation");
-      c->units_host.resize(cap);
-      c->units_count = tx::tc_build_units(p, lengths_host, cu_host, c->units_host.data());
+      if ((e = ensure_units(c, words)) != cudaSuccess) return cuda_fail(c, e, "work list allocation");
+      c->units_host.resize((size_t)cap + words);
+      uint32_t *work = c->units_host.data() + cap;
+      c->units_count = tx::tc_build_units(p, lengths_host, cu_host, c->sms, c->units_host.data(),
+                                          work);
+      const uint32_t upload = c->units_count + tx::tc_grid(c->units_count, c->sms) + 1;
       // Pageable source: the call returns once the data is staged, so the host vector
       // can be rebuilt by the next call.
       if (c->units_count &&
-          (e = cudaMemcpyAsync(c->units, c->units_host.data(), c->units_count * sizeof(uint32_t),
+          (e = cudaMemcpyAsync(c->units, work, upload * sizeof(uint32_t),
                                cudaMemcpyHostToDevice, stream)) != cudaSuccess)
         return cuda_fail(c, e, "work list upload");
       c->units_key = key;
