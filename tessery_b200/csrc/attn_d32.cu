@@ -78,17 +78,24 @@ __device__ __forceinline__ float d32_ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// Dot product of 16 query elements (8 packed pairs) with 16 staged key elements.
-__device__ __forceinline__ float d32_dot16(const uint64_t (&q)[8], const float *kr) {
-  uint64_t s0 = d32_f2(0.f, 0.f), s1 = s0;
+// Dot products of two rows' 16 query elements (8 packed pairs each) with 16 staged key
+// elements, read once for both rows.
+__device__ __forceinline__ void d32_dot16x2(const uint64_t (&qa)[8], const uint64_t (&qb)[8],
+                                            const float *kr, float *da, float *db) {
+  uint64_t a0 = d32_f2(0.f, 0.f), a1 = a0, b0 = a0, b1 = a0;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const float4 t = ((const float4 *)kr)[i];
-    s0 = d32_fma2(q[2 * i], d32_f2(t.x, t.y), s0);
-    s1 = d32_fma2(q[2 * i + 1], d32_f2(t.z, t.w), s1);
+    const uint64_t k0 = d32_f2(t.x, t.y), k1 = d32_f2(t.z, t.w);
+    a0 = d32_fma2(qa[2 * i], k0, a0);
+    a1 = d32_fma2(qa[2 * i + 1], k1, a1);
+    b0 = d32_fma2(qb[2 * i], k0, b0);
+    b1 = d32_fma2(qb[2 * i + 1], k1, b1);
   }
-  const float2 a = d32_unpack(s0), b = d32_unpack(s1);
-  return (a.x + a.y) + (b.x + b.y);
+  const float2 x0 = d32_unpack(a0), x1 = d32_unpack(a1), y0 = d32_unpack(b0),
+               y1 = d32_unpack(b1);
+  *da = (x0.x + x0.y) + (x1.x + x1.y);
+  *db = (y0.x + y0.y) + (y1.x + y1.y);
 }
 
 // Thread t works on query rows 2(t/2) and 2(t/2)+1 of the CTA's 128 and on head-dimension
@@ -180,15 +187,18 @@ __global__ void __launch_bounds__(kRows, 4) attention_d32_kernel(AttnProblem p) 
     const uint32_t stop = min(cn, wend - c0);
     for (uint32_t j0 = 0; j0 < stop; j0 += kBlock) {
       float s0[kBlock], s1[kBlock];
+      // Blocks wholly inside both rows' key ranges need no mask (warp-uniform test).
+      const bool full = __all_sync(0xffffffffu, c0 + j0 + kBlock <= min(end0, end1));
 #pragma unroll
       for (int j = 0; j < kBlock; ++j) {
         const float *kr = ks + (j0 + j) * kD + 16 * half;
-        float d0 = d32_dot16(qa, kr), d1 = d32_dot16(qb, kr);
+        float d0, d1;
+        d32_dot16x2(qa, qb, kr, &d0, &d1);
         d0 += __shfl_xor_sync(0xffffffffu, d0, 1);
         d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
         const uint32_t key = c0 + j0 + j;
-        s0[j] = key < end0 ? d0 : -INFINITY;
-        s1[j] = key < end1 ? d1 : -INFINITY;
+        s0[j] = full || key < end0 ? d0 : -INFINITY;
+        s1[j] = full || key < end1 ? d1 : -INFINITY;
       }
       float mb0 = s0[0], mb1 = s1[0];
 #pragma unroll
