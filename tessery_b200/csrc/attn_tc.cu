@@ -803,12 +803,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!u.nt) continue;
       const uint32_t qpos = u.q0 + r;
       const uint32_t end = p.causal ? min(qpos + 1, u.n) : u.n;
+      // A warp whose 32 rows all lie past the end of a packed sequence produces no output:
+      // it leaves S in place of P (those rows of O are never stored) and only keeps the
+      // barriers in step.
+      const bool warp_live = __any_sync(0xffffffffu, qpos < u.rows);
       float m_ref = -INFINITY, l = 0.f;
       for (uint32_t j = 0; j < u.nt; ++j, ++tiles) {
         ok = __all_sync(0xffffffffu, wait_phase(bar(kBarSFull + h), tiles & 1, abort_flag,
                                                 p.status, kSiteSFull));
         if (!ok) break;
         tc_fence_after();
+        if (!warp_live) {
+          tc_fence_before();
+          mbar_arrive(bar(kBarPFull + h));
+          continue;
+        }
         const int valid = (int)min(max((int)end - (int)(j * kKeys), 0), kKeys);
         // Pass 1: the tile's row maximum (64 columns in registers at a time).
         float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -901,9 +910,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                                               p.status, kSiteQFull));
       if (!ok) return;
       if (p.q_norm_w) {
+        // Rows past the end of a packed sequence belong to no output: left as loaded.
         const Unit v = decode(p, p.units[ui]);
-        q_transform_row(sbase + kOffQ + b * kQBufBytes + h * kQBytes, r, v.q0 + r,
-                        smem_addr(qw_s), invf_s, p.eps);
+        if (v.q0 + r < v.rows)
+          q_transform_row(sbase + kOffQ + b * kQBufBytes + h * kQBytes, r, v.q0 + r,
+                          smem_addr(qw_s), invf_s, p.eps);
         fence_proxy_async();
       }
       mbar_arrive(bar(kBarQReady + b));
