@@ -261,8 +261,10 @@ static cudaError_t launch_prologue_e(const PrologueProblem &p, cudaStream_t stre
 // ---- bf16 head_dim-128 prologue, written for bandwidth -------------------------------
 // One pass over the rows of one tensor (q or k).  A block of 4 warps covers 16
 // consecutive tokens (padded layout: 16 positions of one sequence, blockIdx.y = the
-// sequence, so its length is read once and blocks past it exit); each warp takes 4
-// tokens and loads the next token's rows while it transforms the current one.  Within a
+// sequence, so its length is read once and blocks past it exit); their rows are
+// contiguous in memory and arrive in shared memory with one bulk asynchronous copy, so
+// the bytes in flight per SM are set by the blocks resident there, not by registers;
+// each warp then transforms 4 tokens and writes them straight to global memory.  Within a
 // token, each half-warp owns one 256-byte row (one head) per load, lane l%16 holding the
 // 16 bytes of columns 8(l%16)..8(l%16)+7, so every load and store moves 512 contiguous
 // bytes per warp.  The rotation partner of column c (c < 64) is column c + 64, held by
@@ -309,38 +311,71 @@ __global__ void __launch_bounds__(128) norm_rope_rows_bf16_kernel(RowPass p) {
   // The attention kernel that follows may be launched early (programmatic dependent
   // launch); it waits for this grid's completion before it reads what this one writes.
   asm volatile("griddepcontrol.launch_dependents;");
+  extern __shared__ __align__(128) uint8_t rows_s[];  // the block's token rows
   __shared__ int32_t cu_s[1025];
+  __shared__ __align__(8) uint64_t full_bar;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t l16 = lane & 15, half = lane >> 4, g = l16 & 7;
   const bool first = l16 < 8;
-  // Tokens of this warp: [t0, t0 + n) of one sequence (padded) or of the packed rows.
-  uint32_t t0, n, pos0 = 0, seq_start = 0;
+  constexpr uint32_t kBlockTokens = 4 * kRowTokensPerWarp;
+  // Tokens of this block: [tb, tb + nb) of one sequence (padded) or of the packed rows.
+  uint32_t tb, nb, pos0 = 0;
   if (p.cu) {
-    const bool cu_shared = p.nseq < 1025;
-    if (cu_shared)
+    tb = blockIdx.x * kBlockTokens;
+    if (tb >= p.tokens) return;
+    nb = min(kBlockTokens, p.tokens - tb);
+    if (p.nseq < 1025)
       for (uint32_t i = threadIdx.x; i <= p.nseq; i += blockDim.x) cu_s[i] = p.cu[i];
-    __syncthreads();
-    t0 = (blockIdx.x * 4 + warp) * kRowTokensPerWarp;
-    if (t0 >= p.tokens) return;
-    n = min((uint32_t)kRowTokensPerWarp, p.tokens - t0);
-    (void)cu_shared;
   } else {
     const uint32_t b = blockIdx.y;
     const uint32_t len = p.lengths ? min(p.lengths[b], p.seq) : p.seq;
-    pos0 = (blockIdx.x * 4 + warp) * kRowTokensPerWarp;
+    pos0 = blockIdx.x * kBlockTokens;
     if (pos0 >= len) return;
-    n = min((uint32_t)kRowTokensPerWarp, len - pos0);
-    t0 = b * p.seq + pos0;
+    nb = min(kBlockTokens, len - pos0);
+    tb = b * p.seq + pos0;
   }
-  // Weights of this lane's columns and of its partner's (bf16 pairs, unpacked per use).
+  const uint32_t row_bytes = p.nheads * 256;
+  const uint32_t full = (uint32_t)__cvta_generic_to_shared(&full_bar);
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(full) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // One bulk copy of the block's consecutive token rows into shared memory.
+    const uint32_t bytes = nb * row_bytes;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full), "r"(bytes)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            (uint32_t)__cvta_generic_to_shared(rows_s)),
+        "l"(p.in + (size_t)tb * p.nheads * 128), "r"(bytes), "r"(full)
+        : "memory");
+  }
+  // Weights of this lane's columns and of its partner's, and its inverse frequencies.
   const uint4 wo = __ldg(reinterpret_cast<const uint4 *>(p.w) + l16);
   const uint4 wp = __ldg(reinterpret_cast<const uint4 *>(p.w) + (l16 ^ 8));
-  float wof[8], wpf[8];
+  float wof[8], wpf[8], invf[8];
   bf16x8_unpack(wo, wof);
   bf16x8_unpack(wp, wpf);
-  auto position = [&](uint32_t i) -> uint32_t {
-    if (!p.cu) return pos0 + i;
-    const uint32_t tok = t0 + i;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) invf[e] = p.inv_freq[8 * g + e];
+  // Bounded wait for the copy (it completes unless the copy itself failed).
+  {
+    uint32_t done = 0;
+    const long long t0 = clock64();
+    while (!done) {
+      asm volatile(
+          "{\n\t.reg .pred q;\n\tmbarrier.try_wait.parity.shared::cta.b64 q, [%1], 0;\n\t"
+          "selp.u32 %0, 1, 0, q;\n\t}"
+          : "=r"(done)
+          : "r"(full)
+          : "memory");
+      if (!done && clock64() - t0 > 2000000000ll) return;
+    }
+  }
+  auto position = [&](uint32_t tok) -> uint32_t {
+    if (!p.cu) return pos0 + (tok - tb);
     uint32_t lo = 0, hi = p.nseq;
     if (p.nseq < 1025) {
       while (hi - lo > 1) {
@@ -351,32 +386,33 @@ __global__ void __launch_bounds__(128) norm_rope_rows_bf16_kernel(RowPass p) {
     }
     return tok - (uint32_t)p.cu[find_seq(p.cu, p.nseq, tok)];
   };
-  auto load = [&](uint32_t i, uint4 (&x)[NP]) {
-    const uint16_t *row = p.in + (size_t)(t0 + i) * p.nheads * 128;
+  const uint32_t srow0 = (uint32_t)__cvta_generic_to_shared(rows_s);
+#pragma unroll 1
+  for (uint32_t i = warp * kRowTokensPerWarp; i < min((warp + 1) * kRowTokensPerWarp, nb); ++i) {
+    const uint32_t tok = tb + i;
+    uint4 x[NP];
 #pragma unroll
     for (int j = 0; j < NP; ++j) {
       const uint32_t head = 2 * j + half;
-      x[j] = head < p.nheads ? __ldg(reinterpret_cast<const uint4 *>(row + (size_t)head * 128) + l16)
-                             : make_uint4(0, 0, 0, 0);
+      if (head < p.nheads) {
+        const uint32_t addr = srow0 + i * row_bytes + head * 256 + l16 * 16;
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(x[j].x), "=r"(x[j].y), "=r"(x[j].z), "=r"(x[j].w)
+                     : "r"(addr));
+      } else {
+        x[j] = make_uint4(0, 0, 0, 0);
+      }
     }
-  };
-  uint4 xa[NP], xb[NP];
-  load(0, xa);
-#pragma unroll 1
-  for (uint32_t i = 0; i < n; ++i) {
-    uint4(&x)[NP] = (i & 1) ? xb : xa;
-    uint4(&nx)[NP] = (i & 1) ? xa : xb;
-    if (i + 1 < n) load(i + 1, nx);
-    const float fpos = (float)position(i);
+    const float fpos = (float)position(tok);
     float c1[8], c2[8];  // w_own * cos and -/+ w_partner * sin
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       float sn, cs;
-      sincos_2pi_reduced(fpos * p.inv_freq[8 * g + e], &sn, &cs);
+      sincos_2pi_reduced(fpos * invf[e], &sn, &cs);
       c1[e] = wof[e] * cs;
       c2[e] = first ? -(wpf[e] * sn) : wpf[e] * sn;
     }
-    uint16_t *orow = p.out + (size_t)(t0 + i) * p.nheads * 128;
+    uint16_t *orow = p.out + (size_t)tok * p.nheads * 128;
 #pragma unroll
     for (int j = 0; j < NP; ++j) {
       const uint32_t head = 2 * j + half;
@@ -409,15 +445,22 @@ __global__ void __launch_bounds__(128) norm_rope_rows_bf16_kernel(RowPass p) {
 
 template <int NP>
 static cudaError_t launch_rows(const RowPass &rp, const PrologueProblem &p, cudaStream_t stream) {
+  constexpr uint32_t kBlockTokens = 4 * kRowTokensPerWarp;
   dim3 grid;
   if (rp.cu) {
-    grid = dim3((rp.tokens + 15) / 16, 1, 1);
+    grid = dim3((rp.tokens + kBlockTokens - 1) / kBlockTokens, 1, 1);
   } else {
     if (p.tokens % p.seq) return cudaErrorInvalidValue;
-    grid = dim3((rp.seq + 15) / 16, rp.tokens / rp.seq, 1);
+    grid = dim3((rp.seq + kBlockTokens - 1) / kBlockTokens, rp.tokens / rp.seq, 1);
     if (grid.y > 65535u) return cudaErrorInvalidValue;
   }
-  norm_rope_rows_bf16_kernel<NP><<<grid, 128, 0, stream>>>(rp);
+  const uint32_t smem = kBlockTokens * rp.nheads * 256;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(norm_rope_rows_bf16_kernel<NP>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  norm_rope_rows_bf16_kernel<NP><<<grid, 128, smem, stream>>>(rp);
   return cudaGetLastError();
 }
 
