@@ -299,6 +299,34 @@ __device__ __forceinline__ void bf16x8_unpack(const uint4 &v, float (&f)[8]) {
   }
 }
 
+__device__ __forceinline__ uint64_t pf2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t pf2_bits(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 pf2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t pfma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t pmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// The two bf16 of a word as a float pair (lo first).
+__device__ __forceinline__ uint64_t bf16x2_pf2(uint32_t w) { return pf2_bits(w << 16, w & 0xffff0000u); }
+
 __device__ __forceinline__ void sincos_2pi_reduced(float angle, float *s, float *c) {
   const float k = rintf(angle * 0.159154943091895336f);
   float r = fmaf(k, -6.28318548202514648f, angle);
@@ -404,39 +432,44 @@ __global__ void __launch_bounds__(128) norm_rope_rows_bf16_kernel(RowPass p) {
       }
     }
     const float fpos = (float)position(tok);
-    float c1[8], c2[8];  // w_own * cos and -/+ w_partner * sin
+    uint64_t c1[4], c2[4];  // pairs of w_own * cos and -/+ w_partner * sin
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float sn, cs;
-      sincos_2pi_reduced(fpos * invf[e], &sn, &cs);
-      c1[e] = wof[e] * cs;
-      c2[e] = first ? -(wpf[e] * sn) : wpf[e] * sn;
+    for (int e = 0; e < 4; ++e) {
+      float sn0, cs0, sn1, cs1;
+      sincos_2pi_reduced(fpos * invf[2 * e], &sn0, &cs0);
+      sincos_2pi_reduced(fpos * invf[2 * e + 1], &sn1, &cs1);
+      c1[e] = pf2(wof[2 * e] * cs0, wof[2 * e + 1] * cs1);
+      c2[e] = first ? pf2(-(wpf[2 * e] * sn0), -(wpf[2 * e + 1] * sn1))
+                    : pf2(wpf[2 * e] * sn0, wpf[2 * e + 1] * sn1);
     }
     uint16_t *orow = p.out + (size_t)tok * p.nheads * 128;
 #pragma unroll
     for (int j = 0; j < NP; ++j) {
       const uint32_t head = 2 * j + half;
-      float a[8], b[8];
-      bf16x8_unpack(x[j], a);
-      uint4 px;
-      px.x = __shfl_xor_sync(0xffffffffu, x[j].x, 8);
-      px.y = __shfl_xor_sync(0xffffffffu, x[j].y, 8);
-      px.z = __shfl_xor_sync(0xffffffffu, x[j].z, 8);
-      px.w = __shfl_xor_sync(0xffffffffu, x[j].w, 8);
-      bf16x8_unpack(px, b);
-      float ss = 0.f;
+      const uint32_t xw[4] = {x[j].x, x[j].y, x[j].z, x[j].w};
+      uint64_t a[4], b[4];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss = fmaf(a[e], a[e], ss);
+      for (int e = 0; e < 4; ++e) {
+        a[e] = bf16x2_pf2(xw[e]);
+        b[e] = bf16x2_pf2(__shfl_xor_sync(0xffffffffu, xw[e], 8));
+      }
+      uint64_t ss2 = pmul2(a[0], a[0]);
+#pragma unroll
+      for (int e = 1; e < 4; ++e) ss2 = pfma2(a[e], a[e], ss2);
+      const float2 ssp = pf2_unpack(ss2);
+      float ss = ssp.x + ssp.y;
       ss += __shfl_xor_sync(0xffffffffu, ss, 8);
       ss += __shfl_xor_sync(0xffffffffu, ss, 4);
       ss += __shfl_xor_sync(0xffffffffu, ss, 2);
       ss += __shfl_xor_sync(0xffffffffu, ss, 1);
       const float inv = 1.0f / sqrtf(ss / 128.0f + p.eps);
+      const uint64_t inv2 = pf2(inv, inv);
       uint32_t o[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        o[e] = pack_bf16x2(inv * fmaf(b[2 * e], c2[2 * e], a[2 * e] * c1[2 * e]),
-                           inv * fmaf(b[2 * e + 1], c2[2 * e + 1], a[2 * e + 1] * c1[2 * e + 1]));
+      for (int e = 0; e < 4; ++e) {
+        const float2 r = pf2_unpack(pmul2(inv2, pfma2(b[e], c2[e], pmul2(a[e], c1[e]))));
+        o[e] = pack_bf16x2(r.x, r.y);
+      }
       if (head < p.nheads)
         reinterpret_cast<uint4 *>(orow + (size_t)head * 128)[l16] = make_uint4(o[0], o[1], o[2], o[3]);
     }
