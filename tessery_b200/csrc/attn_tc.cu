@@ -823,6 +823,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
+          // Keys masked for every row of the warp (causal diagonal, ragged end) are skipped.
+          if (__all_sync(0xffffffffu, half * 64 >= valid)) break;
           uint32_t xa[32], xb[32];
           tmem_ld32(tS + half * 64, xa);
           tmem_ld32(tS + half * 64 + 32, xb);
@@ -875,6 +877,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t x[32], packed[16];
+          if (__all_sync(0xffffffffu, c * 32 >= valid)) {  // masked for every row of the warp
+#pragma unroll
+            for (int t = 0; t < 16; ++t) packed[t] = 0u;
+            tmem_st16(tS + c * 16, packed);
+            continue;
+          }
           tmem_ld32(tS + c * 32, x);
           tmem_ld_wait();
           if (valid >= kKeys) l += exp_chunk<false>(x, c, valid, p.scale_log2, m_ref, packed);
