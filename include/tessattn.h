@@ -7,7 +7,8 @@
  *
  *   - Plain C types only: opaque handles, raw pointers, sizes.  No C++ or framework
  *     types cross the boundary.
- *   - Status codes (int): TX_OK (0), TX_EINVAL (1, rejected before any GPU work),
+ *   - Status codes (int): TX_OK (0), TX_EINVAL (1, rejected before any GPU work, or by
+ *     a kernel's own argument check, reported at the next tx_sync / tx_finish),
  *     TX_ECUDA (2, CUDA runtime error), TX_ETIMEOUT (3, a bounded device-side wait gave
  *     up; the kernel returned and the context stays usable).  tx_last_error() gives a
  *     one-line, payload-free description for the calling context.
@@ -152,6 +153,10 @@ int tx_profile_read(void *ctx, double *seconds, uint32_t count);
  * cu_seqlens_host: optional host copies; when given, they are validated and used to
  * build an exact, longest-first work list; when NULL the work list covers every tile
  * and the kernels skip empty tiles by reading the device array.
+ * Short sequences (seq, or max_len for varlen, at most 32; dim 128; bf16 in; at most 4
+ * query heads per kv head) run as one kernel launch with the q/k prologue inside; a
+ * varlen sequence found longer than 32 on the device (cu_seqlens_host NULL and a wrong
+ * max_len) is reported as TX_EINVAL by tx_sync / tx_finish.
  * stream: a cudaStream_t, or NULL for the context's stream.
  * Returns TX_OK when the work has been queued; errors from inside kernels are reported
  * by tx_sync / tx_finish. */

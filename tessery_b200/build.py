@@ -17,7 +17,8 @@ from pathlib import Path
 PACKAGE = Path(__file__).resolve().parent
 CSRC = PACKAGE / "csrc"
 LIBRARY = PACKAGE / "libtessattn.so"
-SOURCES = ["runtime.cu", "simt_kernels.cu", "attn_d32.cu", "attn_tc.cu", "noalloc.cu", "pool.cu"]
+SOURCES = ["runtime.cu", "simt_kernels.cu", "attn_d32.cu", "attn_tc.cu", "attn_short.cu", "noalloc.cu",
+           "pool.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -65,6 +65,14 @@ struct PoolProblem {
 };
 cudaError_t launch_pool_project(const PoolProblem &p, cudaStream_t stream);
 
+// Short sequences (at most 32 tokens each), head_dim 128, bf16 q/k/v, up to 4 query heads
+// per kv head: one CTA per (sequence, kv head) with the q/k RMSNorm + RoPE fused (q_w,
+// k_w optional).  A sequence longer than 32 in a device cu_seqlens is reported in
+// `status` as a bad argument.
+bool short_attention_supported(const AttnProblem &p);
+cudaError_t launch_attention_short(const AttnProblem &p, const uint16_t *q_w, const uint16_t *k_w,
+                                   float eps, float theta, int *status, cudaStream_t stream);
+
 // Bandwidth-oriented fp32 kernel for head_dim 32 (BERT/BGE shapes).
 cudaError_t launch_attention_d32(const AttnProblem &p, cudaStream_t stream);
 

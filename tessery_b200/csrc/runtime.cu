@@ -131,6 +131,8 @@ int check_status(Ctx *c) {
       snprintf(msg, sizeof msg, "device wait timed out (site %d)", (st >> 8) & 0xffff);
       return fail(c, TX_ETIMEOUT, msg);
     }
+    if ((st & 0xff) == TX_EINVAL)
+      return fail(c, TX_EINVAL, "a kernel rejected its arguments on the device");
     snprintf(msg, sizeof msg, "device reported status %d", st);
     return fail(c, TX_ECUDA, msg);
   }
@@ -185,6 +187,17 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
   if ((uint64_t)p.total * p.heads * p.dim >= (1ull << 40))
     return fail(c, TX_EINVAL, "problem too large");
 
+  // Short sequences: one launch with the q/k prologue fused, no scratch or work list.
+  if (p.in_dtype == TX_BF16 && tx::short_attention_supported(p)) {
+    cudaError_t e = cudaSetDevice(c->device);
+    if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
+    if ((e = tx::launch_attention_short(p, q_w, k_w, eps, theta, c->status, stream)) !=
+        cudaSuccess)
+      return cuda_fail(c, e, "attention launch");
+    c->last_kernel = "short_d128";
+    ++c->launches;
+    return TX_OK;
+  }
   const bool tc_path = p.in_dtype == TX_BF16 && p.scale > 0.f && tx::tc_attention_supported(p);
   const bool d32_path = !tc_path && p.dim == 32 &&
                         p.batch <= 65535u && p.heads <= 65535u &&

@@ -177,12 +177,98 @@ def test_qwen_varlen_bf16_tensor_core(runtime, nseq, seed):
 
 
 def test_short_tails_both_shapes(runtime):
-    for kind, route in (("qwen", "tc_bf16_d128"), ("bge", "d32")):
+    for kind, route in (("qwen", "short_d128"), ("bge", "d32")):
         w = workloads.short_tails(kind, batch=32, seed=41)
         got = run_workload(runtime, w)
         assert runtime.last_kernel() == route
         want = qwen_oracle(w)
         assert np.max(np.abs(got - want)) <= BF16_GATE, kind
+
+
+def _short_oracle(q, k, v, lengths, causal, qw, kw, eps=1e-6, theta=1e6):
+    qf, kf, vf = (from_bf16_bits(a) for a in (q, k, v))
+    if qw is not None:
+        b, L = qf.shape[:2]
+        pos = np.broadcast_to(np.arange(L), (b, L))
+        qf, kf = oracle.qk_norm_rope(qf, kf, qw, kw, eps, theta, pos)
+    return oracle.attention_padded(qf, kf, vf, lengths, causal, 128**-0.5)
+
+
+@pytest.mark.parametrize("group", [1, 2, 4])
+def test_short_sequence_kernel_padded(runtime, group):
+    """Sequences of at most 32 tokens: the one-launch kernel with the q/k prologue inside,
+    GQA groups 1/2/4, empty / single-token / full sequences and padded query rows, causal
+    and bidirectional, with and without the prologue, fp32 and bf16 output.  A sequence
+    with no valid key gives NaN rows (0/0), as the reference's running sums do."""
+    rng = np.random.default_rng(60 + group)
+    kv, L = 2, 32
+    heads = kv * group
+    lengths = np.array([0, 1, 2, 17, 31, 32], np.uint32)
+    B = len(lengths)
+    q = to_bf16_bits(rng.normal(size=(B, L, heads, 128)).astype(np.float32))
+    k = to_bf16_bits(rng.normal(size=(B, L, kv, 128)).astype(np.float32))
+    v = to_bf16_bits(rng.normal(size=(B, L, kv, 128)).astype(np.float32))
+    qw = to_bf16_bits(1 + 0.02 * rng.normal(size=128).astype(np.float32))
+    kw = to_bf16_bits(1 + 0.02 * rng.normal(size=128).astype(np.float32))
+    for causal in (True, False):
+        for pro in (True, False):
+            extra = dict(q_norm_weight=qw, k_norm_weight=kw, eps=1e-6, theta=1e6) if pro else {}
+            want = _short_oracle(q, k, v, lengths, causal, qw if pro else None, kw)
+            for out_dtype in ("float32", "bf16"):
+                got = attention(q, k, v, lengths=lengths, causal=causal, out_dtype=out_dtype,
+                                runtime=runtime, **extra)
+                assert runtime.last_kernel() == "short_d128"
+                if out_dtype == "bf16":
+                    got = from_bf16_bits(got)
+                assert np.isnan(got[0]).all() and np.isfinite(got[1:]).all()
+                assert np.max(np.abs(got[1:] - want[1:])) <= BF16_GATE, (causal, pro, out_dtype)
+
+
+def test_short_sequence_kernel_varlen_matches_tensor_core(runtime):
+    """Packed short sequences through the short kernel and, with one sequence made longer
+    than 32, through the tensor-core kernel: the rows of the common sequences agree."""
+    w = workloads.short_tails("qwen", batch=24, seed=43)
+    got = run_workload(runtime, w)
+    assert runtime.last_kernel() == "short_d128"
+    assert np.max(np.abs(got - qwen_oracle(w))) <= BF16_GATE
+    lengths = np.diff(w.cu_seqlens).astype(np.int64)
+    long = workloads.short_tails("qwen", batch=24, seed=43)
+    extra = 40
+    cu = np.concatenate([[0], np.cumsum(np.append(lengths, extra))]).astype(np.int32)
+    rng = np.random.default_rng(7)
+    pad = lambda a: np.concatenate([a, to_bf16_bits(rng.normal(size=(extra,) + a.shape[1:])
+                                                    .astype(np.float32))])
+    long.q, long.k, long.v = pad(w.q), pad(w.k), pad(w.v)
+    long.cu_seqlens, long.seq = cu, extra
+    got_tc = run_workload(runtime, long)
+    assert runtime.last_kernel() == "tc_bf16_d128"
+    assert np.max(np.abs(got_tc[: got.shape[0]] - got)) <= BF16_GATE
+
+
+def test_short_sequence_kernel_rejects_long_sequence_on_device(runtime):
+    """max_len claims 32 but the device offsets hold a 40-token sequence and no host copy
+    was given: the kernel's own check reports an invalid argument at the next sync (the
+    over-long sequence is not touched), and the context stays usable."""
+    rng = np.random.default_rng(9)
+    total, heads, kv = 50, 4, 2
+    cu = np.array([0, 10, 50], np.int32)
+    arrays = {n: to_bf16_bits(rng.normal(size=(total, h, 128)).astype(np.float32))
+              for n, h in (("q", heads), ("k", kv), ("v", kv))}
+    bufs = {n: runtime.buffer(a.nbytes, np.ascontiguousarray(a)) for n, a in arrays.items()}
+    cub = runtime.buffer(cu.nbytes, cu)
+    out = runtime.buffer(total * heads * 128 * 4)
+    try:
+        runtime.attention_varlen_device(bufs["q"].device_ptr, bufs["k"].device_ptr,
+                                        bufs["v"].device_ptr, cub.device_ptr, out.device_ptr,
+                                        nseq=2, total=total, max_len=32, heads=heads, kv_heads=kv,
+                                        dim=128, in_dtype=TX_BF16, out_dtype=TX_F32, causal=True)
+        assert runtime.last_kernel() == "short_d128"
+        with pytest.raises(InvalidInputError):
+            runtime.sync()
+        runtime.sync()  # cleared: the next call starts clean
+    finally:
+        for b in [*bufs.values(), cub, out]:
+            b.close()
 
 
 @pytest.mark.parametrize("out_dtype", ["float32", "bf16"])
