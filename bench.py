@@ -598,7 +598,7 @@ def rooflines(w, name: str, kernel: str, att_s: float, pro_s: float | None):
            "algorithmic_bytes_per_launch": att_bytes}
     kname = {"tc_bf16_d128": "attn_tc_kernel", "d32": "attention_d32_kernel",
              "simt": "attention_simt_kernel", "short_d128": "attn_short_kernel"}.get(kernel, kernel)
-    if kernel == "tc_bf16_d128":
+    if kernel in ("tc_bf16_d128", "short_d128"):  # bf16 tensor-core contractions
         t_c = flops / (peaks["bf16_tflops"] * 1e12)
         comp = {"achieved": flops / att_s / 1e12, "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": flops / att_s / 1e12 / peaks["bf16_tflops"],
