@@ -174,6 +174,28 @@ int tx_attention_varlen(void *ctx, const void *q, const void *k, const void *v,
                         int out_dtype, int causal, float scale, const uint16_t *q_norm_w,
                         const uint16_t *k_norm_w, float eps, float theta, void *stream);
 
+/* Host-buffer forms of the two entry points above: q, k, v, out, lengths / cu_seqlens and
+ * the norm weights are HOST pointers (page-locked memory, e.g. from tx_host_alloc, lets the
+ * copies overlap; pageable memory works too).  They stand in for the reference's
+ * host-side sequence around one attention dispatch -- Buffer uploads (metal.py:94-119),
+ * the dispatch (metal.py:532-569) and the read-back (metal.py:650-662) -- in one call.
+ * The sequences are split into chunks of whole sequences; chunk i's rows are copied in
+ * while chunk i-1 is computed and chunk i-2 copied out, so transfer in both directions
+ * overlaps and the kernels hide behind it.  Results equal the device-pointer entry points'
+ * bit for bit.  Returns when the output is in `out` (kernel errors included); device
+ * memory for the copies is kept by the context and grows to the largest call. */
+int tx_attention_padded_host(void *ctx, const void *q, const void *k, const void *v,
+                             const uint32_t *lengths, void *out, uint32_t batch, uint32_t seq,
+                             uint32_t heads, uint32_t kv_heads, uint32_t dim, int in_dtype,
+                             int out_dtype, int causal, float scale, const uint16_t *q_norm_w,
+                             const uint16_t *k_norm_w, float eps, float theta);
+
+int tx_attention_varlen_host(void *ctx, const void *q, const void *k, const void *v,
+                             const int32_t *cu_seqlens, uint32_t nseq, uint32_t total, void *out,
+                             uint32_t heads, uint32_t kv_heads, uint32_t dim, int in_dtype,
+                             int out_dtype, int causal, float scale, const uint16_t *q_norm_w,
+                             const uint16_t *k_norm_w, float eps, float theta);
+
 /* Standalone fused q/k prologue (qwen3.py:216-237 as one pass): RMSNorm with bf16
  * weights then split-half RoPE, reading q/k in `in_dtype` and writing bf16 or f32
  * (`out_dtype`) to q_out/k_out (which may alias q/k when the types match).  q (with

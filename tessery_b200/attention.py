@@ -4,7 +4,8 @@ qwen3.py:216-237 optionally fused in front).
 
 Inputs are float32 arrays, or uint16 arrays holding bf16 bit patterns (the convention
 the reference uses for bf16 data, kernels.metal:10).  Device memory is reused across
-calls through the runtime's named workspace buffers; results are copied back to host.
+calls (the runtime's named workspace buffers, and for attention the context's own copy
+buffers); results are copied back to host.
 """
 
 from __future__ import annotations
@@ -83,28 +84,26 @@ def attention(
         raise InvalidInputError()
     qw = kw = None
     if q_norm_weight is not None:
-        qw = _upload(rt, "q_norm_weight", np.asarray(q_norm_weight, dtype=np.uint16))
+        qw = np.ascontiguousarray(q_norm_weight, dtype=np.uint16)
+        if qw.shape != (q.shape[-1],):
+            raise InvalidInputError()
     if k_norm_weight is not None:
-        kw = _upload(rt, "k_norm_weight", np.asarray(k_norm_weight, dtype=np.uint16))
+        kw = np.ascontiguousarray(k_norm_weight, dtype=np.uint16)
+        if kw.shape != (q.shape[-1],):
+            raise InvalidInputError()
     out_np_dtype = np.float32 if out_code == native.TX_F32 else np.uint16
     if (lengths is None) == (cu_seqlens is None):
         raise InvalidInputError()
+    sel: dict = {}
     if lengths is not None:
         if q.ndim != 4 or k.ndim != 4 or k.shape != v.shape:
             raise InvalidInputError()
         batch, seq, heads, dim = q.shape
         if k.shape[:2] != (batch, seq) or k.shape[3] != dim:
             raise InvalidInputError()
-        lens = np.ascontiguousarray(lengths, dtype=np.uint32)
-        if lens.shape != (batch,):
+        sel["lengths"] = np.ascontiguousarray(lengths, dtype=np.uint32)
+        if sel["lengths"].shape != (batch,):
             raise InvalidInputError()
-        ptrs = [_upload(rt, n, a) for n, a in (("q", q), ("k", k), ("v", v), ("lengths", lens))]
-        dev_out = rt.workspace("out", q.size * np.dtype(out_np_dtype).itemsize)
-        rt.attention_padded_device(
-            *ptrs, dev_out.device_ptr, batch=batch, seq=seq, heads=heads, kv_heads=k.shape[2],
-            dim=dim, in_dtype=code, out_dtype=out_code, causal=causal, scale=scale,
-            lengths_host=lens, q_norm_weight=qw, k_norm_weight=kw, eps=eps, theta=theta,
-        )
     else:
         if q.ndim != 3 or k.ndim != 3 or k.shape != v.shape:
             raise InvalidInputError()
@@ -112,24 +111,18 @@ def attention(
         cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
         if cu.ndim != 1 or cu.size < 2 or k.shape[0] != total or k.shape[2] != dim:
             raise InvalidInputError()
-        nseq = cu.size - 1
-        max_len = int(np.max(np.diff(cu))) if nseq else 0
-        if max_len <= 0:
+        if int(np.max(np.diff(cu))) <= 0:
             raise InvalidInputError()
-        ptrs = [_upload(rt, n, a) for n, a in (("q", q), ("k", k), ("v", v), ("cu", cu))]
-        dev_out = rt.workspace("out", q.size * np.dtype(out_np_dtype).itemsize)
-        rt.attention_varlen_device(
-            *ptrs, dev_out.device_ptr, nseq=nseq, total=total, max_len=max_len, heads=heads,
-            kv_heads=k.shape[1], dim=dim, in_dtype=code, out_dtype=out_code, causal=causal,
-            scale=scale, cu_seqlens_host=cu, q_norm_weight=qw, k_norm_weight=kw, eps=eps,
-            theta=theta,
-        )
-    rt.sync()
+        sel["cu_seqlens"] = cu
     if out is None:
         out = np.empty(q.shape, dtype=out_np_dtype)
     elif out.shape != q.shape or out.dtype != out_np_dtype or not out.flags.c_contiguous:
         raise InvalidInputError()
-    _raise_for(rt._lib.tx_read(dev_out.pointer, out.ctypes.data, out.nbytes))
+    # Host arrays straight into the host-buffer entry point: the library moves the
+    # sequences through in chunks whose copies in, kernels and copies out overlap.
+    rt.attention_host(q, k, v, out, in_dtype=code, out_dtype=out_code, causal=causal,
+                      scale=scale, q_norm_weight=qw, k_norm_weight=kw, eps=eps, theta=theta,
+                      **sel)
     return out
 
 

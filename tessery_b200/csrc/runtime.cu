@@ -22,6 +22,8 @@
 namespace {
 
 constexpr uint32_t kAbiVersion = 3;
+constexpr uint32_t kHostChunks = 8;              // most chunks of a host-buffer call
+constexpr size_t kHostChunkBytes = 16u << 20;     // bytes moved per chunk, at least
 
 struct Ctx;
 
@@ -60,6 +62,13 @@ struct Ctx {
   std::set<Buf *> buffers;
   const char *last_kernel = "";
   uint64_t launches = 0;  // kernels this context has launched
+  // host-buffer entry points: device copies of the caller's arrays, a copy-in and a
+  // copy-out stream beside `stream`, and an event pair per chunk
+  void *hp_mem = nullptr;
+  size_t hp_bytes = 0;
+  cudaStream_t hp_up = nullptr, hp_down = nullptr;
+  cudaEvent_t hp_ev[2 * kHostChunks] = {};
+  std::vector<int32_t> hp_cu;  // per-chunk cu_seqlens, rebased to each chunk's first row
 };
 
 std::mutex g_create_mu;
@@ -290,6 +299,165 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
   return TX_OK;
 }
 
+// Host-buffer attention: q/k/v/out (and lengths or cu_seqlens) in host memory.  The
+// sequences are split into up to kHostChunks chunks of whole sequences; chunk i's rows are
+// copied in on one stream, its kernels run on the context's stream once they have
+// landed, and its output rows are copied out on a third stream, so copies in, kernels and
+// copies out of different chunks overlap (with page-locked host memory the two copy
+// directions run at once).  Returns after the last output row is in host memory.
+int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const int32_t *cu,
+                       const uint16_t *q_w, const uint16_t *k_w, float eps, float theta) {
+  if (!p.q || !p.k || !p.v || !p.out) return fail(c, TX_EINVAL, "null tensor pointer");
+  if (!lengths && !cu) return fail(c, TX_EINVAL, "lengths or cu_seqlens required");
+  if (p.in_dtype != TX_F32 && p.in_dtype != TX_BF16) return fail(c, TX_EINVAL, "bad in_dtype");
+  if (p.out_dtype != TX_F32 && p.out_dtype != TX_BF16) return fail(c, TX_EINVAL, "bad out_dtype");
+  if (!p.heads || !p.kv_heads || !p.dim || p.dim > 256 || !p.batch)
+    return fail(c, TX_EINVAL, "bad shape");
+  const uint32_t nseq = p.batch;
+  if (cu) {
+    if (cu[0] != 0) return fail(c, TX_EINVAL, "cu_seqlens[0] must be 0");
+    for (uint32_t s = 0; s < nseq; ++s)
+      if (cu[s + 1] < cu[s]) return fail(c, TX_EINVAL, "cu_seqlens must not decrease");
+    if ((uint32_t)cu[nseq] != p.total) return fail(c, TX_EINVAL, "cu_seqlens[nseq] != total");
+  } else {
+    if (!p.seq) return fail(c, TX_EINVAL, "batch and seq must be positive");
+    if ((uint64_t)nseq * p.seq > 0xffffffffull) return fail(c, TX_EINVAL, "too many tokens");
+    p.total = nseq * p.seq;
+  }
+  const size_t ein = p.in_dtype == TX_BF16 ? 2 : 4, eout = p.out_dtype == TX_BF16 ? 2 : 4;
+  const size_t qrow = (size_t)p.heads * p.dim * ein, kvrow = (size_t)p.kv_heads * p.dim * ein;
+  const size_t orow = (size_t)p.heads * p.dim * eout, rows = p.total;
+  if (!rows) return TX_OK;
+  // Chunks: first[i] = first sequence of chunk i, balanced by rows.
+  const size_t moved = rows * (qrow + 2 * kvrow + orow);
+  uint32_t nch = (uint32_t)std::min<size_t>({(moved + kHostChunkBytes - 1) / kHostChunkBytes,
+                                             (size_t)kHostChunks, (size_t)nseq});
+  nch = std::max(nch, 1u);
+  auto row_of = [&](uint32_t s) -> size_t { return cu ? (size_t)cu[s] : (size_t)s * p.seq; };
+  uint32_t first[kHostChunks + 1];
+  first[0] = 0;
+  uint32_t used = 1;
+  for (uint32_t i = 1; i < nch; ++i) {
+    const size_t target = rows * i / nch;
+    uint32_t s = first[used - 1] + 1;
+    while (s < nseq && row_of(s) < target) ++s;
+    if (s >= nseq) break;
+    first[used++] = s;
+  }
+  first[used] = nseq;
+  nch = used;
+  // Device memory: q, k, v, out, then lengths or the rebased cu_seqlens, then the weights.
+  auto up256 = [](size_t b) { return (b + 255) & ~(size_t)255; };
+  const size_t oq = 0, ok = oq + up256(rows * qrow), ov = ok + up256(rows * kvrow);
+  const size_t oo = ov + up256(rows * kvrow), om = oo + up256(rows * orow);
+  const size_t meta = cu ? (size_t)(nseq + nch) * 4 : (size_t)nseq * 4;
+  const size_t ow = om + up256(meta), need = ow + 2 * up256((size_t)p.dim * 2);
+  cudaError_t e = cudaSetDevice(c->device);
+  if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
+  if (c->hp_bytes < need) {
+    if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(c, e, "synchronize");
+    if (c->hp_mem) cudaFree(c->hp_mem);
+    c->hp_mem = nullptr;
+    c->hp_bytes = 0;
+    if ((e = cudaMalloc(&c->hp_mem, need)) != cudaSuccess) return cuda_fail(c, e, "host-path buffers");
+    c->hp_bytes = need;
+  }
+  if (!c->hp_up) {
+    if ((e = cudaStreamCreateWithFlags(&c->hp_up, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaStreamCreateWithFlags(&c->hp_down, cudaStreamNonBlocking)) != cudaSuccess)
+      return cuda_fail(c, e, "copy streams");
+    for (cudaEvent_t &ev : c->hp_ev)
+      if ((e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess)
+        return cuda_fail(c, e, "copy events");
+  }
+  uint8_t *dev = (uint8_t *)c->hp_mem;
+  const uint8_t *hq = (const uint8_t *)p.q, *hk = (const uint8_t *)p.k, *hv = (const uint8_t *)p.v;
+  uint8_t *ho = (uint8_t *)p.out;
+  // Drains every stream of this call (no copy may touch the caller's memory after return).
+  auto drain = [&]() {
+    cudaStreamSynchronize(c->hp_up);
+    cudaStreamSynchronize(c->stream);
+    cudaStreamSynchronize(c->hp_down);
+  };
+  // Nothing of an earlier call may still read these buffers.
+  if ((e = cudaStreamWaitEvent(c->hp_up, c->scratch_done, 0)) != cudaSuccess)
+    return cuda_fail(c, e, "stream wait");
+  if (cu) {
+    c->hp_cu.resize(nseq + nch);
+    for (uint32_t i = 0; i < nch; ++i)
+      for (uint32_t s = first[i]; s <= first[i + 1]; ++s)
+        c->hp_cu[first[i] + i + (s - first[i])] = cu[s] - cu[first[i]];
+    e = cudaMemcpyAsync(dev + om, c->hp_cu.data(), meta, cudaMemcpyHostToDevice, c->hp_up);
+  } else {
+    e = cudaMemcpyAsync(dev + om, lengths, meta, cudaMemcpyHostToDevice, c->hp_up);
+  }
+  if (e == cudaSuccess && q_w)
+    e = cudaMemcpyAsync(dev + ow, q_w, (size_t)p.dim * 2, cudaMemcpyHostToDevice, c->hp_up);
+  if (e == cudaSuccess && k_w)
+    e = cudaMemcpyAsync(dev + ow + up256((size_t)p.dim * 2), k_w, (size_t)p.dim * 2,
+                        cudaMemcpyHostToDevice, c->hp_up);
+  if (e != cudaSuccess) {
+    drain();
+    return cuda_fail(c, e, "copy in");
+  }
+  const uint16_t *dqw = q_w ? (const uint16_t *)(dev + ow) : nullptr;
+  const uint16_t *dkw = k_w ? (const uint16_t *)(dev + ow + up256((size_t)p.dim * 2)) : nullptr;
+  for (uint32_t i = 0; i < nch; ++i) {
+    const size_t r0 = row_of(first[i]), r1 = row_of(first[i + 1]), n = r1 - r0;
+    if ((e = cudaMemcpyAsync(dev + oq + r0 * qrow, hq + r0 * qrow, n * qrow,
+                             cudaMemcpyHostToDevice, c->hp_up)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(dev + ok + r0 * kvrow, hk + r0 * kvrow, n * kvrow,
+                             cudaMemcpyHostToDevice, c->hp_up)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(dev + ov + r0 * kvrow, hv + r0 * kvrow, n * kvrow,
+                             cudaMemcpyHostToDevice, c->hp_up)) != cudaSuccess ||
+        (e = cudaEventRecord(c->hp_ev[2 * i], c->hp_up)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(c->stream, c->hp_ev[2 * i], 0)) != cudaSuccess) {
+      drain();
+      return cuda_fail(c, e, "copy in");
+    }
+    tx::AttnProblem pc = p;
+    pc.q = dev + oq + r0 * qrow;
+    pc.k = dev + ok + r0 * kvrow;
+    pc.v = dev + ov + r0 * kvrow;
+    pc.out = dev + oo + r0 * orow;
+    pc.batch = first[i + 1] - first[i];
+    const int32_t *cu_chunk = nullptr;
+    if (cu) {
+      cu_chunk = c->hp_cu.data() + first[i] + i;
+      pc.cu_seqlens = (const int32_t *)(dev + om) + first[i] + i;
+      pc.lengths = nullptr;
+      pc.total = (uint32_t)n;
+      uint32_t mx = 0;
+      for (uint32_t s = 0; s < pc.batch; ++s) mx = std::max<uint32_t>(mx, cu_chunk[s + 1] - cu_chunk[s]);
+      pc.seq = std::max(mx, 1u);
+    } else {
+      pc.lengths = (const uint32_t *)(dev + om) + first[i];
+      pc.cu_seqlens = nullptr;
+    }
+    const int rc = run_attention(c, pc, cu ? nullptr : lengths + first[i], cu_chunk, dqw, dkw,
+                                 eps, theta, c->stream);
+    if (rc != TX_OK) {
+      drain();
+      return rc;
+    }
+    if ((e = cudaEventRecord(c->hp_ev[2 * i + 1], c->stream)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(c->hp_down, c->hp_ev[2 * i + 1], 0)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(ho + r0 * orow, dev + oo + r0 * orow, n * orow,
+                             cudaMemcpyDeviceToHost, c->hp_down)) != cudaSuccess) {
+      drain();
+      return cuda_fail(c, e, "copy out");
+    }
+  }
+  // The next call's copies in wait for this one's kernels and copies out.
+  if ((e = cudaEventRecord(c->scratch_done, c->hp_down)) != cudaSuccess) {
+    drain();
+    return cuda_fail(c, e, "event");
+  }
+  drain();
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(c, e, "host-buffer attention");
+  return check_status(c);
+}
+
 // Profiling hooks around one dispatch of an open command.
 void prof_begin(Ctx *c) {
   if (!c->profile) return;
@@ -375,6 +543,11 @@ void tx_destroy(void *ctx) {
     if (c->ev_begin) cudaEventDestroy(c->ev_begin);
     if (c->ev_end) cudaEventDestroy(c->ev_end);
     if (c->scratch_done) cudaEventDestroy(c->scratch_done);
+    if (c->hp_mem) cudaFree(c->hp_mem);
+    for (cudaEvent_t ev : c->hp_ev)
+      if (ev) cudaEventDestroy(ev);
+    if (c->hp_up) cudaStreamDestroy(c->hp_up);
+    if (c->hp_down) cudaStreamDestroy(c->hp_down);
     if (c->stream) cudaStreamDestroy(c->stream);
   }
   delete c;
@@ -709,6 +882,42 @@ int tx_attention_varlen(void *ctx, const void *q, const void *k, const void *v,
   p.scale = scale;
   return run_attention(c, p, nullptr, cu_seqlens_host, q_norm_w, k_norm_w, eps, theta,
                        stream ? (cudaStream_t)stream : c->stream);
+}
+
+int tx_attention_padded_host(void *ctx, const void *q, const void *k, const void *v,
+                             const uint32_t *lengths, void *out, uint32_t batch, uint32_t seq,
+                             uint32_t heads, uint32_t kv_heads, uint32_t dim, int in_dtype,
+                             int out_dtype, int causal, float scale, const uint16_t *q_norm_w,
+                             const uint16_t *k_norm_w, float eps, float theta) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (c->open) return fail(c, TX_EINVAL, "a command is open");
+  tx::AttnProblem p{};
+  p.q = q; p.k = k; p.v = v; p.out = out;
+  p.batch = batch; p.seq = seq; p.heads = heads; p.kv_heads = kv_heads; p.dim = dim;
+  p.in_dtype = in_dtype; p.out_dtype = out_dtype; p.causal = causal ? 1 : 0; p.scale = scale;
+  if (!lengths) return fail(c, TX_EINVAL, "lengths required");
+  for (uint32_t b = 0; b < batch; ++b)
+    if (lengths[b] > seq) return fail(c, TX_EINVAL, "length exceeds seq");
+  return run_attention_host(c, p, lengths, nullptr, q_norm_w, k_norm_w, eps, theta);
+}
+
+int tx_attention_varlen_host(void *ctx, const void *q, const void *k, const void *v,
+                             const int32_t *cu_seqlens, uint32_t nseq, uint32_t total, void *out,
+                             uint32_t heads, uint32_t kv_heads, uint32_t dim, int in_dtype,
+                             int out_dtype, int causal, float scale, const uint16_t *q_norm_w,
+                             const uint16_t *k_norm_w, float eps, float theta) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (c->open) return fail(c, TX_EINVAL, "a command is open");
+  if (!cu_seqlens) return fail(c, TX_EINVAL, "cu_seqlens required");
+  tx::AttnProblem p{};
+  p.q = q; p.k = k; p.v = v; p.out = out;
+  p.batch = nseq; p.total = total; p.heads = heads; p.kv_heads = kv_heads; p.dim = dim;
+  p.in_dtype = in_dtype; p.out_dtype = out_dtype; p.causal = causal ? 1 : 0; p.scale = scale;
+  return run_attention_host(c, p, nullptr, cu_seqlens, q_norm_w, k_norm_w, eps, theta);
 }
 
 int tx_qk_norm_rope(void *ctx, const void *q, const void *k, void *q_out, void *k_out,

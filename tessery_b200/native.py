@@ -57,6 +57,16 @@ SIGNATURES: dict[str, tuple[list[Any], Any]] = {
          _i32, _f32, _vp, _vp, _f32, _f32, _vp],
         _i32,
     ),
+    "tx_attention_padded_host": (
+        [_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _i32, _i32, _i32, _f32,
+         _vp, _vp, _f32, _f32],
+        _i32,
+    ),
+    "tx_attention_varlen_host": (
+        [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _vp, _u32, _u32, _u32, _i32, _i32, _i32, _f32,
+         _vp, _vp, _f32, _f32],
+        _i32,
+    ),
     "tx_qk_norm_rope": (
         [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _vp, _u32, _vp, _u32, _u32, _u32, _i32, _i32, _vp,
          _vp, _f32, _f32, _vp],

@@ -317,6 +317,54 @@ class CudaRuntime:
                  "threads": threads}
             )
 
+    # ---- typed entry points (host arrays) ------------------------------------------------
+    def attention_host(
+        self,
+        q: NDArray[Any],
+        k: NDArray[Any],
+        v: NDArray[Any],
+        out: NDArray[Any],
+        *,
+        lengths: NDArray[np.uint32] | None = None,
+        cu_seqlens: NDArray[np.int32] | None = None,
+        in_dtype: int,
+        out_dtype: int,
+        causal: bool = True,
+        scale: float | None = None,
+        q_norm_weight: NDArray[np.uint16] | None = None,
+        k_norm_weight: NDArray[np.uint16] | None = None,
+        eps: float = 1e-6,
+        theta: float = 1e6,
+    ) -> None:
+        """Attention from host arrays into the host array `out` (tx_attention_*_host): the
+        sequences go through in chunks whose copies in, kernels and copies out overlap.
+        Arrays must be C-contiguous; padded q [B, L, H, d] with lengths [B] (uint32), or
+        packed q [T, H, d] with cu_seqlens [nseq+1] (int32)."""
+        self._check_open()
+        arrays = [q, k, v, out] + [a for a in (lengths, cu_seqlens, q_norm_weight, k_norm_weight)
+                                   if a is not None]
+        if any(not a.flags.c_contiguous for a in arrays):
+            raise InvalidInputError()
+        qw = None if q_norm_weight is None else q_norm_weight.ctypes.data
+        kw = None if k_norm_weight is None else k_norm_weight.ctypes.data
+        dim = q.shape[-1]
+        sc = dim**-0.5 if scale is None else scale
+        if lengths is not None:
+            batch, seq, heads = q.shape[:3]
+            rc = self._lib.tx_attention_padded_host(
+                self._pointer, q.ctypes.data, k.ctypes.data, v.ctypes.data, lengths.ctypes.data,
+                out.ctypes.data, batch, seq, heads, k.shape[2], dim, in_dtype, out_dtype,
+                int(bool(causal)), sc, qw, kw, eps, theta,
+            )
+        else:
+            total, heads = q.shape[:2]
+            rc = self._lib.tx_attention_varlen_host(
+                self._pointer, q.ctypes.data, k.ctypes.data, v.ctypes.data, cu_seqlens.ctypes.data,
+                cu_seqlens.size - 1, total, out.ctypes.data, heads, k.shape[1], dim, in_dtype,
+                out_dtype, int(bool(causal)), sc, qw, kw, eps, theta,
+            )
+        _raise_for(rc)
+
     # ---- typed entry points (device pointers) -------------------------------------------
     def attention_padded_device(
         self,

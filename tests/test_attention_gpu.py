@@ -408,6 +408,64 @@ def test_typed_dtype_codes():
     assert (TX_F32, TX_BF16) == (0, 1)
 
 
+def _device_path(rt, w):
+    """The same workload through the device-pointer entry point, one call, one launch set."""
+    arrays = {n: np.ascontiguousarray(a) for n, a in (("q", w.q), ("k", w.k), ("v", w.v),
+                                                        ("qw", w.q_norm_weight),
+                                                        ("kw", w.k_norm_weight))}
+    if w.layout == "padded":
+        arrays["sel"] = w.lengths.astype(np.uint32)
+    else:
+        arrays["sel"] = w.cu_seqlens.astype(np.int32)
+    bufs = {n: rt.buffer(a.nbytes, a) for n, a in arrays.items()}
+    out = rt.buffer(w.q.size * 4)
+    try:
+        D = w.dim
+        kw = dict(in_dtype=TX_BF16, out_dtype=TX_F32, causal=w.causal,
+                  q_norm_weight=bufs["qw"].device_ptr, k_norm_weight=bufs["kw"].device_ptr)
+        if w.layout == "padded":
+            B, L, H = w.q.shape[:3]
+            rt.attention_padded_device(bufs["q"].device_ptr, bufs["k"].device_ptr,
+                                       bufs["v"].device_ptr, bufs["sel"].device_ptr,
+                                       out.device_ptr, batch=B, seq=L, heads=H,
+                                       kv_heads=w.kv_heads, dim=D, lengths_host=arrays["sel"], **kw)
+        else:
+            T, H = w.q.shape[:2]
+            cu = arrays["sel"]
+            rt.attention_varlen_device(bufs["q"].device_ptr, bufs["k"].device_ptr,
+                                       bufs["v"].device_ptr, bufs["sel"].device_ptr,
+                                       out.device_ptr, nseq=cu.size - 1, total=T,
+                                       max_len=int(np.max(np.diff(cu))), heads=H,
+                                       kv_heads=w.kv_heads, dim=D, cu_seqlens_host=cu, **kw)
+        rt.sync()
+        return rt.read(out, w.q.shape)
+    finally:
+        for b in [*bufs.values(), out]:
+            b.close()
+
+
+def test_host_buffer_entry_points_match_device_path(runtime):
+    """The NumPy call goes through the host-buffer entry points, which split the sequences
+    into chunks (8 here: 134 MB / 100 MB moved) and overlap copies with kernels; every row
+    equals the single device-pointer call bit for bit, padded and packed, and with
+    page-locked arrays as with pageable ones."""
+    from tessery_b200.host import pinned_copy, pinned_empty
+
+    padded = workloads.qwen_padded(batch=16, seq=512, seed=27)
+    packed = workloads.qwen_varlen(seed=28, lengths=workloads.varlen_lengths(64, 28))
+    for w in (padded, packed):
+        want = _device_path(runtime, w)
+        got = run_workload(runtime, w)
+        assert np.array_equal(got, want), w.layout
+        sel = ({"lengths": pinned_copy(w.lengths.astype(np.uint32))} if w.layout == "padded"
+               else {"cu_seqlens": pinned_copy(w.cu_seqlens.astype(np.int32))})
+        hout = pinned_empty(w.q.shape, np.float32)
+        attention(pinned_copy(w.q), pinned_copy(w.k), pinned_copy(w.v), causal=w.causal,
+                  scale=w.scale, q_norm_weight=w.q_norm_weight, k_norm_weight=w.k_norm_weight,
+                  eps=w.eps, theta=w.theta, runtime=runtime, out=hout, **sel)
+        assert np.array_equal(hout, want), w.layout
+
+
 def test_composed_prologue_matches_one_call(runtime):
     """k-only prologue over the valid rows (tx_qk_norm_rope with device lengths), then
     attention with only the q weight, equals the one-call path bit for bit."""
