@@ -49,14 +49,6 @@ __host__ __device__ constexpr uint32_t smem_bytes(uint32_t g) {
   return (g * kMaxRows * kRS + 2 * kMaxRows * kRS) * 2 + (1 + g) * kMaxRows * 256;
 }
 
-// sin and cos of a float angle: Cody-Waite reduction by 2*pi to [-pi, pi], then the
-// hardware approximations (the same evaluation as the tensor-core path's prologue).
-__device__ __forceinline__ void sincos_reduced(float angle, float *s, float *c) {
-  const float k = rintf(angle * 0.159154943091895336f);
-  float r = fmaf(k, -6.28318548202514648f, angle);
-  r = fmaf(k, 1.74845553e-07f, r);
-  __sincosf(r, s, c);
-}
 
 // D = A B + D for one m16n8k16 tile (bf16 A and B, fp32 accumulators).
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,

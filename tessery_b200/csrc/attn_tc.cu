@@ -449,15 +449,6 @@ __device__ __forceinline__ uint64_t bf16x2_f2(uint32_t w) {
   return f2_bits(w << 16, w & 0xffff0000u);
 }
 
-// sin and cos of a float angle: Cody-Waite reduction by 2*pi (2*pi split into a float
-// head and a float tail) to [-pi, pi], then the hardware approximations, which are
-// accurate to about 2^-21 absolute on that interval.
-__device__ __forceinline__ void sincos_reduced(float angle, float *s, float *c) {
-  const float k = rintf(angle * 0.159154943091895336f);
-  float r = fmaf(k, -6.28318548202514648f, angle);
-  r = fmaf(k, 1.74845553e-07f, r);
-  __sincosf(r, s, c);
-}
 
 __device__ __forceinline__ uint32_t u4_at(const uint4 &v, int e) {
   return e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w;

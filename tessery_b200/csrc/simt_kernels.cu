@@ -327,12 +327,6 @@ __device__ __forceinline__ uint64_t pmul2(uint64_t a, uint64_t b) {
 // The two bf16 of a word as a float pair (lo first).
 __device__ __forceinline__ uint64_t bf16x2_pf2(uint32_t w) { return pf2_bits(w << 16, w & 0xffff0000u); }
 
-__device__ __forceinline__ void sincos_2pi_reduced(float angle, float *s, float *c) {
-  const float k = rintf(angle * 0.159154943091895336f);
-  float r = fmaf(k, -6.28318548202514648f, angle);
-  r = fmaf(k, 1.74845553e-07f, r);
-  __sincosf(r, s, c);
-}
 
 template <int NP>  // row pairs per token: ceil(nheads / 2)
 __global__ void __launch_bounds__(128) norm_rope_rows_bf16_kernel(RowPass p) {
@@ -436,8 +430,8 @@ __global__ void __launch_bounds__(128) norm_rope_rows_bf16_kernel(RowPass p) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       float sn0, cs0, sn1, cs1;
-      sincos_2pi_reduced(fpos * invf[2 * e], &sn0, &cs0);
-      sincos_2pi_reduced(fpos * invf[2 * e + 1], &sn1, &cs1);
+      sincos_reduced(fpos * invf[2 * e], &sn0, &cs0);
+      sincos_reduced(fpos * invf[2 * e + 1], &sn1, &cs1);
       c1[e] = pf2(wof[2 * e] * cs0, wof[2 * e + 1] * cs1);
       c2[e] = first ? pf2(-(wpf[2 * e] * sn0), -(wpf[2 * e + 1] * sn1))
                     : pf2(wpf[2 * e] * sn0, wpf[2 * e + 1] * sn1);
