@@ -536,7 +536,12 @@ def run_ours(args):
         dist.all_reduce(e2e_stats, op=dist.ReduceOp.MAX)
     e2e_tokens_all = tokens_all / args.steps * args.e2e_steps
     e2e_value = e2e_tokens_all / float(e2e_stats[0])
-    h2d = hq.nbytes + hk.nbytes + hv.nbytes + sum(
+    # Bytes that cross the link: in the padded layout the library copies only the valid
+    # k and v rows (the padded ones, never attended, are zeroed on the device).
+    kv_bytes = hk.nbytes + hv.nbytes
+    if w.layout == "padded":
+        kv_bytes = 2 * w.valid_tokens() * w.kv_heads * w.dim * hk.itemsize
+    h2d = hq.nbytes + kv_bytes + sum(
         a.nbytes for a in [*hsel.values(), *[x for x in hpro.values()
                                              if isinstance(x, np.ndarray)]])
     d2h = result.nbytes

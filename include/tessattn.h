@@ -181,8 +181,9 @@ int tx_attention_varlen(void *ctx, const void *q, const void *k, const void *v,
  * the dispatch (metal.py:532-569) and the read-back (metal.py:650-662) -- in one call.
  * The sequences are split into chunks of whole sequences; chunk i's rows are copied in
  * while chunk i-1 is computed and chunk i-2 copied out, so transfer in both directions
- * overlaps and the kernels hide behind it.  Results equal the device-pointer entry points'
- * bit for bit.  Returns when the output is in `out` (kernel errors included); device
+ * overlaps and the kernels hide behind it.  In the padded layout only the valid k and v
+ * rows are copied (the rest, never attended, are zeroed on the device).  Results equal the
+ * device-pointer entry points' bit for bit.  Returns when the output is in `out` (kernel errors included); device
  * memory for the copies is kept by the context and grows to the largest call. */
 int tx_attention_padded_host(void *ctx, const void *q, const void *k, const void *v,
                              const uint32_t *lengths, void *out, uint32_t batch, uint32_t seq,

@@ -404,12 +404,28 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
   const uint16_t *dkw = k_w ? (const uint16_t *)(dev + ow + up256((size_t)p.dim * 2)) : nullptr;
   for (uint32_t i = 0; i < nch; ++i) {
     const size_t r0 = row_of(first[i]), r1 = row_of(first[i + 1]), n = r1 - r0;
+    // k and v rows of the chunk.  Padded layout: only each sequence's valid rows cross the
+    // link; its rows at or past the length are never attended (their keys are masked) and
+    // are zeroed on the device instead, so the masked products stay exact zeros.
+    auto copy_kv = [&](size_t region, const uint8_t *h) -> cudaError_t {
+      if (cu)
+        return cudaMemcpyAsync(dev + region + r0 * kvrow, h + r0 * kvrow, n * kvrow,
+                               cudaMemcpyHostToDevice, c->hp_up);
+      cudaError_t err = cudaSuccess;
+      for (uint32_t b = first[i]; b < first[i + 1] && err == cudaSuccess; ++b) {
+        const size_t s0 = (size_t)b * p.seq, nv = lengths[b];
+        if (nv)
+          err = cudaMemcpyAsync(dev + region + s0 * kvrow, h + s0 * kvrow, nv * kvrow,
+                                cudaMemcpyHostToDevice, c->hp_up);
+        if (err == cudaSuccess && nv < p.seq)
+          err = cudaMemsetAsync(dev + region + (s0 + nv) * kvrow, 0, (p.seq - nv) * kvrow,
+                                c->hp_up);
+      }
+      return err;
+    };
     if ((e = cudaMemcpyAsync(dev + oq + r0 * qrow, hq + r0 * qrow, n * qrow,
                              cudaMemcpyHostToDevice, c->hp_up)) != cudaSuccess ||
-        (e = cudaMemcpyAsync(dev + ok + r0 * kvrow, hk + r0 * kvrow, n * kvrow,
-                             cudaMemcpyHostToDevice, c->hp_up)) != cudaSuccess ||
-        (e = cudaMemcpyAsync(dev + ov + r0 * kvrow, hv + r0 * kvrow, n * kvrow,
-                             cudaMemcpyHostToDevice, c->hp_up)) != cudaSuccess ||
+        (e = copy_kv(ok, hk)) != cudaSuccess || (e = copy_kv(ov, hv)) != cudaSuccess ||
         (e = cudaEventRecord(c->hp_ev[2 * i], c->hp_up)) != cudaSuccess ||
         (e = cudaStreamWaitEvent(c->stream, c->hp_ev[2 * i], 0)) != cudaSuccess) {
       drain();
