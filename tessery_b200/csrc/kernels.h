@@ -73,6 +73,11 @@ bool short_attention_supported(const AttnProblem &p);
 cudaError_t launch_attention_short(const AttnProblem &p, const uint16_t *q_w, const uint16_t *k_w,
                                    float eps, float theta, int *status, cudaStream_t stream);
 
+// Zeroes rows [min(lengths[s], seq), seq) of each sequence s < batch in one or two padded
+// row-major tensors (b may be NULL), row_bytes per row.
+cudaError_t launch_zero_padded_rows(void *a, void *b, const uint32_t *lengths, uint32_t batch,
+                                    uint32_t seq, size_t row_bytes, cudaStream_t stream);
+
 // Bandwidth-oriented fp32 kernel for head_dim 32 (BERT/BGE shapes).
 cudaError_t launch_attention_d32(const AttnProblem &p, cudaStream_t stream);
 

@@ -56,6 +56,8 @@ struct Ctx {
   uint32_t *units = nullptr;
   size_t units_cap = 0;
   std::vector<uint32_t> units_host;
+  uint32_t *hp_units = nullptr;  // page-locked work lists of one host-buffer call
+  size_t hp_units_cap = 0;
   uint64_t units_key = 0;
   uint32_t units_count = 0;
   cudaEvent_t scratch_done = nullptr;  // last launch that read scratch
@@ -157,9 +159,12 @@ struct Params64 {
 static_assert(sizeof(Params64) == 64, "Params block is 64 bytes");
 
 // Core of the typed entry points (padded when cu == nullptr).
+// `units_dev` / `units_n`: a work list already on the device (host-buffer calls upload
+// every chunk's list in one copy ahead of the data); NULL builds and uploads it here.
 int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
                   const int32_t *cu_host, const uint16_t *q_w, const uint16_t *k_w, float eps,
-                  float theta, cudaStream_t stream) {
+                  float theta, cudaStream_t stream, const uint32_t *units_dev = nullptr,
+                  uint32_t units_n = 0) {
   if (!p.q || !p.k || !p.v || !p.out) return fail(c, TX_EINVAL, "null tensor pointer");
   if (p.cu_seqlens == nullptr && p.lengths == nullptr)
     return fail(c, TX_EINVAL, "lengths or cu_seqlens required");
@@ -222,7 +227,7 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
   // attention kernel is launched as a programmatic dependent of the prologue and may
   // start while the prologue runs, so everything it reads besides k must already be in
   // place in stream order.
-  if (tc_path) {
+  if (tc_path && !units_dev) {
     const uint32_t cap = tx::tc_max_units(p), words = tx::tc_work_words(p, c->sms);
     uint64_t key = 1469598103934665603ull;
     uint32_t hdr[8] = {p.batch, p.seq, p.heads, p.kv_heads, (uint32_t)p.causal,
@@ -278,7 +283,8 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
   }
 
   if (tc_path) {
-    if ((e = tx::launch_attention_tc(p, c->units, c->units_count, c->sms, c->status, tc_q_w, eps,
+    if ((e = tx::launch_attention_tc(p, units_dev ? units_dev : c->units,
+                                     units_dev ? units_n : c->units_count, c->sms, c->status, tc_q_w, eps,
                                      theta, stream)) != cudaSuccess)
       return cuda_fail(c, e, "attention launch");
     c->last_kernel = "tc_bf16_d128";
@@ -346,12 +352,45 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
   }
   first[used] = nseq;
   nch = used;
-  // Device memory: q, k, v, out, then lengths or the rebased cu_seqlens, then the weights.
+  if (cu) {  // each chunk's cu_seqlens, rebased to the chunk's first row
+    c->hp_cu.resize(nseq + nch);
+    for (uint32_t i = 0; i < nch; ++i)
+      for (uint32_t s = first[i]; s <= first[i + 1]; ++s)
+        c->hp_cu[first[i] + i + (s - first[i])] = cu[s] - cu[first[i]];
+  }
+  // Chunk i as a problem on device pointers (base = the device copy buffers).
   auto up256 = [](size_t b) { return (b + 255) & ~(size_t)255; };
   const size_t oq = 0, ok = oq + up256(rows * qrow), ov = ok + up256(rows * kvrow);
   const size_t oo = ov + up256(rows * kvrow), om = oo + up256(rows * orow);
   const size_t meta = cu ? (size_t)(nseq + nch) * 4 : (size_t)nseq * 4;
-  const size_t ow = om + up256(meta), need = ow + 2 * up256((size_t)p.dim * 2);
+  const size_t ow = om + up256(meta), ou = ow + 2 * up256((size_t)p.dim * 2);
+  auto chunk_problem = [&](uint32_t i, uint8_t *dev) -> tx::AttnProblem {
+    const size_t r0 = row_of(first[i]), r1 = row_of(first[i + 1]);
+    tx::AttnProblem pc = p;
+    pc.q = dev + oq + r0 * qrow;
+    pc.k = dev + ok + r0 * kvrow;
+    pc.v = dev + ov + r0 * kvrow;
+    pc.out = dev + oo + r0 * orow;
+    pc.batch = first[i + 1] - first[i];
+    if (cu) {
+      const int32_t *cc = c->hp_cu.data() + first[i] + i;
+      pc.cu_seqlens = (const int32_t *)(dev + om) + first[i] + i;
+      pc.lengths = nullptr;
+      pc.total = (uint32_t)(r1 - r0);
+      uint32_t mx = 0;
+      for (uint32_t s = 0; s < pc.batch; ++s) mx = std::max<uint32_t>(mx, cc[s + 1] - cc[s]);
+      pc.seq = std::max(mx, 1u);
+    } else {
+      pc.lengths = (const uint32_t *)(dev + om) + first[i];
+      pc.cu_seqlens = nullptr;
+    }
+    return pc;
+  };
+  // Device memory: q, k, v, out, lengths or the rebased cu_seqlens, the weights, then the
+  // tensor-core work lists of the chunks (bounded by their shapes).
+  size_t wl_words = 0;
+  for (uint32_t i = 0; i < nch; ++i) wl_words += tx::tc_work_words(chunk_problem(i, nullptr), c->sms);
+  const size_t need = ou + up256(wl_words * 4);
   cudaError_t e = cudaSetDevice(c->device);
   if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
   if (c->hp_bytes < need) {
@@ -362,6 +401,15 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
     if ((e = cudaMalloc(&c->hp_mem, need)) != cudaSuccess) return cuda_fail(c, e, "host-path buffers");
     c->hp_bytes = need;
   }
+  if (c->hp_units_cap < wl_words) {  // every earlier call has drained: nothing reads it
+    if (c->hp_units) cudaFreeHost(c->hp_units);
+    c->hp_units = nullptr;
+    c->hp_units_cap = 0;
+    if (wl_words &&
+        (e = cudaHostAlloc((void **)&c->hp_units, wl_words * 4, cudaHostAllocDefault)) != cudaSuccess)
+      return cuda_fail(c, e, "work list staging");
+    c->hp_units_cap = wl_words;
+  }
   if (!c->hp_up) {
     if ((e = cudaStreamCreateWithFlags(&c->hp_up, cudaStreamNonBlocking)) != cudaSuccess ||
         (e = cudaStreamCreateWithFlags(&c->hp_down, cudaStreamNonBlocking)) != cudaSuccess)
@@ -371,6 +419,26 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
         return cuda_fail(c, e, "copy events");
   }
   uint8_t *dev = (uint8_t *)c->hp_mem;
+  // Work lists of the chunks that take the tensor-core kernel, built here and uploaded in
+  // one copy ahead of the data: a small copy queued on the compute stream would wait in
+  // the copy engine behind the bulk copies of every chunk queued before it.
+  size_t wl_off[kHostChunks];
+  uint32_t wl_n[kHostChunks];
+  bool wl_tc[kHostChunks];
+  size_t wl_used = 0;
+  for (uint32_t i = 0; i < nch; ++i) {
+    const tx::AttnProblem pc = chunk_problem(i, dev);
+    wl_tc[i] = pc.in_dtype == TX_BF16 && !tx::short_attention_supported(pc) && pc.scale > 0.f &&
+               tx::tc_attention_supported(pc);
+    wl_off[i] = wl_used;
+    wl_n[i] = 0;
+    if (!wl_tc[i]) continue;
+    c->units_host.resize(tx::tc_max_units(pc));
+    wl_n[i] = tx::tc_build_units(pc, cu ? nullptr : lengths + first[i],
+                                 cu ? c->hp_cu.data() + first[i] + i : nullptr, c->sms,
+                                 c->units_host.data(), c->hp_units + wl_used);
+    wl_used += tx::tc_work_words(pc, c->sms);
+  }
   const uint8_t *hq = (const uint8_t *)p.q, *hk = (const uint8_t *)p.k, *hv = (const uint8_t *)p.v;
   uint8_t *ho = (uint8_t *)p.out;
   // Drains every stream of this call (no copy may touch the caller's memory after return).
@@ -382,20 +450,17 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
   // Nothing of an earlier call may still read these buffers.
   if ((e = cudaStreamWaitEvent(c->hp_up, c->scratch_done, 0)) != cudaSuccess)
     return cuda_fail(c, e, "stream wait");
-  if (cu) {
-    c->hp_cu.resize(nseq + nch);
-    for (uint32_t i = 0; i < nch; ++i)
-      for (uint32_t s = first[i]; s <= first[i + 1]; ++s)
-        c->hp_cu[first[i] + i + (s - first[i])] = cu[s] - cu[first[i]];
+  if (cu)
     e = cudaMemcpyAsync(dev + om, c->hp_cu.data(), meta, cudaMemcpyHostToDevice, c->hp_up);
-  } else {
+  else
     e = cudaMemcpyAsync(dev + om, lengths, meta, cudaMemcpyHostToDevice, c->hp_up);
-  }
   if (e == cudaSuccess && q_w)
     e = cudaMemcpyAsync(dev + ow, q_w, (size_t)p.dim * 2, cudaMemcpyHostToDevice, c->hp_up);
   if (e == cudaSuccess && k_w)
     e = cudaMemcpyAsync(dev + ow + up256((size_t)p.dim * 2), k_w, (size_t)p.dim * 2,
                         cudaMemcpyHostToDevice, c->hp_up);
+  if (e == cudaSuccess && wl_used)
+    e = cudaMemcpyAsync(dev + ou, c->hp_units, wl_used * 4, cudaMemcpyHostToDevice, c->hp_up);
   if (e != cudaSuccess) {
     drain();
     return cuda_fail(c, e, "copy in");
@@ -405,21 +470,23 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
   for (uint32_t i = 0; i < nch; ++i) {
     const size_t r0 = row_of(first[i]), r1 = row_of(first[i + 1]), n = r1 - r0;
     // k and v rows of the chunk.  Padded layout: only each sequence's valid rows cross the
-    // link; its rows at or past the length are never attended (their keys are masked) and
-    // are zeroed on the device instead, so the masked products stay exact zeros.
+    // link (a run of full sequences in one copy); its rows at or past the length are never
+    // attended (their keys are masked) and are zeroed on the device by a kernel on the
+    // compute stream instead, so the masked products stay exact zeros.
     auto copy_kv = [&](size_t region, const uint8_t *h) -> cudaError_t {
       if (cu)
         return cudaMemcpyAsync(dev + region + r0 * kvrow, h + r0 * kvrow, n * kvrow,
                                cudaMemcpyHostToDevice, c->hp_up);
       cudaError_t err = cudaSuccess;
-      for (uint32_t b = first[i]; b < first[i + 1] && err == cudaSuccess; ++b) {
-        const size_t s0 = (size_t)b * p.seq, nv = lengths[b];
+      for (uint32_t b = first[i]; b < first[i + 1] && err == cudaSuccess;) {
+        const size_t s0 = (size_t)b * p.seq;
+        uint32_t b1 = b;  // sequences b .. b1 are full except possibly b1
+        while (b1 + 1 < first[i + 1] && lengths[b1] == p.seq) ++b1;
+        const size_t nv = (size_t)(b1 - b) * p.seq + lengths[b1];
         if (nv)
           err = cudaMemcpyAsync(dev + region + s0 * kvrow, h + s0 * kvrow, nv * kvrow,
                                 cudaMemcpyHostToDevice, c->hp_up);
-        if (err == cudaSuccess && nv < p.seq)
-          err = cudaMemsetAsync(dev + region + (s0 + nv) * kvrow, 0, (p.seq - nv) * kvrow,
-                                c->hp_up);
+        b = b1 + 1;
       }
       return err;
     };
@@ -427,31 +494,20 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
                              cudaMemcpyHostToDevice, c->hp_up)) != cudaSuccess ||
         (e = copy_kv(ok, hk)) != cudaSuccess || (e = copy_kv(ov, hv)) != cudaSuccess ||
         (e = cudaEventRecord(c->hp_ev[2 * i], c->hp_up)) != cudaSuccess ||
-        (e = cudaStreamWaitEvent(c->stream, c->hp_ev[2 * i], 0)) != cudaSuccess) {
+        (e = cudaStreamWaitEvent(c->stream, c->hp_ev[2 * i], 0)) != cudaSuccess ||
+        (!cu && (e = tx::launch_zero_padded_rows(dev + ok + r0 * kvrow, dev + ov + r0 * kvrow,
+                                                 (const uint32_t *)(dev + om) + first[i],
+                                                 first[i + 1] - first[i], p.seq, kvrow,
+                                                 c->stream)) != cudaSuccess)) {
       drain();
       return cuda_fail(c, e, "copy in");
     }
-    tx::AttnProblem pc = p;
-    pc.q = dev + oq + r0 * qrow;
-    pc.k = dev + ok + r0 * kvrow;
-    pc.v = dev + ov + r0 * kvrow;
-    pc.out = dev + oo + r0 * orow;
-    pc.batch = first[i + 1] - first[i];
-    const int32_t *cu_chunk = nullptr;
-    if (cu) {
-      cu_chunk = c->hp_cu.data() + first[i] + i;
-      pc.cu_seqlens = (const int32_t *)(dev + om) + first[i] + i;
-      pc.lengths = nullptr;
-      pc.total = (uint32_t)n;
-      uint32_t mx = 0;
-      for (uint32_t s = 0; s < pc.batch; ++s) mx = std::max<uint32_t>(mx, cu_chunk[s + 1] - cu_chunk[s]);
-      pc.seq = std::max(mx, 1u);
-    } else {
-      pc.lengths = (const uint32_t *)(dev + om) + first[i];
-      pc.cu_seqlens = nullptr;
-    }
-    const int rc = run_attention(c, pc, cu ? nullptr : lengths + first[i], cu_chunk, dqw, dkw,
-                                 eps, theta, c->stream);
+    const tx::AttnProblem pc = chunk_problem(i, dev);
+    const int rc = run_attention(c, pc, cu ? nullptr : lengths + first[i],
+                                 cu ? c->hp_cu.data() + first[i] + i : nullptr, dqw, dkw, eps,
+                                 theta, c->stream,
+                                 wl_tc[i] ? (const uint32_t *)(dev + ou) + wl_off[i] : nullptr,
+                                 wl_n[i]);
     if (rc != TX_OK) {
       drain();
       return rc;
@@ -560,6 +616,7 @@ void tx_destroy(void *ctx) {
     if (c->ev_end) cudaEventDestroy(c->ev_end);
     if (c->scratch_done) cudaEventDestroy(c->scratch_done);
     if (c->hp_mem) cudaFree(c->hp_mem);
+    if (c->hp_units) cudaFreeHost(c->hp_units);
     for (cudaEvent_t ev : c->hp_ev)
       if (ev) cudaEventDestroy(ev);
     if (c->hp_up) cudaStreamDestroy(c->hp_up);
