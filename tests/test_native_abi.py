@@ -65,6 +65,12 @@ def test_null_handles_are_rejected_without_a_device():
     assert lib.tx_buffer(None, None, 16) is None
     assert lib.tx_gpu_seconds(None) == -1.0
     assert lib.tx_launch_count(None) == 0
+    # The host-buffer attention entry points refuse a missing context before touching
+    # any pointer.
+    assert lib.tx_attention_padded_host(None, None, None, None, None, None, 1, 1, 1, 1, 128, 1,
+                                        0, 1, 0.1, None, None, 1e-6, 1e6) == native.TX_EINVAL
+    assert lib.tx_attention_varlen_host(None, None, None, None, None, 1, 1, None, 1, 1, 128, 1,
+                                        0, 1, 0.1, None, None, 1e-6, 1e6) == native.TX_EINVAL
 
 
 @pytest.mark.parametrize("changed_during_load", [False, True])
