@@ -140,7 +140,9 @@ int tx_profile_read(void *ctx, double *seconds, uint32_t count);
  *           sequence s spans rows cu_seqlens[s] .. cu_seqlens[s+1]-1.
  * Semantics (kernels.metal:78-103): query row at position p of a sequence of length n
  * attends to keys [0, causal ? min(p+1, n) : n); padded query rows (p >= n) are
- * computed too and attend to [0, n); kv head = head / (heads / kv_heads).
+ * computed too and attend to [0, n); kv head = head / (heads / kv_heads).  Padded k/v
+ * rows (positions >= n) must be finite: they are read inside the last key tile and
+ * multiplied by zero probabilities.
  * `scale` multiplies q.k (the reference passes dim^-0.5).
  * in_dtype: TX_F32 or TX_BF16 for q, k, v.  out_dtype: TX_F32 or TX_BF16.
  * q_norm_w / k_norm_w: bf16 bit patterns [dim] (kernels.metal:53-63 reads its weight
