@@ -259,12 +259,14 @@ static cudaError_t launch_prologue_e(const PrologueProblem &p, cudaStream_t stre
 }
 
 // ---- bf16 head_dim-128 prologue, written for bandwidth -------------------------------
-// One pass over the rows of one tensor (q or k).  A block of 4 warps covers 16
-// consecutive tokens (padded layout: 16 positions of one sequence, blockIdx.y = the
+// One pass over the rows of one tensor (q or k).  A block of 4 warps covers 12
+// consecutive tokens (padded layout: 12 positions of one sequence, blockIdx.y = the
 // sequence, so its length is read once and blocks past it exit); their rows are
 // contiguous in memory and arrive in shared memory with one bulk asynchronous copy, so
 // the bytes in flight per SM are set by the blocks resident there, not by registers;
-// each warp then transforms 4 tokens and writes them straight to global memory.  Within a
+// each warp then transforms 3 tokens and writes them straight to global memory (3 per
+// warp measured faster than 2 or 4 at the Qwen shapes: more blocks in flight than with
+// 4, no second wave as with 2).  Within a
 // token, each half-warp owns one 256-byte row (one head) per load, lane l%16 holding the
 // 16 bytes of columns 8(l%16)..8(l%16)+7, so every load and store moves 512 contiguous
 // bytes per warp.  The rotation partner of column c (c < 64) is column c + 64, held by
@@ -275,7 +277,7 @@ static cudaError_t launch_prologue_e(const PrologueProblem &p, cudaStream_t stre
 // products are shared by all heads.  The angle is the float product pos * inv_freq[c];
 // its sine and cosine come from a Cody-Waite reduction by 2*pi and the hardware
 // approximations (about 2^-21 absolute error).
-constexpr int kRowTokensPerWarp = 4;
+constexpr int kRowTokensPerWarp = 3;
 
 struct RowPass {
   const uint16_t *in;
@@ -482,7 +484,9 @@ static cudaError_t launch_rows(const RowPass &rp, const PrologueProblem &p, cuda
     if (grid.y > 65535u) return cudaErrorInvalidValue;
   }
   const uint32_t smem = kBlockTokens * rp.nheads * 256;
-  if (smem > 48 * 1024) {
+  // The 48 KB default covers static and dynamic shared memory together (the kernel's
+  // static arrays take ~4 KB): opt in above that.
+  if (smem + 8 * 1024 > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(norm_rope_rows_bf16_kernel<NP>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
