@@ -5,8 +5,9 @@
 //
 // At these lengths a whole (sequence, kv head) problem fits in one CTA's shared memory:
 // the K and V rows of the sequence and the Q rows of every query head that reads them.
-// One CTA per (sequence, kv head) loads them once, normalises and rotates q and k in
-// place (k rows are used by exactly this CTA, so the k prologue needs no separate pass),
+// One CTA (8 warps) per (sequence, kv head) loads them once, normalises and rotates q and
+// k in shared memory (k rows are used by exactly this CTA, so the k prologue needs no
+// separate pass),
 // computes S = Q K^T, the masked softmax and O = P V with register-level tensor-core
 // MMAs (mma.sync m16n8k16, bf16 operands, fp32 accumulators: each warp owns 16 query
 // rows, S stays in registers and becomes the A operand of P V), and writes O.  No
@@ -48,7 +49,6 @@ struct Params {
 __host__ __device__ constexpr uint32_t smem_bytes(uint32_t g) {
   return (g * kMaxRows * kRS + 2 * kMaxRows * kRS) * 2 + (1 + g) * kMaxRows * 256;
 }
-
 
 // D = A B + D for one m16n8k16 tile (bf16 A and B, fp32 accumulators).
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
