@@ -104,26 +104,9 @@ def profile_traffic(workload: str) -> dict:
 
 # ---- workloads ----------------------------------------------------------------------------
 def make_workload(name: str, rank: int, world: int, scaled_batch: int = 4096):
-    from tessery_b200 import shard_sequences, workloads
+    from tessery_b200 import workloads
 
-    if name == "qwen_padded":
-        lengths = np.random.default_rng(2).integers(32, 513, size=32 * world)
-        owned = shard_sequences(lengths, world, causal=True)[rank]
-        return workloads.qwen_padded(batch=len(owned), seq=512, seed=2 + 1000 * rank,
-                                     lengths=lengths[owned])
-    if name == "qwen_varlen":
-        lengths = workloads.varlen_lengths(256, 3)
-        owned = shard_sequences(lengths, world, causal=True)[rank]
-        return workloads.qwen_varlen(seed=3 + 1000 * rank, lengths=lengths[owned])
-    if name == "bge":
-        return workloads.bge(batch=4, seq=128, seed=1 + 1000 * rank)
-    if name == "bge_scaled":
-        return workloads.bge(batch=scaled_batch, seq=128, seed=1 + 1000 * rank)
-    if name == "tails_qwen":
-        return workloads.short_tails("qwen", batch=32, seed=4 + 1000 * rank)
-    if name == "tails_bge":
-        return workloads.short_tails("bge", batch=32, seed=4 + 1000 * rank)
-    raise ValueError(name)
+    return workloads.benchmark_workload(name, rank, world, scaled_batch)
 
 
 def scaling_of(name: str) -> str:

@@ -59,6 +59,14 @@ const char *tx_last_error(void *ctx);
 /* Number of streaming multiprocessors of the context's device. */
 int tx_device_sms(void *ctx);
 
+/* Limit, in SM clock cycles, of each bounded wait inside the tensor-core attention
+ * kernel launched by this context (0 restores the default, about one second).  A wait
+ * that runs out makes the kernel drain what it has in flight and return, and the next
+ * tx_sync / tx_finish reports TX_ETIMEOUT; the context stays usable.  Counterpart of the
+ * status check of mi_finish (runtime.mm:217-253): lets a test make that error path run
+ * without any fault.  Returns TX_EINVAL for a negative limit. */
+int tx_set_wait_limit(void *ctx, int64_t cycles);
+
 /* Name of the last attention kernel this context launched ("tc_bf16_d128",
  * "simt", "d32_f32") or "" -- the route a call took, as the reference's tests read
  * kernel names from MetalRuntime.diagnostics()["dispatches"] (metal.py:208-234). */
@@ -77,6 +85,12 @@ void *tx_buffer(void *ctx, const void *host, uint64_t size);
 
 /* Replaces mi_free (runtime.mm:78-80). */
 void tx_free(void *buffer);
+
+/* Memory accounting of the context's buffers (the counters metal.py:94-119 keeps per
+ * Buffer and diagnostics() reports, metal.py:208-234): out[0] bytes live now, out[1] the
+ * most bytes ever live at once, out[2] allocations made, out[3] bytes allocated in all.
+ * Scratch the context owns for its kernels is not counted. */
+int tx_memory_stats(void *ctx, uint64_t *out);
 
 /* Replaces mi_read (runtime.mm:81-86): synchronous device-to-host copy of the first
  * `bytes` bytes.  Returns 1 when bytes exceeds the buffer size. */
@@ -141,8 +155,8 @@ int tx_profile_read(void *ctx, double *seconds, uint32_t count);
  * Semantics (kernels.metal:78-103): query row at position p of a sequence of length n
  * attends to keys [0, causal ? min(p+1, n) : n); padded query rows (p >= n) are
  * computed too and attend to [0, n); kv head = head / (heads / kv_heads).  Padded k/v
- * rows (positions >= n) must be finite: they are read inside the last key tile and
- * multiplied by zero probabilities.
+ * rows (positions >= n) are never attended and may hold any value, NaN and Inf included
+ * (the reference never reads them, kernels.metal:89-99).
  * `scale` multiplies q.k (the reference passes dim^-0.5).
  * in_dtype: TX_F32 or TX_BF16 for q, k, v.  out_dtype: TX_F32 or TX_BF16.
  * q_norm_w / k_norm_w: bf16 bit patterns [dim] (kernels.metal:53-63 reads its weight
@@ -184,7 +198,7 @@ int tx_attention_varlen(void *ctx, const void *q, const void *k, const void *v,
  * The sequences are split into chunks of whole sequences; chunk i's rows are copied in
  * while chunk i-1 is computed and chunk i-2 copied out, so transfer in both directions
  * overlaps and the kernels hide behind it.  In the padded layout only the valid k and v
- * rows are copied (the rest, never attended, are zeroed on the device).  Results equal the
+ * rows are copied (the rest are never attended).  Results equal the
  * device-pointer entry points' bit for bit.  Returns when the output is in `out` (kernel errors included); device
  * memory for the copies is kept by the context and grows to the largest call. */
 int tx_attention_padded_host(void *ctx, const void *q, const void *k, const void *v,
@@ -243,11 +257,13 @@ int tx_pool_project(void *ctx, const void *x, int in_dtype, const uint32_t *leng
  * heads, or of one head when the query heads per kv head are odd:
  * batch * heads/2 (or heads) * ceil(seq/128) units); larger problems are rejected with
  * TX_EINVAL before any pointer is used.  The first call on a device looks up that array's
- * device address (with the device current) and should come before any stream
- * capture.  All calls share the array and it keeps the last call's contents: calls
- * whose work overlaps on the GPU race.  status: device int the kernel sets to
- * TX_ETIMEOUT | site << 8 if a bounded wait gives up (zeroed by this call first), or
- * NULL.  Returns TX_OK once queued on `stream` (NULL: the legacy default stream). */
+ * device address (with the device current) and loads the kernel's code, which places
+ * the array and the code in device memory: make one such call per device at start-up,
+ * before memory is reserved and before any stream capture.  All calls share the array
+ * and it keeps the last call's contents: calls whose work overlaps on the GPU race.
+ * status (required, device int): zeroed by this call, then set by the kernel to
+ * TX_ETIMEOUT | site << 8 if a bounded wait gives up; read it after the stream has
+ * drained.  Returns TX_OK once queued on `stream` (NULL: the legacy default stream). */
 int tx_attention_padded_noalloc(const void *q, const void *k, const void *v,
                                 const uint32_t *lengths, const uint32_t *lengths_host,
                                 void *out, uint32_t batch, uint32_t seq, uint32_t heads,

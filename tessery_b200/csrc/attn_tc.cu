@@ -45,9 +45,11 @@
 // than 8 (log2 units), so every probability stays below 2^8 and the normalised result
 // is unchanged.
 //
-// Every wait is bounded (about a second); a wait that gives up records
-// TX_ETIMEOUT | site<<8 in the context status word, raises a CTA-wide abort flag, and
-// all roles drain their in-flight copies and MMAs before TMEM is freed and the CTA exits.
+// Every wait is bounded (a per-launch limit, about a second by default); a wait that
+// gives up records TX_ETIMEOUT | site<<8 in the context status word, raises a CTA-wide
+// abort flag, and all roles drain their in-flight copies and MMAs before TMEM is freed
+// and the CTA exits.  The drains themselves wait for work already issued, which completes
+// by itself; they are bounded by the default limit.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -138,6 +140,7 @@ struct Params {
   int *status;
   const uint16_t *q_norm_w;  // fused q prologue when non-NULL
   float eps;
+  long long wait_cycles;     // limit of every bounded wait, in SM clock cycles
   float inv_freq[64];        // RoPE theta^(-2c/128), c < 64
 };
 
@@ -213,15 +216,16 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
 // indexed by a run-time slot would live in local memory).
 __device__ __forceinline__ uint32_t bit(uint32_t word, uint32_t i) { return (word >> i) & 1u; }
 
-// Bounded wait for the phase with parity `parity` of barrier `bar`.
+// Bounded wait for the phase with parity `parity` of barrier `bar`; gives up after
+// `limit` SM cycles.
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int *abort_flag,
-                                        int *status, int site) {
+                                        int *status, int site, long long limit) {
   if (mbar_test(bar, parity)) return true;
   long long t0 = clock64();
   while (true) {
     if (mbar_test(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       *abort_flag = 1;
       report_status(status, kStatusTimeout | (site << 8));
       return false;
@@ -609,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto load_kv = [&](const CUtensorMap *map, const Unit &u, uint32_t j) {
         const uint32_t slot = loads & (kStages - 1), round = loads / kStages;
         if (round > 0 && !(ok = wait_phase(bar(kBarKVEmpty + slot), (round - 1) & 1,
-                                           abort_flag, p.status, kSiteKVEmpty)))
+                                           abort_flag, p.status, kSiteKVEmpty, p.wait_cycles)))
           return;
         const uint32_t dst = sbase + kOffKV + slot * kKVBytes;
         mbar_expect_tx(bar(kBarKVFull + slot), kKVBytes);
@@ -649,7 +653,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (nxt < p.n_units) load_q(nxt, 1);
       // K may be written by the kernel launched just before this one (the k prologue):
       // with a programmatic dependent launch this grid starts while that one drains, so
-      // wait for it before the first K load.  Q and V are the caller's inputs.
+      // wait for it before the first K load.  Q, V, the lengths and the work list were in
+      // place before the prologue started (the launch is programmatic only then).
       asm volatile("griddepcontrol.wait;" ::: "memory");
       for (uint32_t k = 0; ok && cur < p.n_units; ++k) {
         const Unit u = decode(p, p.units[cur]);
@@ -664,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok && ahead < p.n_units) {
           const uint32_t b = k & 1;
           if ((ok = wait_phase(bar(kBarQEmpty + b), (k >> 1) & 1, abort_flag, p.status,
-                               kSiteQEmpty)))
+                               kSiteQEmpty, p.wait_cycles)))
             load_q(ahead, b);
         }
         cur = nxt;
@@ -684,26 +689,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Per work unit: S_h = Q_h K_0^T for both heads; then per key tile j: for each head,
     // O_h (+)= P_h V_j and at once S_h = Q_h K_{j+1}^T into the columns P_h.V has just
     // read (tcgen05.mma of one thread run in order), so one head's softmax overlaps the
-    // other head's products.
-    if (lane == 0) {
-      uint32_t loads = 0, units_done = 0;
-      uint32_t pbits = 0, obits = 0;  // parities: P-full per head, O-free per head
-      bool ok = true, issued = false;
-      uint32_t qbuf = 0;  // Q buffer of the current unit
-      // The next ring slot (a K or V tile, in load order): wait for it.
-      auto take = [&](uint32_t *slot) -> bool {
-        *slot = loads & (kStages - 1);
-        if (!(ok = wait_phase(bar(kBarKVFull + *slot), (loads / kStages) & 1, abort_flag,
-                              p.status, kSiteKVFull)))
-          return false;
-        ++loads;
-        tc_fence_after();
-        return true;
-      };
-      // S_h = Q_h K^T (M=128, N=128 keys, K=128) from the K tile in ring slot `slot`.
-      // Descriptors of step 0; step ks adds its byte offset / 16 to the start-address
-      // field (addresses stay below 256 KB, so the field never carries).
-      auto qk_head = [&](uint32_t h, uint32_t slot) {
+    // other head's products.  The whole warp follows the schedule (its waits are
+    // warp-wide); lane 0 issues the MMAs and commits, and all lanes clear the V rows at
+    // or past a sequence's end in the unit's last key tile.
+    const bool leader = lane == 0;
+    uint32_t loads = 0, units_done = 0;
+    uint32_t pbits = 0, obits = 0;  // parities: P-full per head, O-free per head
+    bool ok = true, issued = false;
+    uint32_t qbuf = 0;  // Q buffer of the current unit
+    auto wait_all = [&](uint32_t b, uint32_t parity, int site) -> bool {
+      return __all_sync(0xffffffffu,
+                        wait_phase(b, parity, abort_flag, p.status, site, p.wait_cycles));
+    };
+    auto commit = [&](uint32_t b) {
+      if (leader) umma_commit(b);
+    };
+    // The next ring slot (a K or V tile, in load order): wait for it.
+    auto take = [&](uint32_t *slot) -> bool {
+      *slot = loads & (kStages - 1);
+      if (!(ok = wait_all(bar(kBarKVFull + *slot), (loads / kStages) & 1, kSiteKVFull)))
+        return false;
+      ++loads;
+      tc_fence_after();
+      return true;
+    };
+    // S_h = Q_h K^T (M=128, N=128 keys, K=128) from the K tile in ring slot `slot`.
+    // Descriptors of step 0; step ks adds its byte offset / 16 to the start-address
+    // field (addresses stay below 256 KB, so the field never carries).
+    auto qk_head = [&](uint32_t h, uint32_t slot) {
+      if (leader) {
         const uint64_t kd = kmajor_desc(sbase + kOffKV + slot * kKVBytes, 0, kKVAtom);
         const uint64_t qd =
             kmajor_desc(sbase + kOffQ + qbuf * kQBufBytes + h * kQBytes, 0, kQAtom);
@@ -713,10 +727,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma(d, qd + (uint64_t)((ks >> 2) * (kQAtom >> 4) + (ks & 3) * 2),
                kd + (uint64_t)((ks >> 2) * (kKVAtom >> 4) + (ks & 3) * 2), kIdescQK, ks > 0);
         umma_commit(bar(kBarSFull + h));
-        issued = true;
-      };
-      // O_h (+)= P_h V with P_h (bf16, 128 keys) in the first 64 columns of S_h.
-      auto pv_head = [&](uint32_t h, uint32_t slot, uint32_t acc) {
+      }
+      issued = true;
+    };
+    // O_h (+)= P_h V with P_h (bf16, 128 keys) in the first 64 columns of S_h.
+    auto pv_head = [&](uint32_t h, uint32_t slot, uint32_t acc) {
+      if (leader) {
         const uint64_t vd = mnmajor_desc(sbase + kOffKV + slot * kKVBytes, 0);
         const uint32_t pt = tmem + h * 256, d = tmem + h * 256 + 128;
 #pragma unroll
@@ -724,58 +740,66 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_ts(d, pt + ks * 8, vd + (uint64_t)(ks * (2048 >> 4)), kIdescPV,
                   (acc || ks > 0) ? 1u : 0u);
         umma_commit(bar(kBarPVDone + h));
-      };
-      for (uint32_t ui = p.offsets[blockIdx.x]; ok && ui < p.offsets[blockIdx.x + 1]; ++ui) {
-        const Unit u = decode(p, p.units[ui]);
-        if (!u.nt) continue;
-        // Work unit k uses Q buffer k % 2 (fill k / 2 of that buffer).
-        qbuf = units_done & 1;
-        if (!(ok = wait_phase(bar(kBarQReady + qbuf), (units_done >> 1) & 1, abort_flag,
-                              p.status, kSiteQReady)))
-          break;
-        ++units_done;
-        tc_fence_after();
-        uint32_t slotK;
-        if (!take(&slotK)) break;
-        for (uint32_t h = 0; h < nh; ++h) qk_head(h, slotK);
-        umma_commit(bar(kBarKVEmpty + slotK));
-        if (u.nt == 1) umma_commit(bar(kBarQEmpty + qbuf));  // the unit's last Q.K^T
-        for (uint32_t j = 0; ok && j < u.nt; ++j) {
-          uint32_t slotV;
-          if (!take(&slotV)) break;
-          const bool more = j + 1 < u.nt;
-          for (uint32_t h = 0; h < nh && ok; ++h) {
-            if (!(ok = wait_phase(bar(kBarPFull + h), bit(pbits, h), abort_flag, p.status,
-                                  kSitePFull)))
-              break;
-            pbits ^= 1u << h;
-            if (j == 0 && units_done > 1) {
-              // O_h still holds the previous unit until the epilogue has read it.
-              if (!(ok = wait_phase(bar(kBarOFree + h), bit(obits, h), abort_flag, p.status,
-                                    kSiteOFree)))
-                break;
-              obits ^= 1u << h;
-            }
-            tc_fence_after();
-            pv_head(h, slotV, j > 0);
-            if (more) {
-              if (h == 0 && !take(&slotK)) break;
-              qk_head(h, slotK);
-            }
+      }
+    };
+    // Rows [first, 128) of the V tile in ring slot `slot` set to zero: those keys lie at or
+    // past the sequence's end (padding, or the next packed sequence), their probabilities
+    // are zero, and zero times a non-finite value would not be.  Whole 128-byte rows of
+    // both 64-column atoms, so the swizzle does not matter.
+    auto clear_v_rows = [&](uint32_t slot, uint32_t first) {
+      const uint32_t base = sbase + kOffKV + slot * kKVBytes;
+      for (uint32_t i = first * 16 + lane; i < 128u * 16u; i += 32) {
+        const uint32_t row = i >> 4, atom = (i >> 3) & 1u, c = i & 7u;
+        st_shared_v4(base + atom * kKVAtom + row * 128 + c * 16, 0u, 0u, 0u, 0u);
+      }
+      fence_proxy_async();  // generic-proxy writes seen by the tensor core's reads
+      __syncwarp();
+    };
+    for (uint32_t ui = p.offsets[blockIdx.x]; ok && ui < p.offsets[blockIdx.x + 1]; ++ui) {
+      const Unit u = decode(p, p.units[ui]);
+      if (!u.nt) continue;
+      // Work unit k uses Q buffer k % 2 (fill k / 2 of that buffer).
+      qbuf = units_done & 1;
+      if (!(ok = wait_all(bar(kBarQReady + qbuf), (units_done >> 1) & 1, kSiteQReady))) break;
+      ++units_done;
+      tc_fence_after();
+      uint32_t slotK;
+      if (!take(&slotK)) break;
+      for (uint32_t h = 0; h < nh; ++h) qk_head(h, slotK);
+      commit(bar(kBarKVEmpty + slotK));
+      if (u.nt == 1) commit(bar(kBarQEmpty + qbuf));  // the unit's last Q.K^T
+      for (uint32_t j = 0; ok && j < u.nt; ++j) {
+        uint32_t slotV;
+        if (!take(&slotV)) break;
+        if (u.n < (j + 1) * kKeys) clear_v_rows(slotV, u.n - j * kKeys);
+        const bool more = j + 1 < u.nt;
+        for (uint32_t h = 0; h < nh && ok; ++h) {
+          if (!(ok = wait_all(bar(kBarPFull + h), bit(pbits, h), kSitePFull))) break;
+          pbits ^= 1u << h;
+          if (j == 0 && units_done > 1) {
+            // O_h still holds the previous unit until the epilogue has read it.
+            if (!(ok = wait_all(bar(kBarOFree + h), bit(obits, h), kSiteOFree))) break;
+            obits ^= 1u << h;
           }
-          if (!ok) break;
-          umma_commit(bar(kBarKVEmpty + slotV));
+          tc_fence_after();
+          pv_head(h, slotV, j > 0);
           if (more) {
-            umma_commit(bar(kBarKVEmpty + slotK));
-            if (j + 2 == u.nt) umma_commit(bar(kBarQEmpty + qbuf));  // Q.K^T of the last tile
+            if (h == 0 && !take(&slotK)) break;
+            qk_head(h, slotK);
           }
         }
+        if (!ok) break;
+        commit(bar(kBarKVEmpty + slotV));
+        if (more) {
+          commit(bar(kBarKVEmpty + slotK));
+          if (j + 2 == u.nt) commit(bar(kBarQEmpty + qbuf));  // Q.K^T of the last tile
+        }
       }
-      if (issued) {
-        // Wait until every MMA this thread issued has completed (normal exit and abort).
-        umma_commit(bar(kBarDrain));
-        drain_phase(bar(kBarDrain), 0);
-      }
+    }
+    if (issued && leader) {
+      // Wait until every MMA this thread issued has completed (normal exit and abort).
+      umma_commit(bar(kBarDrain));
+      drain_phase(bar(kBarDrain), 0);
     }
     __syncwarp();
   } else if (warp < kEpiWarp0) {
@@ -801,7 +825,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m_ref = -INFINITY, l = 0.f;
       for (uint32_t j = 0; j < u.nt; ++j, ++tiles) {
         ok = __all_sync(0xffffffffu, wait_phase(bar(kBarSFull + h), tiles & 1, abort_flag,
-                                                p.status, kSiteSFull));
+                                                p.status, kSiteSFull, p.wait_cycles));
         if (!ok) break;
         tc_fence_after();
         if (!warp_live) {
@@ -906,7 +930,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // it to the issuer (which waits for every head slot).
     auto prepare = [&](uint32_t ui, uint32_t b, uint32_t phase) {
       ok = __all_sync(0xffffffffu, wait_phase(bar(kBarQFull + b), phase & 1, abort_flag,
-                                              p.status, kSiteQFull));
+                                              p.status, kSiteQFull, p.wait_cycles));
       if (!ok) return;
       if (p.q_norm_w) {
         // Rows past the end of a packed sequence belong to no output: left as loaded.
@@ -949,11 +973,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         // two units ahead of this epilogue: their next-but-one unit needs O_h freed).
         ok = __all_sync(0xffffffffu,
                         wait_phase(bar(kBarLReady + 2 * h + (lcount & 1)), (lcount >> 1) & 1,
-                                   abort_flag, p.status, kSiteLReady));
+                                   abort_flag, p.status, kSiteLReady, p.wait_cycles));
         if (!ok) return;
         const float l = rowsum_s[(h * 2 + (lcount & 1)) * 128 + r];
         ok = __all_sync(0xffffffffu, wait_phase(bar(kBarPVDone + h), last_pv & 1, abort_flag,
-                                                p.status, kSitePVDone));
+                                                p.status, kSitePVDone, p.wait_cycles));
         if (!ok) return;
         tc_fence_after();
         const float inv = 1.0f / l;
@@ -1273,9 +1297,15 @@ bool make_map(CUtensorMap *map, const void *base, uint32_t rows, uint32_t heads,
 
 }  // namespace
 
+cudaError_t tc_preload() {
+  cudaFuncAttributes attr;
+  return cudaFuncGetAttributes(&attr, tc::attn_tc_kernel);
+}
+
 cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uint32_t n_units,
                                 int num_sms, int *status, const uint16_t *q_norm_w, float eps,
-                                float theta, cudaStream_t stream) {
+                                float theta, cudaStream_t stream, bool after_prologue,
+                                long long wait_cycles) {
   if (!n_units) return cudaSuccess;
   CUtensorMap mq, mk, mv, mo;
   const uint32_t rows = p.total;
@@ -1305,12 +1335,16 @@ cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uin
   prm.status = status;
   prm.q_norm_w = q_norm_w;
   prm.eps = eps;
+  prm.wait_cycles = wait_cycles > 0 ? wait_cycles : tc::kWaitCycles;
   for (int i = 0; i < 64; ++i)
     prm.inv_freq[i] = (float)std::pow((double)theta, -2.0 * (double)i / 128.0);
   const uint32_t grid = std::min(tc_grid(n_units, num_sms), 1024u);
-  // Programmatic dependent launch: the CTAs may start (barrier set-up, tensor-memory
-  // allocation, Q loads and the q prologue) while the previous kernel on the stream
-  // finishes; the producer waits for it before reading K (griddepcontrol.wait).
+  // Programmatic dependent launch, only right after this library's k prologue: the CTAs
+  // may then start (barrier set-up, tensor-memory allocation, Q loads and the q prologue)
+  // while the prologue finishes, and the producer waits for it before reading K
+  // (griddepcontrol.wait).  Everything else the kernel reads was written before the
+  // prologue started.  After any other kernel (a caller's kernel that may have just
+  // written q or the lengths) the launch is an ordinary stream-ordered one.
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(tc::kThreads);
@@ -1320,7 +1354,7 @@ cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uin
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = after_prologue ? 1 : 0;
   e = cudaLaunchKernelEx(&cfg, tc::attn_tc_kernel, mq, mk, mv, mo, prm);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();

@@ -73,10 +73,6 @@ bool short_attention_supported(const AttnProblem &p);
 cudaError_t launch_attention_short(const AttnProblem &p, const uint16_t *q_w, const uint16_t *k_w,
                                    float eps, float theta, int *status, cudaStream_t stream);
 
-// Zeroes rows [min(lengths[s], seq), seq) of each sequence s < batch in one or two padded
-// row-major tensors (b may be NULL), row_bytes per row.
-cudaError_t launch_zero_padded_rows(void *a, void *b, const uint32_t *lengths, uint32_t batch,
-                                    uint32_t seq, size_t row_bytes, cudaStream_t stream);
 
 // Bandwidth-oriented fp32 kernel for head_dim 32 (BERT/BGE shapes).
 cudaError_t launch_attention_d32(const AttnProblem &p, cudaStream_t stream);
@@ -87,9 +83,15 @@ cudaError_t launch_attention_d32(const AttnProblem &p, cudaStream_t stream);
 bool tc_attention_supported(const AttnProblem &p);
 // q_norm_w: bf16 q RMSNorm weight [128] applied with RoPE to each Q tile in the kernel
 // (NULL: q is used as given).
+// after_prologue: the kernel launched just before on `stream` is this library's k
+// prologue (the launch may then overlap its tail, programmatic dependent launch).
+// wait_cycles: limit of each bounded wait in SM cycles (<= 0: about a second).
 cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uint32_t n_units,
                                 int num_sms, int *status, const uint16_t *q_norm_w, float eps,
-                                float theta, cudaStream_t stream);
+                                float theta, cudaStream_t stream, bool after_prologue,
+                                long long wait_cycles);
+// Loads the tensor-core kernel's module on the current device (no launch).
+cudaError_t tc_preload();
 // Host-side work-list construction for launch_attention_tc (same num_sms for both).
 // `sorted` is host scratch of tc_max_units words; `work` (tc_work_words words) receives
 // the n units grouped by CTA followed by grid+1 offsets; returns n.  The launcher takes

@@ -26,8 +26,8 @@ namespace {
 constexpr uint32_t kNoAllocMaxUnits = 32768;
 // The work list also holds one offset per CTA of the grid, plus one.
 constexpr uint32_t kNoAllocMaxOffsets = 1025;
-// Word 0: status word used when the caller passes no status pointer.  Words 64..: the
-// work list (units grouped by CTA, then the offsets).
+// Words 0..63 are unused (they keep the work list 256-byte aligned after the header of
+// earlier versions); words 64..: the work list (units grouped by CTA, then the offsets).
 constexpr uint32_t kHeaderWords = 64;
 
 static __device__ __align__(256) uint32_t
@@ -51,7 +51,8 @@ extern "C" int tx_attention_padded_noalloc(const void *q, const void *k, const v
                                            uint32_t heads, uint32_t kv_heads, int out_dtype,
                                            int causal, float scale, const uint16_t *q_norm_w,
                                            float eps, float theta, int *status, void *stream) {
-  if (!q || !k || !v || !lengths || !lengths_host || !out) return TX_EINVAL;
+  // The status word is required: a bounded wait that gives up is reported only there.
+  if (!q || !k || !v || !lengths || !lengths_host || !out || !status) return TX_EINVAL;
   if (out_dtype != TX_F32 && out_dtype != TX_BF16) return TX_EINVAL;
   if (!batch || !seq || !(scale > 0.f) || !(scale < 1e30f)) return TX_EINVAL;
   if ((uint64_t)batch * seq > 0xffffffffull) return TX_EINVAL;
@@ -72,6 +73,9 @@ extern "C" int tx_attention_padded_noalloc(const void *q, const void *k, const v
     // One-time set-up for this device (the caller's current device).
     void *ptr = nullptr;
     if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return TX_ECUDA;
+    // Loads the kernel's module now (with lazy module loading its code would otherwise be
+    // placed in device memory at the first launch, a later allocation).
+    if (tx::tc_preload() != cudaSuccess) return TX_ECUDA;
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
       return TX_ECUDA;
@@ -80,7 +84,7 @@ extern "C" int tx_attention_padded_noalloc(const void *q, const void *k, const v
   }
   uint32_t *scratch = g_noalloc_ptr[device];
   cudaStream_t s = (cudaStream_t)stream;
-  int *st = status ? status : (int *)scratch;
+  int *st = status;
   const int sms = g_noalloc_sms[device];
   if (sms < 1 || tx::tc_grid(tx::tc_max_units(p), sms) + 1 > kNoAllocMaxOffsets) return TX_EINVAL;
   // tc_build_units sorts and balances with fixed-size arrays on the stack and the static
@@ -93,6 +97,6 @@ extern "C" int tx_attention_padded_noalloc(const void *q, const void *k, const v
                            cudaMemcpyHostToDevice, s) != cudaSuccess)
     return TX_ECUDA;
   cudaError_t e = tx::launch_attention_tc(p, scratch + kHeaderWords, n, sms, st, q_norm_w, eps,
-                                          theta, s);
+                                          theta, s, /*after_prologue=*/false, /*wait_cycles=*/0);
   return e == cudaSuccess ? TX_OK : TX_ECUDA;
 }

@@ -21,7 +21,7 @@
 
 namespace {
 
-constexpr uint32_t kAbiVersion = 3;
+constexpr uint32_t kAbiVersion = 4;
 constexpr uint32_t kHostChunks = 8;              // most chunks of a host-buffer call
 constexpr size_t kHostChunkBytes = 16u << 20;     // bytes moved per chunk, at least
 
@@ -62,8 +62,12 @@ struct Ctx {
   uint32_t units_count = 0;
   cudaEvent_t scratch_done = nullptr;  // last launch that read scratch
   std::set<Buf *> buffers;
+  // Accounting of the buffers above: bytes live now, the most ever live at once, and
+  // the number and bytes of every allocation made.
+  uint64_t mem_live = 0, mem_peak = 0, mem_allocs = 0, mem_alloc_bytes = 0;
   const char *last_kernel = "";
   uint64_t launches = 0;  // kernels this context has launched
+  long long wait_cycles = 0;  // bounded-wait limit of the tensor-core kernel (0: default)
   // host-buffer entry points: device copies of the caller's arrays, a copy-in and a
   // copy-out stream beside `stream`, and an event pair per chunk
   void *hp_mem = nullptr;
@@ -283,9 +287,11 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
   }
 
   if (tc_path) {
+    // pro_k: the k prologue was the launch just before on this stream.
     if ((e = tx::launch_attention_tc(p, units_dev ? units_dev : c->units,
-                                     units_dev ? units_n : c->units_count, c->sms, c->status, tc_q_w, eps,
-                                     theta, stream)) != cudaSuccess)
+                                     units_dev ? units_n : c->units_count, c->sms, c->status,
+                                     tc_q_w, eps, theta, stream, pro_k, c->wait_cycles)) !=
+        cudaSuccess)
       return cuda_fail(c, e, "attention launch");
     c->last_kernel = "tc_bf16_d128";
     ++c->launches;
@@ -471,8 +477,8 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
     const size_t r0 = row_of(first[i]), r1 = row_of(first[i + 1]), n = r1 - r0;
     // k and v rows of the chunk.  Padded layout: only each sequence's valid rows cross the
     // link (a run of full sequences in one copy); its rows at or past the length are never
-    // attended (their keys are masked) and are zeroed on the device by a kernel on the
-    // compute stream instead, so the masked products stay exact zeros.
+    // attended, and every kernel either skips them or clears them on chip, so the device
+    // rows there may hold whatever an earlier call left.
     auto copy_kv = [&](size_t region, const uint8_t *h) -> cudaError_t {
       if (cu)
         return cudaMemcpyAsync(dev + region + r0 * kvrow, h + r0 * kvrow, n * kvrow,
@@ -494,11 +500,7 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
                              cudaMemcpyHostToDevice, c->hp_up)) != cudaSuccess ||
         (e = copy_kv(ok, hk)) != cudaSuccess || (e = copy_kv(ov, hv)) != cudaSuccess ||
         (e = cudaEventRecord(c->hp_ev[2 * i], c->hp_up)) != cudaSuccess ||
-        (e = cudaStreamWaitEvent(c->stream, c->hp_ev[2 * i], 0)) != cudaSuccess ||
-        (!cu && (e = tx::launch_zero_padded_rows(dev + ok + r0 * kvrow, dev + ov + r0 * kvrow,
-                                                 (const uint32_t *)(dev + om) + first[i],
-                                                 first[i + 1] - first[i], p.seq, kvrow,
-                                                 c->stream)) != cudaSuccess)) {
+        (e = cudaStreamWaitEvent(c->stream, c->hp_ev[2 * i], 0)) != cudaSuccess) {
       drain();
       return cuda_fail(c, e, "copy in");
     }
@@ -633,6 +635,15 @@ const char *tx_last_error(void *ctx) {
 
 int tx_device_sms(void *ctx) { return ctx ? ((Ctx *)ctx)->sms : 0; }
 
+int tx_set_wait_limit(void *ctx, int64_t cycles) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (cycles < 0) return fail(c, TX_EINVAL, "wait limit must be >= 0");
+  c->wait_cycles = (long long)cycles;
+  return TX_OK;
+}
+
 const char *tx_last_kernel(void *ctx) { return ctx ? ((Ctx *)ctx)->last_kernel : ""; }
 
 uint64_t tx_launch_count(void *ctx) { return ctx ? ((Ctx *)ctx)->launches : 0; }
@@ -660,6 +671,10 @@ void *tx_buffer(void *ctx, const void *host, uint64_t size) {
   }
   Buf *b = new Buf{c, d, size};
   c->buffers.insert(b);
+  c->mem_live += size;
+  c->mem_peak = std::max(c->mem_peak, c->mem_live);
+  ++c->mem_allocs;
+  c->mem_alloc_bytes += size;
   return b;
 }
 
@@ -673,7 +688,19 @@ void tx_free(void *buffer) {
   cudaStreamSynchronize(c->stream);
   cudaFree(b->dev);
   c->buffers.erase(b);
+  c->mem_live -= b->size;
   delete b;
+}
+
+int tx_memory_stats(void *ctx, uint64_t *out) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c || !out) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  out[0] = c->mem_live;
+  out[1] = c->mem_peak;
+  out[2] = c->mem_allocs;
+  out[3] = c->mem_alloc_bytes;
+  return TX_OK;
 }
 
 int tx_read(void *buffer, void *out, uint64_t bytes) {

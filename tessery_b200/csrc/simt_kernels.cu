@@ -519,37 +519,6 @@ static cudaError_t launch_rows_pass(const void *in, void *out, const uint16_t *w
   }
 }
 
-// Block (s, y) clears its share of sequence s's rows past the length, 16 bytes per store
-// when the row size allows it.
-__global__ void zero_padded_rows_kernel(uint8_t *a, uint8_t *b, const uint32_t *lengths,
-                                        uint32_t seq, size_t row_bytes) {
-  const uint32_t s = blockIdx.x;
-  const uint32_t len = min(lengths[s], seq);
-  const size_t start = ((size_t)s * seq + len) * row_bytes, bytes = (size_t)(seq - len) * row_bytes;
-  const size_t step = (size_t)blockDim.x * gridDim.y;
-  const size_t first = threadIdx.x + (size_t)blockIdx.y * blockDim.x;
-  if (row_bytes % 16 == 0) {
-    for (size_t i = first; i < bytes / 16; i += step) {
-      reinterpret_cast<uint4 *>(a + start)[i] = make_uint4(0, 0, 0, 0);
-      if (b) reinterpret_cast<uint4 *>(b + start)[i] = make_uint4(0, 0, 0, 0);
-    }
-  } else {
-    for (size_t i = first; i < bytes; i += step) {
-      a[start + i] = 0;
-      if (b) b[start + i] = 0;
-    }
-  }
-}
-
-cudaError_t launch_zero_padded_rows(void *a, void *b, const uint32_t *lengths, uint32_t batch,
-                                    uint32_t seq, size_t row_bytes, cudaStream_t stream) {
-  if (!batch || !seq || !row_bytes) return cudaSuccess;
-  if (batch > 0x7fffffffu) return cudaErrorInvalidValue;
-  zero_padded_rows_kernel<<<dim3(batch, 4), 256, 0, stream>>>((uint8_t *)a, (uint8_t *)b, lengths,
-                                                              seq, row_bytes);
-  return cudaGetLastError();
-}
-
 cudaError_t launch_qk_norm_rope(const PrologueProblem &problem, cudaStream_t stream) {
   if (!problem.tokens || (!problem.q && !problem.k)) return cudaSuccess;
   if (problem.dim > 256) return cudaErrorInvalidValue;

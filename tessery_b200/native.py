@@ -16,7 +16,7 @@ from typing import Any
 
 from .errors import NativeBuildError
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 LIBRARY_NAME = "libtessattn.so"
 
 TX_OK, TX_EINVAL, TX_ECUDA, TX_ETIMEOUT = 0, 1, 2, 3
@@ -30,10 +30,12 @@ SIGNATURES: dict[str, tuple[list[Any], Any]] = {
     "tx_destroy": ([_vp], None),
     "tx_last_error": ([_vp], ct.c_char_p),
     "tx_device_sms": ([_vp], _i32),
+    "tx_set_wait_limit": ([_vp, ct.c_int64], _i32),
     "tx_last_kernel": ([_vp], ct.c_char_p),
     "tx_launch_count": ([_vp], _u64),
     "tx_buffer": ([_vp, _vp, _u64], _vp),
     "tx_free": ([_vp], None),
+    "tx_memory_stats": ([_vp, ct.POINTER(_u64)], _i32),
     "tx_read": ([_vp, _vp, _u64], _i32),
     "tx_write": ([_vp, _vp, _u64], _i32),
     "tx_buffer_device_ptr": ([_vp], _vp),

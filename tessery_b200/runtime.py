@@ -11,7 +11,6 @@ packing, the fused q/k prologue).  NumPy in, NumPy out; no PyTorch dependency.
 from __future__ import annotations
 
 import ctypes as ct
-import struct
 import threading
 from collections import Counter
 from collections.abc import Iterator, Sequence
@@ -51,21 +50,14 @@ def _raise_for(rc: int) -> None:
 
 
 class Buffer:
-    """Owned device buffer (counterpart of metal.py:94-119)."""
+    """Handle of one device allocation made by the native context (the role of
+    metal.py:94-119's Buffer).  The context owns the memory and its accounting
+    (tx_memory_stats); this object only names the allocation for the Python side."""
 
-    def __init__(self, runtime: CudaRuntime, size: int, data: NDArray[Any] | None) -> None:
+    def __init__(self, runtime: CudaRuntime, handle: int, size: int) -> None:
         self.runtime = runtime
+        self.pointer: int | None = handle
         self.size = size
-        self.pointer: int | None = runtime._lib.tx_buffer(
-            runtime._pointer, None if data is None else data.ctypes.data, size
-        )
-        if not self.pointer:
-            raise InferenceError()
-        runtime.active_bytes += size
-        runtime._allocations += 1
-        runtime._allocated_bytes += size
-        runtime.peak_bytes = max(runtime.peak_bytes, runtime.active_bytes)
-        runtime._buffers.add(self)
 
     @property
     def device_ptr(self) -> int:
@@ -80,17 +72,53 @@ class Buffer:
         _raise_for(self.runtime._lib.tx_write(self.pointer, data.ctypes.data, data.nbytes))
 
     def close(self) -> None:
-        with self.runtime._lock:
-            if getattr(self, "pointer", None):
-                self.runtime._lib.tx_free(self.pointer)
-                self.pointer = None
-                self.runtime.active_bytes -= self.size
+        handle, self.pointer = self.pointer, None
+        if handle:
+            with self.runtime._lock:
+                self.runtime._lib.tx_free(handle)
 
     def __del__(self) -> None:
         try:
             self.close()
         except Exception:
             pass
+
+
+class _Params(ct.Structure):
+    """The 64-byte kernel parameter block of kernels.metal:5-8 (twelve uint32, four
+    float), laid out field by field as the library's Params64 reads it."""
+
+    _fields_ = [(name, ct.c_uint32) for name in (
+        "n", "rows", "cols", "k", "heads", "kv_heads", "seq", "batch", "dim", "group",
+        "bidirectional", "first_token")] + [
+        (name, ct.c_float) for name in ("eps", "theta", "scale", "reserved")]
+
+
+class _Command:
+    """One open command: what was dispatched into it, for the profile and the counters.
+    Closing it either commits (tx_finish) or discards (tx_abort) the queued work."""
+
+    def __init__(self, runtime: CudaRuntime) -> None:
+        self.runtime = runtime
+        self.log: list[dict[str, Any]] = []
+
+    def commit(self) -> None:
+        rt = self.runtime
+        _raise_for(rt._lib.tx_finish(rt._pointer))
+        if rt._profile is not None:
+            seconds = (ct.c_double * len(self.log))()
+            if rt._lib.tx_profile_read(rt._pointer, seconds, len(self.log)) != native.TX_OK:
+                raise InferenceError()
+            for entry, t in zip(self.log, seconds, strict=True):
+                rt._profile.append({**entry, "gpu_seconds": float(t)})
+        rt._commands += 1
+        t = rt._lib.tx_gpu_seconds(rt._pointer)
+        if t >= 0:
+            rt._gpu_seconds += t
+            rt._gpu_samples += 1
+
+    def discard(self) -> None:
+        self.runtime._lib.tx_abort(self.runtime._pointer)
 
 
 class CudaRuntime:
@@ -103,19 +131,14 @@ class CudaRuntime:
             raise CudaUnavailableError()
         self.device = device
         self._lock = threading.RLock()
-        self._recording = False
+        self._open: _Command | None = None
         self._buffers: WeakSet[Buffer] = WeakSet()
         self._workspace: dict[str, Buffer] = {}
-        self.active_bytes = 0
-        self.peak_bytes = 0
-        self._allocations = 0
-        self._allocated_bytes = 0
         self._commands = 0
         self._gpu_samples = 0
         self._gpu_seconds = 0.0
         self._dispatches: Counter[str] = Counter()
         self._profile: list[dict[str, Any]] | None = None
-        self._profile_command: list[dict[str, Any]] = []
 
     # ---- bookkeeping ------------------------------------------------------------------
     @property
@@ -131,23 +154,47 @@ class CudaRuntime:
         """Kernels launched by this runtime's context so far."""
         return int(self._lib.tx_launch_count(self._pointer))
 
+    def set_wait_limit(self, cycles: int) -> None:
+        """Limit, in SM clock cycles, of each bounded wait of the tensor-core kernel
+        (0 restores the default, about a second).  A wait that runs out is reported as
+        DeviceTimeoutError by the next sync; the runtime stays usable."""
+        self._check_open()
+        _raise_for(self._lib.tx_set_wait_limit(self._pointer, int(cycles)))
+
     def last_error(self) -> str:
         raw = self._lib.tx_last_error(self._pointer)
         return raw.decode() if raw else ""
 
+    def _memory(self) -> tuple[int, int, int, int]:
+        """(live bytes, peak live bytes, allocations, allocated bytes) of the context."""
+        stats = (ct.c_uint64 * 4)()
+        if not self._pointer or self._lib.tx_memory_stats(self._pointer, stats) != native.TX_OK:
+            return (0, 0, 0, 0)
+        return tuple(int(x) for x in stats)  # type: ignore[return-value]
+
+    @property
+    def active_bytes(self) -> int:
+        return self._memory()[0]
+
+    @property
+    def peak_bytes(self) -> int:
+        return self._memory()[1]
+
     def diagnostics(self) -> dict[str, Any]:
+        """Counters under the key names of MetalRuntime.diagnostics (metal.py:208-234)."""
         with self._lock:
+            live, peak, count, total = self._memory()
             return {
                 "native_library_sha256": self._lib._tessery_sha256,
                 "native_library_path": self._lib._tessery_path,
-                "allocations": self._allocations,
-                "allocated_bytes": self._allocated_bytes,
+                "allocations": count,
+                "allocated_bytes": total,
                 "completed_commands": self._commands,
                 "gpu_timed_commands": self._gpu_samples,
                 "gpu_seconds": self._gpu_seconds,
                 "dispatches": dict(self._dispatches),
-                "active_bytes": self.active_bytes,
-                "peak_bytes": self.peak_bytes,
+                "active_bytes": live,
+                "peak_bytes": peak,
             }
 
     def _check_open(self) -> None:
@@ -156,18 +203,26 @@ class CudaRuntime:
 
     # ---- buffers (metal.py:354-373, 650-662) -------------------------------------------
     def buffer(self, size: int, data: NDArray[Any] | None = None) -> Buffer:
+        """A device buffer of `size` bytes, filled from `data` (C-contiguous, exactly
+        `size` bytes) or with zeros."""
+        size_ok = type(size) is int and 0 < size <= 2**40
+        data_ok = data is None or (data.flags.c_contiguous and data.nbytes == size)
+        if not (size_ok and data_ok):
+            raise InvalidInputError()
         with self._lock:
             self._check_open()
-            if type(size) is not int or not 0 < size <= 2**40:
-                raise InvalidInputError()
-            if data is not None and (not data.flags.c_contiguous or data.nbytes != size):
-                raise InvalidInputError()
-            return Buffer(self, size, data)
+            source = None if data is None else data.ctypes.data
+            handle = self._lib.tx_buffer(self._pointer, source, size)
+            if not handle:
+                raise InferenceError()
+            made = Buffer(self, handle, size)
+            self._buffers.add(made)
+            return made
 
     def read(self, buffer: Buffer, shape: tuple[int, ...], dtype=np.float32) -> NDArray[Any]:
         with self._lock:
             self._check_open()
-            if self._recording or buffer.runtime is not self or not buffer.pointer:
+            if self._open is not None or buffer.runtime is not self or not buffer.pointer:
                 raise InferenceError()
             result = np.empty(shape, dtype=dtype)
             if result.nbytes != buffer.size:
@@ -190,55 +245,45 @@ class CudaRuntime:
     # ---- commands (metal.py:375-414) --------------------------------------------------
     @contextmanager
     def command(self) -> Iterator[None]:
+        """Brackets dispatches into one stream-ordered command.  A clean exit waits for
+        the command and raises its error, if any; an exception discards it."""
         with self._lock:
             self._check_open()
-            if self._recording:
+            if self._open is not None:
                 raise InferenceError()
-            if self._lib.tx_begin(self._pointer):
-                self._lib.tx_abort(self._pointer)
+            if self._lib.tx_begin(self._pointer) != native.TX_OK:
                 raise InferenceError()
-            self._recording = True
-            self._profile_command.clear()
+            current = self._open = _Command(self)
             try:
                 yield
-                rc = self._lib.tx_finish(self._pointer)
-                if rc:
-                    _raise_for(rc)
-                if self._profile is not None:
-                    timings = (ct.c_double * len(self._profile_command))()
-                    if self._lib.tx_profile_read(self._pointer, timings, len(timings)):
-                        raise InferenceError()
-                    self._profile.extend(
-                        dict(record, gpu_seconds=float(seconds))
-                        for record, seconds in zip(self._profile_command, timings, strict=True)
-                    )
-                self._commands += 1
-                gpu_seconds = self._lib.tx_gpu_seconds(self._pointer)
-                if gpu_seconds >= 0:
-                    self._gpu_seconds += gpu_seconds
-                    self._gpu_samples += 1
+            except BaseException:
+                current.discard()
+                raise
+            else:
+                try:
+                    current.commit()
+                except BaseException:
+                    current.discard()
+                    raise
             finally:
-                self._lib.tx_abort(self._pointer)
-                self._recording = False
-                self._profile_command.clear()
+                self._open = None
 
     @contextmanager
     def profile_kernels(self) -> Iterator[list[dict[str, Any]]]:
-        """Per-dispatch device timings (CUDA events), counterpart of metal.py:236-258."""
+        """Per-dispatch device timings (CUDA events), counterpart of metal.py:236-258:
+        one record per dispatch of the commands run inside the block."""
         with self._lock:
             self._check_open()
-            if self._recording or self._profile is not None:
+            if self._open is not None or self._profile is not None:
                 raise InferenceError()
-            if self._lib.tx_profile_enable(self._pointer, 1):
+            if self._lib.tx_profile_enable(self._pointer, 1) != native.TX_OK:
                 raise InferenceError()
-            records: list[dict[str, Any]] = []
-            self._profile = records
+            self._profile = records = []
             try:
                 yield records
             finally:
-                self._lib.tx_profile_enable(self._pointer, 0)
                 self._profile = None
-                self._profile_command.clear()
+                self._lib.tx_profile_enable(self._pointer, 0)
 
     # ---- kernel routing (metal.py:532-648) ----------------------------------------------
     def _attention(
@@ -296,26 +341,24 @@ class CudaRuntime:
         bidirectional: int = 0,
         first_token: int = 0,
     ) -> None:
-        if not self._recording or any(not b.pointer or b.runtime is not self for b in buffers):
+        current = self._open
+        if current is None:
             raise InferenceError()
-        parameters = struct.pack(
-            "<12I4f",
-            n, rows, cols, k, heads, kv_heads, seq, batch, dim, group,
-            int(bidirectional), int(first_token), eps, theta, scale, 0.0,
-        )
-        pointers = (ct.c_void_p * len(buffers))(*(b.pointer for b in buffers))
-        rc = self._lib.tx_dispatch(
-            self._pointer, name.encode("ascii"), pointers, len(buffers), parameters,
-            len(parameters), threads, group_size,
-        )
-        if rc:
-            _raise_for(rc)
+        handles = []
+        for b in buffers:
+            if b.runtime is not self or not b.pointer:
+                raise InferenceError()
+            handles.append(b.pointer)
+        block = _Params(n=n, rows=rows, cols=cols, k=k, heads=heads, kv_heads=kv_heads, seq=seq,
+                        batch=batch, dim=dim, group=group, bidirectional=int(bidirectional),
+                        first_token=int(first_token), eps=eps, theta=theta, scale=scale)
+        slots = (ct.c_void_p * max(len(handles), 1))(*handles)
+        _raise_for(self._lib.tx_dispatch(self._pointer, name.encode("ascii"), slots, len(handles),
+                                         ct.addressof(block), ct.sizeof(block), threads,
+                                         group_size))
         self._dispatches[name] += 1
-        if self._profile is not None:
-            self._profile_command.append(
-                {"kernel": name, "rows": rows, "cols": cols, "seq": seq, "heads": heads,
-                 "threads": threads}
-            )
+        current.log.append({"kernel": name, "rows": rows, "cols": cols, "seq": seq,
+                            "heads": heads, "threads": threads})
 
     # ---- typed entry points (host arrays) ------------------------------------------------
     def attention_host(
@@ -513,7 +556,7 @@ class CudaRuntime:
     # ---- lifecycle ----------------------------------------------------------------------
     def close(self) -> None:
         with self._lock:
-            if self._recording or self._profile is not None:
+            if self._open is not None or self._profile is not None:
                 raise InferenceError()
             if self._pointer:
                 for buffer in list(self._buffers):

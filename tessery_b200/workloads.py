@@ -182,3 +182,35 @@ def short_tails(kind: str = "qwen", batch: int = 32, seed: int = 4, lo: int = 2,
     return Workload(f"{kind}_short_tails", "varlen", q, k, v, heads, kv, dim, causal,
                     dim**-0.5, "bf16", int(lengths.max()), cu_seqlens=cu, q_norm_weight=q_w,
                     k_norm_weight=k_w, seed=seed)
+
+
+def benchmark_workload(name: str, rank: int = 0, world: int = 1,
+                       scaled_batch: int = 4096) -> Workload:
+    """The seeded input of one benchmark workload as rank `rank` of `world` sees it.
+
+    qwen_padded: 32 sequences per rank, lengths ~ U[32, 512] from seed 2 over all ranks,
+    assigned longest first; qwen_varlen: the 256 log-normal sequences of seed 3, split
+    across the ranks; bge / bge_scaled: batch 4 / `scaled_batch`, seed 1; tails_qwen /
+    tails_bge: 32 sequences of U[2, 32], seed 4.  Ranks other than 0 draw their tensors
+    from seed + 1000 * rank.
+    """
+    from .partition import shard_sequences
+
+    if name == "qwen_padded":
+        lengths = np.random.default_rng(2).integers(32, 513, size=32 * world)
+        owned = shard_sequences(lengths, world, causal=True)[rank]
+        return qwen_padded(batch=len(owned), seq=512, seed=2 + 1000 * rank,
+                           lengths=lengths[owned])
+    if name == "qwen_varlen":
+        lengths = varlen_lengths(256, 3)
+        owned = shard_sequences(lengths, world, causal=True)[rank]
+        return qwen_varlen(seed=3 + 1000 * rank, lengths=lengths[owned])
+    if name == "bge":
+        return bge(batch=4, seq=128, seed=1 + 1000 * rank)
+    if name == "bge_scaled":
+        return bge(batch=scaled_batch, seq=128, seed=1 + 1000 * rank)
+    if name == "tails_qwen":
+        return short_tails("qwen", batch=32, seed=4 + 1000 * rank)
+    if name == "tails_bge":
+        return short_tails("bge", batch=32, seed=4 + 1000 * rank)
+    raise ValueError(name)

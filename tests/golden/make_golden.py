@@ -1,8 +1,9 @@
 """Generates the golden fixtures that pin the CPU oracle to the reference.
 
-Runs in a container where the reference project is mounted (default
-/root/reference, override with TESSERY_REFERENCE).  It imports the reference's own
-kernel test module (tests/real_metal/test_kernels.py) and calls its attention, RoPE,
+Runs where the reference project's source tree is available; its root directory is
+given as the first argument or in the TESSERY_REFERENCE environment variable.  It
+imports the reference's own kernel test module (tests/real_metal/test_kernels.py) and
+calls its attention, RoPE,
 RMSNorm and pooling tests, unmodified and with their own seeds, grids and tolerances,
 against a fake runtime whose kernels are computed by ``oracle``.  Every
 ``numpy.testing.assert_allclose`` the reference tests make is intercepted to record the
@@ -15,7 +16,7 @@ expected values (flat indices + float64 values), their moments, and the oracle's
 abs deviation.  The GPU tests regenerate the inputs, check the hashes, and compare the
 CUDA output with these samples and with the oracle.
 
-Usage: python tests/golden/make_golden.py
+Usage: python tests/golden/make_golden.py <reference project root>
 """
 
 from __future__ import annotations
@@ -35,7 +36,13 @@ sys.path.insert(0, str(REPO))
 
 import oracle  # noqa: E402
 
-REFERENCE = Path(os.environ.get("TESSERY_REFERENCE", "/root/reference"))
+def reference_root() -> Path:
+    """The reference project's root: argv[1], else $TESSERY_REFERENCE."""
+    given = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TESSERY_REFERENCE")
+    if not given:
+        sys.exit("usage: make_golden.py <reference project root> (or set TESSERY_REFERENCE)")
+    return Path(given)
+
 OUT = Path(__file__).resolve().parent / "reference_kernels.npz"
 SAMPLES = 512
 
@@ -129,8 +136,9 @@ class OracleEngine:
 
 
 def load_reference_tests():
-    sys.path.insert(0, str(REFERENCE / "src"))
-    path = REFERENCE / "tests" / "real_metal" / "test_kernels.py"
+    root = reference_root()
+    sys.path.insert(0, str(root / "src"))
+    path = root / "tests" / "real_metal" / "test_kernels.py"
     spec = importlib.util.spec_from_file_location("reference_test_kernels", path)
     module = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(module)

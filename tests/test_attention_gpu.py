@@ -2,7 +2,7 @@
 
 Tolerances (written here, per path):
   float32 kernels        : the reference's own gate, atol 2e-6 / rtol 2e-5 vs float64,
-                           and <= 1e-4 max abs at BASELINE sizes.
+                           and <= 1e-4 max abs at the benchmark sizes.
   bf16 in / fp32 accum   : <= 2e-2 max abs vs a float64 oracle fed the same
                            bf16-rounded inputs (prologue computed in float64).
 """
@@ -337,8 +337,9 @@ def test_tensor_core_any_gqa_group(runtime, heads, kv_heads):
 
 
 def test_full_size_qwen_properties(runtime):
-    """BASELINE config 2 at full size: spot-check sequences against the oracle, and
-    size-independent properties (padded == varlen on valid rows, determinism)."""
+    """The padded Qwen benchmark shape at full size (32 x 512): size-independent
+    properties (padded == varlen on valid rows, determinism) and spot sequences against
+    the oracle (every sequence is checked in test_full_configs_gpu.py)."""
     w = workloads.qwen_padded(seed=2)
     got = run_workload(runtime, w)
     again = run_workload(runtime, w)
@@ -494,3 +495,125 @@ def test_composed_prologue_matches_one_call(runtime):
     assert np.array_equal(got, one_call)
     for b in list(bufs.values()) + [kn, out]:
         b.close()
+
+
+# ---- padded k/v rows hold anything ---------------------------------------------------------
+def _poison_padding(a, lengths, value):
+    """Sets rows at positions >= length of a padded [B, L, H, d] array to `value`."""
+    a = a.copy()
+    for b, n in enumerate(lengths):
+        a[b, int(n):] = value
+    return a
+
+
+def _padded_device_call(rt, q, k, v, lengths, *, in_dtype, causal, scale, qw=None, kw=None):
+    B, L, H, D = q.shape
+    arrays = [np.ascontiguousarray(a) for a in (q, k, v, lengths.astype(np.uint32))]
+    bufs = [rt.buffer(a.nbytes, a) for a in arrays]
+    wbufs = [rt.buffer(w.nbytes, np.ascontiguousarray(w)) for w in (qw, kw) if w is not None]
+    out = rt.buffer(q.size * 4)
+    try:
+        extra = {}
+        if qw is not None:
+            extra = dict(q_norm_weight=wbufs[0].device_ptr, k_norm_weight=wbufs[1].device_ptr)
+        rt.attention_padded_device(*(b.device_ptr for b in bufs), out.device_ptr, batch=B,
+                                   seq=L, heads=H, kv_heads=k.shape[2], dim=D,
+                                   in_dtype=in_dtype, out_dtype=TX_F32, causal=causal,
+                                   scale=scale, lengths_host=arrays[3], **extra)
+        rt.sync()
+        return rt.read(out, q.shape)
+    finally:
+        for b in [*bufs, *wbufs, out]:
+            b.close()
+
+
+@pytest.mark.parametrize("route", ["tc_bf16_d128", "short_d128", "d32", "simt"])
+def test_padded_kv_rows_may_hold_nan_or_inf(runtime, route):
+    """k/v rows at or past a sequence's length hold NaN (k) and Inf (v): every route
+    returns the oracle's rows, all finite, as the reference, which never reads those rows
+    (kernels.metal:89-99)."""
+    rng = np.random.default_rng(71)
+    if route in ("tc_bf16_d128", "short_d128"):
+        L = 300 if route == "tc_bf16_d128" else 32
+        lengths = np.array([L, 129, 1, 200] if L == 300 else [32, 5, 17, 1])
+        w = workloads.qwen_padded(batch=4, seq=L, seed=72, lengths=lengths)
+        k = _poison_padding(w.k, lengths, np.uint16(0x7FC0))  # bf16 NaN
+        v = _poison_padding(w.v, lengths, np.uint16(0x7F80))  # bf16 +Inf
+        got = _padded_device_call(runtime, w.q, k, v, lengths, in_dtype=TX_BF16, causal=True,
+                                  scale=w.scale, qw=w.q_norm_weight, kw=w.k_norm_weight)
+        want = qwen_oracle(w)
+        gate = BF16_GATE
+    else:
+        D = 32 if route == "d32" else 64
+        lengths = np.array([128, 1, 70])
+        q, k, v = (rng.normal(size=(3, 128, 4, D)).astype(np.float32) for _ in range(3))
+        k = _poison_padding(k, lengths, np.float32(np.nan))
+        v = _poison_padding(v, lengths, np.float32(np.inf))
+        got = _padded_device_call(runtime, q, k, v, lengths, in_dtype=TX_F32, causal=False,
+                                  scale=D**-0.5)
+        want = oracle.attention_padded(q, k, v, lengths, False, D**-0.5)
+        gate = 1e-4
+    assert runtime.last_kernel() == route
+    assert np.isfinite(got).all()
+    assert np.max(np.abs(got - want)) <= gate
+
+
+def test_attention_reads_q_written_by_the_kernel_just_before(runtime):
+    """A kernel writes q (here the library's own prologue, into a fresh buffer) and the
+    attention call that reads it follows at once on the same stream, with no k prologue
+    in between: the attention kernel is then launched in plain stream order and sees q."""
+    w = workloads.qwen_padded(batch=3, seq=384, seed=73, lengths=np.array([384, 130, 2]))
+    rt = runtime
+    B, L, H, D = w.q.shape
+    bufs = {n: rt.buffer(a.nbytes, np.ascontiguousarray(a)) for n, a in
+            (("q", w.q), ("k", w.k), ("v", w.v), ("len", w.lengths.astype(np.uint32)),
+             ("qw", w.q_norm_weight), ("kw", w.k_norm_weight))}
+    qn, kn = rt.buffer(w.q.nbytes), rt.buffer(w.k.nbytes)
+    out = rt.buffer(w.q.size * 4)
+    try:
+        rt.qk_norm_rope_device(None, bufs["k"].device_ptr, None, kn.device_ptr, tokens=B * L,
+                               seq=L, heads=H, kv_heads=8, dim=D, q_norm_weight=None,
+                               k_norm_weight=bufs["kw"].device_ptr, in_dtype=TX_BF16,
+                               out_dtype=TX_BF16)
+        for _ in range(3):
+            rt.qk_norm_rope_device(bufs["q"].device_ptr, None, qn.device_ptr, None,
+                                   tokens=B * L, seq=L, heads=H, kv_heads=8, dim=D,
+                                   q_norm_weight=bufs["qw"].device_ptr, k_norm_weight=None,
+                                   in_dtype=TX_BF16, out_dtype=TX_BF16)
+            rt.attention_padded_device(qn.device_ptr, kn.device_ptr, bufs["v"].device_ptr,
+                                       bufs["len"].device_ptr, out.device_ptr, batch=B, seq=L,
+                                       heads=H, kv_heads=8, dim=D, in_dtype=TX_BF16,
+                                       out_dtype=TX_F32, causal=True, lengths_host=w.lengths)
+            rt.sync()
+            assert rt.last_kernel() == "tc_bf16_d128"
+            got = rt.read(out, w.q.shape)
+            assert np.max(np.abs(got - qwen_oracle(w))) <= BF16_GATE
+            rt.qk_norm_rope_device(bufs["v"].device_ptr, None, qn.device_ptr, None,
+                                   tokens=B * L, seq=L, heads=H, kv_heads=8, dim=D,
+                                   q_norm_weight=bufs["qw"].device_ptr, k_norm_weight=None,
+                                   in_dtype=TX_BF16, out_dtype=TX_BF16)  # scribble over q
+            rt.sync()
+    finally:
+        for b in [*bufs.values(), qn, kn, out]:
+            b.close()
+
+
+def test_device_wait_timeout_is_reported_and_context_recovers(runtime):
+    """With the bounded-wait limit set to one cycle, the first wait of the tensor-core
+    kernel that is not already satisfied gives up: the kernel drains its copies and
+    products and returns, the host sees DeviceTimeoutError, and the same context then
+    computes the right result with the default limit (counterpart of the status check of
+    mi_finish, runtime.mm:217-253)."""
+    from tessery_b200 import DeviceTimeoutError
+
+    w = workloads.qwen_padded(batch=2, seq=256, seed=74, lengths=np.array([256, 100]))
+    runtime.set_wait_limit(1)
+    try:
+        with pytest.raises(DeviceTimeoutError):
+            _device_path(runtime, w)
+        assert "timed out" in runtime.last_error()
+    finally:
+        runtime.set_wait_limit(0)
+    got = _device_path(runtime, w)
+    assert runtime.last_kernel() == "tc_bf16_d128"
+    assert np.max(np.abs(got - qwen_oracle(w))) <= BF16_GATE

@@ -33,12 +33,20 @@ def test_attention_route_and_grid(seq, dim, expected):
 
 
 def test_params_block_layout_matches_reference():
-    # metal.py:596-614 packs "<12I4f"; the library reads the same 64 bytes.
+    # metal.py:596-614 packs "<12I4f"; the runtime builds the same 64 bytes field by field.
+    import ctypes as ct
+
+    from tessery_b200.runtime import _Params
+
     block = struct.pack("<12I4f", 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 1, 0, 1e-6, 1e6, 0.125, 0.0)
     assert len(block) == 64
     fields = struct.unpack("<12I4f", block)
     assert fields[4:7] == (5, 6, 7) and fields[10] == 1
     assert fields[14] == pytest.approx(0.125)
+    ours = _Params(n=1, rows=2, cols=3, k=4, heads=5, kv_heads=6, seq=7, batch=8, dim=9,
+                   group=10, bidirectional=1, first_token=0, eps=1e-6, theta=1e6, scale=0.125)
+    assert ct.sizeof(ours) == 64
+    assert bytes(ours) == block
 
 
 def test_status_codes_map_to_stable_errors():
