@@ -253,7 +253,7 @@ int tx_pool_project(void *ctx, const void *x, int in_dtype, const uint32_t *leng
  * Path: the tensor-core kernel only (bf16 q/k/v on the current device, head_dim 128,
  * at most 64 query heads); q_norm_w (or NULL) applies the fused q RMSNorm + RoPE, while
  * k must already be normalised (tx_qk_norm_rope).  Its only scratch, the work list, is
- * a static device array of 32768 units (one unit = 128 query rows of a pair of query
+ * a static device array of 16384 units (one unit = 128 query rows of a pair of query
  * heads, or of one head when the query heads per kv head are odd:
  * batch * heads/2 (or heads) * ceil(seq/128) units); larger problems are rejected with
  * TX_EINVAL before any pointer is used.  The first call on a device looks up that array's

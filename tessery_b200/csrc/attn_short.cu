@@ -169,8 +169,8 @@ __global__ void __launch_bounds__(kThreads) attn_short_kernel(const __grid_const
         const float yb0 = x[u][2] * inv * __uint_as_float(wh[u] << 16);
         const float yb1 = x[u][3] * inv * __uint_as_float(wh[u] & 0xffff0000u);
         float s0, c0, s1, c1;
-        sincos_reduced((float)pos[u] * f0, &s0, &c0);
-        sincos_reduced((float)pos[u] * f1, &s1, &c1);
+        rope_sincos((float)pos[u] * f0, &s0, &c0);
+        rope_sincos((float)pos[u] * f1, &s1, &c1);
         x[u][0] = ya0 * c0 - yb0 * s0;
         x[u][2] = ya0 * s0 + yb0 * c0;
         x[u][1] = ya1 * c1 - yb1 * s1;

@@ -59,6 +59,7 @@
 #include "common.cuh"
 #include "kernels.h"
 
+
 namespace tx {
 namespace tc {
 
@@ -90,7 +91,7 @@ constexpr float kRescaleThreshold = 8.0f;        // log2 units
 // "b" = Q buffer.
 enum : uint32_t {
   kBarQFull = 0,                      // + b: the unit's Q tiles landed (TMA bytes)
-  kBarQReady = kBarQFull + 2,         // + b: Q tiles transformed (128 per head slot)
+  kBarQReady = kBarQFull + 2,         // + b: Q tiles transformed (256 arrivals)
   kBarQEmpty = kBarQReady + 2,        // + b: every Q.K^T reading the buffer ran (commit)
   kBarKVFull = kBarQEmpty + 2,        // + ring slot
   kBarKVEmpty = kBarKVFull + kStages,
@@ -119,23 +120,33 @@ enum : int {
 };
 
 // ---- unit encoding --------------------------------------------------------------------
-// bits 0..7 query tile, 8..13 head pair (or head), 14..31 sequence.
+// Sort key of a unit on the host: bits 0..7 query tile, 8..13 head pair (or head),
+// 14..31 sequence.
 __host__ __device__ __forceinline__ uint32_t encode_unit(uint32_t seq, uint32_t idx,
                                                          uint32_t tile) {
   return (seq << 14) | (idx << 8) | tile;
 }
+// A unit in the work list: two words.  With the lengths known on the host ("exact"):
+// x = tile | head pair << 8 | valid keys << 14, y = row of position 0 of the sequence,
+// so the kernel decodes a unit without reading the lengths.  Otherwise x = tile | head
+// pair << 8 and y = the sequence index, and the kernel reads the device lengths.
+__host__ __device__ __forceinline__ uint2 unit_words(uint32_t tile, uint32_t idx, uint32_t n,
+                                                    uint32_t y) {
+  return make_uint2(tile | (idx << 8) | (n << 14), y);
+}
 
 struct Params {
-  const uint32_t *units;    // work units, grouped by CTA
+  const uint2 *units;       // work units, grouped by CTA
   const uint32_t *offsets;  // CTA c runs units [offsets[c], offsets[c+1])
   uint32_t n_units;
+  int exact;                // units carry their valid keys and first row
   const uint32_t *lengths;  // padded
   const int32_t *cu;        // varlen (NULL for padded)
   void *out;
   uint32_t seq;             // padded L (rows per sequence)
   uint32_t heads, group;    // query heads; query heads per kv head
   uint32_t nh;              // heads per unit: 2 (pairs) or 1
-  int causal, out_bf16;
+  int causal;
   float scale_log2;
   int *status;
   const uint16_t *q_norm_w;  // fused q prologue when non-NULL
@@ -155,17 +166,21 @@ struct Unit {
   bool live;       // the tile holds rows to write
 };
 
-__device__ __forceinline__ Unit decode(const Params &p, uint32_t code) {
+__device__ __forceinline__ Unit decode(const Params &p, uint2 w) {
   Unit u;
-  uint32_t s = code >> 14, idx = (code >> 8) & 63u, t = code & 255u;
-  if (p.cu) {
-    int32_t a = p.cu[s], b = p.cu[s + 1];
+  const uint32_t idx = (w.x >> 8) & 63u, t = w.x & 255u;
+  if (p.exact) {
+    u.n = w.x >> 14;
+    u.tok0 = w.y;
+    u.rows = p.cu ? u.n : p.seq;
+  } else if (p.cu) {
+    const int32_t a = p.cu[w.y], b = p.cu[w.y + 1];
     u.tok0 = (uint32_t)a;
     u.n = b > a ? (uint32_t)(b - a) : 0u;
     u.rows = u.n;
   } else {
-    u.tok0 = s * p.seq;
-    u.n = min(p.lengths[s], p.seq);
+    u.tok0 = w.y * p.seq;
+    u.n = min(p.lengths[w.y], p.seq);
     u.rows = p.seq;
   }
   u.q0 = t * kQRows;
@@ -185,6 +200,26 @@ __device__ __forceinline__ uint32_t next_work(const Params &p, uint32_t from) {
     if (decode(p, p.units[ui]).nt) return ui;
   return p.n_units;
 }
+
+// Walks this CTA's units in order with the words of the next unit loaded one unit ahead,
+// so that the load's latency hides behind the current unit's work.
+struct UnitCursor {
+  uint32_t ui, end;
+  uint2 w;
+  __device__ __forceinline__ UnitCursor(const Params &p) {
+    ui = p.offsets[blockIdx.x];
+    end = p.offsets[blockIdx.x + 1];
+    w = ui < end ? p.units[ui] : make_uint2(0u, 0u);
+  }
+  __device__ __forceinline__ bool more() const { return ui < end; }
+  // The current unit; starts the load of the next one and advances.
+  __device__ __forceinline__ Unit take(const Params &p) {
+    const uint2 cur = w;
+    if (ui + 1 < end) w = p.units[ui + 1];
+    ++ui;
+    return decode(p, cur);
+  }
+};
 
 // ---- PTX wrappers ---------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
@@ -459,58 +494,92 @@ __device__ __forceinline__ uint32_t u4_at(const uint4 &v, int e) {
 }
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
-__device__ __forceinline__ void acc_squares(float (&ssq)[4], const uint4 &v) {
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const uint32_t x = u4_at(v, e);
-    ssq[e] = fmaf(bf16_lo(x), bf16_lo(x), ssq[e]);
-    ssq[e] = fmaf(bf16_hi(x), bf16_hi(x), ssq[e]);
-  }
-}
 
-// In-place q RMSNorm + RoPE of row r of one head's Q tile (`q_tile`: 128 rows x 128
-// bf16, two 64-column atoms, 128-byte swizzle).  Arithmetic per element follows
-// kernels.metal:53-74: x * inv * w, then the rotation of (element c, element c + 64)
-// by pos * inv_freq[c].  `w_s` is the shared-memory address of the bf16 weights.
-__device__ __forceinline__ void q_transform_row(uint32_t q_tile, uint32_t r, uint32_t pos,
-                                                uint32_t w_s, const float *inv_freq, float eps) {
-  const uint32_t sw = r & 7;
-  const uint32_t row = q_tile + r * 128;
-  float ssq[4] = {0.f, 0.f, 0.f, 0.f};
+// In-place q RMSNorm + RoPE of one half of row `row` in each of the `nh` head tiles of a
+// unit's Q buffer (`qbuf`: per head 128 rows x 128 bf16, two 64-column atoms, 128-byte
+// swizzle).  Half `half` covers rotation columns c in [32 half, 32 half + 32) and their
+// partners c + 64; lanes 2i and 2i+1 hold the two halves of one row and add their sums
+// of squares by shuffle, so the calling warp must run this with all lanes (`live` false
+// for a row that belongs to no output: the lane only takes part in the shuffle).
+// Per element pair this is kernels.metal:53-74 -- a = x_c * inv * w_c,
+// b = x_{c+64} * inv * w_{c+64}, then (a cos - b sin, a sin + b cos) with the angle
+// pos * inv_freq[c] -- regrouped as inv * (x_c (w_c cos) - x_{c+64} (w_{c+64} sin)) and
+// inv * (x_c (w_c sin) + x_{c+64} (w_{c+64} cos)), so that the four weighted sines and
+// cosines of a column are computed once for both heads.  `w_s` is the shared-memory
+// address of the bf16 weights.
+__device__ __forceinline__ void q_transform_half_row(uint32_t qbuf, uint32_t nh, uint32_t row,
+                                                     uint32_t half, uint32_t pos, bool live,
+                                                     uint32_t w_s, const float *inv_freq,
+                                                     float eps) {
+  const uint32_t sw = row & 7;
+  uint64_t inv2[2];
 #pragma unroll
-  for (int c = 0; c < 16; ++c)
-    acc_squares(ssq, ld_shared_v4(row + (c >> 3) * kQAtom + (((c & 7) ^ sw) << 4)));
-  const float inv = 1.0f / sqrtf(((ssq[0] + ssq[1]) + (ssq[2] + ssq[3])) / 128.0f + eps);
-  const uint64_t inv2 = f2(inv, inv);
+  for (uint32_t hd = 0; hd < 2; ++hd) {
+    uint64_t acc[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
+    if (live && hd < nh) {
+      const uint32_t ra = qbuf + hd * kQBytes + row * 128;
+#pragma unroll
+      for (uint32_t c = 0; c < 4; ++c) {
+        const uint32_t off = ((4 * half + c) ^ sw) << 4;
+        const uint4 lo = ld_shared_v4(ra + off), hi = ld_shared_v4(ra + kQAtom + off);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint64_t xl = bf16x2_f2(u4_at(lo, e)), xh = bf16x2_f2(u4_at(hi, e));
+          acc[0] = fma2(xl, xl, acc[0]);
+          acc[1] = fma2(xh, xh, acc[1]);
+        }
+      }
+    }
+    const float2 a0 = f2_unpack(acc[0]), a1 = f2_unpack(acc[1]);
+    float sum = (a0.x + a0.y) + (a1.x + a1.y);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    const float inv = 1.0f / sqrtf(sum / 128.0f + eps);
+    inv2[hd] = f2(inv, inv);
+  }
+  if (!live) return;
   const float fpos = (float)pos;
 #pragma unroll 1
-  for (int g = 0; g < 8; ++g) {  // 16-byte chunk g: columns 8g..8g+7 and 64+8g..
+  for (uint32_t c = 0; c < 4; ++c) {  // 16-byte chunk g: columns 8g..8g+7 and 64+8g..
+    const uint32_t g = 4 * half + c, off = (g ^ sw) << 4;
     float co[8], si[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sincos_reduced(fpos * inv_freq[8 * g + e], &si[e], &co[e]);
+    for (int e = 0; e < 8; ++e) rope_sincos(fpos * inv_freq[8 * g + e], &si[e], &co[e]);
     const uint4 wa = ld_shared_v4(w_s + 16 * g), wb = ld_shared_v4(w_s + 128 + 16 * g);
-    const uint4 lo = ld_shared_v4(row + ((g ^ sw) << 4));
-    const uint4 hi = ld_shared_v4(row + kQAtom + ((g ^ sw) << 4));
-    uint32_t out_lo[4], out_hi[4];
+    // Per column pair e (columns 8g+2e, 8g+2e+1): w_c cos, -w_p sin, w_c sin, w_p cos.
+    uint64_t fa[4], fb[4], fc[4], fd[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {  // columns c = 8g+2e, c+1 and their partners c+64, c+65
-      const uint64_t a = mul2(mul2(bf16x2_f2(u4_at(lo, e)), inv2), bf16x2_f2(u4_at(wa, e)));
-      const uint64_t b = mul2(mul2(bf16x2_f2(u4_at(hi, e)), inv2), bf16x2_f2(u4_at(wb, e)));
+    for (int e = 0; e < 4; ++e) {
+      const uint64_t wc = bf16x2_f2(u4_at(wa, e)), wp = bf16x2_f2(u4_at(wb, e));
       const uint64_t cs = f2(co[2 * e], co[2 * e + 1]), sn = f2(si[2 * e], si[2 * e + 1]);
-      const uint64_t nsn = f2(-si[2 * e], -si[2 * e + 1]);
-      const float2 ra = f2_unpack(fma2(a, cs, mul2(b, nsn)));  // a*cos - b*sin
-      const float2 rb = f2_unpack(fma2(a, sn, mul2(b, cs)));   // a*sin + b*cos
-      out_lo[e] = pack_bf16x2(ra.x, ra.y);
-      out_hi[e] = pack_bf16x2(rb.x, rb.y);
+      fa[e] = mul2(wc, cs);
+      fb[e] = mul2(wp, f2(-si[2 * e], -si[2 * e + 1]));
+      fc[e] = mul2(wc, sn);
+      fd[e] = mul2(wp, cs);
     }
-    st_shared_v4(row + ((g ^ sw) << 4), out_lo[0], out_lo[1], out_lo[2], out_lo[3]);
-    st_shared_v4(row + kQAtom + ((g ^ sw) << 4), out_hi[0], out_hi[1], out_hi[2], out_hi[3]);
+#pragma unroll
+    for (uint32_t hd = 0; hd < 2; ++hd) {
+      if (hd >= nh) break;
+      const uint32_t ra = qbuf + hd * kQBytes + row * 128;
+      const uint4 lo = ld_shared_v4(ra + off), hi = ld_shared_v4(ra + kQAtom + off);
+      uint32_t out_lo[4], out_hi[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint64_t xc = bf16x2_f2(u4_at(lo, e)), xp = bf16x2_f2(u4_at(hi, e));
+        const float2 ra2 = f2_unpack(mul2(fma2(xp, fb[e], mul2(xc, fa[e])), inv2[hd]));
+        const float2 rb2 = f2_unpack(mul2(fma2(xp, fd[e], mul2(xc, fc[e])), inv2[hd]));
+        out_lo[e] = pack_bf16x2(ra2.x, ra2.y);
+        out_hi[e] = pack_bf16x2(rb2.x, rb2.y);
+      }
+      st_shared_v4(ra + off, out_lo[0], out_lo[1], out_lo[2], out_lo[3]);
+      st_shared_v4(ra + kQAtom + off, out_hi[0], out_hi[1], out_hi[2], out_hi[3]);
+    }
   }
 }
 
-// exp2(x*sl - m) of one 32-key chunk of a row (0 for keys at or past `valid` when
-// kMasked), as 16 bf16 pairs; returns the chunk's sum.
-template <bool kMasked>
+// exp2(x*sl - m) of one 32-key chunk of a row (0 for keys at or past `valid`), as 16 bf16
+// pairs; returns the chunk's sum.  One code path for full and masked chunks: the kernel's
+// warp roles share each sub-partition's instruction cache, so smaller code runs faster
+// than a separate unmasked copy.
 __device__ __forceinline__ float exp_chunk(const uint32_t (&x)[32], int c, int valid, float sl,
                                            float m, uint32_t (&packed)[16]) {
   const uint64_t sl2 = f2(sl, sl), nm2 = f2(-m, -m);
@@ -520,10 +589,8 @@ __device__ __forceinline__ float exp_chunk(const uint32_t (&x)[32], int c, int v
     const int k0 = c * 32 + 2 * t;
     const float2 z = f2_unpack(fma2(f2_bits(x[2 * t], x[2 * t + 1]), sl2, nm2));
     float p0 = ex2(z.x), p1 = ex2(z.y);
-    if (kMasked) {
-      p0 = k0 < valid ? p0 : 0.f;
-      p1 = k0 + 1 < valid ? p1 : 0.f;
-    }
+    p0 = k0 < valid ? p0 : 0.f;
+    p1 = k0 + 1 < valid ? p1 : 0.f;
     sum[t & 1] = add2(sum[t & 1], f2(p0, p1));
     packed[t] = pack_bf16x2(p0, p1);
   }
@@ -531,9 +598,19 @@ __device__ __forceinline__ float exp_chunk(const uint32_t (&x)[32], int c, int v
   return (s0.x + s1.x) + (s0.y + s1.y);
 }
 
+// max(a, b, c) in one instruction.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // ---- the kernel -----------------------------------------------------------------------
 // 96 registers per thread: 18 warps put 5 warps on some SM sub-partition, whose 16K
 // registers then allow 102 each.
+// kOutBf16: bf16 output (else fp32), one instantiation each so that a launch carries
+// only its own epilogue.
+template <bool kOutBf16>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_k,
@@ -560,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int h = 0; h < 2; ++h) {
       mbar_init(bar(kBarQFull + h), 1);
-      mbar_init(bar(kBarQReady + h), 128 * nh);
+      mbar_init(bar(kBarQReady + h), 256);  // every thread of both aux warpgroups
       mbar_init(bar(kBarQEmpty + h), 1);
       mbar_init(bar(kBarSFull + h), 1);
       mbar_init(bar(kBarPFull + h), 128);
@@ -755,8 +832,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async();  // generic-proxy writes seen by the tensor core's reads
       __syncwarp();
     };
-    for (uint32_t ui = p.offsets[blockIdx.x]; ok && ui < p.offsets[blockIdx.x + 1]; ++ui) {
-      const Unit u = decode(p, p.units[ui]);
+    for (UnitCursor uc(p); ok && uc.more();) {
+      const Unit u = uc.take(p);
       if (!u.nt) continue;
       // Work unit k uses Q buffer k % 2 (fill k / 2 of that buffer).
       qbuf = units_done & 1;
@@ -812,9 +889,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tO = tS + 128;
     uint32_t tiles = 0, units_seen = 0;  // key tiles and work units processed
     bool ok = true;
-    for (uint32_t ui = p.offsets[blockIdx.x]; ok && h < nh && ui < p.offsets[blockIdx.x + 1];
-         ++ui) {
-      const Unit u = decode(p, p.units[ui]);
+    for (UnitCursor uc(p); ok && h < nh && uc.more();) {
+      const Unit u = uc.take(p);
       if (!u.nt) continue;
       const uint32_t qpos = u.q0 + r;
       const uint32_t end = p.causal ? min(qpos + 1, u.n) : u.n;
@@ -844,19 +920,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tS + half * 64, xa);
           tmem_ld32(tS + half * 64 + 32, xb);
           tmem_ld_wait();
-          if (valid >= kKeys) {
+          const float ninf = -INFINITY;
 #pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              mq[t & 1] = fmaxf(mq[t & 1], __uint_as_float(xa[t]));
-              mq[2 + (t & 1)] = fmaxf(mq[2 + (t & 1)], __uint_as_float(xb[t]));
-            }
-          } else {
-#pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              if (half * 64 + t < valid) mq[t & 1] = fmaxf(mq[t & 1], __uint_as_float(xa[t]));
-              if (half * 64 + 32 + t < valid)
-                mq[2 + (t & 1)] = fmaxf(mq[2 + (t & 1)], __uint_as_float(xb[t]));
-            }
+          for (int t = 0; t < 32; t += 2) {  // keys at or past `valid` do not count
+            const int ka = half * 64 + t, kb = ka + 32;
+            mq[t & 2 ? 1 : 0] = fmax3(mq[t & 2 ? 1 : 0],
+                                      ka < valid ? __uint_as_float(xa[t]) : ninf,
+                                      ka + 1 < valid ? __uint_as_float(xa[t + 1]) : ninf);
+            mq[t & 2 ? 3 : 2] = fmax3(mq[t & 2 ? 3 : 2],
+                                      kb < valid ? __uint_as_float(xb[t]) : ninf,
+                                      kb + 1 < valid ? __uint_as_float(xb[t + 1]) : ninf);
           }
         }
         const float mt = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * p.scale_log2;
@@ -900,8 +973,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tmem_ld32(tS + c * 32, x);
           tmem_ld_wait();
-          if (valid >= kKeys) l += exp_chunk<false>(x, c, valid, p.scale_log2, m_ref, packed);
-          else l += exp_chunk<true>(x, c, valid, p.scale_log2, m_ref, packed);
+          l += exp_chunk(x, c, valid, p.scale_log2, m_ref, packed);
           tmem_st16(tS + c * 16, packed);
         }
         tmem_st_wait();
@@ -915,10 +987,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++units_seen;
     }
   } else {
-    // ---------------- q prologue and epilogue (warpgroup h: head slot h; thread = row) -
+    // ---------------- q prologue and epilogue --------------------------------------------
+    // Warpgroup h transforms rows [64h, 64h + 64) of every head tile of the next unit (two
+    // lanes per row), then writes the epilogue of head slot h (thread = row = TMEM lane).
     const uint32_t h = (uint32_t)(warp - kEpiWarp0) >> 2;
     const uint32_t wq = (uint32_t)warp & 3;
     const uint32_t r = wq * 32 + lane;
+    const uint32_t xrow = 64 * h + (r >> 1), xhalf = r & 1;  // this thread's transform share
     const uint32_t lane_base = (wq * 32u) << 16;
     uint32_t lcount = 0;  // work units whose row sums were taken
     uint32_t tiles = 0;   // key tiles of the work units finished so far
@@ -926,8 +1001,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     const uint32_t srow = (uint32_t)lane * 128, sw = (uint32_t)lane & 7;
     const uint32_t stage0 = sbase + kOffStage + (h * 4 + wq) * kStageSlots * kChunkBytes;
-    // Wait for fill `phase` of buffer b, apply the q prologue to this head's tile, hand
-    // it to the issuer (which waits for every head slot).
+    // Wait for fill `phase` of buffer b, apply the q prologue to this thread's share of
+    // the unit's tiles, hand them to the issuer (which waits for all 256 threads).
     auto prepare = [&](uint32_t ui, uint32_t b, uint32_t phase) {
       ok = __all_sync(0xffffffffu, wait_phase(bar(kBarQFull + b), phase & 1, abort_flag,
                                               p.status, kSiteQFull, p.wait_cycles));
@@ -935,9 +1010,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.q_norm_w) {
         // Rows past the end of a packed sequence belong to no output: left as loaded.
         const Unit v = decode(p, p.units[ui]);
-        if (v.q0 + r < v.rows)
-          q_transform_row(sbase + kOffQ + b * kQBufBytes + h * kQBytes, r, v.q0 + r,
-                          smem_addr(qw_s), invf_s, p.eps);
+        q_transform_half_row(sbase + kOffQ + b * kQBufBytes, nh, xrow, xhalf, v.q0 + xrow,
+                             v.q0 + xrow < v.rows, smem_addr(qw_s), invf_s, p.eps);
         fence_proxy_async();
       }
       mbar_arrive(bar(kBarQReady + b));
@@ -984,7 +1058,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tO = tmem + lane_base + h * 256 + 128;
         const uint32_t head = v.head0 + h;
         const size_t orow = ((size_t)(v.tok0 + qpos) * p.heads + head) * 128;
-        if (!p.out_bf16) {
+        if (!kOutBf16) {
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {  // 32 fp32 columns = one 128-byte staging row
             uint32_t x[32];
@@ -1049,20 +1123,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // The q prologue of work unit 0, then per work unit k: the q prologue of work unit
     // k+1 (whose tiles the producer loaded while unit k-1 ran), then the epilogue of k.
-    uint32_t next = h < nh ? next_work(p, p.offsets[blockIdx.x]) : p.n_units;
+    // Both warpgroups transform every unit; a warpgroup whose head slot is unused (one
+    // head per unit) writes no epilogue.
+    const bool epi = h < nh;
+    uint32_t next = next_work(p, p.offsets[blockIdx.x]);
     if (next < p.n_units) prepare(next, 0, 0);
     next = next < p.n_units ? next_work(p, next + 1) : p.n_units;
     uint32_t k = 0;  // work units done
-    for (uint32_t ui = p.offsets[blockIdx.x]; ok && h < nh && ui < p.offsets[blockIdx.x + 1];
-         ++ui) {
-      const Unit u = decode(p, p.units[ui]);
+    for (UnitCursor uc(p); ok && uc.more();) {
+      const Unit u = uc.take(p);
       if (!u.live) continue;
       if (!u.nt) {
+        if (!epi) continue;
         // Zero valid keys: 0/0, as the reference's running sums give.
         const uint32_t qpos = u.q0 + r;
         if (qpos < u.rows) {
           const size_t orow = ((size_t)(u.tok0 + qpos) * p.heads + u.head0 + h) * 128;
-          if (p.out_bf16) {
+          if (kOutBf16) {
             uint16_t *o = (uint16_t *)p.out + orow;
             for (int c = 0; c < 128; ++c) o[c] = 0x7fc0u;
           } else {
@@ -1077,7 +1154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         next = next_work(p, next + 1);
       }
-      epilogue(u);
+      if (epi) epilogue(u);
       ++k;
     }
     if (lane == 0) bulk_wait_all();
@@ -1127,7 +1204,10 @@ uint32_t tc_grid(uint32_t n_units, int num_sms) {
 }
 
 uint32_t tc_work_words(const AttnProblem &p, int num_sms) {
-  return tc_max_units(p) + (uint32_t)std::max(num_sms, 1) + 1;
+  // Two words per unit, then the offsets; rounded to 16 bytes so that consecutive lists
+  // (one per chunk of a host-buffer call) keep their units 8-byte aligned.
+  const uint32_t w = 2 * tc_max_units(p) + (uint32_t)std::max(num_sms, 1) + 1;
+  return (w + 3) & ~3u;
 }
 
 namespace {
@@ -1195,7 +1275,8 @@ struct LoadHeap {
 // counting sort on the key tiles, stable, so the units of one (sequence, query tile) --
 // whose heads share K/V tiles through their kv head -- stay adjacent), then assigned in
 // that order to the least-loaded CTA (longest-processing-time scheduling) and written
-// grouped by CTA, followed by the grid+1 offsets of the groups.
+// grouped by CTA as two words each (unit_words), followed by the grid+1 offsets of the
+// groups.
 uint32_t tc_build_units(const AttnProblem &p, const uint32_t *lengths_host, const int32_t *cu_host,
                         int num_sms, uint32_t *sorted, uint32_t *work) {
   constexpr uint32_t kMaxTiles = 511;
@@ -1223,7 +1304,24 @@ uint32_t tc_build_units(const AttnProblem &p, const uint32_t *lengths_host, cons
       for (uint32_t i = 0; i < per_tile; ++i) sorted[start[c]++] = tc::encode_unit(s, i, t);
     }
   const uint32_t grid = tc_grid(total, num_sms);
-  uint32_t *offsets = work + total;
+  uint32_t *offsets = work + 2 * total;
+  // The words of unit `code` (see unit_words): valid keys and first row when the lengths
+  // are known here, else the sequence index for the kernel to look up.
+  const bool exact = p.cu_seqlens ? cu_host != nullptr : lengths_host != nullptr;
+  auto words = [&](uint32_t code) -> uint2 {
+    const uint32_t s = code >> 14, idx = (code >> 8) & 63u, t = code & 255u;
+    if (!exact) return tc::unit_words(t, idx, 0u, s);
+    uint32_t n, tok0;
+    if (p.cu_seqlens) {
+      const int32_t a = cu_host[s], b = cu_host[s + 1];
+      n = b > a ? (uint32_t)(b - a) : 0u;
+      tok0 = (uint32_t)a;
+    } else {
+      n = std::min(lengths_host[s], p.seq);
+      tok0 = s * p.seq;
+    }
+    return tc::unit_words(t, idx, n, tok0);
+  };
   if (!total) {
     offsets[0] = 0;
     return 0;
@@ -1244,8 +1342,14 @@ uint32_t tc_build_units(const AttnProblem &p, const uint32_t *lengths_host, cons
       const uint32_t cost =
           unit_cost(unit_tiles(p, lengths_host, cu_host, code >> 14, code & 255u, &rows));
       const uint32_t cta = heap.take(cost);
-      if (pass == 0) ++cursor[cta];
-      else work[cursor[cta]++] = code;
+      if (pass == 0) {
+        ++cursor[cta];
+      } else {
+        const uint2 w = words(code);
+        work[2 * cursor[cta]] = w.x;
+        work[2 * cursor[cta] + 1] = w.y;
+        ++cursor[cta];
+      }
     }
     if (pass == 0) {
       uint32_t acc = 0;
@@ -1299,13 +1403,14 @@ bool make_map(CUtensorMap *map, const void *base, uint32_t rows, uint32_t heads,
 
 cudaError_t tc_preload() {
   cudaFuncAttributes attr;
-  return cudaFuncGetAttributes(&attr, tc::attn_tc_kernel);
+  cudaError_t e = cudaFuncGetAttributes(&attr, tc::attn_tc_kernel<false>);
+  return e == cudaSuccess ? cudaFuncGetAttributes(&attr, tc::attn_tc_kernel<true>) : e;
 }
 
 cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uint32_t n_units,
                                 int num_sms, int *status, const uint16_t *q_norm_w, float eps,
                                 float theta, cudaStream_t stream, bool after_prologue,
-                                long long wait_cycles) {
+                                long long wait_cycles, bool exact_units) {
   if (!n_units) return cudaSuccess;
   CUtensorMap mq, mk, mv, mo;
   const uint32_t rows = p.total;
@@ -1314,14 +1419,17 @@ cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uin
       !make_map(&mv, p.v, rows, p.kv_heads, false, tc::kKeys) ||
       !make_map(&mo, p.out, rows, p.heads, p.out_dtype == 0, 32))
     return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(tc::attn_tc_kernel,
+  const bool out_bf16 = p.out_dtype == 1;
+  auto kernel = out_bf16 ? tc::attn_tc_kernel<true> : tc::attn_tc_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)tc::kSmemBytes);
   if (e != cudaSuccess) return e;
   tc::Params prm;
-  prm.units = units;
-  prm.offsets = units + n_units;
+  prm.units = reinterpret_cast<const uint2 *>(units);
+  prm.offsets = units + 2 * n_units;
   prm.n_units = n_units;
+  prm.exact = exact_units ? 1 : 0;
   prm.lengths = p.lengths;
   prm.cu = p.cu_seqlens;
   prm.out = p.out;
@@ -1330,7 +1438,6 @@ cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uin
   prm.group = p.heads / p.kv_heads;
   prm.nh = heads_per_unit(p);
   prm.causal = p.causal;
-  prm.out_bf16 = p.out_dtype == 1;
   prm.scale_log2 = p.scale * 1.4426950408889634f;
   prm.status = status;
   prm.q_norm_w = q_norm_w;
@@ -1355,7 +1462,7 @@ cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uin
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = after_prologue ? 1 : 0;
-  e = cudaLaunchKernelEx(&cfg, tc::attn_tc_kernel, mq, mk, mv, mo, prm);
+  e = cudaLaunchKernelEx(&cfg, kernel, mq, mk, mv, mo, prm);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -60,13 +60,15 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // sin and cos of a float angle (a RoPE angle, position x inverse frequency): Cody-Waite
-// reduction by 2*pi (2*pi split into a float head and a float tail) to [-pi, pi], then the
-// hardware approximations, accurate to about 2^-21 absolute on that interval.
-__device__ __forceinline__ void sincos_reduced(float angle, float *s, float *c) {
+// reduction by 2*pi (2*pi split into a float head and a float tail; each product k * part
+// is exact inside its fma) to [-pi, pi], then the hardware approximations, accurate to
+// about 2^-21 absolute on that interval.  (A quadrant reduction with Taylor polynomials on
+// the FMA pipe was measured slower inside the attention kernel.)
+__device__ __forceinline__ void rope_sincos(float angle, float *sn, float *cs) {
   const float k = rintf(angle * 0.159154943091895336f);
   float r = fmaf(k, -6.28318548202514648f, angle);
   r = fmaf(k, 1.74845553e-07f, r);
-  __sincosf(r, s, c);
+  __sincosf(r, sn, cs);
 }
 
 // Records the first failure in the context's status word.

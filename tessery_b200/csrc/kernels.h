@@ -86,16 +86,23 @@ bool tc_attention_supported(const AttnProblem &p);
 // after_prologue: the kernel launched just before on `stream` is this library's k
 // prologue (the launch may then overlap its tail, programmatic dependent launch).
 // wait_cycles: limit of each bounded wait in SM cycles (<= 0: about a second).
+// exact_units: the work list was built with host lengths (tc_units_exact).
 cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uint32_t n_units,
                                 int num_sms, int *status, const uint16_t *q_norm_w, float eps,
                                 float theta, cudaStream_t stream, bool after_prologue,
-                                long long wait_cycles);
+                                long long wait_cycles, bool exact_units);
+// Whether tc_build_units writes units with their lengths (host lengths or cu_seqlens of
+// the problem's layout given).
+inline bool tc_units_exact(const AttnProblem &p, const uint32_t *lengths_host,
+                           const int32_t *cu_host) {
+  return p.cu_seqlens ? cu_host != nullptr : lengths_host != nullptr;
+}
 // Loads the tensor-core kernel's module on the current device (no launch).
 cudaError_t tc_preload();
 // Host-side work-list construction for launch_attention_tc (same num_sms for both).
 // `sorted` is host scratch of tc_max_units words; `work` (tc_work_words words) receives
-// the n units grouped by CTA followed by grid+1 offsets; returns n.  The launcher takes
-// `work` (on the device) and n.
+// the n units grouped by CTA (two words each) followed by grid+1 offsets; returns n.
+// The launcher takes `work` (on the device, 8-byte aligned) and n.
 uint32_t tc_max_units(const AttnProblem &p);
 uint32_t tc_work_words(const AttnProblem &p, int num_sms);
 uint32_t tc_grid(uint32_t n_units, int num_sms);

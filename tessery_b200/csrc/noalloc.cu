@@ -22,8 +22,8 @@
 namespace {
 
 // Capacity of the work list: units = batch * heads/2 * ceil(seq / 128) (heads, not
-// pairs, when the query heads per kv head are odd).
-constexpr uint32_t kNoAllocMaxUnits = 32768;
+// pairs, when the query heads per kv head are odd); two words per unit.
+constexpr uint32_t kNoAllocMaxUnits = 16384;
 // The work list also holds one offset per CTA of the grid, plus one.
 constexpr uint32_t kNoAllocMaxOffsets = 1025;
 // Words 0..63 are unused (they keep the work list 256-byte aligned after the header of
@@ -31,7 +31,7 @@ constexpr uint32_t kNoAllocMaxOffsets = 1025;
 constexpr uint32_t kHeaderWords = 64;
 
 static __device__ __align__(256) uint32_t
-    g_noalloc_scratch[kHeaderWords + kNoAllocMaxUnits + kNoAllocMaxOffsets];
+    g_noalloc_scratch[kHeaderWords + 2 * kNoAllocMaxUnits + kNoAllocMaxOffsets + 3];
 
 // Device address of g_noalloc_scratch per device, looked up once with that device
 // current.  In host code the array's name is only a host-side stand-in, not a device
@@ -41,7 +41,7 @@ uint32_t *g_noalloc_ptr[64] = {};
 int g_noalloc_sms[64] = {};
 // Host work space for building the work list (under the mutex).
 uint32_t g_host_sorted[kNoAllocMaxUnits];
-uint32_t g_host_work[kNoAllocMaxUnits + kNoAllocMaxOffsets];
+uint32_t g_host_work[2 * kNoAllocMaxUnits + kNoAllocMaxOffsets + 3];
 
 }  // namespace
 
@@ -90,13 +90,14 @@ extern "C" int tx_attention_padded_noalloc(const void *q, const void *k, const v
   // tc_build_units sorts and balances with fixed-size arrays on the stack and the static
   // host arrays above: no allocation.
   const uint32_t n = tx::tc_build_units(p, lengths_host, nullptr, sms, g_host_sorted, g_host_work);
-  const uint32_t words = n + tx::tc_grid(n, sms) + 1;
+  const uint32_t words = 2 * n + tx::tc_grid(n, sms) + 1;
   // The array keeps the previous call's contents: the status word must start at zero.
   if (cudaMemsetAsync(st, 0, sizeof(int), s) != cudaSuccess) return TX_ECUDA;
   if (n && cudaMemcpyAsync(scratch + kHeaderWords, g_host_work, words * sizeof(uint32_t),
                            cudaMemcpyHostToDevice, s) != cudaSuccess)
     return TX_ECUDA;
   cudaError_t e = tx::launch_attention_tc(p, scratch + kHeaderWords, n, sms, st, q_norm_w, eps,
-                                          theta, s, /*after_prologue=*/false, /*wait_cycles=*/0);
+                                          theta, s, /*after_prologue=*/false, /*wait_cycles=*/0,
+                                          /*exact_units=*/true);
   return e == cudaSuccess ? TX_OK : TX_ECUDA;
 }

@@ -245,7 +245,7 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
       uint32_t *work = c->units_host.data() + cap;
       c->units_count = tx::tc_build_units(p, lengths_host, cu_host, c->sms, c->units_host.data(),
                                           work);
-      const uint32_t upload = c->units_count + tx::tc_grid(c->units_count, c->sms) + 1;
+      const uint32_t upload = 2 * c->units_count + tx::tc_grid(c->units_count, c->sms) + 1;
       // Pageable source: the call returns once the data is staged, so the host vector
       // can be rebuilt by the next call.
       if (c->units_count &&
@@ -290,7 +290,8 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
     // pro_k: the k prologue was the launch just before on this stream.
     if ((e = tx::launch_attention_tc(p, units_dev ? units_dev : c->units,
                                      units_dev ? units_n : c->units_count, c->sms, c->status,
-                                     tc_q_w, eps, theta, stream, pro_k, c->wait_cycles)) !=
+                                     tc_q_w, eps, theta, stream, pro_k, c->wait_cycles,
+                                     tx::tc_units_exact(p, lengths_host, cu_host))) !=
         cudaSuccess)
       return cuda_fail(c, e, "attention launch");
     c->last_kernel = "tc_bf16_d128";

@@ -275,8 +275,8 @@ static cudaError_t launch_prologue_e(const PrologueProblem &p, cudaStream_t stre
 // for the first half, a*sin + b*cos for the second), regrouped as
 // inv * (own * (w_own * cos) -/+ partner * (w_partner * sin)) so that the per-token
 // products are shared by all heads.  The angle is the float product pos * inv_freq[c];
-// its sine and cosine come from a Cody-Waite reduction by 2*pi and the hardware
-// approximations (about 2^-21 absolute error).
+// its sine and cosine come from rope_sincos (a Cody-Waite reduction by 2*pi and the
+// hardware approximations, about 2^-21 absolute error).
 constexpr int kRowTokensPerWarp = 3;
 
 struct RowPass {
@@ -432,8 +432,8 @@ __global__ void __launch_bounds__(128) norm_rope_rows_bf16_kernel(RowPass p) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       float sn0, cs0, sn1, cs1;
-      sincos_reduced(fpos * invf[2 * e], &sn0, &cs0);
-      sincos_reduced(fpos * invf[2 * e + 1], &sn1, &cs1);
+      rope_sincos(fpos * invf[2 * e], &sn0, &cs0);
+      rope_sincos(fpos * invf[2 * e + 1], &sn1, &cs1);
       c1[e] = pf2(wof[2 * e] * cs0, wof[2 * e + 1] * cs1);
       c2[e] = first ? pf2(-(wpf[2 * e] * sn0), -(wpf[2 * e + 1] * sn1))
                     : pf2(wpf[2 * e] * sn0, wpf[2 * e + 1] * sn1);

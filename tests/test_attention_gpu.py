@@ -405,6 +405,24 @@ def test_prologue_matches_oracle(runtime):
     np.testing.assert_allclose(from_bf16_bits(bk), wk, rtol=2 ** -8, atol=1e-6)
 
 
+def test_prologue_at_long_positions_matches_oracle(runtime):
+    """RoPE angles up to ~3e4 radians (one sequence of 30000 tokens): the FMA-pipe sine and
+    cosine after the quadrant reduction stay within the float32 gate."""
+    from tessery_b200 import qk_norm_rope
+
+    rng = np.random.default_rng(52)
+    tokens = 30000
+    q = rng.normal(size=(tokens, 2, 128)).astype(np.float32)
+    k = rng.normal(size=(tokens, 1, 128)).astype(np.float32)
+    qw = to_bf16_bits(1 + 0.02 * rng.normal(size=128).astype(np.float32))
+    kw = to_bf16_bits(1 + 0.02 * rng.normal(size=128).astype(np.float32))
+    for theta in (1e4, 1e6):
+        want_q, want_k = oracle.qk_norm_rope(q, k, qw, kw, 1e-6, theta, np.arange(tokens))
+        got_q, got_k = qk_norm_rope(q, k, qw, kw, seq=tokens, theta=theta, runtime=runtime)
+        np.testing.assert_allclose(got_q, want_q, atol=2e-5, rtol=2e-5)
+        np.testing.assert_allclose(got_k, want_k, atol=2e-5, rtol=2e-5)
+
+
 def test_typed_dtype_codes():
     assert (TX_F32, TX_BF16) == (0, 1)
 

@@ -90,9 +90,9 @@ def test_noalloc_matches_existing_entry_point_twice(runtime):
 def test_noalloc_rejects_problems_beyond_the_static_work_list(runtime):
     lib = native.load()
     # The problem is rejected on the host before any pointer is used; the pointers below
-    # are a 256-byte buffer, so the size must exceed the 32768-unit list by a wide margin
+    # are a 256-byte buffer, so the size must exceed the 16384-unit list by a wide margin
     # however units are counted (per head: 129 x 16 x 64 = 132096; per head pair: 66048).
-    B, L, capacity = 129, 8192, 32768
+    B, L, capacity = 129, 8192, 16384
     tiles = L // 128
     assert B * (16 // 2) * tiles >= 2 * capacity
     lengths = np.full(B, 1, np.uint32)
