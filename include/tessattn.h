@@ -34,8 +34,10 @@ enum {
   TX_ETIMEOUT = 3
 };
 
-/* Element types of attention inputs/outputs. */
-enum { TX_F32 = 0, TX_BF16 = 1 };
+/* Element types of attention inputs/outputs.  TX_BF16X2 (tx_rms_norm_rows output only): a
+ * bf16 pair -- hi = bf16(v) in the output array, lo = bf16(v - hi) in a second array of the
+ * same shape right after it -- which keeps about 16 significant bits of v. */
+enum { TX_F32 = 0, TX_BF16 = 1, TX_BF16X2 = 2 };
 
 /* ABI version; bumped on any signature change.  The Python loader refuses a library
  * whose version differs, as metal.py:84-90 refuses a stale native build. */
@@ -115,8 +117,10 @@ int tx_begin(void *ctx);
 
 /* Replaces mi_dispatch (runtime.mm:109-146).  `name` selects a kernel by the
  * reference's kernel names ("rms_norm", "rope", "attention", "attention_tiled",
- * "attention_tail_32", "attention_tail_128") plus this library's additions
- * ("attention_d32", "qk_norm_rope").  `buffers` are tx_buffer handles in the
+ * "attention_tail_32", "attention_tail_128", "pool_project", "embedding4", "linear4",
+ * "linear4_tiled", "linear4_tail", "linear4_16x32_k64", "linear4_32x32_k64",
+ * "linear4_small3", "silu_gate", "add"; fp32 like the reference) plus this library's
+ * additions ("attention_d32", "qk_norm_rope").  `buffers` are tx_buffer handles in the
  * reference's slot order, `params` is the reference's 64-byte Params block
  * (kernels.metal:5-8, packed "<12I4f" by metal.py:596-614), and `threads`/`group`
  * are the reference's Metal grid, from which the row/batch counts are derived exactly
@@ -270,6 +274,62 @@ int tx_attention_padded_noalloc(const void *q, const void *k, const void *v,
                                 uint32_t kv_heads, int out_dtype, int causal, float scale,
                                 const uint16_t *q_norm_w, float eps, float theta, int *status,
                                 void *stream);
+
+/* ---- the Qwen3 embedding forward around the attention -----------------------------
+
+ * The layer loop of Qwen3Backend.forward (qwen3.py:112-296) is built from these plus
+ * tx_attention_varlen and tx_pool_project.  Weights come as the reference stores them
+ * (qwen3.py:70-73): uint4 codes `packed` [rows, cols / 8] (code i of a word in bits
+ * 4i..4i+3), bf16 `scales` and `biases` [rows, cols / 64]; element (r, c) =
+ * code * scale + bias (weight4, kernels.metal:11-19).  All pointers are device pointers;
+ * stream NULL: the context's stream. */
+
+/* Epilogues of tx_linear. */
+enum {
+  TX_LINEAR_STORE_F32 = 0,  /* out fp32 [m, n] = x . w^T */
+  TX_LINEAR_STORE_BF16 = 1, /* out bf16 [m, n] */
+  TX_LINEAR_ADD_F32 = 2,    /* out fp32 [m, n] += x . w^T (the residual add, qwen3.py:151-152) */
+  TX_LINEAR_GATED_BF16 = 3  /* out bf16 [m, n / 2]: silu(gate) * up, w rows interleaved in
+                               blocks of 128 gate then 128 up rows (gated4 + silu_gate,
+                               kernels.metal:333-337, 609-733) */
+};
+
+/* Dequantises a uint4 weight matrix once into bf16 [rows, cols] (out), the operand layout
+ * of tx_linear, and, when out_lo is non-NULL, the rounding residue of every weight into
+ * out_lo (the lo half of a bf16 pair).  Replaces the per-use decode of weight4
+ * (kernels.metal:11-19) inside the reference's linear4* kernels.  cols % 64 == 0; out and
+ * out_lo 16-byte aligned. */
+int tx_dequant4(void *ctx, const uint32_t *packed, const uint16_t *scales,
+                const uint16_t *biases, uint16_t *out, uint16_t *out_lo, uint32_t rows,
+                uint32_t cols, void *stream);
+
+/* fp32 x [n] as a bf16 pair: out[i] = bf16(x[i]), out[n + i] = bf16(x[i] - out[i]). */
+int tx_split_bf16(void *ctx, const float *x, uint16_t *out, uint64_t n, void *stream);
+
+/* Replaces the "embedding4" dispatch (kernels.metal:21-28): out fp32 [tokens, cols], row
+ * t = dequantised row ids[t] of the table.  An id >= vocab gives a NaN row and is reported
+ * as TX_EINVAL by the next tx_sync / tx_finish.  cols % 64 == 0. */
+int tx_embedding4(void *ctx, const uint32_t *ids, uint32_t tokens, const uint32_t *packed,
+                  const uint16_t *scales, const uint16_t *biases, float *out, uint32_t cols,
+                  uint32_t vocab, void *stream);
+
+/* Replaces the "rms_norm" dispatch on the hidden rows (kernels.metal:53-63, called at
+ * qwen3.py:135-143): out[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * bf16(w), written bf16
+ * (out_dtype TX_BF16, the projections' operand) or fp32.  x fp32 [rows, cols], cols % 4
+ * == 0. */
+int tx_rms_norm_rows(void *ctx, const float *x, const uint16_t *w, void *out, int out_dtype,
+                     uint32_t rows, uint32_t cols, float eps, void *stream);
+
+/* Replaces the reference's _linear4 / _gated4 routing (metal.py:416-530) on dequantised
+ * weights: x bf16 [m, k] times w bf16 [n, k] transposed, fp32 accumulation on tensor cores,
+ * epilogue `mode` (TX_LINEAR_*).  With w_lo (and optionally x_lo), the lo halves of bf16
+ * pairs, the product is x.w + x.w_lo (+ x_lo.w), which carries about 16 significant bits
+ * of each operand instead of 8 (the reference computes in fp32); the gated epilogue then
+ * writes a bf16 pair (hi [m, n/2] then lo [m, n/2]).  n % 256 == 0, k % 64 == 0,
+ * pointers 16-byte aligned, x_lo only with w_lo; otherwise TX_EINVAL. */
+int tx_linear(void *ctx, const uint16_t *x, const uint16_t *x_lo, const uint16_t *w,
+              const uint16_t *w_lo, void *out, uint32_t m, uint32_t n, uint32_t k, int mode,
+              void *stream);
 
 /* Waits for all work queued on `stream` (NULL: context stream) and reports kernel
  * errors, including device-side wait timeouts, as a status code. */

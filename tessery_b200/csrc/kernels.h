@@ -109,4 +109,29 @@ uint32_t tc_grid(uint32_t n_units, int num_sms);
 uint32_t tc_build_units(const AttnProblem &p, const uint32_t *lengths_host,
                         const int32_t *cu_host, int num_sms, uint32_t *sorted, uint32_t *work);
 
+// Qwen3 forward pieces (qwen_ops.cu, linear.cu).
+cudaError_t launch_dequant4(const uint32_t *packed, const uint16_t *scales,
+                            const uint16_t *biases, uint16_t *out, uint16_t *out_lo, uint32_t rows,
+                            uint32_t cols, cudaStream_t stream);
+cudaError_t launch_embedding4(const uint32_t *ids, uint32_t tokens, const uint32_t *packed,
+                              const uint16_t *scales, const uint16_t *biases, float *out,
+                              uint32_t cols, uint32_t vocab, int *status, cudaStream_t stream);
+// out_kind: 0 fp32, 1 bf16, 2 bf16 pair (hi then lo).
+cudaError_t launch_rms_norm_rows(const float *x, const uint16_t *w, void *out, int out_kind,
+                                 uint32_t rows, uint32_t cols, float eps, cudaStream_t stream);
+cudaError_t launch_split_bf16(const float *x, uint16_t *out, uint64_t n, cudaStream_t stream);
+// fp32 kernels behind the reference's Params-block dispatch names (linear4, silu_gate, add).
+cudaError_t launch_linear4_f32(const float *x, const uint32_t *packed, const uint16_t *scales,
+                               const uint16_t *biases, float *out, uint32_t t0, uint32_t t1,
+                               uint32_t cols, uint32_t k, cudaStream_t stream);
+cudaError_t launch_silu_gate(float *gate, const float *up, uint64_t n, cudaStream_t stream);
+cudaError_t launch_add(const float *a, const float *b, float *out, uint64_t n,
+                       cudaStream_t stream);
+bool linear_supported(uint32_t m, uint32_t n, uint32_t k, int mode, const void *x, const void *w,
+                      const void *out);
+// x_lo / w_lo (or NULL): the lo halves of bf16 pairs (x_lo needs w_lo); see linear.cu.
+cudaError_t launch_linear(const void *x, const void *x_lo, const void *w, const void *w_lo,
+                          void *out, uint32_t m, uint32_t n, uint32_t k, int mode, int *status,
+                          long long wait_cycles, cudaStream_t stream);
+
 }  // namespace tx

@@ -21,7 +21,7 @@
 
 namespace {
 
-constexpr uint32_t kAbiVersion = 4;
+constexpr uint32_t kAbiVersion = 6;
 constexpr uint32_t kHostChunks = 8;              // most chunks of a host-buffer call
 constexpr size_t kHostChunkBytes = 16u << 20;     // bytes moved per chunk, at least
 
@@ -856,6 +856,70 @@ int tx_dispatch(void *ctx, const char *name, void **buffers, uint32_t count, con
       c->last_kernel = "pool_project";
     }
     prof_end(c);
+  } else if (n == "embedding4") {
+    // buffers [ids, packed, scales, biases, out]; n = tokens * cols (kernels.metal:21-28)
+    const uint32_t cols = pr.cols;
+    if (count != 5 || !cols || cols % 64 || pr.n % cols)
+      return fail(c, TX_EINVAL, "embedding4: bad arguments");
+    const uint64_t tokens = pr.n / cols, vocab = b[1]->size / ((uint64_t)cols / 2);
+    if (b[0]->size < tokens * 4 || b[2]->size < vocab * (cols / 64) * 2 ||
+        b[3]->size < vocab * (cols / 64) * 2 || b[4]->size < (uint64_t)pr.n * 4 || !vocab)
+      return fail(c, TX_EINVAL, "embedding4: buffer too small");
+    prof_begin(c);
+    e = tx::launch_embedding4((const uint32_t *)b[0]->dev, (uint32_t)tokens,
+                              (const uint32_t *)b[1]->dev, (const uint16_t *)b[2]->dev,
+                              (const uint16_t *)b[3]->dev, (float *)b[4]->dev, cols,
+                              (uint32_t)vocab, c->status, c->stream);
+    if (e == cudaSuccess) ++c->launches;
+    prof_end(c);
+  } else if (n.rfind("linear4", 0) == 0) {
+    // buffers [x, packed, scales, biases, out], fp32 (kernels.metal:32-51 and the tiled
+    // variants :491-608, 658-773, routed by metal.py:416-483); the rows each variant covers
+    // follow from its grid: [n, ...) for the 8-row tiles and tails, [0, ...) for the
+    // 16- and 32-row tiles.
+    const uint32_t rows = pr.rows, cols = pr.cols, k = pr.k;
+    if (count != 5 || !rows || !cols || !k || k % 64) return fail(c, TX_EINVAL, "linear4: bad arguments");
+    const uint64_t tiles32 = (uint64_t)(cols / 32);
+    uint64_t t0 = 0, t1 = rows;
+    if (n == "linear4") {
+      t0 = pr.n;
+      t1 = std::min<uint64_t>(rows, t0 + 4 * (threads / 32 / cols));
+    } else if (n == "linear4_tiled") {
+      if (!tiles32) return fail(c, TX_EINVAL, "linear4: bad grid");
+      t0 = pr.n;
+      t1 = std::min<uint64_t>(rows, t0 + 8 * (threads / (tiles32 * 128)));
+    } else if (n == "linear4_tail") {
+      t0 = pr.n;
+    } else if (n == "linear4_16x32_k64" || n == "linear4_32x32_k64") {
+      if (!tiles32) return fail(c, TX_EINVAL, "linear4: bad grid");
+      const uint64_t tile = n == "linear4_16x32_k64" ? 16 : 32;
+      t1 = std::min<uint64_t>(rows, tile * (threads / (tiles32 * 256)));
+    } else if (n != "linear4_small3") {
+      return fail(c, TX_EINVAL, "unknown kernel name");
+    }
+    if (b[0]->size < (uint64_t)rows * k * 4 || b[1]->size < (uint64_t)cols * (k / 8) * 4 ||
+        b[2]->size < (uint64_t)cols * (k / 64) * 2 || b[3]->size < (uint64_t)cols * (k / 64) * 2 ||
+        b[4]->size < (uint64_t)rows * cols * 4)
+      return fail(c, TX_EINVAL, "linear4: buffer too small");
+    prof_begin(c);
+    e = tx::launch_linear4_f32((const float *)b[0]->dev, (const uint32_t *)b[1]->dev,
+                               (const uint16_t *)b[2]->dev, (const uint16_t *)b[3]->dev,
+                               (float *)b[4]->dev, (uint32_t)std::min<uint64_t>(t0, rows),
+                               (uint32_t)t1, cols, k, c->stream);
+    if (e == cudaSuccess) ++c->launches;
+    prof_end(c);
+  } else if (n == "silu_gate" || n == "add") {
+    // silu_gate [gate, up] in place (kernels.metal:333-337); add [a, b, out] (:300-304)
+    const bool silu = n == "silu_gate";
+    if (count != (silu ? 2u : 3u)) return fail(c, TX_EINVAL, "elementwise: bad arguments");
+    for (uint32_t i = 0; i < count; ++i)
+      if (b[i]->size < (uint64_t)pr.n * 4) return fail(c, TX_EINVAL, "elementwise: buffer too small");
+    prof_begin(c);
+    e = silu ? tx::launch_silu_gate((float *)b[0]->dev, (const float *)b[1]->dev, pr.n, c->stream)
+             : tx::launch_add((const float *)b[0]->dev, (const float *)b[1]->dev,
+                              (float *)b[2]->dev, pr.n, c->stream);
+    if (e == cudaSuccess) ++c->launches;
+    prof_end(c);
   } else if (n == "qk_norm_rope") {
     // buffers: q, k (f32, in place), q_norm weight, k_norm weight (bf16); n = tokens
     if (count != 4 || !pr.heads || !pr.kv_heads || !pr.seq)
@@ -1077,6 +1141,94 @@ int tx_pool_project(void *ctx, const void *x, int in_dtype, const uint32_t *leng
   cudaError_t e = tx::launch_pool_project(p, stream ? (cudaStream_t)stream : c->stream);
   if (e != cudaSuccess) return cuda_fail(c, e, "pool launch");
   c->last_kernel = "pool_project";
+  ++c->launches;
+  return TX_OK;
+}
+
+int tx_dequant4(void *ctx, const uint32_t *packed, const uint16_t *scales,
+                const uint16_t *biases, uint16_t *out, uint16_t *out_lo, uint32_t rows,
+                uint32_t cols, void *stream) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!packed || !scales || !biases || !out) return fail(c, TX_EINVAL, "null pointer");
+  if (!rows || !cols || cols % 64 || (uintptr_t)out % 16 || (uintptr_t)out_lo % 16 ||
+      (uintptr_t)packed % 4)
+    return fail(c, TX_EINVAL, "dequant4: cols % 64 == 0, aligned pointers");
+  cudaSetDevice(c->device);
+  cudaError_t e = tx::launch_dequant4(packed, scales, biases, out, out_lo, rows, cols,
+                                      stream ? (cudaStream_t)stream : c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "dequant4 launch");
+  ++c->launches;
+  return TX_OK;
+}
+
+int tx_split_bf16(void *ctx, const float *x, uint16_t *out, uint64_t n, void *stream) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!x || !out) return fail(c, TX_EINVAL, "null pointer");
+  cudaSetDevice(c->device);
+  cudaError_t e = tx::launch_split_bf16(x, out, n, stream ? (cudaStream_t)stream : c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "split launch");
+  ++c->launches;
+  return TX_OK;
+}
+
+int tx_embedding4(void *ctx, const uint32_t *ids, uint32_t tokens, const uint32_t *packed,
+                  const uint16_t *scales, const uint16_t *biases, float *out, uint32_t cols,
+                  uint32_t vocab, void *stream) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!ids || !packed || !scales || !biases || !out) return fail(c, TX_EINVAL, "null pointer");
+  if (!cols || cols % 64 || !vocab || (uintptr_t)out % 16)
+    return fail(c, TX_EINVAL, "embedding4: cols % 64 == 0, vocab > 0");
+  cudaSetDevice(c->device);
+  cudaError_t e = tx::launch_embedding4(ids, tokens, packed, scales, biases, out, cols, vocab,
+                                        c->status, stream ? (cudaStream_t)stream : c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "embedding4 launch");
+  ++c->launches;
+  return TX_OK;
+}
+
+int tx_rms_norm_rows(void *ctx, const float *x, const uint16_t *w, void *out, int out_dtype,
+                     uint32_t rows, uint32_t cols, float eps, void *stream) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!x || !w || !out) return fail(c, TX_EINVAL, "null pointer");
+  if (out_dtype != TX_F32 && out_dtype != TX_BF16 && out_dtype != TX_BF16X2)
+    return fail(c, TX_EINVAL, "bad out_dtype");
+  if (!cols || cols % 4 || (uintptr_t)x % 16 || (uintptr_t)out % 16 || (uintptr_t)w % 8 ||
+      !(eps >= 0.f))
+    return fail(c, TX_EINVAL, "rms_norm_rows: cols % 4 == 0, aligned pointers");
+  cudaSetDevice(c->device);
+  const int kind = out_dtype == TX_F32 ? 0 : out_dtype == TX_BF16 ? 1 : 2;
+  cudaError_t e = tx::launch_rms_norm_rows(x, w, out, kind, rows, cols, eps,
+                                           stream ? (cudaStream_t)stream : c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "rms_norm_rows launch");
+  ++c->launches;
+  return TX_OK;
+}
+
+int tx_linear(void *ctx, const uint16_t *x, const uint16_t *x_lo, const uint16_t *w,
+              const uint16_t *w_lo, void *out, uint32_t m, uint32_t n, uint32_t k, int mode,
+              void *stream) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!x || !w || !out) return fail(c, TX_EINVAL, "null pointer");
+  if (x_lo && !w_lo) return fail(c, TX_EINVAL, "linear: x_lo needs w_lo");
+  if (!m) return TX_OK;
+  if (!tx::linear_supported(m, n, k, mode, x, w, out) || (uintptr_t)x_lo % 16 ||
+      (uintptr_t)w_lo % 16)
+    return fail(c, TX_EINVAL, "linear: n % 256 == 0, k % 64 == 0, aligned pointers, mode");
+  cudaSetDevice(c->device);
+  cudaError_t e = tx::launch_linear(x, x_lo, w, w_lo, out, m, n, k, mode, c->status,
+                                    c->wait_cycles, stream ? (cudaStream_t)stream : c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "linear launch");
+  c->last_kernel = "linear";
   ++c->launches;
   return TX_OK;
 }

@@ -16,11 +16,12 @@ from typing import Any
 
 from .errors import NativeBuildError
 
-ABI_VERSION = 4
+ABI_VERSION = 6
 LIBRARY_NAME = "libtessattn.so"
 
 TX_OK, TX_EINVAL, TX_ECUDA, TX_ETIMEOUT = 0, 1, 2, 3
-TX_F32, TX_BF16 = 0, 1
+TX_F32, TX_BF16, TX_BF16X2 = 0, 1, 2
+TX_LINEAR_STORE_F32, TX_LINEAR_STORE_BF16, TX_LINEAR_ADD_F32, TX_LINEAR_GATED_BF16 = 0, 1, 2, 3
 
 _vp, _u32, _u64, _i32, _f32 = ct.c_void_p, ct.c_uint32, ct.c_uint64, ct.c_int, ct.c_float
 
@@ -79,6 +80,11 @@ SIGNATURES: dict[str, tuple[list[Any], Any]] = {
         _i32,
     ),
     "tx_sync": ([_vp, _vp], _i32),
+    "tx_dequant4": ([_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _vp], _i32),
+    "tx_split_bf16": ([_vp, _vp, _vp, _u64, _vp], _i32),
+    "tx_embedding4": ([_vp, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _u32, _vp], _i32),
+    "tx_rms_norm_rows": ([_vp, _vp, _vp, _vp, _i32, _u32, _u32, _f32, _vp], _i32),
+    "tx_linear": ([_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _i32, _vp], _i32),
     "tx_attention_padded_noalloc": (
         [_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _i32, _i32, _f32, _vp, _f32,
          _f32, _vp, _vp],

@@ -548,6 +548,44 @@ class CudaRuntime:
         )
         _raise_for(rc)
 
+    # ---- the Qwen3 forward around the attention (device pointers) -----------------------
+    def dequant4_device(self, packed: int, scales: int, biases: int, out: int, *, rows: int,
+                        cols: int, out_lo: int | None = None, stream: int | None = None) -> None:
+        """uint4 weights (weight4, kernels.metal:11-19) into bf16 [rows, cols], and their
+        rounding residues into out_lo when given (tx_dequant4)."""
+        self._check_open()
+        _raise_for(self._lib.tx_dequant4(self._pointer, packed, scales, biases, out, out_lo, rows,
+                                         cols, stream))
+
+    def split_bf16_device(self, x: int, out: int, *, n: int, stream: int | None = None) -> None:
+        """fp32 x [n] as a bf16 pair: out [n] = bf16(x), out + n: the residue (tx_split_bf16)."""
+        self._check_open()
+        _raise_for(self._lib.tx_split_bf16(self._pointer, x, out, n, stream))
+
+    def embedding4_device(self, ids: int, out: int, *, tokens: int, packed: int, scales: int,
+                          biases: int, cols: int, vocab: int, stream: int | None = None) -> None:
+        """Token rows of a uint4 embedding table as fp32 (embedding4, kernels.metal:21-28)."""
+        self._check_open()
+        _raise_for(self._lib.tx_embedding4(self._pointer, ids, tokens, packed, scales, biases,
+                                           out, cols, vocab, stream))
+
+    def rms_norm_rows_device(self, x: int, weight: int, out: int, *, rows: int, cols: int,
+                             eps: float = 1e-6, out_dtype: int = native.TX_BF16,
+                             stream: int | None = None) -> None:
+        """Row RMSNorm of fp32 x with a bf16 weight (kernels.metal:53-63) (tx_rms_norm_rows)."""
+        self._check_open()
+        _raise_for(self._lib.tx_rms_norm_rows(self._pointer, x, weight, out, out_dtype, rows,
+                                              cols, eps, stream))
+
+    def linear_device(self, x: int, w: int, out: int, *, m: int, n: int, k: int, mode: int,
+                      x_lo: int | None = None, w_lo: int | None = None,
+                      stream: int | None = None) -> None:
+        """Tensor-core x [m, k] . w [n, k]^T with a TX_LINEAR_* epilogue; with the lo halves
+        of bf16 pairs (w_lo, and x_lo), the split-operand product (tx_linear)."""
+        self._check_open()
+        _raise_for(self._lib.tx_linear(self._pointer, x, x_lo, w, w_lo, out, m, n, k, mode,
+                                       stream))
+
     def sync(self, stream: int | None = None) -> None:
         """Waits for queued work and reports kernel errors (tx_sync)."""
         self._check_open()

@@ -8,7 +8,8 @@ RMSNorm and pooling tests, unmodified and with their own seeds, grids and tolera
 against a fake runtime whose kernels are computed by ``oracle``.  Every
 ``numpy.testing.assert_allclose`` the reference tests make is intercepted to record the
 reference's expected array (its own NumPy formula) and the verdict, then forwarded to
-NumPy, so a failing comparison fails this script.
+NumPy, so a failing comparison fails this script (assert_array_equal checks are
+recorded the same way, with zero tolerance).
 
 Output: tests/golden/reference_kernels.npz with, per case, the kernel name and
 parameters, SHA-256 of every input array, a deterministic sample of the reference's
@@ -35,6 +36,7 @@ REPO = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(REPO))
 
 import oracle  # noqa: E402
+from oracle.qwen3 import dequant4  # noqa: E402
 
 def reference_root() -> Path:
     """The reference project's root: argv[1], else $TESSERY_REFERENCE."""
@@ -53,6 +55,7 @@ KERNEL_TESTS = [
     "test_rope_and_silu",
     "test_rms_and_pool",
     "test_bidirectional_attention_and_cls_pool",
+    "test_quantized_embedding_and_linear",
 ]
 
 
@@ -126,6 +129,21 @@ class OracleEngine:
             lengths = buffers[1].view(np.uint32)
             out = oracle.pool_project(x, lengths, dim, bool(kw.get("first_token", 0)))
             buffers[2].write(out.astype(np.float32))
+        elif name == "embedding4":
+            cols = kw["cols"]
+            ids = buffers[0].view(np.uint32)
+            packed = buffers[1].view(np.uint32).reshape(-1, cols // 8)
+            groups = (-1, cols // 64)
+            table = dequant4(packed, buffers[2].view(np.uint16).reshape(groups),
+                             buffers[3].view(np.uint16).reshape(groups))
+            buffers[4].write(table[ids].astype(np.float32))
+        elif name == "linear4":
+            rows, cols, k = kw["rows"], kw["cols"], kw["k"]
+            x = buffers[0].view(np.float32).reshape(rows, k).astype(np.float64)
+            w = dequant4(buffers[1].view(np.uint32).reshape(cols, k // 8),
+                         buffers[2].view(np.uint16).reshape(cols, k // 64),
+                         buffers[3].view(np.uint16).reshape(cols, k // 64))
+            buffers[4].write((x @ w.T).astype(np.float32))
         elif name == "silu_gate":  # harness only: the RoPE test also exercises silu_gate
             a = buffers[0].view(np.float32).astype(np.float64)
             b = buffers[1].view(np.float32).astype(np.float64)
@@ -183,11 +201,17 @@ def main() -> None:
                 checks.append((actual.copy(), desired.astype(np.float64).copy(), rtol, atol))
                 return original(actual, desired, rtol=rtol, atol=atol, **kw)
 
+            def capture_equal(actual, desired, **kw):
+                capture(actual, desired, rtol=0.0, atol=0.0)
+
+            original_equal = np.testing.assert_array_equal
             np.testing.assert_allclose = capture
+            np.testing.assert_array_equal = capture_equal
             try:
                 function(OracleEngine(log), **params)
             finally:
                 np.testing.assert_allclose = original
+                np.testing.assert_array_equal = original_equal
             for index, (actual, desired, rtol, atol) in enumerate(checks):
                 flat = desired.reshape(-1)
                 count = min(SAMPLES, flat.size)

@@ -17,7 +17,7 @@ import numpy as np
 
 FIXTURE = Path(__file__).resolve().parent / "golden" / "reference_kernels.npz"
 PATH_KERNELS = {"attention", "attention_tiled", "attention_tail_32", "attention_tail_128",
-                "rope", "rms_norm", "pool_project"}
+                "rope", "rms_norm", "pool_project", "embedding4", "linear4"}
 
 
 def sha(a: np.ndarray) -> str:
@@ -113,6 +113,18 @@ def regenerate(case: Case) -> dict:
         if case.check == 0:
             return {"q": q, "k": k, "v": v, "lengths": lengths}
         return {"x": q.reshape(batch, seq, heads * dim), "lengths": lengths}
+    if t == "test_quantized_embedding_and_linear":
+        rng = np.random.default_rng(1)
+        code = rng.integers(0, 16, size=(8, 128), dtype=np.uint32)
+        packed = np.bitwise_or.reduce(
+            code.reshape(8, 16, 8) << np.arange(0, 32, 4, dtype=np.uint32), axis=-1)
+        scales = _bf16_truncate(np.full((8, 2), 0.125))
+        biases = _bf16_truncate(np.full((8, 2), -0.5))
+        ids = np.array([7, 1, 3], np.uint32)
+        if case.check == 0:
+            return {"ids": ids, "packed": packed, "scales": scales, "biases": biases}
+        x = rng.normal(size=(3, 128)).astype(np.float32)
+        return {"x": x, "packed": packed, "scales": scales, "biases": biases}
     raise KeyError(t)
 
 

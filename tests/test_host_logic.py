@@ -132,3 +132,13 @@ def test_bf16_conversion_rounds_to_nearest_even():
     import oracle
 
     assert np.array_equal(oracle.bf16_bits(x), bits)
+
+
+def test_gate_up_interleave_blocks():
+    from tessery_b200.qwen3 import interleave_gate_up
+
+    g = np.arange(256 * 3).reshape(256, 3)
+    u = -g
+    fused = interleave_gate_up(g, u)
+    assert np.array_equal(fused[:128], g[:128]) and np.array_equal(fused[128:256], u[:128])
+    assert np.array_equal(fused[256:384], g[128:]) and np.array_equal(fused[384:], u[128:])

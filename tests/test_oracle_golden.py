@@ -4,6 +4,7 @@ import numpy as np
 import pytest
 
 import oracle
+import oracle.qwen3
 from golden_cases import compare, inputs_match, load_cases, regenerate
 
 CASES = load_cases()
@@ -24,6 +25,11 @@ def run_oracle(case, inputs):
     if case.kernel == "pool_project":
         return oracle.pool_project(inputs["x"], inputs["lengths"], d["dim"],
                                    bool(d.get("first_token", 0)))
+    if case.kernel in ("embedding4", "linear4"):
+        table = oracle.qwen3.dequant4(inputs["packed"], inputs["scales"], inputs["biases"])
+        if case.kernel == "embedding4":
+            return table[inputs["ids"]]
+        return inputs["x"].astype(np.float64) @ table.T
     raise KeyError(case.kernel)
 
 
