@@ -26,6 +26,10 @@ One step = one pass of the hot path over one batch of synthetic input.  Workload
                GPU, lengths ~ U[32, 512]; the final RMSNorm of the last valid token of
                each sequence fused with last-token pooling and L2 normalisation
                (metric: sequences/s; a latency figure, 32 rows of 4 KB).
+  qwen_forward the whole Qwen3-0.6B embedding forward around the attention: 28 layers,
+               uint4 random weights (seed 9; scales N(0,0.02), biases N(0,0.01)), 32 texts
+               per GPU of U[32, 512] random token ids (seed 5), packed, last-token pooling,
+               1024-d L2-normalised output (metric: texts/s; weak scaling, 32 per GPU).
 
 Multi-GPU (torchrun, N ranks): sequences are assigned to ranks longest-first; shards are
 independent, so there is no collective on the data path (torch.distributed is used only
@@ -62,7 +66,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "attention tokens/s at Qwen3-0.6B shape & % of bf16 TC peak, 1/2/4/8 B200"
 WORKLOADS = ("qwen_padded", "qwen_varlen", "bge", "bge_scaled", "tails_qwen", "tails_bge",
-             "pool_qwen")
+             "pool_qwen", "qwen_forward")
 # FP32 FMA throughput of the SIMT cores: 148 SMs x 128 lanes x 2 flops x 1.965 GHz
 # (nominal; packed f32x2 FMA doubles it).  Used for the head_dim-32 compute floor.
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
@@ -806,10 +810,201 @@ def run_pool(args):
         dist.destroy_process_group()
 
 
+# ---- the whole Qwen3 embedding forward (the layers around the attention) ------------------
+FORWARD_METRIC = "Qwen3-0.6B embedding forward texts/s (28 layers, uint4 weights)"
+
+
+def forward_texts(rank: int, world: int):
+    """32 texts per rank: lengths U[32, 512] (seed 5) over 32 * world texts, assigned
+    longest first; random token ids (seed 5 + 1000 * rank)."""
+    from tessery_b200 import shard_sequences
+    from tessery_b200.qwen3 import Qwen3Config
+
+    cfg = Qwen3Config()
+    lengths = np.random.default_rng(5).integers(32, 513, size=32 * world)
+    owned = lengths[shard_sequences(lengths, world, causal=True)[rank]]
+    rng = np.random.default_rng(5 + 1000 * rank)
+    ids = rng.integers(0, cfg.vocab, size=(owned.size, int(owned.max())), dtype=np.int64)
+    return cfg, ids, owned
+
+
+def forward_config(world: int) -> dict:
+    return {"workload": "qwen_forward", "global_batch": 32 * world, "seq_len": "U[32,512]",
+            "layers": 28, "hidden": 1024, "heads": 16, "kv_heads": 8, "head_dim": 128,
+            "intermediate": 3072, "vocab": 151669, "weights": "uint4 random (seed 9)",
+            "pooling": "last token, L2-normalised 1024-d", "layout": "packed (cu_seqlens)",
+            "parallelism": f"text shards x{world} (longest first), no collective",
+            "l2": "not flushed: per-step activations and weights exceed L2 (126 MB)"}
+
+
+def forward_cpu(weights, cfg, ids, lengths, n: int) -> float:
+    """The reference's float32 forward (oracle/qwen3.py) on the first n texts; seconds."""
+    import oracle.qwen3 as oq
+
+    start = time.perf_counter()
+    for i in range(n):
+        oq.qwen3_forward(weights, cfg, ids[i:i + 1, :lengths[i]], lengths[i:i + 1], cfg.hidden,
+                         dtype=np.float32)
+    return time.perf_counter() - start
+
+
+def run_forward_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    from tessery_b200.qwen3 import random_weights
+
+    cfg, ids, lengths = forward_texts(0, world)
+    weights = random_weights(cfg, seed=9)
+    forward_cpu(weights, cfg, ids, lengths, 1)  # warm-up (BLAS threads, page-in)
+    n = 2  # texts per step: a bounded sample of the workload
+    total = sum(forward_cpu(weights, cfg, ids, lengths, n) for _ in range(args.steps))
+    value = n * args.steps / total
+    line = {"metric": FORWARD_METRIC, "value": value, "unit": "texts/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": forward_config(world), "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": "texts/s", "cores": cpu_threads(),
+                             "os_cpu_count": os.cpu_count(), "kind": "port",
+                             "sample": f"first {n} texts per step (lengths {[int(v) for v in lengths[:n]]}), "
+                                       "float32 NumPy restatement of qwen3.py:112-296",
+                             "cpu_model": cpu_model()},
+            "e2e": {"value": value, "unit": "texts/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_forward(args):
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    from tessery_b200 import CudaRuntime
+    from tessery_b200.qwen3 import Qwen3Encoder, random_weights
+
+    rt = CudaRuntime(local)
+    cfg, ids, lengths = forward_texts(rank, world)
+    weights = random_weights(cfg, seed=9)
+    model = Qwen3Encoder(weights, cfg, runtime=rt)
+    dev = torch.device("cuda", local)
+    cu_host = np.zeros(lengths.size + 1, np.int32)
+    cu_host[1:] = np.cumsum(lengths)
+    tokens = np.concatenate([ids[b, :lengths[b]] for b in range(lengths.size)]).astype(np.uint32)
+    ids_d = torch.from_numpy(tokens.view(np.int32)).to(dev)
+    cu_d = torch.from_numpy(cu_host).to(dev)
+    pooled = torch.empty((lengths.size, cfg.hidden), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    sptr = stream.cuda_stream
+
+    def step():
+        model.enqueue(ids_d.data_ptr(), cu_d.data_ptr(), cu_host, pooled.data_ptr(), cfg.hidden,
+                      stream=sptr)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(physical_gpu(local))
+    sampler.start()
+    t_end = time.perf_counter() + args.soak_seconds
+    while time.perf_counter() < t_end:
+        step()
+        torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = rt.launch_count()
+    for i in range(args.steps):
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    launches = rt.launch_count() - launches0
+    clocks = sampler.stop()
+    rt.sync(sptr)
+    ms = [s.elapsed_time(e) for s, e in zip(starts, ends, strict=True)]
+    stats = torch.tensor([sum(ms) * 1e-3], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    total_s = float(stats[0])
+    value = lengths.size * world * args.steps / total_s
+
+    # e2e through Qwen3Encoder.forward: host token ids in, pooled rows back.
+    model.forward(ids, lengths, dimensions=cfg.hidden)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        result = model.forward(ids, lengths, dimensions=cfg.hidden)
+    e2e_stats = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(e2e_stats, op=dist.ReduceOp.MAX)
+    e2e_value = lengths.size * world * args.e2e_steps / float(e2e_stats[0])
+    assert np.allclose(np.linalg.norm(result, axis=1), 1.0, atol=1e-4)
+
+    peaks = measured_peaks()
+    flops = model.flops(lengths)
+    mean_s = statistics.mean(ms) * 1e-3
+    peak = peaks["bf16_tflops_sustained"] or peaks["bf16_tflops"]
+    roof = {"bound": "tensor", "kernel": "whole forward (linear_kernel dominant)",
+            "achieved": flops / mean_s / 1e12, "peak": peak, "unit": "TFLOP/s",
+            "frac": flops / mean_s / 1e12 / peak, "algorithmic_flops_per_step": flops,
+            "peak_source": f"{peaks['source']} sustained bf16 (a long multi-kernel step)",
+            "traffic": None}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        forward_cpu(weights, cfg, ids, lengths, 1)
+        n = 4
+        sec = forward_cpu(weights, cfg, ids, lengths, n)
+        cpu = {"value": n / sec, "unit": "texts/s", "cores": cpu_threads(),
+               "os_cpu_count": os.cpu_count(), "kind": "port",
+               "sample": f"first {n} of {lengths.size} texts (lengths {[int(v) for v in lengths[:n]]}), float32 "
+                         "NumPy restatement of qwen3.py:112-296",
+               "cpu_model": cpu_model()}
+    if rank == 0:
+        line = {"metric": FORWARD_METRIC, "value": value, "unit": "texts/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": 1e3 * total_s / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded random uint4 weights and token ids)",
+                "config": forward_config(world), "roofline": roof,
+                "tokens_per_s": int(lengths.sum()) * world * args.steps / total_s,
+                "route": "linear_kernel + attn_tc_kernel + row kernels", "cpu_baseline": cpu,
+                "e2e": {"value": e2e_value, "unit": "texts/s",
+                        "h2d_bytes_per_step": int(lengths.sum()) * 4 + (lengths.size + 1) * 4,
+                        "d2h_bytes_per_step": int(result.nbytes), "steps": args.e2e_steps,
+                        "path": "tessery_b200.qwen3.Qwen3Encoder.forward (token ids in, pooled "
+                                "rows out)"},
+                "gpu_launches": launches, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    model.close()
+    rt.close()
+    if dist:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.workload == "pool_qwen":
         run_pool_reference(args) if args.impl == "reference" else run_pool(args)
+        return
+    if args.workload == "qwen_forward":
+        run_forward_reference(args) if args.impl == "reference" else run_forward(args)
         return
     if args.impl == "reference":
         run_reference(args)
