@@ -83,6 +83,9 @@ def parse_args():
                    help="per-GPU batch of bge_scaled (smaller for profiler captures)")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--one-process", action="store_true",
+                   help="drive --gpus devices from this one process through the sharded "
+                        "entry points (tessery_b200.sharded) and report their e2e figure")
     p.add_argument("--soak-seconds", type=float, default=1.5,
                    help="step loop run under the clock sampler right before the timed region")
     return p.parse_args()
@@ -277,6 +280,25 @@ def sample_size(w, target_seconds: float) -> int:
     return int(max(1, min(w.batch, target_seconds / max(seconds / n0, 1e-6))))
 
 
+def one_core(run, target_seconds: float) -> dict:
+    """`run(seconds) -> (value, sample)` with every BLAS pool limited to one thread."""
+    try:
+        from threadpoolctl import threadpool_limits
+    except ImportError:
+        return {"value": None, "cores": 1, "sample": "threadpoolctl missing"}
+    with threadpool_limits(limits=1):
+        value, sample = run(target_seconds)
+    return {"value": value, "cores": 1, "sample": sample}
+
+
+def host_cores() -> dict:
+    try:
+        affinity = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        affinity = None
+    return {"os_cpu_count": os.cpu_count(), "affinity_cpus": affinity}
+
+
 def cpu_baseline_run(w, target_seconds: float = 6.0) -> dict:
     n = sample_size(w, target_seconds)
     times = []
@@ -285,10 +307,17 @@ def cpu_baseline_run(w, target_seconds: float = 6.0) -> dict:
         times.append(seconds)
     sec = min(times)
     prologue = ", q/k prologue included" if w.q_norm_weight is not None else ""
+
+    def single(seconds_target):
+        n1 = sample_size(w, seconds_target)
+        s1, t1 = cpu_formula(w, n1)
+        return t1 / s1, f"first {n1} sequences (valid tokens {t1}), one run"
+
     return {"value": tokens / sec, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
             "sample": f"first {n} of {w.batch} sequences of the workload (valid tokens {tokens}),"
                       f" float32 NumPy{prologue}, best of 2",
-            "cpu_model": cpu_model()}
+            "cpu_model": cpu_model(), **host_cores(),
+            "one_core": one_core(single, target_seconds / 2)}
 
 
 def run_reference(args):
@@ -527,8 +556,24 @@ def run_ours(args):
         dist.all_reduce(e2e_stats, op=dist.ReduceOp.MAX)
     e2e_tokens_all = tokens_all / args.steps * args.e2e_steps
     e2e_value = e2e_tokens_all / float(e2e_stats[0])
+    # The same calls with the workload's own (pageable) NumPy arrays and a library-owned
+    # output, as a plain NumPy caller makes them.
+    def pageable_step():
+        return attention(w.q, w.k, w.v, causal=w.causal, scale=w.scale, runtime=rt, **{
+            k_: np.asarray(v_) for k_, v_ in hsel.items()}, **hpro)
+
+    pageable_step()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        pageable_step()
+    pageable = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(pageable, op=dist.ReduceOp.MAX)
+    pageable_value = e2e_tokens_all / float(pageable[0])
     # Bytes that cross the link: in the padded layout the library copies only the valid
-    # k and v rows (the padded ones, never attended, are zeroed on the device).
+    # k and v rows (the padded ones are never read).
     kv_bytes = hk.nbytes + hv.nbytes
     if w.layout == "padded":
         kv_bytes = 2 * w.valid_tokens() * w.kv_heads * w.dim * hk.itemsize
@@ -562,6 +607,11 @@ def run_ours(args):
                 "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
                         "path": "tessery_b200.attention (NumPy in/out, pinned host buffers)"},
+                "e2e_pageable": {"value": pageable_value, "unit": "tokens/s",
+                                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                                 "steps": args.e2e_steps,
+                                 "path": "tessery_b200.attention (the workload's pageable "
+                                         "NumPy arrays, library-owned output)"},
                 "gpu_launches": launches, "wall_s_timed_region": wall, "clocks": clocks}
         if prologue_roof:
             line["prologue_roofline"] = prologue_roof
@@ -998,8 +1048,84 @@ def run_forward(args):
         dist.destroy_process_group()
 
 
+def run_one_process(args):
+    """The whole job of a workload through the one-process multi-GPU entry points: host
+    arrays in, host results out, wall clock around synchronous calls (each call returns
+    after its results are on the host).  qwen_padded: 32 sequences per device; qwen_varlen:
+    the 256 sequences; qwen_forward: 32 texts per device, pooled rows back."""
+    from tessery_b200.sharded import DeviceGroup, ShardedQwen3Encoder, attention_sharded
+    from tessery_b200.workloads import benchmark_workload, qwen_padded
+
+    n = args.gpus
+    group = DeviceGroup(range(n))
+    extra = {}
+    if args.workload == "qwen_forward":
+        from tessery_b200.qwen3 import Qwen3Config, random_weights
+
+        cfg = Qwen3Config()
+        lengths = np.random.default_rng(5).integers(32, 513, size=32 * n)
+        ids = np.random.default_rng(5).integers(0, cfg.vocab, size=(lengths.size, 512))
+        model = ShardedQwen3Encoder(random_weights(cfg, seed=9), cfg, group=group)
+
+        def step():
+            return model.forward(ids, lengths, dimensions=cfg.hidden)
+
+        units, unit, metric = lengths.size, "texts/s", FORWARD_METRIC
+        h2d = int(lengths.sum()) * 4
+        config = forward_config(n)
+        extra["tokens"] = int(lengths.sum())
+    elif args.workload in ("qwen_padded", "qwen_varlen"):
+        if args.workload == "qwen_padded":
+            lengths = np.random.default_rng(2).integers(32, 513, size=32 * n)
+            w = qwen_padded(batch=lengths.size, seq=512, seed=2, lengths=lengths)
+            sel = {"lengths": w.lengths}
+        else:
+            w = benchmark_workload("qwen_varlen", 0, 1)
+            sel = {"cu_seqlens": w.cu_seqlens}
+        model = None
+
+        def step():
+            return attention_sharded(w.q, w.k, w.v, group=group, causal=w.causal, scale=w.scale,
+                                     q_norm_weight=w.q_norm_weight, k_norm_weight=w.k_norm_weight,
+                                     eps=w.eps, theta=w.theta, **sel)
+
+        units, unit, metric = w.valid_tokens(), "tokens/s", metric_of(args.workload)
+        kv_rows = w.valid_tokens() if w.layout == "padded" else w.k.shape[0]
+        h2d = w.q.nbytes + 2 * kv_rows * w.kv_heads * w.dim * w.k.itemsize
+        config = config_block(args.workload, w, n)
+    else:
+        raise SystemExit("--one-process takes qwen_padded, qwen_varlen or qwen_forward")
+    for _ in range(max(args.warmup, 3)):
+        result = step()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        result = step()
+    seconds = time.perf_counter() - t0
+    value = units * args.e2e_steps / seconds
+    config = {**config, "parallelism": f"one process, {n} devices, shards longest first"}
+    line = {"metric": metric, "value": value, "unit": unit, "n_gpus": n,
+            "steps": args.e2e_steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": 1e3 * seconds / args.e2e_steps, "higher_is_better": True,
+            "scaling": scaling_of(args.workload) if args.workload != "qwen_forward" else "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+            "config": config, "impl": "ours-one-process",
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": int(result.nbytes), "steps": args.e2e_steps,
+                    "path": "tessery_b200.sharded (host arrays in, host results out)"},
+            "host_gbs": {"h2d": h2d / (seconds / args.e2e_steps) / 1e9,
+                         "d2h": result.nbytes / (seconds / args.e2e_steps) / 1e9},
+            **extra}
+    print(json.dumps(line), flush=True)
+    if model is not None:
+        model.close()
+    group.close()
+
+
 def main():
     args = parse_args()
+    if args.one_process:
+        run_one_process(args)
+        return
     if args.workload == "pool_qwen":
         run_pool_reference(args) if args.impl == "reference" else run_pool(args)
         return

@@ -267,7 +267,9 @@ int tx_pool_project(void *ctx, const void *x, int in_dtype, const uint32_t *leng
  * and it keeps the last call's contents: calls whose work overlaps on the GPU race.
  * status (required, device int): zeroed by this call, then set by the kernel to
  * TX_ETIMEOUT | site << 8 if a bounded wait gives up; read it after the stream has
- * drained.  Returns TX_OK once queued on `stream` (NULL: the legacy default stream). */
+ * drained.  Returns TX_OK once queued on `stream` (NULL: the legacy default stream),
+ * TX_EINVAL while `stream` is being captured (the work list is copied from host memory
+ * that the next call overwrites). */
 int tx_attention_padded_noalloc(const void *q, const void *k, const void *v,
                                 const uint32_t *lengths, const uint32_t *lengths_host,
                                 void *out, uint32_t batch, uint32_t seq, uint32_t heads,
@@ -330,6 +332,54 @@ int tx_rms_norm_rows(void *ctx, const float *x, const uint16_t *w, void *out, in
 int tx_linear(void *ctx, const uint16_t *x, const uint16_t *x_lo, const uint16_t *w,
               const uint16_t *w_lo, void *out, uint32_t m, uint32_t n, uint32_t k, int mode,
               void *stream);
+
+/* The whole forward as one call: the layer loop of Qwen3Backend.forward
+ * (qwen3.py:112-296; its per-layer dispatch sequence is qwen3.py:191-280, the final norm
+ * and last-token pooling :281-290) queued on the device from native code.  The caller
+ * fills the model description once (device pointers to weights already dequantised by
+ * tx_dequant4, gate and up rows interleaved for TX_LINEAR_GATED_BF16) and then issues one
+ * call per batch; nothing is allocated by the call.  Sequences are packed by cu_seqlens
+ * (no padded rows).  Fast mode: bf16 projection operands, the tensor-core attention.
+ * Precise mode (`precise` != 0): every projection matrix is followed in memory by its
+ * bf16 rounding residues (tx_dequant4 with out_lo = w + n * k), activations enter each
+ * projection as bf16 pairs, q/k/v and the attention are fp32. */
+typedef struct {
+  const uint16_t *input_norm, *post_norm;  /* bf16 [hidden] */
+  const uint16_t *q_norm, *k_norm;         /* bf16 [head_dim] */
+  const uint16_t *q_proj, *k_proj, *v_proj; /* bf16 [heads|kv_heads * head_dim, hidden] */
+  const uint16_t *o_proj;                  /* bf16 [hidden, heads * head_dim] */
+  const uint16_t *gate_up;                 /* bf16 [2 * intermediate, hidden], interleaved */
+  const uint16_t *down;                    /* bf16 [hidden, intermediate] */
+} TxQwen3Layer;
+
+typedef struct {
+  uint32_t hidden, intermediate, layers, heads, kv_heads, head_dim, vocab;
+  float eps, theta;
+  int precise;
+  const uint32_t *embed_packed;            /* uint4 table [vocab, hidden / 8] */
+  const uint16_t *embed_scales, *embed_biases; /* bf16 [vocab, hidden / 64] */
+  const uint16_t *final_norm;              /* bf16 [hidden] */
+  const TxQwen3Layer *layer;               /* host array of `layers` entries */
+} TxQwen3Model;
+
+/* Bytes of device workspace tx_qwen3_forward needs for `tokens` packed tokens (0 when the
+ * model's shapes are not supported: head_dim 128, hidden, heads * head_dim and kv_heads *
+ * head_dim multiples of 256, intermediate a multiple of 128). */
+uint64_t tx_qwen3_workspace_bytes(const TxQwen3Model *model, uint32_t tokens);
+
+/* Pooled, L2-normalised embeddings `pooled` (device fp32 [nseq, dimensions]) of the token
+ * ids `ids` (device uint32 [cu_host[nseq]]) packed by `cu_seqlens` (device int32 [nseq+1],
+ * host copy `cu_host`).  `workspace`: device memory of at least tx_qwen3_workspace_bytes
+ * bytes, 256-byte aligned.  Queued on `stream` (NULL: the context's stream); errors of the
+ * device side (an id >= vocab, a wait that gave up) come from the next tx_sync. */
+int tx_qwen3_forward(void *ctx, const TxQwen3Model *model, const uint32_t *ids,
+                     const int32_t *cu_seqlens, const int32_t *cu_host, uint32_t nseq,
+                     float *pooled, uint32_t dimensions, void *workspace,
+                     uint64_t workspace_bytes, void *stream);
+
+/* Number of CUDA devices visible to this process (0 when none or on error): the devices
+ * a sharded caller creates one context on each. */
+int tx_device_count(void);
 
 /* Waits for all work queued on `stream` (NULL: context stream) and reports kernel
  * errors, including device-side wait timeouts, as a status code. */

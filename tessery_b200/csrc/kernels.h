@@ -134,4 +134,8 @@ cudaError_t launch_linear(const void *x, const void *x_lo, const void *w, const 
                           void *out, uint32_t m, uint32_t n, uint32_t k, int mode, int *status,
                           long long wait_cycles, cudaStream_t stream);
 
+// Records `msg` as the context's last error (tx_last_error) and returns `code`: for entry
+// points built outside runtime.cu on top of the public ones.
+int ctx_fail(void *ctx, int code, const char *msg);
+
 }  // namespace tx

@@ -84,6 +84,11 @@ extern "C" int tx_attention_padded_noalloc(const void *q, const void *k, const v
   }
   uint32_t *scratch = g_noalloc_ptr[device];
   cudaStream_t s = (cudaStream_t)stream;
+  // The work list is copied from a static host array that the next call overwrites: a
+  // captured copy would replay another call's list, so a capturing stream is refused.
+  cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &capturing) != cudaSuccess) return TX_ECUDA;
+  if (capturing != cudaStreamCaptureStatusNone) return TX_EINVAL;
   int *st = status;
   const int sms = g_noalloc_sms[device];
   if (sms < 1 || tx::tc_grid(tx::tc_max_units(p), sms) + 1 > kNoAllocMaxOffsets) return TX_EINVAL;

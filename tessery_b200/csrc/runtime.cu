@@ -21,7 +21,7 @@
 
 namespace {
 
-constexpr uint32_t kAbiVersion = 6;
+constexpr uint32_t kAbiVersion = 7;
 constexpr uint32_t kHostChunks = 8;              // most chunks of a host-buffer call
 constexpr size_t kHostChunkBytes = 16u << 20;     // bytes moved per chunk, at least
 
@@ -552,6 +552,15 @@ void prof_end(Ctx *c) {
 }
 
 }  // namespace
+
+namespace tx {
+int ctx_fail(void *ctx, int code, const char *msg) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return code;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  return fail(c, code, msg);
+}
+}  // namespace tx
 
 extern "C" {
 
@@ -1231,6 +1240,11 @@ int tx_linear(void *ctx, const uint16_t *x, const uint16_t *x_lo, const uint16_t
   c->last_kernel = "linear";
   ++c->launches;
   return TX_OK;
+}
+
+int tx_device_count(void) {
+  int n = 0;
+  return cudaGetDeviceCount(&n) == cudaSuccess && n > 0 ? n : 0;
 }
 
 int tx_sync(void *ctx, void *stream) {

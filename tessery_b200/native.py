@@ -16,7 +16,7 @@ from typing import Any
 
 from .errors import NativeBuildError
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 LIBRARY_NAME = "libtessattn.so"
 
 TX_OK, TX_EINVAL, TX_ECUDA, TX_ETIMEOUT = 0, 1, 2, 3
@@ -24,6 +24,27 @@ TX_F32, TX_BF16, TX_BF16X2 = 0, 1, 2
 TX_LINEAR_STORE_F32, TX_LINEAR_STORE_BF16, TX_LINEAR_ADD_F32, TX_LINEAR_GATED_BF16 = 0, 1, 2, 3
 
 _vp, _u32, _u64, _i32, _f32 = ct.c_void_p, ct.c_uint32, ct.c_uint64, ct.c_int, ct.c_float
+
+
+class TxQwen3Layer(ct.Structure):
+    """Device pointers of one layer's weights (TxQwen3Layer in tessattn.h)."""
+
+    _fields_ = [(name, _vp) for name in (
+        "input_norm", "post_norm", "q_norm", "k_norm", "q_proj", "k_proj", "v_proj", "o_proj",
+        "gate_up", "down")]
+
+
+class TxQwen3Model(ct.Structure):
+    """Shape and weights of a Qwen3 embedding model (TxQwen3Model in tessattn.h)."""
+
+    _fields_ = [
+        *[(name, _u32) for name in ("hidden", "intermediate", "layers", "heads", "kv_heads",
+                                    "head_dim", "vocab")],
+        ("eps", _f32), ("theta", _f32), ("precise", _i32),
+        ("embed_packed", _vp), ("embed_scales", _vp), ("embed_biases", _vp),
+        ("final_norm", _vp), ("layer", ct.POINTER(TxQwen3Layer)),
+    ]
+
 
 SIGNATURES: dict[str, tuple[list[Any], Any]] = {
     "tx_abi_version": ([], _u32),
@@ -80,6 +101,10 @@ SIGNATURES: dict[str, tuple[list[Any], Any]] = {
         _i32,
     ),
     "tx_sync": ([_vp, _vp], _i32),
+    "tx_device_count": ([], _i32),
+    "tx_qwen3_workspace_bytes": ([ct.POINTER(TxQwen3Model), _u32], _u64),
+    "tx_qwen3_forward": (
+        [_vp, ct.POINTER(TxQwen3Model), _vp, _vp, _vp, _u32, _vp, _u32, _vp, _u64, _vp], _i32),
     "tx_dequant4": ([_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _vp], _i32),
     "tx_split_bf16": ([_vp, _vp, _vp, _u64, _vp], _i32),
     "tx_embedding4": ([_vp, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _u32, _vp], _i32),

@@ -21,9 +21,15 @@ def sequence_cost(lengths: NDArray, causal: bool) -> NDArray[np.int64]:
 
 def shard_sequences(lengths: NDArray, world: int, causal: bool = True) -> list[NDArray[np.int64]]:
     """Returns, per rank, the (sorted) indices of the sequences it owns."""
+    return shard_by_cost(sequence_cost(lengths, causal), world)
+
+
+def shard_by_cost(cost: NDArray, world: int) -> list[NDArray[np.int64]]:
+    """Longest-processing-time assignment of items with these costs to `world` ranks:
+    per rank, the (sorted) indices of the items it owns."""
     if world < 1:
         raise ValueError("world must be positive")
-    cost = sequence_cost(lengths, causal)
+    cost = np.asarray(cost, dtype=np.int64)
     order = np.argsort(-cost, kind="stable")
     heap = [(0, r) for r in range(world)]
     owned: list[list[int]] = [[] for _ in range(world)]

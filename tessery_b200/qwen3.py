@@ -19,6 +19,7 @@ NumPy in, NumPy out; device work through the C ABI of libtessattn.so.
 
 from __future__ import annotations
 
+import ctypes as ct
 from dataclasses import dataclass
 
 import numpy as np
@@ -150,6 +151,7 @@ class Qwen3Encoder:
                          for s in ("weight", "scales", "biases")]
                 self._dev[f"{prefix}.mlp.gate_up"] = self._dequantised(*fused)
             rt.sync()
+            self._model = self._describe()
         except BaseException:
             self.close()
             raise
@@ -219,109 +221,39 @@ class Qwen3Encoder:
         """Queues the whole forward on `stream` (None: the context's stream) without
         waiting: token ids `ids` (device uint32 [T]) packed by `cu` (device int32
         [batch + 1], host copy `cu_seqlens`) to pooled embeddings `pooled` (device fp32
-        [batch, dimensions]).  Activations live in the runtime's named workspaces."""
-        if self.precise:
-            self._enqueue_precise(ids, cu, cu_seqlens, pooled, dimensions, stream)
-            return
-        cfg, rt = self.cfg, self.rt
-        H, KV, D, I = cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.intermediate
-        qd, kd = H * D, KV * D
-        T, B = int(cu_seqlens[-1]), int(cu_seqlens.size - 1)
-        max_len = int(np.max(np.diff(cu_seqlens)))
-        ws = rt.workspace
-        x = ws("qwen.x", T * cfg.hidden * 4)          # fp32 residual stream
-        xn = ws("qwen.xn", T * cfg.hidden * 2)        # bf16 normalised rows
-        q, k, v = ws("qwen.q", T * qd * 2), ws("qwen.k", T * kd * 2), ws("qwen.v", T * kd * 2)
-        att = ws("qwen.att", T * qd * 2)              # bf16 attention output
-        gated = ws("qwen.gated", T * I * 2)           # bf16 silu(gate) * up
-        d = self._dev
-        lin = rt.linear_device
-        rt.embedding4_device(ids, x.device_ptr, tokens=T, packed=d["embed.weight"].device_ptr,
-                             scales=d["embed.scales"].device_ptr,
-                             biases=d["embed.biases"].device_ptr, cols=cfg.hidden,
-                             vocab=cfg.vocab, stream=stream)
+        [batch, dimensions]).  One native call (tx_qwen3_forward) queues every launch;
+        the activations live in the runtime's workspace "qwen.forward"."""
+        rt = self.rt
+        cu_host = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+        need = int(rt._lib.tx_qwen3_workspace_bytes(ct.byref(self._model), int(cu_host[-1])))
+        if not need:
+            raise InvalidInputError()
+        ws = rt.workspace("qwen.forward", need)
+        rt.qwen3_forward_device(ct.byref(self._model), ids, cu, cu_host, pooled, dimensions,
+                                ws.device_ptr, ws.size, stream=stream)
+
+    def _describe(self) -> native.TxQwen3Model:
+        """The native model description: shapes and the device pointers of every weight."""
+        cfg, d = self.cfg, self._dev
+        layers = (native.TxQwen3Layer * cfg.layers)()
         for layer in range(cfg.layers):
             p = f"model.layers.{layer}"
-            rt.rms_norm_rows_device(x.device_ptr, d[p + ".input_layernorm"].device_ptr,
-                                    xn.device_ptr, rows=T, cols=cfg.hidden, eps=cfg.eps,
-                                    stream=stream)
-            for name, out, n in (("q_proj", q, qd), ("k_proj", k, kd), ("v_proj", v, kd)):
-                lin(xn.device_ptr, d[f"{p}.self_attn.{name}"].device_ptr, out.device_ptr,
-                    m=T, n=n, k=cfg.hidden, mode=native.TX_LINEAR_STORE_BF16, stream=stream)
-            rt.attention_varlen_device(
-                q.device_ptr, k.device_ptr, v.device_ptr, cu, att.device_ptr, nseq=B, total=T,
-                max_len=max_len, heads=H, kv_heads=KV, dim=D, in_dtype=native.TX_BF16,
-                out_dtype=native.TX_BF16, causal=True, cu_seqlens_host=cu_seqlens,
-                q_norm_weight=d[p + ".self_attn.q_norm"].device_ptr,
-                k_norm_weight=d[p + ".self_attn.k_norm"].device_ptr, eps=cfg.eps,
-                theta=cfg.theta, stream=stream)
-            lin(att.device_ptr, d[f"{p}.self_attn.o_proj"].device_ptr, x.device_ptr, m=T,
-                n=cfg.hidden, k=qd, mode=native.TX_LINEAR_ADD_F32, stream=stream)
-            rt.rms_norm_rows_device(x.device_ptr, d[p + ".post_attention_layernorm"].device_ptr,
-                                    xn.device_ptr, rows=T, cols=cfg.hidden, eps=cfg.eps,
-                                    stream=stream)
-            lin(xn.device_ptr, d[f"{p}.mlp.gate_up"].device_ptr, gated.device_ptr, m=T,
-                n=2 * I, k=cfg.hidden, mode=native.TX_LINEAR_GATED_BF16, stream=stream)
-            lin(gated.device_ptr, d[f"{p}.mlp.down_proj"].device_ptr, x.device_ptr, m=T,
-                n=cfg.hidden, k=I, mode=native.TX_LINEAR_ADD_F32, stream=stream)
-        rt.pool_project_device(x.device_ptr, pooled, batch=B, cols=cfg.hidden, dim=dimensions,
-                               cu_seqlens=cu, norm_weight=d["model.norm"].device_ptr,
-                               eps=cfg.eps, stream=stream)
-
-    def _enqueue_precise(self, ids: int, cu: int, cu_seqlens: NDArray[np.int32], pooled: int,
-                         dimensions: int, stream: int | None) -> None:
-        """enqueue() in precise mode: bf16-pair projection operands (x . w + x . w_lo +
-        x_lo . w), fp32 q/k/v, attention and residual stream."""
-        cfg, rt = self.cfg, self.rt
-        H, KV, D, I = cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.intermediate
-        qd, kd, hid = H * D, KV * D, cfg.hidden
-        T, B = int(cu_seqlens[-1]), int(cu_seqlens.size - 1)
-        max_len = int(np.max(np.diff(cu_seqlens)))
-        ws = rt.workspace
-        x = ws("qwen.x", T * hid * 4)
-        xn = ws("qwen.xn2", 2 * T * hid * 2)          # bf16 pair of the normalised rows
-        q, k, v = ws("qwen.q32", T * qd * 4), ws("qwen.k32", T * kd * 4), ws("qwen.v32", T * kd * 4)
-        att = ws("qwen.att32", T * qd * 4)
-        att2 = ws("qwen.att2", 2 * T * qd * 2)        # bf16 pair of the attention output
-        gated = ws("qwen.gated2", 2 * T * I * 2)      # bf16 pair of silu(gate) * up
-        d = self._dev
-
-        def lin(a: Buffer, a_rows: int, a_cols: int, w: Buffer, out: int, n: int, mode: int):
-            lo = a.device_ptr + a_rows * a_cols * 2
-            rt.linear_device(a.device_ptr, w.device_ptr, out, m=a_rows, n=n, k=a_cols, mode=mode,
-                             x_lo=lo, w_lo=w.device_ptr + n * a_cols * 2, stream=stream)
-
-        rt.embedding4_device(ids, x.device_ptr, tokens=T, packed=d["embed.weight"].device_ptr,
-                             scales=d["embed.scales"].device_ptr,
-                             biases=d["embed.biases"].device_ptr, cols=hid, vocab=cfg.vocab,
-                             stream=stream)
-        for layer in range(cfg.layers):
-            p = f"model.layers.{layer}"
-            rt.rms_norm_rows_device(x.device_ptr, d[p + ".input_layernorm"].device_ptr,
-                                    xn.device_ptr, rows=T, cols=hid, eps=cfg.eps,
-                                    out_dtype=native.TX_BF16X2, stream=stream)
-            for name, out, n in (("q_proj", q, qd), ("k_proj", k, kd), ("v_proj", v, kd)):
-                lin(xn, T, hid, d[f"{p}.self_attn.{name}"], out.device_ptr, n,
-                    native.TX_LINEAR_STORE_F32)
-            rt.attention_varlen_device(
-                q.device_ptr, k.device_ptr, v.device_ptr, cu, att.device_ptr, nseq=B, total=T,
-                max_len=max_len, heads=H, kv_heads=KV, dim=D, in_dtype=native.TX_F32,
-                out_dtype=native.TX_F32, causal=True, cu_seqlens_host=cu_seqlens,
-                q_norm_weight=d[p + ".self_attn.q_norm"].device_ptr,
-                k_norm_weight=d[p + ".self_attn.k_norm"].device_ptr, eps=cfg.eps,
-                theta=cfg.theta, stream=stream)
-            rt.split_bf16_device(att.device_ptr, att2.device_ptr, n=T * qd, stream=stream)
-            lin(att2, T, qd, d[f"{p}.self_attn.o_proj"], x.device_ptr, hid,
-                native.TX_LINEAR_ADD_F32)
-            rt.rms_norm_rows_device(x.device_ptr, d[p + ".post_attention_layernorm"].device_ptr,
-                                    xn.device_ptr, rows=T, cols=hid, eps=cfg.eps,
-                                    out_dtype=native.TX_BF16X2, stream=stream)
-            lin(xn, T, hid, d[f"{p}.mlp.gate_up"], gated.device_ptr, 2 * I,
-                native.TX_LINEAR_GATED_BF16)
-            lin(gated, T, I, d[f"{p}.mlp.down_proj"], x.device_ptr, hid, native.TX_LINEAR_ADD_F32)
-        rt.pool_project_device(x.device_ptr, pooled, batch=B, cols=hid, dim=dimensions,
-                               cu_seqlens=cu, norm_weight=d["model.norm"].device_ptr,
-                               eps=cfg.eps, stream=stream)
+            ptr = {key: d[name].device_ptr for key, name in (
+                ("input_norm", p + ".input_layernorm"),
+                ("post_norm", p + ".post_attention_layernorm"),
+                ("q_norm", p + ".self_attn.q_norm"), ("k_norm", p + ".self_attn.k_norm"),
+                ("q_proj", p + ".self_attn.q_proj"), ("k_proj", p + ".self_attn.k_proj"),
+                ("v_proj", p + ".self_attn.v_proj"), ("o_proj", p + ".self_attn.o_proj"),
+                ("gate_up", p + ".mlp.gate_up"), ("down", p + ".mlp.down_proj"))}
+            layers[layer] = native.TxQwen3Layer(**ptr)
+        self._layers = layers  # the description points into this array
+        return native.TxQwen3Model(
+            hidden=cfg.hidden, intermediate=cfg.intermediate, layers=cfg.layers,
+            heads=cfg.heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, vocab=cfg.vocab,
+            eps=cfg.eps, theta=cfg.theta, precise=int(self.precise),
+            embed_packed=d["embed.weight"].device_ptr, embed_scales=d["embed.scales"].device_ptr,
+            embed_biases=d["embed.biases"].device_ptr, final_norm=d["model.norm"].device_ptr,
+            layer=ct.cast(layers, ct.POINTER(native.TxQwen3Layer)))
 
     def flops(self, lengths: NDArray) -> int:
         """Multiply-add work of one forward over sequences of these lengths, counted as 2

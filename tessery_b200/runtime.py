@@ -586,6 +586,19 @@ class CudaRuntime:
         _raise_for(self._lib.tx_linear(self._pointer, x, x_lo, w, w_lo, out, m, n, k, mode,
                                        stream))
 
+    def qwen3_forward_device(self, model: Any, ids: int, cu_seqlens: int,
+                             cu_host: NDArray[np.int32], pooled: int, dimensions: int,
+                             workspace: int, workspace_bytes: int,
+                             stream: int | None = None) -> None:
+        """Queues the whole Qwen3 embedding forward (tx_qwen3_forward): `model` is a
+        reference to a native.TxQwen3Model, `cu_host` the host copy of the packed
+        sequences' cu_seqlens."""
+        self._check_open()
+        cu_host = np.ascontiguousarray(cu_host, dtype=np.int32)
+        _raise_for(self._lib.tx_qwen3_forward(
+            self._pointer, model, ids, cu_seqlens, cu_host.ctypes.data, cu_host.size - 1,
+            pooled, dimensions, workspace, workspace_bytes, stream))
+
     def sync(self, stream: int | None = None) -> None:
         """Waits for queued work and reports kernel errors (tx_sync)."""
         self._check_open()
