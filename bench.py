@@ -1083,11 +1083,21 @@ def run_one_process(args):
             w = benchmark_workload("qwen_varlen", 0, 1)
             sel = {"cu_seqlens": w.cu_seqlens}
         model = None
+        from tessery_b200.host import pinned_copy, pinned_empty
+
+        # Page-locked inputs and output, as for the one-device e2e figure.
+        hq, hk, hv = pinned_copy(w.q), pinned_copy(w.k), pinned_copy(w.v)
+        hout = pinned_empty(w.q.shape, np.float32)
+        kw = dict(group=group, causal=w.causal, scale=w.scale, q_norm_weight=w.q_norm_weight,
+                  k_norm_weight=w.k_norm_weight, eps=w.eps, theta=w.theta, **sel)
 
         def step():
-            return attention_sharded(w.q, w.k, w.v, group=group, causal=w.causal, scale=w.scale,
-                                     q_norm_weight=w.q_norm_weight, k_norm_weight=w.k_norm_weight,
-                                     eps=w.eps, theta=w.theta, **sel)
+            return attention_sharded(hq, hk, hv, out=hout, **kw)
+
+        def pageable_step():
+            return attention_sharded(w.q, w.k, w.v, **kw)
+
+        extra["pageable"] = pageable_step
 
         units, unit, metric = w.valid_tokens(), "tokens/s", metric_of(args.workload)
         kv_rows = w.valid_tokens() if w.layout == "padded" else w.k.shape[0]
@@ -1102,6 +1112,14 @@ def run_one_process(args):
         result = step()
     seconds = time.perf_counter() - t0
     value = units * args.e2e_steps / seconds
+    pageable = extra.pop("pageable", None)
+    if pageable is not None:
+        pageable()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            pageable()
+        extra["e2e_pageable"] = {"value": units * args.e2e_steps / (time.perf_counter() - t0),
+                                 "unit": unit, "path": "the workload's pageable NumPy arrays"}
     config = {**config, "parallelism": f"one process, {n} devices, shards longest first"}
     line = {"metric": metric, "value": value, "unit": unit, "n_gpus": n,
             "steps": args.e2e_steps, "warmup": max(args.warmup, 3),
@@ -1111,7 +1129,8 @@ def run_one_process(args):
             "config": config, "impl": "ours-one-process",
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": int(result.nbytes), "steps": args.e2e_steps,
-                    "path": "tessery_b200.sharded (host arrays in, host results out)"},
+                    "path": "tessery_b200.sharded (host arrays in, host results out; "
+                            "page-locked for the attention workloads)"},
             "host_gbs": {"h2d": h2d / (seconds / args.e2e_steps) / 1e9,
                          "d2h": result.nbytes / (seconds / args.e2e_steps) / 1e9},
             **extra}

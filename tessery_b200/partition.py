@@ -40,6 +40,28 @@ def shard_by_cost(cost: NDArray, world: int) -> list[NDArray[np.int64]]:
     return [np.array(sorted(o), dtype=np.int64) for o in owned]
 
 
+def shard_ranges(cost: NDArray, world: int) -> list[tuple[int, int]]:
+    """Contiguous, cost-balanced split of items [0, n) into `world` ranges [a, b): cut
+    where the running cost crosses each multiple of total / world.  The ranges of a
+    packed or padded batch are contiguous in memory, so a shard needs no gather; the
+    imbalance is at most about one item's cost."""
+    if world < 1:
+        raise ValueError("world must be positive")
+    cost = np.asarray(cost, dtype=np.float64)
+    prefix = np.concatenate([[0.0], np.cumsum(cost)])
+    total = prefix[-1]
+    cuts = [0]
+    for r in range(1, world):
+        target = total * r / world
+        c = int(np.searchsorted(prefix, target))
+        # The cut nearer to the target, kept monotone.
+        if c > 0 and abs(prefix[c - 1] - target) <= abs(prefix[min(c, cost.size)] - target):
+            c -= 1
+        cuts.append(min(max(c, cuts[-1]), cost.size))
+    cuts.append(cost.size)
+    return [(cuts[r], cuts[r + 1]) for r in range(world)]
+
+
 def pack(lengths: NDArray) -> NDArray[np.int32]:
     """cu_seqlens for sequences laid end to end."""
     n = np.asarray(lengths, dtype=np.int64)

@@ -3,11 +3,13 @@
 The reference runs on one Apple GPU and has no multi-device code; what makes this
 sharding exact is that its attention never mixes sequences (kernels.metal:86-91 indexes
 every load by its own batch row) and its embedding forward is per text
-(qwen3.py:112-296).  So a batch splits into independent shards: sequences are assigned
-longest-processing-time first by their cost (partition.shard_by_cost), every device runs
-its shard on its own context and stream, and no collective is needed on the data path.
-Only results come back: the attention rows of each shard, or just the pooled embeddings
-of the forward.
+(qwen3.py:112-296).  So a batch splits into independent shards, every device runs its
+shard on its own context and stream, and no collective is needed on the data path.  The
+attention splits a batch into contiguous ranges of sequences balanced by cost
+(partition.shard_ranges): each device's inputs and outputs are then views of the
+caller's arrays, moved without a host-side gather (at full link speed when the arrays
+are page-locked).  The forward, whose inputs are token ids, assigns texts longest first
+(partition.shard_by_cost) and copies back only the pooled embeddings.
 
 One host thread per device issues that device's calls.  Every call into the native
 library releases the interpreter lock for its whole duration (the host-buffer attention
@@ -27,8 +29,7 @@ from numpy.typing import NDArray
 from . import native
 from .attention import attention
 from .errors import CudaUnavailableError, InvalidInputError
-from .host import pinned_empty
-from .partition import pack, sequence_cost, shard_by_cost
+from .partition import sequence_cost, shard_by_cost, shard_ranges
 from .runtime import CudaRuntime
 
 
@@ -51,7 +52,6 @@ class DeviceGroup:
             raise InvalidInputError()
         self.runtimes: list[CudaRuntime] = []
         self._pool: ThreadPoolExecutor | None = None
-        self._staging: dict[tuple[int, str], NDArray] = {}
         try:
             for d in self.devices:
                 self.runtimes.append(CudaRuntime(d))
@@ -63,18 +63,6 @@ class DeviceGroup:
 
     def __len__(self) -> int:
         return len(self.devices)
-
-    def staging(self, index: int, name: str, shape: tuple[int, ...], dtype: Any) -> NDArray:
-        """A page-locked host array of this shape for device `index`, reused across calls
-        (grown when too small): the host side of that device's copies."""
-        dtype = np.dtype(dtype)
-        nbytes = int(np.prod(shape)) * dtype.itemsize
-        key = (index, name)
-        buf = self._staging.get(key)
-        if buf is None or buf.nbytes < nbytes:
-            buf = pinned_empty((max(nbytes, 1),), np.uint8)
-            self._staging[key] = buf
-        return buf[:nbytes].view(dtype).reshape(shape)
 
     def run(self, fn: Callable[[CudaRuntime, Any], Any], work: Sequence[Any]) -> list[Any]:
         """fn(runtime, work[i]) for every device i at the same time; results in device
@@ -108,47 +96,12 @@ class DeviceGroup:
         for rt in self.runtimes:
             rt.close()
         self.runtimes = []
-        self._staging.clear()
 
     def __enter__(self) -> DeviceGroup:
         return self
 
     def __exit__(self, *_: object) -> None:
         self.close()
-
-
-def _gather(dst: NDArray, src: NDArray, starts: NDArray[np.int64], counts: NDArray[np.int64]
-            ) -> None:
-    """dst = the blocks src[starts[i] : starts[i] + counts[i]] laid end to end along axis
-    0 (one contiguous copy per block: sequences are contiguous in both layouts)."""
-    at = 0
-    for a, n in zip(starts.tolist(), counts.tolist(), strict=True):
-        dst[at:at + n] = src[a:a + n]
-        at += n
-
-
-def _scatter(dst: NDArray, src: NDArray, starts: NDArray[np.int64],
-             counts: NDArray[np.int64]) -> None:
-    """The inverse of _gather."""
-    at = 0
-    for a, n in zip(starts.tolist(), counts.tolist(), strict=True):
-        dst[a:a + n] = src[at:at + n]
-        at += n
-
-
-def _stage(group: DeviceGroup, i: int, starts: NDArray[np.int64], counts: NDArray[np.int64],
-           q: NDArray, k: NDArray, v: NDArray, out_dtype: Any
-           ) -> tuple[NDArray, NDArray, NDArray, NDArray]:
-    """Device i's blocks of q, k and v gathered into its page-locked staging arrays, and a
-    staging array for its output rows."""
-    rows = int(counts.sum())
-    staged = []
-    for name, a in (("q", q), ("k", k), ("v", v)):
-        s = group.staging(i, name, (rows, *a.shape[1:]), a.dtype)
-        _gather(s, a, starts, counts)
-        staged.append(s)
-    staged.append(group.staging(i, "out", (rows, *q.shape[1:]), out_dtype))
-    return staged[0], staged[1], staged[2], staged[3]
 
 
 def attention_sharded(
@@ -191,16 +144,14 @@ def attention_sharded(
         lens = np.asarray(lengths)
         if lens.ndim != 1 or q.ndim != 4 or lens.size != q.shape[0]:
             raise InvalidInputError()
-        owned = shard_by_cost(sequence_cost(lens, causal), len(group))
+        ranges = shard_ranges(sequence_cost(lens, causal), len(group))
 
-        def padded(rt: CudaRuntime, job: tuple[int, NDArray[np.int64]]) -> None:
-            i, seqs = job
-            ones = np.ones_like(seqs)
-            qs, ks, vs, os_ = _stage(group, i, seqs, ones, q, k, v, out_np)
-            attention(qs, ks, vs, lengths=lens[seqs], runtime=rt, out=os_, **common)
-            _scatter(out, os_, seqs, ones)
+        def padded(rt: CudaRuntime, span: tuple[int, int]) -> None:
+            a, b = span
+            attention(q[a:b], k[a:b], v[a:b], lengths=lens[a:b], runtime=rt, out=out[a:b],
+                      **common)
 
-        group.run(padded, [(i, o) if o.size else None for i, o in enumerate(owned)])
+        group.run(padded, [r if r[1] > r[0] else None for r in ranges])
         return out
     cu = np.asarray(cu_seqlens, dtype=np.int64)
     if cu.ndim != 1 or cu.size < 2 or q.ndim != 3 or int(cu[-1]) != q.shape[0]:
@@ -208,15 +159,15 @@ def attention_sharded(
     lens = np.diff(cu)
     if np.any(lens <= 0):
         raise InvalidInputError()
-    owned = shard_by_cost(sequence_cost(lens, causal), len(group))
+    ranges = shard_ranges(sequence_cost(lens, causal), len(group))
 
-    def packed(rt: CudaRuntime, job: tuple[int, NDArray[np.int64]]) -> None:
-        i, seqs = job
-        qs, ks, vs, os_ = _stage(group, i, cu[seqs], lens[seqs], q, k, v, out_np)
-        attention(qs, ks, vs, cu_seqlens=pack(lens[seqs]), runtime=rt, out=os_, **common)
-        _scatter(out, os_, cu[seqs], lens[seqs])
+    def packed(rt: CudaRuntime, span: tuple[int, int]) -> None:
+        a, b = span
+        r0, r1 = int(cu[a]), int(cu[b])
+        attention(q[r0:r1], k[r0:r1], v[r0:r1], cu_seqlens=(cu[a:b + 1] - r0).astype(np.int32),
+                  runtime=rt, out=out[r0:r1], **common)
 
-    group.run(packed, [(i, o) if o.size else None for i, o in enumerate(owned)])
+    group.run(packed, [r if r[1] > r[0] else None for r in ranges])
     return out
 
 
