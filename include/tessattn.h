@@ -291,9 +291,14 @@ enum {
   TX_LINEAR_STORE_F32 = 0,  /* out fp32 [m, n] = x . w^T */
   TX_LINEAR_STORE_BF16 = 1, /* out bf16 [m, n] */
   TX_LINEAR_ADD_F32 = 2,    /* out fp32 [m, n] += x . w^T (the residual add, qwen3.py:151-152) */
-  TX_LINEAR_GATED_BF16 = 3  /* out bf16 [m, n / 2]: silu(gate) * up, w rows interleaved in
+  TX_LINEAR_GATED_BF16 = 3, /* out bf16 [m, n / 2]: silu(gate) * up, w rows interleaved in
                                blocks of 128 gate then 128 up rows (gated4 + silu_gate,
-                               kernels.metal:333-337, 609-733) */
+                               kernels.metal:333-337, 609-733); bf16 operands only */
+  TX_LINEAR_GELU_SPLIT = 4  /* out = gelu(x . w^T + bias) (erf form, gelu_f32,
+                               kernels.metal:381-391) written as the next GEMM's split
+                               operand: hi [m, n] then lo [m, n], each in the operand
+                               format (bf16, or fp32 holding hi = TF32-rounded value and
+                               lo = value - hi) */
 };
 
 /* Dequantises a uint4 weight matrix once into bf16 [rows, cols] (out), the operand layout
@@ -323,15 +328,21 @@ int tx_rms_norm_rows(void *ctx, const float *x, const uint16_t *w, void *out, in
                      uint32_t rows, uint32_t cols, float eps, void *stream);
 
 /* Replaces the reference's _linear4 / _gated4 routing (metal.py:416-530) on dequantised
- * weights: x bf16 [m, k] times w bf16 [n, k] transposed, fp32 accumulation on tensor cores,
- * epilogue `mode` (TX_LINEAR_*).  With w_lo (and optionally x_lo), the lo halves of bf16
- * pairs, the product is x.w + x.w_lo (+ x_lo.w), which carries about 16 significant bits
- * of each operand instead of 8 (the reference computes in fp32); the gated epilogue then
- * writes a bf16 pair (hi [m, n/2] then lo [m, n/2]).  n % 256 == 0, k % 64 == 0,
- * pointers 16-byte aligned, x_lo only with w_lo; otherwise TX_EINVAL. */
-int tx_linear(void *ctx, const uint16_t *x, const uint16_t *x_lo, const uint16_t *w,
-              const uint16_t *w_lo, void *out, uint32_t m, uint32_t n, uint32_t k, int mode,
-              void *stream);
+ * weights and its f32 projections matmul_bias_f32* (kernels.metal:438-487, bert.py:127-133):
+ * out = x [m, k] times w [n, k] transposed, plus bias (fp32 [n], or NULL), fp32
+ * accumulation on tensor cores, epilogue `mode` (TX_LINEAR_*).  fmt TX_BF16: bf16
+ * operands; TX_F32: fp32 operands read as TF32.  With x_lo and w_lo (both or neither), the
+ * lo parts of split operands, the product is x.w + x.w_lo + x_lo.w: bf16 pairs carry about
+ * 16 significant bits of each operand, TF32 pairs (hi = TF32-rounded value, lo = value -
+ * hi, see tx_split_tf32) about 22, the fp32 path's accuracy; the gated epilogue then writes a
+ * bf16 pair (hi [m, n/2] then lo [m, n/2]).  part: outputs split by columns -- column
+ * block p of width `part` goes to its own [m, part] matrix, the p-th of n / part
+ * consecutive ones (part == n: one [m, n] matrix).  Needs n and part multiples of 128
+ * (256 for the gated epilogue), k a multiple of 64 (bf16) or 32 (TF32), pointers 16-byte
+ * aligned; otherwise TX_EINVAL. */
+int tx_linear(void *ctx, const void *x, const void *x_lo, const void *w, const void *w_lo,
+              const float *bias, void *out, uint32_t m, uint32_t n, uint32_t k, int mode,
+              int fmt, uint32_t part, void *stream);
 
 /* The whole forward as one call: the layer loop of Qwen3Backend.forward
  * (qwen3.py:112-296; its per-layer dispatch sequence is qwen3.py:191-280, the final norm
@@ -376,6 +387,74 @@ int tx_qwen3_forward(void *ctx, const TxQwen3Model *model, const uint32_t *ids,
                      const int32_t *cu_seqlens, const int32_t *cu_host, uint32_t nseq,
                      float *pooled, uint32_t dimensions, void *workspace,
                      uint64_t workspace_bytes, void *stream);
+
+/* ---- the BERT (BGE-small) fp32 forward around the head_dim-32 attention -------------
+
+ * BertBackend.forward (bert.py:104-235) is built from these plus tx_linear (fmt TX_F32,
+ * TF32 split operands), tx_attention_varlen and tx_pool_project; tx_bert_forward runs the
+ * whole loop.  Weights are fp32 as the reference stores them (bert.py:55-66).  All
+ * pointers are device pointers; stream NULL: the context's stream. */
+
+/* fp32 x [n] as the split operand of the TF32 GEMM: out[i] = x[i] rounded to TF32 (kept
+ * in fp32), out[n + i] = x[i] - out[i] (exact).  n % 4 == 0, 16-byte aligned pointers. */
+int tx_split_tf32(void *ctx, const float *x, float *out, uint64_t n, void *stream);
+
+/* Replaces the "layer_norm" dispatch (kernels.metal:362-373) on hidden rows: out[r] =
+ * (x[r] - mean) / sqrt(var + eps) * w + b (out may be x), and, when `pair` is non-NULL, the
+ * next GEMM's split operand of out: split TX_F32 (TF32 pair, hi [rows, cols] then lo, fp32)
+ * or TX_BF16X2 (bf16 pair).  cols at most 1024. */
+int tx_layer_norm_rows(void *ctx, const float *x, const float *w, const float *b, float *out,
+                       void *pair, int split, uint32_t rows, uint32_t cols, float eps,
+                       void *stream);
+
+/* Replaces the "embedding_position" dispatch (kernels.metal:353-361) followed by the
+ * embeddings' layer_norm (bert.py:174-190): out[t] = LayerNorm(words[ids[t]] + types[0] +
+ * positions[pos(t)]), pos(t) = index of t inside its sequence (packed by cu_seqlens with
+ * nseq sequences, or t % seq when cu_seqlens is NULL); `pair` / `split` as in
+ * tx_layer_norm_rows.  An id >= vocab or a position >= max_pos gives a NaN row and
+ * TX_EINVAL at the next tx_sync. */
+int tx_bert_embed(void *ctx, const uint32_t *ids, const int32_t *cu_seqlens, uint32_t nseq,
+                  uint32_t seq, uint32_t tokens, const float *words, const float *positions,
+                  const float *types, uint32_t vocab, uint32_t max_pos, const float *ln_w,
+                  const float *ln_b, float eps, float *out, void *pair, int split, uint32_t cols,
+                  void *stream);
+
+/* One encoder layer's weights.  Projection matrices are TF32 split operands of their fp32
+ * weights (tx_split_tf32: hi [n, k] then lo [n, k]); qkv is the query, key and value
+ * matrices stacked ([3 * hidden, hidden], biases likewise); LayerNorm weights and biases
+ * fp32 [hidden]. */
+typedef struct {
+  const float *qkv_w, *qkv_b;   /* [2][3 hidden, hidden], [3 hidden] */
+  const float *o_w, *o_b;       /* attention.output.dense */
+  const float *ln1_w, *ln1_b;   /* attention.output.LayerNorm */
+  const float *i_w, *i_b;       /* intermediate.dense [2][intermediate, hidden] */
+  const float *out_w, *out_b;   /* output.dense [2][hidden, intermediate] */
+  const float *ln2_w, *ln2_b;   /* output.LayerNorm */
+} TxBertLayer;
+
+typedef struct {
+  uint32_t hidden, intermediate, layers, heads, vocab, max_pos;
+  float eps;
+  int precise;                  /* 1: three TF32 products per GEMM (fp32 accuracy); 0: one */
+  const float *words, *positions, *types; /* embedding tables [rows, hidden] */
+  const float *ln_w, *ln_b;     /* embeddings.LayerNorm */
+  const TxBertLayer *layer;     /* host array of `layers` entries */
+} TxBertModel;
+
+/* Bytes of device workspace tx_bert_forward needs for `tokens` packed tokens (0 when the
+ * shapes are not supported: hidden and intermediate multiples of 128, hidden at most
+ * 1024, hidden % heads == 0). */
+uint64_t tx_bert_workspace_bytes(const TxBertModel *model, uint32_t tokens);
+
+/* CLS embeddings `pooled` (device fp32 [nseq, hidden], L2-normalised: pool_project with
+ * first_token, kernels.metal:339-349) of token ids `ids` (device uint32 [cu_host[nseq]])
+ * packed by `cu_seqlens` (device, host copy `cu_host`): embeddings, then per layer the
+ * fused q/k/v projection, bidirectional attention over each sequence's tokens, the output
+ * projection added to the residual stream and LayerNorm, the GELU MLP added and LayerNorm
+ * (bert.py:191-231).  Nothing is allocated by the call. */
+int tx_bert_forward(void *ctx, const TxBertModel *model, const uint32_t *ids,
+                    const int32_t *cu_seqlens, const int32_t *cu_host, uint32_t nseq,
+                    float *pooled, void *workspace, uint64_t workspace_bytes, void *stream);
 
 /* Number of CUDA devices visible to this process (0 when none or on error): the devices
  * a sharded caller creates one context on each. */

@@ -71,6 +71,21 @@ __device__ __forceinline__ void rope_sincos(float angle, float *sn, float *cs) {
   __sincosf(r, sn, cs);
 }
 
+// GELU in the erf form, 0.5 v (1 + erf(v / sqrt 2)), with erf from the rational
+// approximation 7.1.26 of Abramowitz and Stegun (|error| <= 1.5e-7), as the reference's
+// gelu_f32 evaluates it (kernels.metal:381-391): for z = |v| / sqrt 2,
+// t = 1 / (1 + 0.3275911 z), tail = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^(-z^2)
+// = 1 - erf(z), and gelu = 0.5 v tail for v < 0, 0.5 v (2 - tail) otherwise.
+__device__ __forceinline__ float gelu_erf(float v) {
+  const float z = fabsf(v) * 0.70710678118654752f;
+  const float t = 1.0f / (1.0f + 0.3275911f * z);
+  const float poly =
+      ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t +
+       0.254829592f) * t;
+  const float tail = poly * expf(-z * z);
+  return 0.5f * v * (v < 0.0f ? tail : 2.0f - tail);
+}
+
 // Records the first failure in the context's status word.
 __device__ __forceinline__ void report_status(int *status, int code) {
   if (status) atomicCAS(status, 0, code);

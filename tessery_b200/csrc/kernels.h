@@ -127,12 +127,51 @@ cudaError_t launch_linear4_f32(const float *x, const uint32_t *packed, const uin
 cudaError_t launch_silu_gate(float *gate, const float *up, uint64_t n, cudaStream_t stream);
 cudaError_t launch_add(const float *a, const float *b, float *out, uint64_t n,
                        cudaStream_t stream);
-bool linear_supported(uint32_t m, uint32_t n, uint32_t k, int mode, const void *x, const void *w,
-                      const void *out);
-// x_lo / w_lo (or NULL): the lo halves of bf16 pairs (x_lo needs w_lo); see linear.cu.
+// Output tile width of the GEMM for these shapes (0: unsupported).
+uint32_t linear_tile_n(uint32_t n, uint32_t part, int mode);
+// fmt: TX_BF16 (bf16 operands) or TX_F32 (fp32 operands read as TF32); part: output
+// column-block width (see linear.cu).
+bool linear_supported(uint32_t m, uint32_t n, uint32_t k, int mode, int fmt, uint32_t part,
+                      const void *x, const void *w, const void *out);
+// x_lo / w_lo (both or neither): the lo parts of split operands; bias fp32 [n] or NULL.
 cudaError_t launch_linear(const void *x, const void *x_lo, const void *w, const void *w_lo,
-                          void *out, uint32_t m, uint32_t n, uint32_t k, int mode, int *status,
-                          long long wait_cycles, cudaStream_t stream);
+                          const float *bias, void *out, uint32_t m, uint32_t n, uint32_t k,
+                          int mode, int fmt, uint32_t part, int *status, long long wait_cycles,
+                          cudaStream_t stream);
+
+// ---- BERT fp32 forward (bert_ops.cu) ----
+// Word + token-type-0 + absolute-position embeddings of `tokens` tokens, LayerNorm'd; the
+// position of a token is its index inside its packed sequence (cu, nseq) or t % seq.
+struct BertEmbedProblem {
+  const uint32_t *ids;
+  const int32_t *cu;  // NULL: padded layout with `seq` rows per sequence
+  uint32_t nseq, seq, tokens, cols, vocab, max_pos;
+  const float *words, *positions, *types, *ln_w, *ln_b;
+  float eps;
+  float *out;   // fp32 [tokens, cols]
+  void *pair;   // split operand of the next GEMM (or NULL), format `split`
+  int split;    // TX_F32: TF32 pair in fp32 containers; TX_BF16X2: bf16 pair
+  int *status;
+};
+bool bert_cols_ok(uint32_t cols);
+cudaError_t launch_bert_embed(const BertEmbedProblem &p, cudaStream_t stream);
+cudaError_t launch_layer_norm_rows(const float *x, const float *w, const float *b, float *out,
+                                   void *pair, int split, uint32_t rows, uint32_t cols, float eps,
+                                   cudaStream_t stream);
+cudaError_t launch_split_tf32(const float *x, float *out, uint64_t n, cudaStream_t stream);
+cudaError_t launch_gelu(float *x, uint32_t n, cudaStream_t stream);
+cudaError_t launch_add_bias(float *x, const float *bias, uint32_t n, uint32_t cols,
+                            cudaStream_t stream);
+cudaError_t launch_silu(const float *x, float *out, uint32_t n, cudaStream_t stream);
+cudaError_t launch_transpose(const float *x, float *out, uint32_t rows, uint32_t cols,
+                             cudaStream_t stream);
+cudaError_t launch_embedding_position(const uint32_t *ids, const float *words,
+                                      const float *positions, const float *types, float *out,
+                                      uint32_t n, uint32_t cols, uint32_t seq,
+                                      cudaStream_t stream);
+cudaError_t launch_matmul_f32(const float *a, const float *bt, const float *bias, float *out,
+                              uint32_t row0, uint32_t rows, uint32_t cols, uint32_t k,
+                              cudaStream_t stream);
 
 // Records `msg` as the context's last error (tx_last_error) and returns `code`: for entry
 // points built outside runtime.cu on top of the public ones.

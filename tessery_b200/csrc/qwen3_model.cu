@@ -110,7 +110,7 @@ int tx_qwen3_forward(void *ctx, const TxQwen3Model *model, const uint32_t *ids,
                     int mode) {
     const uint16_t *a_lo = m.precise ? a + uint64_t(T) * kdim : nullptr;
     const uint16_t *w_lo = m.precise ? w + uint64_t(n) * kdim : nullptr;
-    return tx_linear(ctx, a, a_lo, w, w_lo, out, T, n, kdim, mode, stream);
+    return tx_linear(ctx, a, a_lo, w, w_lo, nullptr, out, T, n, kdim, mode, TX_BF16, n, stream);
   };
   const int norm_out = m.precise ? TX_BF16X2 : TX_BF16;
 

@@ -21,7 +21,7 @@
 
 namespace {
 
-constexpr uint32_t kAbiVersion = 7;
+constexpr uint32_t kAbiVersion = 8;
 constexpr uint32_t kHostChunks = 8;              // most chunks of a host-buffer call
 constexpr size_t kHostChunkBytes = 16u << 20;     // bytes moved per chunk, at least
 
@@ -929,6 +929,95 @@ int tx_dispatch(void *ctx, const char *name, void **buffers, uint32_t count, con
                               (float *)b[2]->dev, pr.n, c->stream);
     if (e == cudaSuccess) ++c->launches;
     prof_end(c);
+  } else if (n == "layer_norm") {
+    // [x, w, bias, out], one threadgroup of `group` threads per row (kernels.metal:362-373)
+    if (count != 4 || threads % group) return fail(c, TX_EINVAL, "layer_norm: bad arguments");
+    const uint64_t rows = threads / group, bytes = rows * pr.cols * 4;
+    if (!tx::bert_cols_ok(pr.cols))
+      return fail(c, TX_EINVAL, "layer_norm: cols at most 1024");
+    if (b[0]->size < bytes || b[3]->size < bytes || b[1]->size < pr.cols * 4u ||
+        b[2]->size < pr.cols * 4u)
+      return fail(c, TX_EINVAL, "layer_norm: buffer too small");
+    prof_begin(c);
+    e = tx::launch_layer_norm_rows((const float *)b[0]->dev, (const float *)b[1]->dev,
+                                   (const float *)b[2]->dev, (float *)b[3]->dev, nullptr, TX_F32,
+                                   (uint32_t)rows, pr.cols, pr.eps, c->stream);
+    if (e == cudaSuccess) ++c->launches;
+    prof_end(c);
+  } else if (n == "embedding_position") {
+    // [ids, words, positions, types, out], n = tokens * cols (kernels.metal:353-361)
+    if (count != 5 || !pr.cols || !pr.seq || pr.n % pr.cols)
+      return fail(c, TX_EINVAL, "embedding_position: bad arguments");
+    const uint64_t tokens = pr.n / pr.cols;
+    if (b[0]->size < tokens * 4 || b[4]->size < (uint64_t)pr.n * 4 ||
+        b[2]->size < (uint64_t)std::min<uint64_t>(tokens, pr.seq) * pr.cols * 4 ||
+        b[3]->size < pr.cols * 4u)
+      return fail(c, TX_EINVAL, "embedding_position: buffer too small");
+    prof_begin(c);
+    e = tx::launch_embedding_position((const uint32_t *)b[0]->dev, (const float *)b[1]->dev,
+                                      (const float *)b[2]->dev, (const float *)b[3]->dev,
+                                      (float *)b[4]->dev, pr.n, pr.cols, pr.seq, c->stream);
+    if (e == cudaSuccess) ++c->launches;
+    prof_end(c);
+  } else if (n == "gelu_f32" || n == "add_bias" || n == "silu_f32") {
+    // gelu_f32 [x] in place (:381-391), add_bias [x, bias] (:376-379), silu_f32 [x, out]
+    // (:328-331); n elements
+    const uint32_t want = n == "gelu_f32" ? 1u : 2u;
+    if (count != want || (n == "add_bias" && !pr.cols))
+      return fail(c, TX_EINVAL, "elementwise: bad arguments");
+    if (b[0]->size < (uint64_t)pr.n * 4 || (n == "silu_f32" && b[1]->size < (uint64_t)pr.n * 4) ||
+        (n == "add_bias" && b[1]->size < pr.cols * 4u))
+      return fail(c, TX_EINVAL, "elementwise: buffer too small");
+    prof_begin(c);
+    if (n == "gelu_f32")
+      e = tx::launch_gelu((float *)b[0]->dev, pr.n, c->stream);
+    else if (n == "add_bias")
+      e = tx::launch_add_bias((float *)b[0]->dev, (const float *)b[1]->dev, pr.n, pr.cols,
+                              c->stream);
+    else
+      e = tx::launch_silu((const float *)b[0]->dev, (float *)b[1]->dev, pr.n, c->stream);
+    if (e == cudaSuccess) ++c->launches;
+    prof_end(c);
+  } else if (n == "transpose_f32") {
+    // [x, out], x [rows, cols] (kernels.metal:323-326)
+    const uint64_t bytes = (uint64_t)pr.rows * pr.cols * 4;
+    if (count != 2 || b[0]->size < bytes || b[1]->size < bytes)
+      return fail(c, TX_EINVAL, "transpose_f32: bad arguments");
+    prof_begin(c);
+    e = tx::launch_transpose((const float *)b[0]->dev, (float *)b[1]->dev, pr.rows, pr.cols,
+                             c->stream);
+    if (e == cudaSuccess) ++c->launches;
+    prof_end(c);
+  } else if (n.rfind("matmul", 0) == 0) {
+    // [a, bt, out(, bias)]: out[r, c] = a[r, :] . bt[c, :] (+ bias[c]) (kernels.metal:306-321,
+    // 392-487).  The rows each name covers follow from its grid as in the reference:
+    // matmul_f32 / matmul_bias_f32 take 4 rows per threadgroup per output column starting at
+    // row n; the tiled and chunk32 forms take 8 rows per threadgroup per 32 columns from 0.
+    const bool bias = n == "matmul_bias_f32" || n == "matmul_bias_f32_chunk32";
+    const bool tiles = n == "matmul_f32_tiled" || n == "matmul_f32_chunk32" ||
+                       n == "matmul_bias_f32_chunk32";
+    if (!bias && !tiles && n != "matmul_f32") return fail(c, TX_EINVAL, "unknown kernel name");
+    if (count != (bias ? 4u : 3u) || !pr.rows || !pr.cols || !pr.k || threads % group)
+      return fail(c, TX_EINVAL, "matmul: bad arguments");
+    const uint64_t groups = threads / group;
+    uint64_t row0 = 0, row_end = 0;
+    if (tiles) {
+      if (pr.cols % 32) return fail(c, TX_EINVAL, "matmul: tiled forms need cols % 32 == 0");
+      const uint64_t per = pr.cols / 32;
+      row_end = std::min<uint64_t>(pr.rows, 8 * ((groups + per - 1) / per));
+    } else {
+      row0 = pr.n;
+      row_end = std::min<uint64_t>(pr.rows, row0 + 4 * ((groups + pr.cols - 1) / pr.cols));
+    }
+    if (b[0]->size < (uint64_t)pr.rows * pr.k * 4 || b[1]->size < (uint64_t)pr.cols * pr.k * 4 ||
+        b[2]->size < (uint64_t)pr.rows * pr.cols * 4 || (bias && b[3]->size < pr.cols * 4u))
+      return fail(c, TX_EINVAL, "matmul: buffer too small");
+    prof_begin(c);
+    e = tx::launch_matmul_f32((const float *)b[0]->dev, (const float *)b[1]->dev,
+                              bias ? (const float *)b[3]->dev : nullptr, (float *)b[2]->dev,
+                              (uint32_t)row0, (uint32_t)row_end, pr.cols, pr.k, c->stream);
+    if (e == cudaSuccess) ++c->launches;
+    prof_end(c);
   } else if (n == "qk_norm_rope") {
     // buffers: q, k (f32, in place), q_norm weight, k_norm weight (bf16); n = tokens
     if (count != 4 || !pr.heads || !pr.kv_heads || !pr.seq)
@@ -1221,23 +1310,82 @@ int tx_rms_norm_rows(void *ctx, const float *x, const uint16_t *w, void *out, in
   return TX_OK;
 }
 
-int tx_linear(void *ctx, const uint16_t *x, const uint16_t *x_lo, const uint16_t *w,
-              const uint16_t *w_lo, void *out, uint32_t m, uint32_t n, uint32_t k, int mode,
-              void *stream) {
+int tx_linear(void *ctx, const void *x, const void *x_lo, const void *w, const void *w_lo,
+              const float *bias, void *out, uint32_t m, uint32_t n, uint32_t k, int mode,
+              int fmt, uint32_t part, void *stream) {
   Ctx *c = (Ctx *)ctx;
   if (!c) return TX_EINVAL;
   std::lock_guard<std::recursive_mutex> g(c->mu);
   if (!x || !w || !out) return fail(c, TX_EINVAL, "null pointer");
-  if (x_lo && !w_lo) return fail(c, TX_EINVAL, "linear: x_lo needs w_lo");
+  if (!x_lo != !w_lo) return fail(c, TX_EINVAL, "linear: x_lo and w_lo go together");
   if (!m) return TX_OK;
-  if (!tx::linear_supported(m, n, k, mode, x, w, out) || (uintptr_t)x_lo % 16 ||
-      (uintptr_t)w_lo % 16)
-    return fail(c, TX_EINVAL, "linear: n % 256 == 0, k % 64 == 0, aligned pointers, mode");
+  if (!tx::linear_supported(m, n, k, mode, fmt, part, x, w, out) || (uintptr_t)x_lo % 16 ||
+      (uintptr_t)w_lo % 16 || (uintptr_t)bias % 16 || (bias && mode == TX_LINEAR_GATED_BF16))
+    return fail(c, TX_EINVAL,
+                "linear: n, part % 128 == 0, k % 64 (bf16) or 32 (f32), aligned pointers, mode");
   cudaSetDevice(c->device);
-  cudaError_t e = tx::launch_linear(x, x_lo, w, w_lo, out, m, n, k, mode, c->status,
-                                    c->wait_cycles, stream ? (cudaStream_t)stream : c->stream);
+  cudaError_t e = tx::launch_linear(x, x_lo, w, w_lo, bias, out, m, n, k, mode, fmt, part,
+                                    c->status, c->wait_cycles,
+                                    stream ? (cudaStream_t)stream : c->stream);
   if (e != cudaSuccess) return cuda_fail(c, e, "linear launch");
-  c->last_kernel = "linear";
+  c->last_kernel = fmt == TX_F32 ? "linear_tf32" : "linear";
+  ++c->launches;
+  return TX_OK;
+}
+
+int tx_split_tf32(void *ctx, const float *x, float *out, uint64_t n, void *stream) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!x || !out) return fail(c, TX_EINVAL, "null pointer");
+  if (n % 4 || (uintptr_t)x % 16 || (uintptr_t)out % 16)
+    return fail(c, TX_EINVAL, "split_tf32: n % 4 == 0, 16-byte aligned pointers");
+  cudaSetDevice(c->device);
+  cudaError_t e = tx::launch_split_tf32(x, out, n, stream ? (cudaStream_t)stream : c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "split_tf32 launch");
+  ++c->launches;
+  return TX_OK;
+}
+
+int tx_layer_norm_rows(void *ctx, const float *x, const float *w, const float *b, float *out,
+                       void *pair, int split, uint32_t rows, uint32_t cols, float eps,
+                       void *stream) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!x || !w || !b || !out) return fail(c, TX_EINVAL, "null pointer");
+  if (!tx::bert_cols_ok(cols) || (pair && split != TX_F32 && split != TX_BF16X2) ||
+      !(eps >= 0.f))
+    return fail(c, TX_EINVAL, "layer_norm_rows: cols at most 1024, split format");
+  cudaSetDevice(c->device);
+  cudaError_t e = tx::launch_layer_norm_rows(x, w, b, out, pair, split, rows, cols, eps,
+                                             stream ? (cudaStream_t)stream : c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "layer_norm_rows launch");
+  ++c->launches;
+  return TX_OK;
+}
+
+int tx_bert_embed(void *ctx, const uint32_t *ids, const int32_t *cu_seqlens, uint32_t nseq,
+                  uint32_t seq, uint32_t tokens, const float *words, const float *positions,
+                  const float *types, uint32_t vocab, uint32_t max_pos, const float *ln_w,
+                  const float *ln_b, float eps, float *out, void *pair, int split, uint32_t cols,
+                  void *stream) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  if (!ids || !words || !positions || !types || !ln_w || !ln_b || !out)
+    return fail(c, TX_EINVAL, "null pointer");
+  if (!tx::bert_cols_ok(cols) || !vocab || !max_pos || (cu_seqlens ? !nseq : !seq) ||
+      (pair && split != TX_F32 && split != TX_BF16X2) || !(eps >= 0.f))
+    return fail(c, TX_EINVAL, "bert_embed: bad arguments");
+  tx::BertEmbedProblem p{};
+  p.ids = ids; p.cu = cu_seqlens; p.nseq = nseq; p.seq = seq; p.tokens = tokens; p.cols = cols;
+  p.vocab = vocab; p.max_pos = max_pos; p.words = words; p.positions = positions;
+  p.types = types; p.ln_w = ln_w; p.ln_b = ln_b; p.eps = eps; p.out = out; p.pair = pair;
+  p.split = split; p.status = c->status;
+  cudaSetDevice(c->device);
+  cudaError_t e = tx::launch_bert_embed(p, stream ? (cudaStream_t)stream : c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "bert_embed launch");
   ++c->launches;
   return TX_OK;
 }

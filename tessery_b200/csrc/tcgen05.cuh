@@ -119,6 +119,17 @@ __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, ui
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// The same with 32-bit operands read as TF32 (kind::tf32: 8 elements of K per instruction,
+// the low 13 mantissa bits of each operand ignored).
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // D (+)= A B with A read from tensor memory (lane = row, two bf16 of K per column).
 __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
                                         uint32_t idesc, uint32_t accumulate) {
@@ -240,6 +251,12 @@ __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w 
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
 
+
+// x rounded to the nearest TF32 value (10 explicit mantissa bits; ties away from zero),
+// kept in an fp32 container; x - tf32_round(x) is exact in fp32.
+__device__ __forceinline__ float tf32_round(float x) {
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xffffe000u);
+}
 
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {

@@ -16,12 +16,13 @@ from typing import Any
 
 from .errors import NativeBuildError
 
-ABI_VERSION = 7
+ABI_VERSION = 8
 LIBRARY_NAME = "libtessattn.so"
 
 TX_OK, TX_EINVAL, TX_ECUDA, TX_ETIMEOUT = 0, 1, 2, 3
 TX_F32, TX_BF16, TX_BF16X2 = 0, 1, 2
 TX_LINEAR_STORE_F32, TX_LINEAR_STORE_BF16, TX_LINEAR_ADD_F32, TX_LINEAR_GATED_BF16 = 0, 1, 2, 3
+TX_LINEAR_GELU_SPLIT = 4
 
 _vp, _u32, _u64, _i32, _f32 = ct.c_void_p, ct.c_uint32, ct.c_uint64, ct.c_int, ct.c_float
 
@@ -43,6 +44,26 @@ class TxQwen3Model(ct.Structure):
         ("eps", _f32), ("theta", _f32), ("precise", _i32),
         ("embed_packed", _vp), ("embed_scales", _vp), ("embed_biases", _vp),
         ("final_norm", _vp), ("layer", ct.POINTER(TxQwen3Layer)),
+    ]
+
+
+class TxBertLayer(ct.Structure):
+    """Device pointers of one BERT layer's weights (TxBertLayer in tessattn.h)."""
+
+    _fields_ = [(name, _vp) for name in (
+        "qkv_w", "qkv_b", "o_w", "o_b", "ln1_w", "ln1_b", "i_w", "i_b", "out_w", "out_b",
+        "ln2_w", "ln2_b")]
+
+
+class TxBertModel(ct.Structure):
+    """Shape and weights of a BERT encoder (TxBertModel in tessattn.h)."""
+
+    _fields_ = [
+        *[(name, _u32) for name in ("hidden", "intermediate", "layers", "heads", "vocab",
+                                    "max_pos")],
+        ("eps", _f32), ("precise", _i32),
+        ("words", _vp), ("positions", _vp), ("types", _vp), ("ln_w", _vp), ("ln_b", _vp),
+        ("layer", ct.POINTER(TxBertLayer)),
     ]
 
 
@@ -102,6 +123,14 @@ SIGNATURES: dict[str, tuple[list[Any], Any]] = {
     ),
     "tx_sync": ([_vp, _vp], _i32),
     "tx_device_count": ([], _i32),
+    "tx_split_tf32": ([_vp, _vp, _vp, _u64, _vp], _i32),
+    "tx_layer_norm_rows": ([_vp, _vp, _vp, _vp, _vp, _vp, _i32, _u32, _u32, _f32, _vp], _i32),
+    "tx_bert_embed": (
+        [_vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp, _u32, _u32, _vp, _vp, _f32, _vp, _vp,
+         _i32, _u32, _vp], _i32),
+    "tx_bert_workspace_bytes": ([ct.POINTER(TxBertModel), _u32], _u64),
+    "tx_bert_forward": (
+        [_vp, ct.POINTER(TxBertModel), _vp, _vp, _vp, _u32, _vp, _vp, _u64, _vp], _i32),
     "tx_qwen3_workspace_bytes": ([ct.POINTER(TxQwen3Model), _u32], _u64),
     "tx_qwen3_forward": (
         [_vp, ct.POINTER(TxQwen3Model), _vp, _vp, _vp, _u32, _vp, _u32, _vp, _u64, _vp], _i32),
@@ -109,7 +138,8 @@ SIGNATURES: dict[str, tuple[list[Any], Any]] = {
     "tx_split_bf16": ([_vp, _vp, _vp, _u64, _vp], _i32),
     "tx_embedding4": ([_vp, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _u32, _vp], _i32),
     "tx_rms_norm_rows": ([_vp, _vp, _vp, _vp, _i32, _u32, _u32, _f32, _vp], _i32),
-    "tx_linear": ([_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _i32, _vp], _i32),
+    "tx_linear": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _i32, _i32, _u32, _vp],
+                  _i32),
     "tx_attention_padded_noalloc": (
         [_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _i32, _i32, _f32, _vp, _f32,
          _f32, _vp, _vp],

@@ -360,6 +360,52 @@ class CudaRuntime:
         current.log.append({"kernel": name, "rows": rows, "cols": cols, "seq": seq,
                             "heads": heads, "threads": threads})
 
+    def _matmul_f32(self, buffers: Sequence[Buffer], *, rows: int, cols: int, k: int) -> None:
+        """out [rows, cols] = a [rows, k] . bt [cols, k]^T over [a, bt, out]: the call shape of
+        MetalRuntime._matmul_f32 (metal.py:664-700), one fp32 dispatch covering every row."""
+        self._dispatch("matmul_f32", buffers, threads=((rows + 3) // 4) * cols * 32,
+                       group_size=32, rows=rows, cols=cols, k=k)
+
+    def _matmul_bias_f32(self, buffers: Sequence[Buffer], *, rows: int, cols: int,
+                         k: int) -> None:
+        """The affine projection over [a, bt, out, bias] (metal.py:702-731)."""
+        self._dispatch("matmul_bias_f32", buffers, threads=((rows + 3) // 4) * cols * 32,
+                       group_size=32, rows=rows, cols=cols, k=k)
+
+    def add(self, a: NDArray[np.float32], b: NDArray[np.float32]) -> NDArray[np.float32]:
+        """Elementwise a + b on the device (MetalRuntime.add, metal.py:733-748)."""
+        if a.shape != b.shape or a.dtype != np.float32 or b.dtype != np.float32 or not a.size:
+            raise InferenceError()
+        with self._lock:
+            bufs = [self.buffer(x.nbytes, np.ascontiguousarray(x)) for x in (a, b)]
+            bufs.append(self.buffer(a.nbytes))
+            try:
+                with self.command():
+                    self._dispatch("add", bufs, threads=a.size, n=a.size)
+                return self.read(bufs[-1], a.shape)
+            finally:
+                for x in bufs:
+                    x.close()
+
+    def matmul(self, a: NDArray[np.float32], b: NDArray[np.float32]) -> NDArray[np.float32]:
+        """General float32 [M, K] @ [K, N] on the device (MetalRuntime.matmul,
+        metal.py:750-780)."""
+        if (a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[0] or a.dtype != np.float32
+                or b.dtype != np.float32 or not a.size or not b.size):
+            raise InferenceError()
+        m, k = a.shape
+        n = b.shape[1]
+        with self._lock:
+            bufs = [self.buffer(x.nbytes, np.ascontiguousarray(x)) for x in (a, b.T)]
+            bufs.append(self.buffer(m * n * 4))
+            try:
+                with self.command():
+                    self._matmul_f32(bufs, rows=m, cols=n, k=k)
+                return self.read(bufs[-1], (m, n))
+            finally:
+                for x in bufs:
+                    x.close()
+
     # ---- typed entry points (host arrays) ------------------------------------------------
     def attention_host(
         self,
@@ -579,12 +625,14 @@ class CudaRuntime:
 
     def linear_device(self, x: int, w: int, out: int, *, m: int, n: int, k: int, mode: int,
                       x_lo: int | None = None, w_lo: int | None = None,
-                      stream: int | None = None) -> None:
-        """Tensor-core x [m, k] . w [n, k]^T with a TX_LINEAR_* epilogue; with the lo halves
-        of bf16 pairs (w_lo, and x_lo), the split-operand product (tx_linear)."""
+                      bias: int | None = None, fmt: int = native.TX_BF16,
+                      part: int | None = None, stream: int | None = None) -> None:
+        """Tensor-core x [m, k] . w [n, k]^T (+ bias) with a TX_LINEAR_* epilogue; fmt
+        TX_BF16 or TX_F32 (TF32 operands); with the lo parts of split operands (x_lo and
+        w_lo), the three-product form; part: output column-block width (tx_linear)."""
         self._check_open()
-        _raise_for(self._lib.tx_linear(self._pointer, x, x_lo, w, w_lo, out, m, n, k, mode,
-                                       stream))
+        _raise_for(self._lib.tx_linear(self._pointer, x, x_lo, w, w_lo, bias, out, m, n, k, mode,
+                                       fmt, n if part is None else part, stream))
 
     def qwen3_forward_device(self, model: Any, ids: int, cu_seqlens: int,
                              cu_host: NDArray[np.int32], pooled: int, dimensions: int,
@@ -598,6 +646,43 @@ class CudaRuntime:
         _raise_for(self._lib.tx_qwen3_forward(
             self._pointer, model, ids, cu_seqlens, cu_host.ctypes.data, cu_host.size - 1,
             pooled, dimensions, workspace, workspace_bytes, stream))
+
+    # ---- the BERT fp32 forward around the attention (device pointers) -------------------
+    def split_tf32_device(self, x: int, out: int, *, n: int, stream: int | None = None) -> None:
+        """fp32 x [n] as a TF32 operand pair out [2][n] (tx_split_tf32)."""
+        self._check_open()
+        _raise_for(self._lib.tx_split_tf32(self._pointer, x, out, n, stream))
+
+    def layer_norm_rows_device(self, x: int, weight: int, bias: int, out: int, *, rows: int,
+                               cols: int, eps: float, pair: int | None = None,
+                               split: int = native.TX_F32, stream: int | None = None) -> None:
+        """Row LayerNorm (kernels.metal:362-373), optionally writing the next GEMM's split
+        operand `pair` (tx_layer_norm_rows)."""
+        self._check_open()
+        _raise_for(self._lib.tx_layer_norm_rows(self._pointer, x, weight, bias, out, pair, split,
+                                                rows, cols, eps, stream))
+
+    def bert_embed_device(self, ids: int, out: int, *, tokens: int, cols: int, words: int,
+                          positions: int, types: int, vocab: int, max_pos: int, ln_w: int,
+                          ln_b: int, eps: float, cu_seqlens: int | None = None, nseq: int = 0,
+                          seq: int = 0, pair: int | None = None, split: int = native.TX_F32,
+                          stream: int | None = None) -> None:
+        """Word + type + position embeddings, LayerNorm'd (tx_bert_embed)."""
+        self._check_open()
+        _raise_for(self._lib.tx_bert_embed(self._pointer, ids, cu_seqlens, nseq, seq, tokens,
+                                           words, positions, types, vocab, max_pos, ln_w, ln_b,
+                                           eps, out, pair, split, cols, stream))
+
+    def bert_forward_device(self, model: Any, ids: int, cu_seqlens: int,
+                            cu_host: NDArray[np.int32], pooled: int, workspace: int,
+                            workspace_bytes: int, stream: int | None = None) -> None:
+        """Queues the whole BERT forward (tx_bert_forward); `model` is a reference to a
+        native.TxBertModel."""
+        self._check_open()
+        cu_host = np.ascontiguousarray(cu_host, dtype=np.int32)
+        _raise_for(self._lib.tx_bert_forward(self._pointer, model, ids, cu_seqlens,
+                                             cu_host.ctypes.data, cu_host.size - 1, pooled,
+                                             workspace, workspace_bytes, stream))
 
     def sync(self, stream: int | None = None) -> None:
         """Waits for queued work and reports kernel errors (tx_sync)."""

@@ -3,8 +3,9 @@
 Runs where the reference project's source tree is available; its root directory is
 given as the first argument or in the TESSERY_REFERENCE environment variable.  It
 imports the reference's own kernel test module (tests/real_metal/test_kernels.py) and
-calls its attention, RoPE,
-RMSNorm and pooling tests, unmodified and with their own seeds, grids and tolerances,
+calls its attention, RoPE, RMSNorm, pooling, uint4 embedding/projection, LayerNorm,
+absolute-embedding, GELU, bias and f32 matmul tests, unmodified and with their own seeds,
+grids and tolerances,
 against a fake runtime whose kernels are computed by ``oracle``.  Every
 ``numpy.testing.assert_allclose`` the reference tests make is intercepted to record the
 reference's expected array (its own NumPy formula) and the verdict, then forwarded to
@@ -36,6 +37,7 @@ REPO = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(REPO))
 
 import oracle  # noqa: E402
+import oracle.bert  # noqa: E402
 from oracle.qwen3 import dequant4  # noqa: E402
 
 def reference_root() -> Path:
@@ -56,6 +58,11 @@ KERNEL_TESTS = [
     "test_rms_and_pool",
     "test_bidirectional_attention_and_cls_pool",
     "test_quantized_embedding_and_linear",
+    "test_layer_norm_and_absolute_embedding",
+    "test_gelu_erf_form_and_bias",
+    "test_general_matmul",
+    "test_tiled_matmul_and_unaligned_fallback",
+    "test_f32_chunked_projections_and_bounded_tail",
 ]
 
 
@@ -84,8 +91,35 @@ class FakeBuffer:
 class OracleEngine:
     """The slice of MetalRuntime the reference kernel tests use, computed by the oracle."""
 
+    active_bytes = 0
+
     def __init__(self, log: list):
         self.log = log
+        self.dispatches: dict[str, int] = {}
+
+    def diagnostics(self):
+        return {"dispatches": dict(self.dispatches)}
+
+    def matmul(self, a, b):
+        """MetalRuntime.matmul (metal.py:750-780): validation, the dispatch names its
+        routing (metal.py:664-700) would record, and the float64 product."""
+        from metal_inference.errors import InferenceError
+
+        if (a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[0] or a.dtype != np.float32
+                or b.dtype != np.float32 or not a.size or not b.size):
+            raise InferenceError()
+        m, k = a.shape
+        n = b.shape[1]
+        if m >= 8 and (n, k) in ((384, 384), (1536, 384), (384, 1536)):
+            names = ["matmul_f32_chunk32"] + (["matmul_f32"] if m % 8 else [])
+        else:
+            tiled = m >= 8 and m % 8 == 0 and n % 32 == 0 and k % 8 == 0 and k <= 512
+            names = ["matmul_f32_tiled" if tiled else "matmul_f32"]
+        for name in names:
+            self.dispatches[name] = self.dispatches.get(name, 0) + 1
+        self.log.append({"kernel": "matmul_f32", "params": {"rows": m, "cols": n, "k": k},
+                         "inputs": [sha(np.ascontiguousarray(a)), sha(np.ascontiguousarray(b.T))]})
+        return (a.astype(np.float64) @ b.astype(np.float64)).astype(np.float32)
 
     def buffer(self, size, data=None):
         return FakeBuffer(size, data)
@@ -144,6 +178,26 @@ class OracleEngine:
                          buffers[2].view(np.uint16).reshape(cols, k // 64),
                          buffers[3].view(np.uint16).reshape(cols, k // 64))
             buffers[4].write((x @ w.T).astype(np.float32))
+        elif name == "layer_norm":
+            cols = kw["cols"]
+            x = buffers[0].view(np.float32).reshape(-1, cols)
+            out = oracle.bert.layer_norm(x, buffers[1].view(np.float32),
+                                         buffers[2].view(np.float32), kw["eps"])
+            buffers[3].write(out.astype(np.float32))
+        elif name == "embedding_position":
+            cols, seq = kw["cols"], kw["seq"]
+            ids = buffers[0].view(np.uint32).reshape(-1, seq)
+            out = oracle.bert.embedding_position(
+                ids, buffers[1].view(np.float32).reshape(-1, cols),
+                buffers[2].view(np.float32).reshape(-1, cols),
+                buffers[3].view(np.float32).reshape(-1, cols))
+            buffers[4].write(out.astype(np.float32))
+        elif name == "gelu_f32":
+            buffers[0].write(oracle.bert.gelu(buffers[0].view(np.float32)).astype(np.float32))
+        elif name == "add_bias":
+            cols = kw["cols"]
+            x = buffers[0].view(np.float32).reshape(-1, cols).astype(np.float64)
+            buffers[0].write((x + buffers[1].view(np.float32)).astype(np.float32))
         elif name == "silu_gate":  # harness only: the RoPE test also exercises silu_gate
             a = buffers[0].view(np.float32).astype(np.float64)
             b = buffers[1].view(np.float32).astype(np.float64)

@@ -17,7 +17,8 @@ import numpy as np
 
 FIXTURE = Path(__file__).resolve().parent / "golden" / "reference_kernels.npz"
 PATH_KERNELS = {"attention", "attention_tiled", "attention_tail_32", "attention_tail_128",
-                "rope", "rms_norm", "pool_project", "embedding4", "linear4"}
+                "rope", "rms_norm", "pool_project", "embedding4", "linear4", "layer_norm",
+                "embedding_position", "gelu_f32", "add_bias", "matmul_f32"}
 
 
 def sha(a: np.ndarray) -> str:
@@ -125,6 +126,38 @@ def regenerate(case: Case) -> dict:
             return {"ids": ids, "packed": packed, "scales": scales, "biases": biases}
         x = rng.normal(size=(3, 128)).astype(np.float32)
         return {"x": x, "packed": packed, "scales": scales, "biases": biases}
+    if t == "test_layer_norm_and_absolute_embedding":
+        rng = np.random.default_rng(37)
+        x = rng.normal(size=(3, 67)).astype(np.float32)
+        scale = rng.normal(size=67).astype(np.float32)
+        bias = rng.normal(size=67).astype(np.float32)
+        if case.check == 0:
+            return {"x": x, "w": scale, "b": bias}
+        words = rng.normal(size=(17, 67)).astype(np.float32)
+        positions = rng.normal(size=(4, 67)).astype(np.float32)
+        types = rng.normal(size=(2, 67)).astype(np.float32)
+        ids = np.array([[1, 3, 0, 0], [5, 6, 7, 8]], np.uint32)
+        return {"ids": ids, "words": words, "positions": positions, "types": types}
+    if t == "test_gelu_erf_form_and_bias":
+        if case.check == 0:
+            return {"x": np.linspace(-12, 12, 10001, dtype=np.float32)}
+        return {"x": np.arange(12, dtype=np.float32).reshape(3, 4),
+                "bias": np.array([-2, -1, 1, 2], np.float32)}
+    if t in ("test_general_matmul", "test_tiled_matmul_and_unaligned_fallback"):
+        m, k, n = p["shape"]
+        rng = np.random.default_rng(7 if t == "test_general_matmul" else 33)
+        a = rng.normal(size=(m, k)).astype(np.float32)
+        b = rng.normal(size=(k, n)).astype(np.float32)
+        return {"a": a, "bt": np.ascontiguousarray(b.T)}
+    if t == "test_f32_chunked_projections_and_bounded_tail":
+        m, n, k = p["m"], p["n"], p["k"]
+        rng = np.random.default_rng(2026 + m)
+        x = rng.normal(size=(m, k)).astype(np.float32)
+        w = rng.normal(size=(n, k)).astype(np.float32)
+        if p["pattern"] == "cancellation":
+            x[:, 1::2] = -x[:, ::2]
+            w[:, 1::2] = w[:, ::2] + np.float32(2**-16)
+        return {"a": x, "bt": w}
     raise KeyError(t)
 
 
