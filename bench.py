@@ -30,6 +30,10 @@ One step = one pass of the hot path over one batch of synthetic input.  Workload
                uint4 random weights (seed 9; scales N(0,0.02), biases N(0,0.01)), 32 texts
                per GPU of U[32, 512] random token ids (seed 5), packed, last-token pooling,
                1024-d L2-normalised output (metric: texts/s; weak scaling, 32 per GPU).
+  bge_forward  the whole BGE-small (BERT) fp32 embedding forward around the head_dim-32
+               attention: 12 layers, random fp32 weights (seed 11), 256 texts per GPU of
+               U[16, 128] random token ids (seed 1), packed, CLS pooling, 384-d output;
+               projections on TF32 tensor cores with split operands (fp32 accuracy).
 
 Multi-GPU (torchrun, N ranks): sequences are assigned to ranks longest-first; shards are
 independent, so there is no collective on the data path (torch.distributed is used only
@@ -66,7 +70,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "attention tokens/s at Qwen3-0.6B shape & % of bf16 TC peak, 1/2/4/8 B200"
 WORKLOADS = ("qwen_padded", "qwen_varlen", "bge", "bge_scaled", "tails_qwen", "tails_bge",
-             "pool_qwen", "qwen_forward")
+             "pool_qwen", "qwen_forward", "bge_forward")
 # FP32 FMA throughput of the SIMT cores: 148 SMs x 128 lanes x 2 flops x 1.965 GHz
 # (nominal; packed f32x2 FMA doubles it).  Used for the head_dim-32 compute floor.
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
@@ -860,42 +864,125 @@ def run_pool(args):
         dist.destroy_process_group()
 
 
-# ---- the whole Qwen3 embedding forward (the layers around the attention) ------------------
+# ---- whole embedding forwards around the attention (Qwen3 and BGE-small) -----------------
 FORWARD_METRIC = "Qwen3-0.6B embedding forward texts/s (28 layers, uint4 weights)"
+BGE_FORWARD_METRIC = "BGE-small embedding forward texts/s (12 layers, fp32)"
 
 
-def forward_texts(rank: int, world: int):
-    """32 texts per rank: lengths U[32, 512] (seed 5) over 32 * world texts, assigned
-    longest first; random token ids (seed 5 + 1000 * rank)."""
-    from tessery_b200 import shard_sequences
-    from tessery_b200.qwen3 import Qwen3Config
+class ForwardSpec:
+    """One whole-forward benchmark: its texts, weights, model, CPU baseline and config."""
 
-    cfg = Qwen3Config()
-    lengths = np.random.default_rng(5).integers(32, 513, size=32 * world)
-    owned = lengths[shard_sequences(lengths, world, causal=True)[rank]]
-    rng = np.random.default_rng(5 + 1000 * rank)
-    ids = rng.integers(0, cfg.vocab, size=(owned.size, int(owned.max())), dtype=np.int64)
-    return cfg, ids, owned
+    def __init__(self, workload: str):
+        self.workload = workload
+        self.qwen = workload == "qwen_forward"
+        self.metric = FORWARD_METRIC if self.qwen else BGE_FORWARD_METRIC
+        self.per_rank = 32 if self.qwen else 256
+        self.weight_seed = 9 if self.qwen else 11
 
+    def cfg(self):
+        if self.qwen:
+            from tessery_b200.qwen3 import Qwen3Config
 
-def forward_config(world: int) -> dict:
-    return {"workload": "qwen_forward", "global_batch": 32 * world, "seq_len": "U[32,512]",
-            "layers": 28, "hidden": 1024, "heads": 16, "kv_heads": 8, "head_dim": 128,
-            "intermediate": 3072, "vocab": 151669, "weights": "uint4 random (seed 9)",
-            "pooling": "last token, L2-normalised 1024-d", "layout": "packed (cu_seqlens)",
-            "parallelism": f"text shards x{world} (longest first), no collective",
-            "l2": "not flushed: per-step activations and weights exceed L2 (126 MB)"}
+            return Qwen3Config()
+        from tessery_b200.bert import BertConfig
 
+        return BertConfig()
 
-def forward_cpu(weights, cfg, ids, lengths, n: int) -> float:
-    """The reference's float32 forward (oracle/qwen3.py) on the first n texts; seconds."""
-    import oracle.qwen3 as oq
+    def texts(self, rank: int, world: int):
+        """per_rank texts per rank, assigned longest first over per_rank * world texts;
+        Qwen: lengths U[32, 512] (seed 5); BGE: U[16, 128] (seed 1, the BGE attention
+        configuration's distribution).  Random token ids (seed + 1000 * rank)."""
+        from tessery_b200 import shard_sequences
 
-    start = time.perf_counter()
-    for i in range(n):
-        oq.qwen3_forward(weights, cfg, ids[i:i + 1, :lengths[i]], lengths[i:i + 1], cfg.hidden,
-                         dtype=np.float32)
-    return time.perf_counter() - start
+        cfg = self.cfg()
+        seed, lo, hi = (5, 32, 512) if self.qwen else (1, 16, 128)
+        lengths = np.random.default_rng(seed).integers(lo, hi + 1, size=self.per_rank * world)
+        owned = lengths[shard_sequences(lengths, world, causal=self.qwen)[rank]]
+        rng = np.random.default_rng(seed + 1000 * rank)
+        ids = rng.integers(0, cfg.vocab, size=(owned.size, int(owned.max())), dtype=np.int64)
+        return cfg, ids, owned
+
+    def weights(self, cfg):
+        if self.qwen:
+            from tessery_b200.qwen3 import random_weights
+        else:
+            from tessery_b200.bert import random_weights
+        return random_weights(cfg, seed=self.weight_seed)
+
+    def model(self, weights, cfg, rt):
+        if self.qwen:
+            from tessery_b200.qwen3 import Qwen3Encoder
+
+            return Qwen3Encoder(weights, cfg, runtime=rt)
+        from tessery_b200.bert import BertEncoder
+
+        return BertEncoder(weights, cfg, runtime=rt)
+
+    def enqueue(self, model, ids, cu, cu_host, pooled, stream):
+        if self.qwen:
+            model.enqueue(ids, cu, cu_host, pooled, model.cfg.hidden, stream=stream)
+        else:
+            model.enqueue(ids, cu, cu_host, pooled, stream=stream)
+
+    def forward(self, model, ids, lengths):
+        if self.qwen:
+            return model.forward(ids, lengths, dimensions=model.cfg.hidden)
+        return model.forward(ids, lengths)
+
+    def cpu(self, weights, cfg, ids, lengths, n: int) -> float:
+        """The reference's float32 forward restated (oracle/) on the first n texts; s."""
+        import oracle.bert as ob
+        import oracle.qwen3 as oq
+
+        start = time.perf_counter()
+        for i in range(n):
+            one, ln = ids[i:i + 1, :lengths[i]], lengths[i:i + 1]
+            if self.qwen:
+                oq.qwen3_forward(weights, cfg, one, ln, cfg.hidden, dtype=np.float32)
+            else:
+                ob.bert_forward(weights, cfg, one, ln, dtype=np.float32)
+        return time.perf_counter() - start
+
+    def cpu_source(self) -> str:
+        return ("float32 NumPy restatement of qwen3.py:112-296" if self.qwen
+                else "float32 NumPy restatement of bert.py:104-235")
+
+    def config(self, world: int) -> dict:
+        if self.qwen:
+            return {"workload": "qwen_forward", "global_batch": 32 * world,
+                    "seq_len": "U[32,512]", "layers": 28, "hidden": 1024, "heads": 16,
+                    "kv_heads": 8, "head_dim": 128, "intermediate": 3072, "vocab": 151669,
+                    "weights": "uint4 random (seed 9)",
+                    "pooling": "last token, L2-normalised 1024-d",
+                    "layout": "packed (cu_seqlens)",
+                    "parallelism": f"text shards x{world} (longest first), no collective",
+                    "l2": "not flushed: per-step activations and weights exceed L2 (126 MB)"}
+        return {"workload": "bge_forward", "global_batch": 256 * world, "seq_len": "U[16,128]",
+                "layers": 12, "hidden": 384, "heads": 12, "head_dim": 32,
+                "intermediate": 1536, "vocab": 30522,
+                "weights": "fp32 random (seed 11; N(0, 0.02^2), LayerNorm 1 + N(0, 0.02^2))",
+                "pooling": "CLS, L2-normalised 384-d", "layout": "packed (cu_seqlens)",
+                "precision": "fp32 path: TF32 split operands, three products, chunked sums",
+                "parallelism": f"text shards x{world} (longest first), no collective",
+                "l2": "not flushed: per-step activations exceed L2 (126 MB)"}
+
+    def roofline(self, flops: float, seconds: float) -> dict:
+        peaks = measured_peaks()
+        bf16 = peaks["bf16_tflops_sustained"] or peaks["bf16_tflops"]
+        achieved = flops / seconds / 1e12
+        if self.qwen:
+            return {"bound": "tensor", "kernel": "whole forward (linear_kernel dominant)",
+                    "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
+                    "frac": achieved / bf16, "algorithmic_flops_per_step": flops,
+                    "peak_source": f"{peaks['source']} sustained bf16 (a long multi-kernel "
+                                   "step)", "traffic": None}
+        # fp32 work on TF32 tensor cores: half the bf16 rate, three products per product.
+        peak = bf16 / 2 / 3
+        return {"bound": "tensor", "kernel": "whole forward (TF32 linear_kernel dominant)",
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "algorithmic_flops_per_step": flops,
+                "peak_source": f"{peaks['source']} sustained bf16 / 2 (TF32 rate) / 3 (split "
+                               "operands)", "traffic": None}
 
 
 def run_forward_reference(args):
@@ -903,22 +990,22 @@ def run_forward_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    from tessery_b200.qwen3 import random_weights
-
-    cfg, ids, lengths = forward_texts(0, world)
-    weights = random_weights(cfg, seed=9)
-    forward_cpu(weights, cfg, ids, lengths, 1)  # warm-up (BLAS threads, page-in)
-    n = 2  # texts per step: a bounded sample of the workload
-    total = sum(forward_cpu(weights, cfg, ids, lengths, n) for _ in range(args.steps))
+    spec = ForwardSpec(args.workload)
+    cfg, ids, lengths = spec.texts(0, world)
+    weights = spec.weights(cfg)
+    spec.cpu(weights, cfg, ids, lengths, 1)  # warm-up (BLAS threads, page-in)
+    n = 2 if spec.qwen else 8  # texts per step: a bounded sample of the workload
+    total = sum(spec.cpu(weights, cfg, ids, lengths, n) for _ in range(args.steps))
     value = n * args.steps / total
-    line = {"metric": FORWARD_METRIC, "value": value, "unit": "texts/s", "n_gpus": world,
+    sample = [int(v) for v in lengths[:n]]
+    line = {"metric": spec.metric, "value": value, "unit": "texts/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": forward_config(world), "impl": "reference",
+            "data": "synthetic", "config": spec.config(world), "impl": "reference",
             "cpu_baseline": {"value": value, "unit": "texts/s", "cores": cpu_threads(),
-                             "os_cpu_count": os.cpu_count(), "kind": "port",
-                             "sample": f"first {n} texts per step (lengths {[int(v) for v in lengths[:n]]}), "
-                                       "float32 NumPy restatement of qwen3.py:112-296",
+                             **host_cores(), "kind": "port",
+                             "sample": f"first {n} texts per step (lengths {sample}), "
+                                       + spec.cpu_source(),
                              "cpu_model": cpu_model()},
             "e2e": {"value": value, "unit": "texts/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -941,12 +1028,12 @@ def run_forward(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     from tessery_b200 import CudaRuntime
-    from tessery_b200.qwen3 import Qwen3Encoder, random_weights
 
+    spec = ForwardSpec(args.workload)
     rt = CudaRuntime(local)
-    cfg, ids, lengths = forward_texts(rank, world)
-    weights = random_weights(cfg, seed=9)
-    model = Qwen3Encoder(weights, cfg, runtime=rt)
+    cfg, ids, lengths = spec.texts(rank, world)
+    weights = spec.weights(cfg)
+    model = spec.model(weights, cfg, rt)
     dev = torch.device("cuda", local)
     cu_host = np.zeros(lengths.size + 1, np.int32)
     cu_host[1:] = np.cumsum(lengths)
@@ -959,8 +1046,7 @@ def run_forward(args):
     sptr = stream.cuda_stream
 
     def step():
-        model.enqueue(ids_d.data_ptr(), cu_d.data_ptr(), cu_host, pooled.data_ptr(), cfg.hidden,
-                      stream=sptr)
+        spec.enqueue(model, ids_d.data_ptr(), cu_d.data_ptr(), cu_host, pooled.data_ptr(), sptr)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -994,52 +1080,49 @@ def run_forward(args):
     total_s = float(stats[0])
     value = lengths.size * world * args.steps / total_s
 
-    # e2e through Qwen3Encoder.forward: host token ids in, pooled rows back.
-    model.forward(ids, lengths, dimensions=cfg.hidden)
+    # e2e through the encoder's forward: host token ids in, pooled rows back.
+    spec.forward(model, ids, lengths)
     if dist:
         dist.barrier()
     t0 = time.perf_counter()
     for _ in range(args.e2e_steps):
-        result = model.forward(ids, lengths, dimensions=cfg.hidden)
+        result = spec.forward(model, ids, lengths)
     e2e_stats = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(e2e_stats, op=dist.ReduceOp.MAX)
     e2e_value = lengths.size * world * args.e2e_steps / float(e2e_stats[0])
     assert np.allclose(np.linalg.norm(result, axis=1), 1.0, atol=1e-4)
 
-    peaks = measured_peaks()
     flops = model.flops(lengths)
-    mean_s = statistics.mean(ms) * 1e-3
-    peak = peaks["bf16_tflops_sustained"] or peaks["bf16_tflops"]
-    roof = {"bound": "tensor", "kernel": "whole forward (linear_kernel dominant)",
-            "achieved": flops / mean_s / 1e12, "peak": peak, "unit": "TFLOP/s",
-            "frac": flops / mean_s / 1e12 / peak, "algorithmic_flops_per_step": flops,
-            "peak_source": f"{peaks['source']} sustained bf16 (a long multi-kernel step)",
-            "traffic": None}
+    roof = spec.roofline(flops, statistics.mean(ms) * 1e-3)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        forward_cpu(weights, cfg, ids, lengths, 1)
-        n = 4
-        sec = forward_cpu(weights, cfg, ids, lengths, n)
-        cpu = {"value": n / sec, "unit": "texts/s", "cores": cpu_threads(),
-               "os_cpu_count": os.cpu_count(), "kind": "port",
-               "sample": f"first {n} of {lengths.size} texts (lengths {[int(v) for v in lengths[:n]]}), float32 "
-                         "NumPy restatement of qwen3.py:112-296",
+        spec.cpu(weights, cfg, ids, lengths, 1)
+        n = 4 if spec.qwen else 16
+        sec = spec.cpu(weights, cfg, ids, lengths, n)
+        sample = [int(v) for v in lengths[:n]]
+        cpu = {"value": n / sec, "unit": "texts/s", "cores": cpu_threads(), **host_cores(),
+               "kind": "port",
+               "sample": f"first {n} of {lengths.size} texts (lengths {sample}), "
+                         + spec.cpu_source(),
                "cpu_model": cpu_model()}
     if rank == 0:
-        line = {"metric": FORWARD_METRIC, "value": value, "unit": "texts/s", "n_gpus": world,
+        line = {"metric": spec.metric, "value": value, "unit": "texts/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": 1e3 * total_s / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic (seeded random uint4 weights and token ids)",
-                "config": forward_config(world), "roofline": roof,
+                "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16" if spec.qwen else "f32 (TF32 split operands)",
+                "data": "synthetic (seeded random weights and token ids)",
+                "config": spec.config(world), "roofline": roof,
                 "tokens_per_s": int(lengths.sum()) * world * args.steps / total_s,
-                "route": "linear_kernel + attn_tc_kernel + row kernels", "cpu_baseline": cpu,
+                "route": "linear_kernel + attn_tc_kernel + row kernels" if spec.qwen
+                         else "linear_kernel (TF32) + attention_d32_kernel + row kernels",
+                "cpu_baseline": cpu,
                 "e2e": {"value": e2e_value, "unit": "texts/s",
                         "h2d_bytes_per_step": int(lengths.sum()) * 4 + (lengths.size + 1) * 4,
                         "d2h_bytes_per_step": int(result.nbytes), "steps": args.e2e_steps,
-                        "path": "tessery_b200.qwen3.Qwen3Encoder.forward (token ids in, pooled "
-                                "rows out)"},
+                        "path": f"tessery_b200 {type(model).__name__}.forward (token ids in, "
+                                "pooled rows out)"},
                 "gpu_launches": launches, "clocks": clocks}
         print(json.dumps(line), flush=True)
     model.close()
@@ -1052,27 +1135,31 @@ def run_one_process(args):
     """The whole job of a workload through the one-process multi-GPU entry points: host
     arrays in, host results out, wall clock around synchronous calls (each call returns
     after its results are on the host).  qwen_padded: 32 sequences per device; qwen_varlen:
-    the 256 sequences; qwen_forward: 32 texts per device, pooled rows back."""
+    the 256 sequences; qwen_forward: 32 texts per device, bge_forward: 256 texts per
+    device, pooled rows back."""
     from tessery_b200.sharded import DeviceGroup, ShardedQwen3Encoder, attention_sharded
     from tessery_b200.workloads import benchmark_workload, qwen_padded
 
     n = args.gpus
     group = DeviceGroup(range(n))
     extra = {}
-    if args.workload == "qwen_forward":
-        from tessery_b200.qwen3 import Qwen3Config, random_weights
+    if args.workload in ("qwen_forward", "bge_forward"):
+        from tessery_b200.sharded import ShardedBertEncoder
 
-        cfg = Qwen3Config()
-        lengths = np.random.default_rng(5).integers(32, 513, size=32 * n)
-        ids = np.random.default_rng(5).integers(0, cfg.vocab, size=(lengths.size, 512))
-        model = ShardedQwen3Encoder(random_weights(cfg, seed=9), cfg, group=group)
+        spec = ForwardSpec(args.workload)
+        cfg = spec.cfg()
+        seed, lo, hi = (5, 32, 512) if spec.qwen else (1, 16, 128)
+        lengths = np.random.default_rng(seed).integers(lo, hi + 1, size=spec.per_rank * n)
+        ids = np.random.default_rng(seed).integers(0, cfg.vocab, size=(lengths.size, hi))
+        sharded = ShardedQwen3Encoder if spec.qwen else ShardedBertEncoder
+        model = sharded(spec.weights(cfg), cfg, group=group)
 
         def step():
-            return model.forward(ids, lengths, dimensions=cfg.hidden)
+            return model.forward(ids, lengths)
 
-        units, unit, metric = lengths.size, "texts/s", FORWARD_METRIC
+        units, unit, metric = lengths.size, "texts/s", spec.metric
         h2d = int(lengths.sum()) * 4
-        config = forward_config(n)
+        config = spec.config(n)
         extra["tokens"] = int(lengths.sum())
     elif args.workload in ("qwen_padded", "qwen_varlen"):
         if args.workload == "qwen_padded":
@@ -1104,7 +1191,8 @@ def run_one_process(args):
         h2d = w.q.nbytes + 2 * kv_rows * w.kv_heads * w.dim * w.k.itemsize
         config = config_block(args.workload, w, n)
     else:
-        raise SystemExit("--one-process takes qwen_padded, qwen_varlen or qwen_forward")
+        raise SystemExit("--one-process takes qwen_padded, qwen_varlen, qwen_forward or "
+                         "bge_forward")
     for _ in range(max(args.warmup, 3)):
         result = step()
     t0 = time.perf_counter()
@@ -1124,7 +1212,7 @@ def run_one_process(args):
     line = {"metric": metric, "value": value, "unit": unit, "n_gpus": n,
             "steps": args.e2e_steps, "warmup": max(args.warmup, 3),
             "ms_per_step": 1e3 * seconds / args.e2e_steps, "higher_is_better": True,
-            "scaling": scaling_of(args.workload) if args.workload != "qwen_forward" else "weak",
+            "scaling": "weak" if args.workload.endswith("_forward") else scaling_of(args.workload),
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
             "config": config, "impl": "ours-one-process",
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": h2d,
@@ -1148,7 +1236,7 @@ def main():
     if args.workload == "pool_qwen":
         run_pool_reference(args) if args.impl == "reference" else run_pool(args)
         return
-    if args.workload == "qwen_forward":
+    if args.workload in ("qwen_forward", "bge_forward"):
         run_forward_reference(args) if args.impl == "reference" else run_forward(args)
         return
     if args.impl == "reference":

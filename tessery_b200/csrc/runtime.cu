@@ -139,8 +139,8 @@ int check_status(Ctx *c) {
   cudaError_t e = cudaMemcpy(&st, c->status, sizeof(int), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(c, e, "status read");
   if (st) {
-    int zero = 0;
-    cudaMemcpy(c->status, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    cudaMemsetAsync(c->status, 0, sizeof(int), c->stream);  // before the next launch
+    cudaStreamSynchronize(c->stream);
     char msg[128];
     if ((st & 0xff) == TX_ETIMEOUT) {
       snprintf(msg, sizeof msg, "device wait timed out (site %d)", (st >> 8) & 0xffff);
@@ -598,7 +598,7 @@ void *tx_create(int device) {
       cudaEventCreate(&c->ev_begin) != cudaSuccess || cudaEventCreate(&c->ev_end) != cudaSuccess ||
       cudaEventCreateWithFlags(&c->scratch_done, cudaEventDisableTiming) != cudaSuccess ||
       cudaMalloc(&c->status, sizeof(int)) != cudaSuccess ||
-      cudaMemset(c->status, 0, sizeof(int)) != cudaSuccess) {
+      cudaMemsetAsync(c->status, 0, sizeof(int), c->stream) != cudaSuccess) {
     g_create_err = "context resources";
     tx_destroy(c);
     return nullptr;
@@ -673,7 +673,12 @@ void *tx_buffer(void *ctx, const void *host, uint64_t size) {
     cudaGetLastError();
     return nullptr;
   }
-  e = host ? cudaMemcpy(d, host, size, cudaMemcpyHostToDevice) : cudaMemset(d, 0, size);
+  // The fill runs on the context's stream, which does not wait for the legacy default
+  // stream (a plain cudaMemset or pageable cudaMemcpy there could land after kernels this
+  // context queues next), and is complete before the buffer is handed out.
+  e = host ? cudaMemcpyAsync(d, host, size, cudaMemcpyHostToDevice, c->stream)
+           : cudaMemsetAsync(d, 0, size, c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
   if (e != cudaSuccess) {
     cuda_fail(c, e, "buffer init");
     cudaFree(d);
@@ -734,8 +739,10 @@ int tx_write(void *buffer, const void *src, uint64_t bytes) {
   if (!buf_ok(b, c)) return TX_EINVAL;
   if (bytes > b->size) return fail(c, TX_EINVAL, "write beyond buffer");
   cudaSetDevice(c->device);
-  cudaError_t e = cudaStreamSynchronize(c->stream);
-  if (e == cudaSuccess) e = cudaMemcpy(b->dev, src, bytes, cudaMemcpyHostToDevice);
+  // Ordered after the context's queued work and complete before returning (a pageable
+  // cudaMemcpy may return before its DMA lands).
+  cudaError_t e = cudaMemcpyAsync(b->dev, src, bytes, cudaMemcpyHostToDevice, c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
   return e == cudaSuccess ? TX_OK : cuda_fail(c, e, "write");
 }
 

@@ -171,21 +171,17 @@ def attention_sharded(
     return out
 
 
-class ShardedQwen3Encoder:
-    """The Qwen3 embedding forward with the texts of a batch split across devices: one
-    Qwen3Encoder (its own copy of the weights) per device, texts assigned longest
-    first by their forward cost, only the pooled rows copied back."""
+class ShardedEncoder:
+    """An embedding model with the texts of a batch split across devices: one encoder
+    (its own copy of the weights, built by `factory(runtime)`) per device, texts assigned
+    longest first by the encoder's forward cost, only the pooled rows copied back."""
 
-    def __init__(self, weights: dict[str, NDArray], cfg: Any = None, *,
-                 group: DeviceGroup, precise: bool = False) -> None:
-        from .qwen3 import Qwen3Config, Qwen3Encoder
-
-        self.cfg = cfg or Qwen3Config()
+    def __init__(self, factory: Callable[[CudaRuntime], Any], group: DeviceGroup) -> None:
         self.group = group
         loaded: list[Any] = [None] * len(group)
 
         def load(rt: CudaRuntime, i: int) -> None:
-            loaded[i] = Qwen3Encoder(weights, self.cfg, runtime=rt, precise=precise)
+            loaded[i] = factory(rt)
 
         self.encoders = loaded
         try:
@@ -194,21 +190,18 @@ class ShardedQwen3Encoder:
             self.close()
             raise
 
-    def forward(self, ids: NDArray, lengths: NDArray, *, dimensions: int | None = None
-                ) -> NDArray[np.float32]:
-        """Pooled, L2-normalised embeddings [batch, dimensions] of right-padded ids
-        [batch, seq] with lengths [batch] (Qwen3Encoder.forward, sharded)."""
+    def _forward(self, ids: NDArray, lengths: NDArray, width: int, **kw: Any
+                 ) -> NDArray[np.float32]:
         ids, lens = np.asarray(ids), np.asarray(lengths)
         if ids.ndim != 2 or lens.shape != (ids.shape[0],):
             raise InvalidInputError()
-        dims = self.cfg.hidden if dimensions is None else int(dimensions)
         costs = np.array([self.encoders[0].flops([n]) for n in lens], dtype=np.int64)
         owned = shard_by_cost(costs, len(self.group))
-        result = np.empty((lens.size, dims), dtype=np.float32)
+        result = np.empty((lens.size, width), dtype=np.float32)
         by_runtime = {id(e.rt): e for e in self.encoders}
 
         def run(rt: CudaRuntime, texts: NDArray[np.int64]) -> None:
-            result[texts] = by_runtime[id(rt)].forward(ids[texts], lens[texts], dimensions=dims)
+            result[texts] = by_runtime[id(rt)].forward(ids[texts], lens[texts], **kw)
 
         self.group.run(run, [o if o.size else None for o in owned])
         return result
@@ -218,3 +211,38 @@ class ShardedQwen3Encoder:
             if e is not None:
                 e.close()
         self.encoders = []
+
+
+class ShardedQwen3Encoder(ShardedEncoder):
+    """Qwen3Encoder (qwen3.py:112-296) over every device of a group."""
+
+    def __init__(self, weights: dict[str, NDArray], cfg: Any = None, *,
+                 group: DeviceGroup, precise: bool = False) -> None:
+        from .qwen3 import Qwen3Config, Qwen3Encoder
+
+        self.cfg = cfg or Qwen3Config()
+        super().__init__(lambda rt: Qwen3Encoder(weights, self.cfg, runtime=rt,
+                                                 precise=precise), group)
+
+    def forward(self, ids: NDArray, lengths: NDArray, *, dimensions: int | None = None
+                ) -> NDArray[np.float32]:
+        """Pooled, L2-normalised embeddings [batch, dimensions] of right-padded ids
+        [batch, seq] with lengths [batch] (Qwen3Encoder.forward, sharded)."""
+        dims = self.cfg.hidden if dimensions is None else int(dimensions)
+        return self._forward(ids, lengths, dims, dimensions=dims)
+
+
+class ShardedBertEncoder(ShardedEncoder):
+    """BertEncoder (bert.py:104-235) over every device of a group."""
+
+    def __init__(self, weights: dict[str, NDArray], cfg: Any = None, *,
+                 group: DeviceGroup, precise: bool = True) -> None:
+        from .bert import BertConfig, BertEncoder
+
+        self.cfg = cfg or BertConfig()
+        super().__init__(lambda rt: BertEncoder(weights, self.cfg, runtime=rt,
+                                                precise=precise), group)
+
+    def forward(self, ids: NDArray, lengths: NDArray) -> NDArray[np.float32]:
+        """CLS embeddings [batch, hidden] of right-padded ids [batch, seq] (sharded)."""
+        return self._forward(ids, lengths, self.cfg.hidden)

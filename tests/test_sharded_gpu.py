@@ -58,3 +58,24 @@ def test_sharded_forward_equals_one_device(group):
         sharded.close()
         single.close()
     np.testing.assert_array_equal(got, want)
+
+
+def test_sharded_bert_forward_equals_one_device(group):
+    from tessery_b200.bert import BertConfig, BertEncoder
+    from tessery_b200.bert import random_weights as bert_weights
+    from tessery_b200.sharded import ShardedBertEncoder
+
+    cfg = BertConfig(layers=2, vocab=1000)
+    weights = bert_weights(cfg, seed=34)
+    rng = np.random.default_rng(34)
+    lengths = rng.integers(1, 128, size=13)
+    ids = rng.integers(0, cfg.vocab, size=(lengths.size, int(lengths.max())))
+    sharded = ShardedBertEncoder(weights, cfg, group=group)
+    single = BertEncoder(weights, cfg, runtime=group.runtimes[0])
+    try:
+        got = sharded.forward(ids, lengths)
+        want = single.forward(ids, lengths)
+    finally:
+        sharded.close()
+        single.close()
+    np.testing.assert_array_equal(got, want)
