@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "../../include/tessattn.h"
 #include "common.cuh"
@@ -28,6 +29,10 @@ namespace tx {
 namespace {
 
 constexpr int kMaxPerLane = 32;  // rows of up to 1024 columns stay in registers
+// The row kernels are instantiated per columns-per-lane bucket (kPer = 4, 8, 12, 16, 24 or
+// 32: rows of up to 32 kPer columns), so that a row takes no more registers than it needs
+// (one 32-entry array for every width left the LayerNorm at 149 registers and one block
+// per SM).
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -38,24 +43,25 @@ __device__ __forceinline__ float warp_sum(float v) {
 // LayerNorm of a row held as v[i] = x[lane + 32 i] (columns below `cols`), in place
 // (kernels.metal:362-373: the mean, then the mean of squared deviations,
 // inv = 1/sqrt(var + eps), (x - mean) * inv * w + b).
-__device__ __forceinline__ void norm_row(float (&v)[kMaxPerLane], uint32_t cols,
-                                         const float *w, const float *b, float eps) {
+template <int kPer>
+__device__ __forceinline__ void norm_row(float (&v)[kPer], uint32_t cols, const float *w,
+                                         const float *b, float eps) {
   const uint32_t lane = threadIdx.x & 31;
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
+  for (int i = 0; i < kPer; ++i)
     if (lane + 32 * i < cols) s += v[i];
   const float mean = warp_sum(s) / (float)cols;
   float q = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
+  for (int i = 0; i < kPer; ++i)
     if (lane + 32 * i < cols) {
       const float d = v[i] - mean;
       q += d * d;
     }
   const float inv = 1.0f / sqrtf(warp_sum(q) / (float)cols + eps);
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
+  for (int i = 0; i < kPer; ++i) {
     const uint32_t c = lane + 32 * i;
     if (c < cols) v[i] = (v[i] - mean) * inv * w[c] + b[c];
   }
@@ -63,12 +69,13 @@ __device__ __forceinline__ void norm_row(float (&v)[kMaxPerLane], uint32_t cols,
 
 // Row r of the split operand `pair` (hi [rows, cols] then lo [rows, cols]): TF32 pair in
 // fp32 containers (split == TX_F32) or a bf16 pair (split == TX_BF16X2).
-__device__ __forceinline__ void write_split(const float (&v)[kMaxPerLane], uint32_t cols,
+template <int kPer>
+__device__ __forceinline__ void write_split(const float (&v)[kPer], uint32_t cols,
                                             uint32_t rows, uint32_t r, void *pair, int split) {
   const uint32_t lane = threadIdx.x & 31;
   const size_t plane = (size_t)rows * cols;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
+  for (int i = 0; i < kPer; ++i)
     if (lane + 32 * i < cols) {
       const size_t at = (size_t)r * cols + lane + 32 * i;
       if (split == TX_F32) {
@@ -97,50 +104,54 @@ __device__ __forceinline__ uint32_t position_of(uint32_t t, const int32_t *cu, u
   return t - (uint32_t)cu[lo];
 }
 
-__global__ void bert_embed_norm_kernel(BertEmbedProblem p) {
+template <int kPer>
+__global__ void __launch_bounds__(256) bert_embed_norm_kernel(BertEmbedProblem p) {
   const uint32_t t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= p.tokens) return;
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t id = p.ids[t];
   const uint32_t pos = position_of(t, p.cu, p.nseq, p.seq);
-  float v[kMaxPerLane];
+  float v[kPer];
   if (id >= p.vocab || pos >= p.max_pos) {
     // An id or position outside the tables: a NaN row, reported as an invalid argument.
     if (lane == 0) report_status(p.status, TX_EINVAL);
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) v[i] = __int_as_float(0x7fc00000);
+    for (int i = 0; i < kPer; ++i) v[i] = __int_as_float(0x7fc00000);
   } else {
     const float *wr = p.words + (size_t)id * p.cols, *pr = p.positions + (size_t)pos * p.cols;
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
+    for (int i = 0; i < kPer; ++i) {
       const uint32_t c = lane + 32 * i;
       if (c < p.cols) v[i] = (wr[c] + p.types[c]) + pr[c];  // kernels.metal:360, type 0
     }
     norm_row(v, p.cols, p.ln_w, p.ln_b, p.eps);
   }
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
+  for (int i = 0; i < kPer; ++i) {
     const uint32_t c = lane + 32 * i;
     if (c < p.cols) p.out[(size_t)t * p.cols + c] = v[i];
   }
   if (p.pair) write_split(v, p.cols, p.tokens, t, p.pair, p.split);
 }
 
-__global__ void layer_norm_rows_kernel(const float *x, const float *w, const float *b,
-                                       float *out, void *pair, int split, uint32_t rows,
-                                       uint32_t cols, float eps) {
+template <int kPer>
+__global__ void __launch_bounds__(256) layer_norm_rows_kernel(const float *x, const float *w,
+                                                              const float *b, float *out,
+                                                              void *pair, int split,
+                                                              uint32_t rows, uint32_t cols,
+                                                              float eps) {
   const uint32_t r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (r >= rows) return;
   const uint32_t lane = threadIdx.x & 31;
-  float v[kMaxPerLane];
+  float v[kPer];
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
+  for (int i = 0; i < kPer; ++i) {
     const uint32_t c = lane + 32 * i;
     if (c < cols) v[i] = x[(size_t)r * cols + c];
   }
   norm_row(v, cols, w, b, eps);
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
+  for (int i = 0; i < kPer; ++i) {
     const uint32_t c = lane + 32 * i;
     if (c < cols) out[(size_t)r * cols + c] = v[i];
   }
@@ -239,11 +250,25 @@ __global__ void matmul_f32_kernel(const float *a, const float *bt, const float *
 
 bool bert_cols_ok(uint32_t cols) { return cols && cols <= 32 * kMaxPerLane; }
 
+// Calls f(std::integral_constant<int, kPer>) for the smallest bucket that holds `cols`.
+template <class F>
+cudaError_t with_per_lane(uint32_t cols, F &&f) {
+  const uint32_t per = (cols + 31) / 32;
+  if (per <= 4) return f(std::integral_constant<int, 4>());
+  if (per <= 8) return f(std::integral_constant<int, 8>());
+  if (per <= 12) return f(std::integral_constant<int, 12>());
+  if (per <= 16) return f(std::integral_constant<int, 16>());
+  if (per <= 24) return f(std::integral_constant<int, 24>());
+  return f(std::integral_constant<int, 32>());
+}
+
 cudaError_t launch_bert_embed(const BertEmbedProblem &p, cudaStream_t stream) {
   if (!bert_cols_ok(p.cols)) return cudaErrorInvalidValue;
   if (!p.tokens) return cudaSuccess;
-  bert_embed_norm_kernel<<<(p.tokens + 7) / 8, 256, 0, stream>>>(p);
-  return cudaGetLastError();
+  return with_per_lane(p.cols, [&](auto per) {
+    bert_embed_norm_kernel<decltype(per)::value><<<(p.tokens + 7) / 8, 256, 0, stream>>>(p);
+    return cudaGetLastError();
+  });
 }
 
 cudaError_t launch_layer_norm_rows(const float *x, const float *w, const float *b, float *out,
@@ -251,9 +276,11 @@ cudaError_t launch_layer_norm_rows(const float *x, const float *w, const float *
                                    cudaStream_t stream) {
   if (!bert_cols_ok(cols)) return cudaErrorInvalidValue;
   if (!rows) return cudaSuccess;
-  layer_norm_rows_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(x, w, b, out, pair, split, rows,
-                                                             cols, eps);
-  return cudaGetLastError();
+  return with_per_lane(cols, [&](auto per) {
+    layer_norm_rows_kernel<decltype(per)::value>
+        <<<(rows + 7) / 8, 256, 0, stream>>>(x, w, b, out, pair, split, rows, cols, eps);
+    return cudaGetLastError();
+  });
 }
 
 cudaError_t launch_split_tf32(const float *x, float *out, uint64_t n, cudaStream_t stream) {
