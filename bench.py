@@ -647,7 +647,8 @@ def rooflines(w, name: str, kernel: str, att_s: float, pro_s: float | None):
            "frac": att_bytes / att_s / 1e9 / peaks["hbm_gbs"],
            "algorithmic_bytes_per_launch": att_bytes}
     kname = {"tc_bf16_d128": "attn_tc_kernel", "d32": "attention_d32_kernel",
-             "simt": "attention_simt_kernel", "short_d128": "attn_short_kernel"}.get(kernel, kernel)
+             "d32_tc": "attn_d32_tc_kernel", "simt": "attention_simt_kernel",
+             "short_d128": "attn_short_kernel"}.get(kernel, kernel)
     if kernel in ("tc_bf16_d128", "short_d128"):  # bf16 tensor-core contractions
         t_c = flops / (peaks["bf16_tflops"] * 1e12)
         comp = {"achieved": flops / att_s / 1e12, "peak": peaks["bf16_tflops"],

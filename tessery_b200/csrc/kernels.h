@@ -29,6 +29,10 @@ cudaError_t launch_rope(float *x, uint32_t n, uint32_t heads, uint32_t seq, uint
                         float theta, cudaStream_t stream);
 // General attention: any dim <= 256, f32/bf16 in, f32/bf16 out, padded or varlen.
 cudaError_t launch_attention_simt(const AttnProblem &p, cudaStream_t stream);
+// head_dim 32, fp32 in and out: scores on tensor cores (TF32 split operands), the softmax
+// and P.V on the FP32 pipe (attn_d32_tc.cu).  `status`: the device status word.
+bool d32_tc_supported(const AttnProblem &p);
+cudaError_t launch_attention_d32_tc(const AttnProblem &p, int *status, cudaStream_t stream);
 
 // Fused q/k RMSNorm + RoPE prologue.  Rows: tokens*heads (q) and tokens*kv_heads (k).
 // q or k may be NULL to transform only the other one.  With `lengths` (padded layout),

@@ -217,7 +217,13 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
     return TX_OK;
   }
   const bool tc_path = p.in_dtype == TX_BF16 && p.scale > 0.f && tx::tc_attention_supported(p);
-  const bool d32_path = !tc_path && p.dim == 32 &&
+  // head_dim 32, fp32: the tensor-core scores kernel while the problem fits one wave of
+  // CTAs (it shortens each CTA: config 1, 24 -> 18 us); beyond, the packed-FMA kernel,
+  // whose thread pairs share every staged value row between two query rows, has the
+  // higher throughput (batch 4096: 1.74 ms against 2.37 ms).
+  const uint64_t d32_ctas = (uint64_t)((p.seq + 127) / 128) * p.heads * p.batch;
+  const bool d32tc_path = !tc_path && tx::d32_tc_supported(p) && d32_ctas <= 2ull * c->sms;
+  const bool d32_path = !tc_path && !d32tc_path && p.dim == 32 &&
                         p.batch <= 65535u && p.heads <= 65535u &&
                         (uintptr_t)p.q % 16 == 0 && (uintptr_t)p.k % 16 == 0 &&
                         (uintptr_t)p.v % 16 == 0 && (uintptr_t)p.out % 16 == 0;
@@ -295,6 +301,11 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
         cudaSuccess)
       return cuda_fail(c, e, "attention launch");
     c->last_kernel = "tc_bf16_d128";
+    ++c->launches;
+  } else if (d32tc_path) {
+    if ((e = tx::launch_attention_d32_tc(p, c->status, stream)) != cudaSuccess)
+      return cuda_fail(c, e, "attention launch");
+    c->last_kernel = "d32_tc";
     ++c->launches;
   } else if (d32_path) {
     if ((e = tx::launch_attention_d32(p, stream)) != cudaSuccess)

@@ -67,7 +67,7 @@ def test_reference_golden_case(runtime, case):
 
 def test_attention_route_follows_head_dim(runtime):
     rng = np.random.default_rng(5)
-    for dim, route in ((32, "d32"), (64, "simt"), (128, "simt")):
+    for dim, route in ((32, "d32_tc"), (64, "simt"), (128, "simt")):
         q = rng.normal(size=(2, 40, 4, dim)).astype(np.float32)
         k = rng.normal(size=(2, 40, 2, dim)).astype(np.float32)
         v = rng.normal(size=k.shape).astype(np.float32)
@@ -86,13 +86,31 @@ def test_attention_route_follows_head_dim(runtime):
 
 
 # ---- BGE d32 fp32 ---------------------------------------------------------------------
-@pytest.mark.parametrize("batch,seq", [(4, 128), (3, 200), (2, 520)])
+def d32_route(runtime, batch, seq, heads=12):
+    """fp32 head_dim 32: tensor-core scores within one wave of CTAs, packed FMA beyond."""
+    ctas = -(-seq // 128) * heads * batch
+    return "d32_tc" if ctas <= 2 * runtime.sms else "d32"
+
+
+@pytest.mark.parametrize("batch,seq", [(4, 128), (3, 200), (2, 520), (30, 128)])
+def test_bge_d32_fp32_device_route(runtime, batch, seq):
+    """Device pointers: one launch, routed by its number of CTAs (d32_route)."""
+    w = workloads.bge(batch=batch, seq=seq, seed=13, min_len=1)
+    got = _padded_device_call(runtime, w.q, w.k, w.v, w.lengths, in_dtype=TX_F32,
+                              causal=False, scale=w.scale)
+    assert runtime.last_kernel() == d32_route(runtime, batch, seq)
+    want = oracle.attention_padded(w.q, w.k, w.v, w.lengths, False, w.scale)
+    np.testing.assert_allclose(got, want, atol=F32_ATOL, rtol=F32_RTOL)
+
+
+@pytest.mark.parametrize("batch,seq", [(4, 128), (3, 200), (2, 520), (30, 128)])
 def test_bge_d32_fp32_matches_oracle(runtime, batch, seq):
     w = workloads.bge(batch=batch, seq=seq, seed=11, min_len=1)
     w.lengths[0] = 1
     w.lengths[-1] = seq
     got = attention(w.q, w.k, w.v, lengths=w.lengths, causal=False, runtime=runtime)
-    assert runtime.last_kernel() == "d32"
+    # Host arrays go through in chunks of whole sequences, routed chunk by chunk.
+    assert runtime.last_kernel() in ("d32_tc", "d32")
     want = oracle.attention_padded(w.q, w.k, w.v, w.lengths, False, w.scale)
     np.testing.assert_allclose(got, want, atol=F32_ATOL, rtol=F32_RTOL)
     assert np.max(np.abs(got - want)) <= 1e-4
@@ -108,7 +126,7 @@ def test_bge_d32_causal_and_varlen(runtime):
                for _ in range(3)]
     for causal in (False, True):
         got = attention(q, k, v, cu_seqlens=cu, causal=causal, runtime=runtime)
-        assert runtime.last_kernel() == "d32"
+        assert runtime.last_kernel() == "d32_tc"
         want = oracle.attention_varlen(q, k, v, cu, causal, 32**-0.5)
         np.testing.assert_allclose(got, want, atol=F32_ATOL, rtol=F32_RTOL)
 
@@ -548,7 +566,7 @@ def _padded_device_call(rt, q, k, v, lengths, *, in_dtype, causal, scale, qw=Non
             b.close()
 
 
-@pytest.mark.parametrize("route", ["tc_bf16_d128", "short_d128", "d32", "simt"])
+@pytest.mark.parametrize("route", ["tc_bf16_d128", "short_d128", "d32_tc", "d32", "simt"])
 def test_padded_kv_rows_may_hold_nan_or_inf(runtime, route):
     """k/v rows at or past a sequence's length hold NaN (k) and Inf (v): every route
     returns the oracle's rows, all finite, as the reference, which never reads those rows
@@ -565,13 +583,19 @@ def test_padded_kv_rows_may_hold_nan_or_inf(runtime, route):
         want = qwen_oracle(w)
         gate = BF16_GATE
     else:
-        D = 32 if route == "d32" else 64
+        D = 64 if route == "simt" else 32
         lengths = np.array([128, 1, 70])
         q, k, v = (rng.normal(size=(3, 128, 4, D)).astype(np.float32) for _ in range(3))
+        if route == "d32":  # bf16 inputs take the FP32-pipe head_dim-32 kernel
+            q, k, v = (from_bf16_bits(to_bf16_bits(a)) for a in (q, k, v))
         k = _poison_padding(k, lengths, np.float32(np.nan))
         v = _poison_padding(v, lengths, np.float32(np.inf))
-        got = _padded_device_call(runtime, q, k, v, lengths, in_dtype=TX_F32, causal=False,
-                                  scale=D**-0.5)
+        if route == "d32":
+            got = _padded_device_call(runtime, *(to_bf16_bits(a) for a in (q, k, v)), lengths,
+                                      in_dtype=TX_BF16, causal=False, scale=D**-0.5)
+        else:
+            got = _padded_device_call(runtime, q, k, v, lengths, in_dtype=TX_F32,
+                                      causal=False, scale=D**-0.5)
         want = oracle.attention_padded(q, k, v, lengths, False, D**-0.5)
         gate = 1e-4
     assert runtime.last_kernel() == route
