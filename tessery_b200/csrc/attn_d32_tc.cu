@@ -17,10 +17,12 @@
 //     M=128, N=128, K=8, twelve instructions) into 128 tensor-memory columns: about 22
 //     significant bits per operand, so the scores carry fp32-level error;
 //   - thread t (tensor-memory lane t = query row t) reads its row of S, takes the
-//     masked maximum, and accumulates exp2(s - m) * v over the tile's keys with packed
-//     f32x2 FMAs (value rows read as shared-memory broadcasts), an online softmax across
-//     tiles with a lazily updated reference maximum (rescaled only when a tile maximum
-//     exceeds it by more than 8), so every probability stays at most 2^8.
+//     masked maximum and forms exp2(s - m); threads 2i and 2i+1 exchange these and each
+//     accumulates both rows' p * v for its half of the head dimension with packed f32x2
+//     FMAs (every value row read as a shared-memory broadcast feeds two rows); the
+//     softmax is online across tiles with a lazily updated reference maximum (rescaled
+//     only when a chunk maximum exceeds it by more than 8), so every probability stays
+//     at most 2^8.
 // Key and value rows at or past a sequence's end are never read (zeros are staged), so
 // padded rows may hold anything.  The single wait (scores ready) is bounded; a wait that
 // gives up records TX_ETIMEOUT | site << 8 and the CTA returns after its MMAs drained.
@@ -143,9 +145,13 @@ __global__ void __launch_bounds__(kRows, 2) attn_d32_tc_kernel(AttnProblem p, in
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem + ((warp * 32u) << 16);
 
-  uint64_t acc[16];  // output row, packed pairs
+  // Threads 2i and 2i+1 (rows 2i and 2i+1) share the output accumulators of both rows,
+  // each for one half of the head dimension (h), so every value-row read from shared
+  // memory feeds two rows; each thread keeps the softmax state of its own row.
+  const uint32_t h = tid & 1;
+  uint64_t acc_e[8], acc_o[8];  // rows 2i and 2i+1, columns 16h..16h+15, packed pairs
 #pragma unroll
-  for (int i = 0; i < 16; ++i) acc[i] = f2(0.f, 0.f);
+  for (int i = 0; i < 8; ++i) acc_e[i] = acc_o[i] = f2(0.f, 0.f);
   float m = -INFINITY, l = 0.f;
   bool ok = true;
   uint32_t phase = 0;
@@ -211,26 +217,39 @@ __global__ void __launch_bounds__(kRows, 2) attn_d32_tc_kernel(AttnProblem p, in
 #pragma unroll
       for (int t = 0; t < 32; ++t)
         if (c * 32 + t < valid) mc = fmaxf(mc, __uint_as_float(r[t]));
+      float cr = 1.0f;  // rescale factor of this thread's row (1: none)
       if (mc > m + 8.0f) {  // also the first chunk with a valid key (m = -inf)
-        const float cr = ex2(m - mc);
-        const uint64_t c2 = f2(cr, cr);
+        cr = ex2(m - mc);
         l *= cr;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = mul2(acc[i], c2);
         m = mc;
       }
-      const float *vc = vs + c * 32 * 32;
+      const float cr_pair = __shfl_xor_sync(0xffffffffu, cr, 1);
+      if (__any_sync(0xffffffffu, cr != 1.0f || cr_pair != 1.0f)) {
+        const float ce = h ? cr_pair : cr, co = h ? cr : cr_pair;
+        const uint64_t ce2 = f2(ce, ce), co2 = f2(co, co);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          acc_e[i] = mul2(acc_e[i], ce2);
+          acc_o[i] = mul2(acc_o[i], co2);
+        }
+      }
+      const float *vc = vs + c * 32 * 32 + 16 * h;
 #pragma unroll
       for (int t = 0; t < 32; ++t) {
         const float pj = c * 32 + t < valid ? ex2(__uint_as_float(r[t]) - m) : 0.f;
         l += pj;
-        const uint64_t p2 = f2(pj, pj);
+        const float pp = __shfl_xor_sync(0xffffffffu, pj, 1);
+        const float pe = h ? pp : pj, po = h ? pj : pp;
+        const uint64_t pe2 = f2(pe, pe), po2 = f2(po, po);
         const float4 *vr = reinterpret_cast<const float4 *>(vc + t * 32);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 4; ++i) {
           const float4 vv = vr[i];
-          acc[2 * i] = fma2(p2, f2(vv.x, vv.y), acc[2 * i]);
-          acc[2 * i + 1] = fma2(p2, f2(vv.z, vv.w), acc[2 * i + 1]);
+          const uint64_t va = f2(vv.x, vv.y), vb = f2(vv.z, vv.w);
+          acc_e[2 * i] = fma2(pe2, va, acc_e[2 * i]);
+          acc_e[2 * i + 1] = fma2(pe2, vb, acc_e[2 * i + 1]);
+          acc_o[2 * i] = fma2(po2, va, acc_o[2 * i]);
+          acc_o[2 * i + 1] = fma2(po2, vb, acc_o[2 * i + 1]);
         }
       }
     }
@@ -238,13 +257,25 @@ __global__ void __launch_bounds__(kRows, 2) attn_d32_tc_kernel(AttnProblem p, in
     tc_fence_before();
     __syncthreads();
   }
-  if (act && ok) {
-    const float inv = 1.0f / l;  // zero valid keys: 0/0, as the reference's sums give
-    float4 *op = reinterpret_cast<float4 *>(out + ((base + pos) * p.heads + head) * 32);
+  {
+    // This thread's half of rows 2i and 2i+1 (zero valid keys: 0/0, as the reference's
+    // sums give).
+    const float l_pair = __shfl_xor_sync(0xffffffffu, l, 1);
+    const float inv_e = 1.0f / (h ? l_pair : l), inv_o = 1.0f / (h ? l : l_pair);
+    const uint32_t pos_e = q0 + (tid & ~1u);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float2 a = f2_unpack(acc[2 * i]), b = f2_unpack(acc[2 * i + 1]);
-      op[i] = make_float4(a.x * inv, a.y * inv, b.x * inv, b.y * inv);
+    for (int r = 0; r < 2; ++r) {
+      const uint32_t prow = pos_e + r;
+      if (!ok || prow >= rows) continue;
+      const uint64_t(&a)[8] = r ? acc_o : acc_e;
+      const float inv = r ? inv_o : inv_e;
+      float4 *op =
+          reinterpret_cast<float4 *>(out + ((base + prow) * p.heads + head) * 32 + 16 * h);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 x0 = f2_unpack(a[2 * i]), x1 = f2_unpack(a[2 * i + 1]);
+        op[i] = make_float4(x0.x * inv, x0.y * inv, x1.x * inv, x1.y * inv);
+      }
     }
   }
   tc_fence_before();
