@@ -17,7 +17,7 @@ from pathlib import Path
 PACKAGE = Path(__file__).resolve().parent
 CSRC = PACKAGE / "csrc"
 LIBRARY = PACKAGE / "libtessattn.so"
-SOURCES = ["runtime.cu", "simt_kernels.cu", "attn_d32.cu", "attn_d32_tc.cu", "attn_tc.cu", "attn_short.cu", "noalloc.cu",
+SOURCES = ["runtime.cu", "simt_kernels.cu", "attn_d32.cu", "attn_d32_tc.cu", "attn_f32_tc.cu", "attn_tc.cu", "attn_short.cu", "noalloc.cu",
            "pool.cu", "linear.cu", "qwen_ops.cu", "qwen3_model.cu",
            "bert_ops.cu", "bert_model.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -33,6 +33,10 @@ cudaError_t launch_attention_simt(const AttnProblem &p, cudaStream_t stream);
 // and P.V on the FP32 pipe (attn_d32_tc.cu).  `status`: the device status word.
 bool d32_tc_supported(const AttnProblem &p);
 cudaError_t launch_attention_d32_tc(const AttnProblem &p, int *status, cudaStream_t stream);
+// head_dim 128, fp32 in and out: scores on tensor cores (TF32 split operands), the softmax
+// and P.V on the FP32 pipe (attn_f32_tc.cu).
+bool f32_tc_supported(const AttnProblem &p);
+cudaError_t launch_attention_f32_tc(const AttnProblem &p, int *status, cudaStream_t stream);
 
 // Fused q/k RMSNorm + RoPE prologue.  Rows: tokens*heads (q) and tokens*kv_heads (k).
 // q or k may be NULL to transform only the other one.  With `lengths` (padded layout),

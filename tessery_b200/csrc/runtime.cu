@@ -227,6 +227,7 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
                         p.batch <= 65535u && p.heads <= 65535u &&
                         (uintptr_t)p.q % 16 == 0 && (uintptr_t)p.k % 16 == 0 &&
                         (uintptr_t)p.v % 16 == 0 && (uintptr_t)p.out % 16 == 0;
+  const bool f32tc_path = !tc_path && !d32tc_path && !d32_path && tx::f32_tc_supported(p);
   cudaError_t e = cudaSetDevice(c->device);
   if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
   bool uses_scratch = prologue || tc_path;
@@ -306,6 +307,11 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
     if ((e = tx::launch_attention_d32_tc(p, c->status, stream)) != cudaSuccess)
       return cuda_fail(c, e, "attention launch");
     c->last_kernel = "d32_tc";
+    ++c->launches;
+  } else if (f32tc_path) {
+    if ((e = tx::launch_attention_f32_tc(p, c->status, stream)) != cudaSuccess)
+      return cuda_fail(c, e, "attention launch");
+    c->last_kernel = "f32_tc";
     ++c->launches;
   } else if (d32_path) {
     if ((e = tx::launch_attention_d32(p, stream)) != cudaSuccess)

@@ -67,7 +67,7 @@ def test_reference_golden_case(runtime, case):
 
 def test_attention_route_follows_head_dim(runtime):
     rng = np.random.default_rng(5)
-    for dim, route in ((32, "d32_tc"), (64, "simt"), (128, "simt")):
+    for dim, route in ((32, "d32_tc"), (64, "simt"), (128, "f32_tc")):
         q = rng.normal(size=(2, 40, 4, dim)).astype(np.float32)
         k = rng.normal(size=(2, 40, 2, dim)).astype(np.float32)
         v = rng.normal(size=k.shape).astype(np.float32)
@@ -129,6 +129,55 @@ def test_bge_d32_causal_and_varlen(runtime):
         assert runtime.last_kernel() == "d32_tc"
         want = oracle.attention_varlen(q, k, v, cu, causal, 32**-0.5)
         np.testing.assert_allclose(got, want, atol=F32_ATOL, rtol=F32_RTOL)
+
+
+# ---- head_dim 128 fp32 (tensor-core scores, TF32 split operands) ---------------------------
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("heads,kv_heads,seq,lengths", [
+    (4, 2, 40, [40, 17]),
+    (16, 8, 300, [300, 129, 1, 64, 0]),
+    (6, 2, 257, [257, 256, 65, 16]),
+    (2, 1, 700, [700, 333]),
+])
+def test_f32_d128_padded_matches_oracle(runtime, causal, heads, kv_heads, seq, lengths):
+    """fp32 in and out, head_dim 128 (the Qwen3 adapter's float buffers): one launch of
+    the tensor-core scores kernel; lengths that are not multiples of the 64-key tile or
+    the 16-key chunk, query blocks past a sequence's end, GQA groups of 2 and 3, and a
+    zero length (NaN rows, as the reference's sums give)."""
+    rng = np.random.default_rng(seq + heads)
+    B = len(lengths)
+    lengths = np.array(lengths, np.uint32)
+    q = rng.normal(size=(B, seq, heads, 128)).astype(np.float32)
+    k, v = (rng.normal(size=(B, seq, kv_heads, 128)).astype(np.float32) for _ in range(2))
+    got = _padded_device_call(runtime, q, k, v, lengths, in_dtype=TX_F32, causal=causal,
+                              scale=128**-0.5)
+    assert runtime.last_kernel() == "f32_tc"
+    want = oracle.attention_padded(q, k, v, lengths, causal, 128**-0.5)
+    empty = lengths == 0
+    assert np.isnan(got[empty]).all()
+    np.testing.assert_allclose(got[~empty], want[~empty], atol=F32_ATOL, rtol=F32_RTOL)
+
+
+def test_f32_d128_varlen_and_large_logits(runtime):
+    """Packed sequences, causal and not, with logits up to ~25 in size (the lazy rescale
+    moves the reference maximum several times within a row).  At this size the fixed gate
+    is beyond float32 arithmetic itself (the reference's formula evaluated in float32
+    misses atol 2e-6 / rtol 2e-5 by 3x on ~450 elements), so the gate is that evaluation's
+    own largest error: the kernel is at least as close to float64 as it."""
+    rng = np.random.default_rng(81)
+    lengths = np.array([1, 63, 64, 65, 200, 511], np.int64)
+    cu = np.zeros(len(lengths) + 1, np.int32)
+    cu[1:] = np.cumsum(lengths)
+    total = int(cu[-1])
+    q = rng.normal(size=(total, 8, 128)).astype(np.float32)
+    k, v = (rng.normal(size=(total, 4, 128)).astype(np.float32) for _ in range(2))
+    q *= np.linspace(0.2, 6.0, total, dtype=np.float32)[:, None, None]
+    for causal in (False, True):
+        got = attention(q, k, v, cu_seqlens=cu, causal=causal, runtime=runtime)
+        assert runtime.last_kernel() == "f32_tc"
+        want = oracle.attention_varlen(q, k, v, cu, causal, 128**-0.5)
+        fp32 = oracle.attention_varlen(q, k, v, cu, causal, 128**-0.5, dtype=np.float32)
+        assert np.max(np.abs(got - want)) <= np.max(np.abs(fp32 - want))
 
 
 # ---- Qwen d128 bf16 (tensor cores) -------------------------------------------------------
@@ -566,7 +615,8 @@ def _padded_device_call(rt, q, k, v, lengths, *, in_dtype, causal, scale, qw=Non
             b.close()
 
 
-@pytest.mark.parametrize("route", ["tc_bf16_d128", "short_d128", "d32_tc", "d32", "simt"])
+@pytest.mark.parametrize("route", ["tc_bf16_d128", "short_d128", "d32_tc", "d32", "f32_tc",
+                                   "simt"])
 def test_padded_kv_rows_may_hold_nan_or_inf(runtime, route):
     """k/v rows at or past a sequence's length hold NaN (k) and Inf (v): every route
     returns the oracle's rows, all finite, as the reference, which never reads those rows
@@ -583,7 +633,7 @@ def test_padded_kv_rows_may_hold_nan_or_inf(runtime, route):
         want = qwen_oracle(w)
         gate = BF16_GATE
     else:
-        D = 64 if route == "simt" else 32
+        D = {"simt": 64, "f32_tc": 128}.get(route, 32)
         lengths = np.array([128, 1, 70])
         q, k, v = (rng.normal(size=(3, 128, 4, D)).astype(np.float32) for _ in range(3))
         if route == "d32":  # bf16 inputs take the FP32-pipe head_dim-32 kernel
