@@ -11,6 +11,10 @@ One step = one pass of the hot path over one batch of synthetic input.  Workload
                Step = the k prologue kernel (RMSNorm + RoPE of the valid k rows) + the
                tcgen05 attention kernel, which applies the q RMSNorm + RoPE to each Q tile
                in shared memory.  Weak scaling: 32*N sequences over N GPUs.
+  qwen_f32     the qwen_padded batch with float32 q/k/v (the reference adapter's float
+               buffers, qwen3.py:238-245): step = one q/k RMSNorm + RoPE launch (fp32, into
+               scratch) + the fp32 head_dim-128 attention (tensor-core TF32 split-operand
+               scores, FP32-pipe softmax and P.V).
   qwen_varlen  the same layer on 256 sequences packed by cu_seqlens (no padding), lengths
                log-normal (median 96, sigma 0.8) clipped to [2, 512].  The 256 sequences
                are split across the N GPUs: strong scaling.
@@ -69,7 +73,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "attention tokens/s at Qwen3-0.6B shape & % of bf16 TC peak, 1/2/4/8 B200"
-WORKLOADS = ("qwen_padded", "qwen_varlen", "bge", "bge_scaled", "tails_qwen", "tails_bge",
+WORKLOADS = ("qwen_padded", "qwen_f32", "qwen_varlen", "bge", "bge_scaled", "tails_qwen", "tails_bge",
              "pool_qwen", "qwen_forward", "bge_forward")
 # FP32 FMA throughput of the SIMT cores: 148 SMs x 128 lanes x 2 flops x 1.965 GHz
 # (nominal; packed f32x2 FMA doubles it).  Used for the head_dim-32 compute floor.
@@ -132,7 +136,7 @@ def metric_of(name: str) -> str:
 
 
 def config_block(name: str, w, world: int) -> dict:
-    per_gpu = {"qwen_padded": 32, "bge": 4, "bge_scaled": w.batch, "tails_qwen": 32,
+    per_gpu = {"qwen_padded": 32, "qwen_f32": 32, "bge": 4, "bge_scaled": w.batch, "tails_qwen": 32,
                "tails_bge": 32}
     glob = 256 if name == "qwen_varlen" else per_gpu[name] * world
     cfg = {"workload": name, "global_batch": glob, "heads": w.heads, "kv_heads": w.kv_heads,
@@ -143,7 +147,8 @@ def config_block(name: str, w, world: int) -> dict:
         cfg["seq_len"] = w.seq
     else:
         cfg["max_len"] = w.seq
-    cfg["lengths"] = {"qwen_padded": "U[32,512] seed 2", "qwen_varlen":
+    cfg["lengths"] = {"qwen_padded": "U[32,512] seed 2", "qwen_f32": "U[32,512] seed 2",
+                      "qwen_varlen":
                       "lognormal(ln 96, 0.8) clip [2,512] seed 3", "bge": "U[16,128] seed 1",
                       "bge_scaled": "U[16,128] seed 1", "tails_qwen": "U[2,32] seed 4",
                       "tails_bge": "U[2,32] seed 4"}[name]
@@ -392,6 +397,10 @@ def run_ours(args):
     # take the short-sequence kernel, which applies the q and k prologue itself: the step
     # is then one attention call with both weights and no separate k pass.
     fused = (prologue and D == 128 and in_code == TX_BF16 and w.seq <= 32 and H // KV <= 4)
+    # fp32 inputs: the library normalises and rotates q and k in one launch of the general
+    # prologue (into scratch), then runs the attention kernel on the results.
+    f32_prologue = prologue and in_code == TX_F32
+    qn = torch.empty_like(q) if f32_prologue else None
     if prologue:
         qw, kw = to_dev(w.q_norm_weight), to_dev(w.k_norm_weight)
         kn = torch.empty_like(k)
@@ -413,18 +422,21 @@ def run_ours(args):
     torch.cuda.set_stream(stream)
     sptr = stream.cuda_stream
     assert sptr != 0
-    def attend(k_in, with_k_weight):
-        extra = dict(q_norm_weight=qw.data_ptr(), eps=w.eps, theta=w.theta) if prologue else {}
+    def attend(k_in, with_k_weight, q_in=None):
+        extra = dict(eps=w.eps, theta=w.theta) if prologue else {}
+        if prologue and q_in is None:
+            extra["q_norm_weight"] = qw.data_ptr()
         if with_k_weight:
             extra["k_norm_weight"] = kw.data_ptr()
+        q_in = q if q_in is None else q_in
         if w.layout == "padded":
-            rt.attention_padded_device(q.data_ptr(), k_in.data_ptr(), v.data_ptr(),
+            rt.attention_padded_device(q_in.data_ptr(), k_in.data_ptr(), v.data_ptr(),
                                        lengths.data_ptr(), out.data_ptr(), batch=B, seq=L,
                                        heads=H, kv_heads=KV, dim=D, in_dtype=in_code,
                                        out_dtype=TX_F32, causal=w.causal, scale=w.scale,
                                        lengths_host=lengths_host, stream=sptr, **extra)
         else:
-            rt.attention_varlen_device(q.data_ptr(), k_in.data_ptr(), v.data_ptr(),
+            rt.attention_varlen_device(q_in.data_ptr(), k_in.data_ptr(), v.data_ptr(),
                                        cu.data_ptr(), out.data_ptr(), nseq=nseq, total=total,
                                        max_len=w.seq, heads=H, kv_heads=KV, dim=D,
                                        in_dtype=in_code, out_dtype=TX_F32, causal=w.causal,
@@ -439,8 +451,20 @@ def run_ours(args):
 
     def split_step(mid):
         # The same two kernels as separate calls with an event between them (for the
-        # per-kernel rooflines): the k prologue into kn, then the attention on kn.
-        if prologue and not fused:
+        # per-kernel rooflines): the k prologue into kn, then the attention on kn (fp32:
+        # the q and k prologue into qn and kn, every row as the library does, then the
+        # attention on them).
+        if f32_prologue:
+            layout = (dict(seq=L) if w.layout == "padded" else
+                      dict(seq=w.seq, cu_seqlens=cu.data_ptr(), nseq=nseq))
+            rt.qk_norm_rope_device(q.data_ptr(), k.data_ptr(), qn.data_ptr(), kn.data_ptr(),
+                                   tokens=tokens_in_layout, heads=H, kv_heads=KV, dim=D,
+                                   q_norm_weight=qw.data_ptr(), k_norm_weight=kw.data_ptr(),
+                                   in_dtype=in_code, out_dtype=in_code, eps=w.eps,
+                                   theta=w.theta, stream=sptr, **layout)
+            mid.record(stream)
+            attend(kn, False, q_in=qn)
+        elif prologue and not fused:
             if w.layout == "padded":
                 rt.qk_norm_rope_device(None, k.data_ptr(), None, kn.data_ptr(),
                                        tokens=tokens_in_layout, seq=L, heads=H, kv_heads=KV,
@@ -588,7 +612,7 @@ def run_ours(args):
 
     roof, prologue_roof = rooflines(w, name, kernel, statistics.mean(att_ms) * 1e-3,
                                     statistics.mean(pro_ms) * 1e-3 if prologue and not fused
-                                    else None)
+                                    else None, pro_qk=f32_prologue)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -626,13 +650,17 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def rooflines(w, name: str, kernel: str, att_s: float, pro_s: float | None):
-    """Roofline of the attention launch and, when present, of the k prologue launch.
+def rooflines(w, name: str, kernel: str, att_s: float, pro_s: float | None,
+              pro_qk: bool = False):
+    """Roofline of the attention launch and, when present, of the prologue launch (the
+    k rows; pro_qk: every q and k row, the fp32 route).
 
     Algorithmic bytes of the attention launch (contract I/O): every q row (padded rows
     produce outputs too), the valid k and v rows, the fp32 output of every q row, the q
     norm weight when the q prologue is fused.  FLOPs: 4 * head_dim * heads per useful
-    (query, key) pair of valid query rows.
+    (query, key) pair of valid query rows.  The fp32 head_dim-128 kernel (f32_tc) does
+    half of them (Q.K^T) on the tensor cores as three TF32 products and the other half
+    (P.V) on the FP32 pipe: its compute floor is the larger of the two pipes' times.
     """
     peaks = measured_peaks()
     traffic = profile_traffic(name)
@@ -648,8 +676,23 @@ def rooflines(w, name: str, kernel: str, att_s: float, pro_s: float | None):
            "algorithmic_bytes_per_launch": att_bytes}
     kname = {"tc_bf16_d128": "attn_tc_kernel", "d32": "attention_d32_kernel",
              "d32_tc": "attn_d32_tc_kernel", "simt": "attention_simt_kernel",
-             "short_d128": "attn_short_kernel"}.get(kernel, kernel)
-    if kernel in ("tc_bf16_d128", "short_d128"):  # bf16 tensor-core contractions
+             "short_d128": "attn_short_kernel", "f32_tc": "attn_f32_tc_kernel"}.get(kernel,
+                                                                                 kernel)
+    if kernel == "f32_tc":
+        tf32 = peaks["bf16_tflops"] / 2
+        t_pv = flops / 2 / (FP32_NOMINAL_TFLOPS * 1e12)
+        t_qk = 3 * flops / 2 / (tf32 * 1e12)
+        t_c = max(t_pv, t_qk)
+        comp = {"achieved": flops / 2 / att_s / 1e12, "peak": FP32_NOMINAL_TFLOPS,
+                "unit": "TFLOP/s", "frac": t_pv / att_s,
+                "algorithmic_flops_per_launch": flops / 2, "work": "P.V on the FP32 pipe",
+                "peak_source": "nominal FP32 FMA, 148 SMs x 128 lanes x 2 x 1.965 GHz",
+                "scores_floor_us": 1e6 * t_qk,
+                "scores_peak": f"TF32 = measured bf16 burst / 2 ({tf32:.0f} TFLOP/s), "
+                               "3 products"}
+        comp_bound, comp_key = "fp32", "fp32"
+        main = hbm if t_hbm >= t_c else comp
+    elif kernel in ("tc_bf16_d128", "short_d128"):  # bf16 tensor-core contractions
         t_c = flops / (peaks["bf16_tflops"] * 1e12)
         comp = {"achieved": flops / att_s / 1e12, "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": flops / att_s / 1e12 / peaks["bf16_tflops"],
@@ -662,7 +705,8 @@ def rooflines(w, name: str, kernel: str, att_s: float, pro_s: float | None):
                 "algorithmic_flops_per_launch": flops,
                 "peak_source": "nominal FP32 FMA, 148 SMs x 128 lanes x 2 x 1.965 GHz"}
         comp_bound, comp_key = "fp32", "fp32"
-    main = hbm if t_hbm >= t_c or comp_bound == "fp32" else comp
+    if kernel != "f32_tc":
+        main = hbm if t_hbm >= t_c or comp_bound == "fp32" else comp
     bound = "hbm" if main is hbm else comp_bound
     roof = {"bound": bound, "kernel": kname, "achieved": main["achieved"],
             "peak": main["peak"], "unit": main["unit"], "frac": main["frac"],
@@ -671,7 +715,14 @@ def rooflines(w, name: str, kernel: str, att_s: float, pro_s: float | None):
             "floor_us": {"hbm": 1e6 * t_hbm, comp_key: 1e6 * t_c},
             "launch_us": 1e6 * att_s}
     pro = None
-    if pro_s is not None:
+    if pro_s is not None and pro_qk:
+        pro_bytes = 2 * (w.q.nbytes + w.k.nbytes) + w.q_norm_weight.nbytes + w.k_norm_weight.nbytes
+        pro = {"bound": "hbm", "kernel": "qk_norm_rope_kernel (every q and k row)",
+               "achieved": pro_bytes / pro_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+               "frac": pro_bytes / pro_s / 1e9 / peaks["hbm_gbs"],
+               "algorithmic_bytes_per_launch": pro_bytes,
+               "traffic": traffic.get("qk_norm_rope_kernel"), "launch_us": 1e6 * pro_s}
+    elif pro_s is not None:
         pro_bytes = 2 * kv_valid_bytes + w.k_norm_weight.nbytes
         pro = {"bound": "hbm", "kernel": "norm_rope_rows_bf16_kernel (k rows)",
                "achieved": pro_bytes / pro_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",

@@ -5,27 +5,31 @@
 // p of a sequence of length n attends to [0, causal ? min(p + 1, n) : n); padded query
 // rows included).
 //
-// Scores on the tensor cores, the rest on the FP32 pipe.  One CTA (4 warps) per (128
+// Scores on the tensor cores, the rest on the FP32 pipe.  One CTA (8 warps) per (128
 // query rows, head, sequence); per tile of 64 keys:
-//   - each warp stages 32 rows a row at a time (lane l: floats 4l..4l+3, so every load
+//   - each warp stages 16 rows a row at a time (lane l: floats 4l..4l+3, so every load
 //     is one coalesced 512-byte row): the CTA's query rows once (scaled by
-//     scale * log2(e)), then per tile warps 0-1 the key rows and warps 2-3 the value rows.
+//     scale * log2(e)), then per tile warps 0-3 the key rows and warps 4-7 the value rows.
 //     Query and key rows are split into TF32 pairs (hi = value rounded to TF32, lo =
 //     value - hi) and stored in the 128-byte-swizzled K-major layout, one 32-float column
-//     block per 128-byte row; value rows are stored as they are;
+//     block per 128-byte row; value rows are stored whole, the odd 32-float quarters with
+//     their 16-byte chunks permuted (chunk i at i ^ 4) so that the two quarters a warp
+//     reads at once fall on different banks;
 //   - one thread issues the scores with tcgen05.mma kind::tf32 (M=128, N=64, K=8) into
 //     three accumulators of 64 tensor-memory columns: Qhi.Khi over columns 0-63 of the
 //     head dimension, Qhi.Khi over columns 64-127, and the corrections Qhi.Klo + Qlo.Khi
 //     (2^-11 of the scores' size), so that no main product takes more than 8 updates (the
 //     tensor core's fp32 accumulation loses bits on long chains) -- about 22 significant
 //     bits per operand;
-//   - thread t (lane t = query row t) adds its row's three partial scores 16 keys at a
-//     time, takes masked chunk maxima and forms exp2(s - m); threads 2i and 2i+1
-//     exchange these and each accumulates both rows' p * v for its half of the head dimension (64 columns) with
-//     packed f32x2 FMAs, every value row read as a shared-memory broadcast feeding two
-//     rows; the softmax is online across tiles with a lazily updated reference maximum
-//     (rescaled only when a chunk maximum exceeds it by more than 8), so every probability
-//     stays at most 2^8.
+//   - warps w and w + 4 both take query rows 32 (w % 4) .. + 31 (tensor-memory lanes of
+//     warp w % 4), each thread one row: it adds the row's three partial scores 16 keys at
+//     a time, takes masked chunk maxima and forms exp2(s - m); threads 2i and 2i+1
+//     exchange these and each accumulates both rows' p * v for one quarter of the head
+//     dimension (32 columns: warps 0-3 the first half, warps 4-7 the second) with packed
+//     f32x2 FMAs, every value row read as a shared-memory broadcast feeding two rows; the
+//     softmax is online across tiles with a lazily updated reference maximum (rescaled
+//     only when a chunk maximum exceeds it by more than 8), so every probability stays at
+//     most 2^8.
 // Key and value rows at or past a sequence's end are never read (zeros are staged).  The
 // single wait (scores ready) is bounded; a wait that gives up records
 // TX_ETIMEOUT | site << 8 and the CTA returns after its MMAs drained.
@@ -41,7 +45,8 @@ namespace f32tc {
 
 using namespace ptx;
 
-constexpr int kRows = 128;  // query rows per CTA = threads = tensor-memory lanes
+constexpr int kRows = 128;  // query rows per CTA = tensor-memory lanes
+constexpr int kThreads = 256;  // two threads per query row (each half of the head dimension)
 constexpr int kKeys = 64;   // keys per tile (N of the score MMA)
 constexpr int kD = 128;
 constexpr uint32_t kQBlock = kRows * 128;  // one 32-column block of Q: 128 rows x 128 B
@@ -61,18 +66,18 @@ constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kKe
 constexpr int kSiteScores = 1;
 
 
-// Rows r0..r0+31 of a tile into shared memory, one warp, a row at a time: row r is read
+// Rows r0..r0+15 of a tile into shared memory, one warp, a row at a time: row r is read
 // from src + r * stride (lane l: floats 4l..4l+3); rows at or past `nvalid` are zeros.
 // kSplit: scaled by `scale`, split into TF32 pairs and stored swizzled (column block
 // b = l / 8 of row r at hi/lo + b * blk + r * 128, 16-byte chunk j = l % 8 at chunk
-// j ^ (r % 8)); otherwise stored plain at hi + r * 512 + 16 l.
+// j ^ (r % 8)); otherwise stored whole at hi + r * 512, chunk l at l ^ 4 when l / 8 is odd.
 template <bool kSplit>
 __device__ __forceinline__ void stage_rows(const float *src, uint64_t stride, uint32_t r0,
                                            uint32_t nvalid, float scale, uint32_t hi,
                                            uint32_t lo, uint32_t blk, uint32_t lane) {
   const uint32_t b = lane >> 3, j = lane & 7;
 #pragma unroll 1
-  for (uint32_t i0 = 0; i0 < 32; i0 += 8) {
+  for (uint32_t i0 = 0; i0 < 16; i0 += 8) {
     float4 x[8];
 #pragma unroll
     for (uint32_t i = 0; i < 8; ++i) {
@@ -94,14 +99,14 @@ __device__ __forceinline__ void stage_rows(const float *src, uint64_t stride, ui
         st_shared_v4(lo + off, __float_as_uint(t.x - h0), __float_as_uint(t.y - h1),
                      __float_as_uint(t.z - h2), __float_as_uint(t.w - h3));
       } else {
-        st_shared_v4(hi + r * (kD * 4) + lane * 16, __float_as_uint(x[i].x),
+        st_shared_v4(hi + r * (kD * 4) + ((lane ^ ((lane >> 1) & 4)) << 4), __float_as_uint(x[i].x),
                      __float_as_uint(x[i].y), __float_as_uint(x[i].z), __float_as_uint(x[i].w));
       }
     }
   }
 }
 
-__global__ void __launch_bounds__(kRows, 1) attn_f32_tc_kernel(AttnProblem p, int *status) {
+__global__ void __launch_bounds__(kThreads, 1) attn_f32_tc_kernel(AttnProblem p, int *status) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned window for the swizzled blocks.
   const uint32_t raw = smem_addr(smem_raw);
@@ -112,6 +117,8 @@ __global__ void __launch_bounds__(kRows, 1) attn_f32_tc_kernel(AttnProblem p, in
   const float *vs = reinterpret_cast<const float *>(smem + kOffV);
 
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, h = tid & 1;
+  // Query row of this thread within the CTA (tensor-memory lane) and its column quarter.
+  const uint32_t quad = warp & 3, row = quad * 32 + lane, quarter = (warp >> 2) * 2 + h;
   const uint32_t qblock = blockIdx.x, head = blockIdx.y, seqi = blockIdx.z;
   const uint32_t kvhead = head / (p.heads / p.kv_heads);
   uint32_t len, rows;
@@ -128,7 +135,7 @@ __global__ void __launch_bounds__(kRows, 1) attn_f32_tc_kernel(AttnProblem p, in
   }
   const uint32_t q0 = qblock * kRows;
   if (q0 >= rows) return;  // uniform over the CTA
-  const uint32_t pos = q0 + tid;
+  const uint32_t pos = q0 + row;
   const uint32_t end = pos < rows ? (p.causal ? min(pos + 1, len) : len) : 0u;
   const uint32_t last = min(q0 + kRows, rows) - 1;
   const uint32_t kend = p.causal ? min(last + 1, len) : len;
@@ -149,33 +156,33 @@ __global__ void __launch_bounds__(kRows, 1) attn_f32_tc_kernel(AttnProblem p, in
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   // The CTA's query rows, pre-scaled into log2 units, as TF32 pairs.
-  stage_rows<true>(q + ((base + q0) * p.heads + head) * kD, (uint64_t)p.heads * kD, warp * 32,
+  stage_rows<true>(q + ((base + q0) * p.heads + head) * kD, (uint64_t)p.heads * kD, warp * 16,
                    rows - q0, p.scale * 1.4426950408889634f, sbase + kOffQ, sbase + kOffQlo,
                    kQBlock, lane);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem + ((warp * 32u) << 16);
+  const uint32_t tS = tmem + ((quad * 32u) << 16);
 
   // Threads 2i and 2i+1 (rows 2i and 2i+1) share the output accumulators of both rows,
-  // each for one half of the head dimension (h); each keeps its own row's softmax state.
-  uint64_t acc_e[32], acc_o[32];  // rows 2i and 2i+1, columns 64h..64h+63, packed pairs
+  // each for one quarter of the head dimension; each keeps its own row's softmax state.
+  uint64_t acc_e[16], acc_o[16];  // rows 2i and 2i+1, columns 32q..32q+31, packed pairs
 #pragma unroll
-  for (int i = 0; i < 32; ++i) acc_e[i] = acc_o[i] = f2(0.f, 0.f);
+  for (int i = 0; i < 16; ++i) acc_e[i] = acc_o[i] = f2(0.f, 0.f);
   float m = -INFINITY, l = 0.f;
   bool ok = true;
   uint32_t phase = 0;
   for (uint32_t c0 = 0; c0 < kend; c0 += kKeys, phase ^= 1) {
-    // Key rows (warps 0-1, split) and value rows (warps 2-3) of the tile; rows past the end
+    // Key rows (warps 0-3, split) and value rows (warps 4-7) of the tile; rows past the end
     // are zeros.
     {
-      const float *src = (warp < 2 ? k : v) + ((base + c0) * p.kv_heads + kvhead) * kD;
-      if (warp < 2)
-        stage_rows<true>(src, kv_stride, warp * 32, kend - c0, 1.0f, sbase + kOffK,
+      const float *src = (warp < 4 ? k : v) + ((base + c0) * p.kv_heads + kvhead) * kD;
+      if (warp < 4)
+        stage_rows<true>(src, kv_stride, warp * 16, kend - c0, 1.0f, sbase + kOffK,
                          sbase + kOffKlo, kKBlock, lane);
       else
-        stage_rows<false>(src, kv_stride, (warp - 2) * 32, kend - c0, 1.0f, sbase + kOffV, 0u,
+        stage_rows<false>(src, kv_stride, (warp - 4) * 16, kend - c0, 1.0f, sbase + kOffV, 0u,
                           0u, lane);
     }
     fence_proxy_async();  // generic stores seen by the tensor core
@@ -252,12 +259,15 @@ __global__ void __launch_bounds__(kRows, 1) attn_f32_tc_kernel(AttnProblem p, in
         const float ce = h ? cr_pair : cr, co = h ? cr : cr_pair;
         const uint64_t ce2 = f2(ce, ce), co2 = f2(co, co);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 16; ++i) {
           acc_e[i] = mul2(acc_e[i], ce2);
           acc_o[i] = mul2(acc_o[i], co2);
         }
       }
-      const float *vc = vs + c * 16 * kD + 64 * h;
+      // This thread's quarter of the value rows: chunk i sits at chunk i ^ 4h, i.e. at
+      // va_lo + 4i for i < 4 and at va_hi + 4i for i >= 4.
+      const float *vq = vs + c * 16 * kD + 32 * quarter;
+      const float *va_lo = vq + 16 * h, *va_hi = vq - 16 * h;
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
         const float pj = c * 16 + t < valid ? ex2(s[t] - m) : 0.f;
@@ -265,10 +275,9 @@ __global__ void __launch_bounds__(kRows, 1) attn_f32_tc_kernel(AttnProblem p, in
         const float pp = __shfl_xor_sync(0xffffffffu, pj, 1);
         const float pe = h ? pp : pj, po = h ? pj : pp;
         const uint64_t pe2 = f2(pe, pe), po2 = f2(po, po);
-        const float4 *vr = reinterpret_cast<const float4 *>(vc + t * kD);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float4 vv = vr[i];
+        for (int i = 0; i < 8; ++i) {
+          const float4 vv = *reinterpret_cast<const float4 *>((i < 4 ? va_lo : va_hi) + t * kD + 4 * i);
           const uint64_t va = f2(vv.x, vv.y), vb = f2(vv.z, vv.w);
           acc_e[2 * i] = fma2(pe2, va, acc_e[2 * i]);
           acc_e[2 * i + 1] = fma2(pe2, vb, acc_e[2 * i + 1]);
@@ -282,21 +291,21 @@ __global__ void __launch_bounds__(kRows, 1) attn_f32_tc_kernel(AttnProblem p, in
     __syncthreads();
   }
   {
-    // This thread's half of rows 2i and 2i+1 (zero valid keys: 0/0, as the reference's
+    // This thread's quarter of rows 2i and 2i+1 (zero valid keys: 0/0, as the reference's
     // sums give).
     const float l_pair = __shfl_xor_sync(0xffffffffu, l, 1);
     const float inv_e = 1.0f / (h ? l_pair : l), inv_o = 1.0f / (h ? l : l_pair);
-    const uint32_t pos_e = q0 + (tid & ~1u);
+    const uint32_t pos_e = q0 + (row & ~1u);
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       const uint32_t prow = pos_e + r;
       if (!ok || prow >= rows) continue;
-      const uint64_t(&a)[32] = r ? acc_o : acc_e;
+      const uint64_t(&a)[16] = r ? acc_o : acc_e;
       const float inv = r ? inv_o : inv_e;
       float4 *op =
-          reinterpret_cast<float4 *>(out + ((base + prow) * p.heads + head) * kD + 64 * h);
+          reinterpret_cast<float4 *>(out + ((base + prow) * p.heads + head) * kD + 32 * quarter);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < 8; ++i) {
         const float2 x0 = f2_unpack(a[2 * i]), x1 = f2_unpack(a[2 * i + 1]);
         op[i] = make_float4(x0.x * inv, x0.y * inv, x1.x * inv, x1.y * inv);
       }
@@ -329,7 +338,7 @@ cudaError_t launch_attention_f32_tc(const AttnProblem &p, int *status, cudaStrea
                                        (int)f32tc::kSmemBytes);
   if (e != cudaSuccess) return e;
   const dim3 grid(qblocks, p.heads, p.batch);
-  f32tc::attn_f32_tc_kernel<<<grid, f32tc::kRows, f32tc::kSmemBytes, stream>>>(p, status);
+  f32tc::attn_f32_tc_kernel<<<grid, f32tc::kThreads, f32tc::kSmemBytes, stream>>>(p, status);
   return cudaGetLastError();
 }
 

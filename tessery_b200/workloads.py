@@ -114,22 +114,24 @@ def bge(batch: int = 4, seq: int = 128, seed: int = 1, min_len: int = 16) -> Wor
 
 
 def qwen_padded(batch: int = 32, seq: int = 512, seed: int = 2, min_len: int = 32,
-                lengths: NDArray | None = None) -> Workload:
+                lengths: NDArray | None = None, dtype: str = "bf16") -> Workload:
     """Qwen3-0.6B attention layer: 16q/8kv heads x 128, causal, right-padded lengths
-    ~ U[min_len, seq], Q/K/V ~ N(0,1) in bf16, q/k RMSNorm weights 1+N(0,0.02) (bf16),
-    eps 1e-6, RoPE theta 1e6."""
+    ~ U[min_len, seq], Q/K/V ~ N(0,1) in bf16 (dtype "f32": the same draws kept in
+    float32, the reference adapter's float buffers), q/k RMSNorm weights 1+N(0,0.02)
+    (bf16), eps 1e-6, RoPE theta 1e6."""
     rng = np.random.default_rng(seed)
     heads, kv, dim = 16, 8, 128
     if lengths is None:
         lengths = rng.integers(min_len, seq + 1, size=batch)
     lengths = np.asarray(lengths, dtype=np.uint32)
-    q = to_bf16_bits(_normal(rng, (batch, seq, heads, dim)))
-    k = to_bf16_bits(_normal(rng, (batch, seq, kv, dim)))
-    v = to_bf16_bits(_normal(rng, (batch, seq, kv, dim)))
+    cast = to_bf16_bits if dtype == "bf16" else (lambda a: a)
+    q = cast(_normal(rng, (batch, seq, heads, dim)))
+    k = cast(_normal(rng, (batch, seq, kv, dim)))
+    v = cast(_normal(rng, (batch, seq, kv, dim)))
     q_w, k_w = _qwen_weights(rng, dim)
-    return Workload("qwen_d128_padded", "padded", q, k, v, heads, kv, dim, True, dim**-0.5,
-                    "bf16", seq, lengths=lengths, q_norm_weight=q_w, k_norm_weight=k_w,
-                    seed=seed)
+    name = "qwen_d128_padded" if dtype == "bf16" else "qwen_d128_padded_f32"
+    return Workload(name, "padded", q, k, v, heads, kv, dim, True, dim**-0.5, dtype, seq,
+                    lengths=lengths, q_norm_weight=q_w, k_norm_weight=k_w, seed=seed)
 
 
 def varlen_lengths(nseq: int, seed: int, median: float = 96.0, sigma: float = 0.8,
@@ -189,8 +191,8 @@ def benchmark_workload(name: str, rank: int = 0, world: int = 1,
     """The seeded input of one benchmark workload as rank `rank` of `world` sees it.
 
     qwen_padded: 32 sequences per rank, lengths ~ U[32, 512] from seed 2 over all ranks,
-    assigned longest first; qwen_varlen: the 256 log-normal sequences of seed 3, split
-    across the ranks; bge / bge_scaled: batch 4 / `scaled_batch`, seed 1; tails_qwen /
+    assigned longest first; qwen_f32: the same batch with float32 inputs; qwen_varlen:
+    the 256 log-normal sequences of seed 3, split across the ranks; bge / bge_scaled: batch 4 / `scaled_batch`, seed 1; tails_qwen /
     tails_bge: 32 sequences of U[2, 32], seed 4.  Ranks other than 0 draw their tensors
     from seed + 1000 * rank.
     """
@@ -201,6 +203,11 @@ def benchmark_workload(name: str, rank: int = 0, world: int = 1,
         owned = shard_sequences(lengths, world, causal=True)[rank]
         return qwen_padded(batch=len(owned), seq=512, seed=2 + 1000 * rank,
                            lengths=lengths[owned])
+    if name == "qwen_f32":
+        lengths = np.random.default_rng(2).integers(32, 513, size=32 * world)
+        owned = shard_sequences(lengths, world, causal=True)[rank]
+        return qwen_padded(batch=len(owned), seq=512, seed=2 + 1000 * rank,
+                           lengths=lengths[owned], dtype="f32")
     if name == "qwen_varlen":
         lengths = varlen_lengths(256, 3)
         owned = shard_sequences(lengths, world, causal=True)[rank]

@@ -2,7 +2,7 @@
 
 The inputs are exactly the ones bench.py times (tessery_b200.workloads.benchmark_workload,
 rank 0 of 1): the padded Qwen batch (32 x 512, seed 2), the 256 packed log-normal
-sequences (seed 3), the BGE batch (4 x 128, seed 1) and both short-tail batches (seed 4).
+sequences (seed 3), the same padded batch in float32, the BGE batch (4 x 128, seed 1) and both short-tail batches (seed 4).
 Each test prints the maximum and the 99.9th percentile of the absolute error, so the
 margin to the gate is on record.
 
@@ -66,6 +66,16 @@ def test_qwen_benchmark_config_every_sequence(runtime, name, route):
     assert runtime.last_kernel() == route
     assert np.isfinite(got).all()
     assert report(name, got, oracle_of(w)) <= BF16_GATE
+
+
+def test_qwen_f32_config_every_sequence(runtime):
+    """The padded Qwen batch with float32 q/k/v (the reference adapter's float buffers):
+    the fp32 prologue and the fp32 head_dim-128 kernel, every row against float64."""
+    w = workloads.benchmark_workload("qwen_f32")
+    got = run(runtime, w)
+    assert runtime.last_kernel() == "f32_tc"
+    assert np.isfinite(got).all()
+    assert report("qwen_f32", got, oracle_of(w)) <= F32_GATE
 
 
 @pytest.mark.parametrize("name", ["bge", "tails_bge"])
