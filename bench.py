@@ -393,28 +393,20 @@ def run_ours(args):
 
     q, k, v = to_dev(w.q), to_dev(w.k), to_dev(w.v)
     prologue = w.q_norm_weight is not None
-    # Sequences of at most 32 tokens (head_dim 128, bf16, up to 4 query heads per kv head)
-    # take the short-sequence kernel, which applies the q and k prologue itself: the step
-    # is then one attention call with both weights and no separate k pass.
-    fused = (prologue and D == 128 and in_code == TX_BF16 and w.seq <= 32 and H // KV <= 4)
     # fp32 inputs: the library normalises and rotates q and k in one launch of the general
     # prologue (into scratch), then runs the attention kernel on the results.
     f32_prologue = prologue and in_code == TX_F32
-    qn = torch.empty_like(q) if f32_prologue else None
     if prologue:
         qw, kw = to_dev(w.q_norm_weight), to_dev(w.k_norm_weight)
-        kn = torch.empty_like(k)
     out = torch.empty(w.q.shape, dtype=torch.float32, device=dev)
     if w.layout == "padded":
         lengths = to_dev(w.lengths.astype(np.uint32).view(np.int32))
         lengths_host = w.lengths.astype(np.uint32)
         B, L = w.q.shape[:2]
-        tokens_in_layout = B * L
     else:
         cu = to_dev(w.cu_seqlens.astype(np.int32))
         cu_host = w.cu_seqlens.astype(np.int32)
         nseq, total = w.batch, int(cu_host[-1])
-        tokens_in_layout = total
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     # A dedicated stream: the legacy default stream has handle 0, which the library reads
     # as "use the context's own stream".
@@ -422,21 +414,19 @@ def run_ours(args):
     torch.cuda.set_stream(stream)
     sptr = stream.cuda_stream
     assert sptr != 0
-    def attend(k_in, with_k_weight, q_in=None):
-        extra = dict(eps=w.eps, theta=w.theta) if prologue else {}
-        if prologue and q_in is None:
-            extra["q_norm_weight"] = qw.data_ptr()
-        if with_k_weight:
-            extra["k_norm_weight"] = kw.data_ptr()
-        q_in = q if q_in is None else q_in
+    def attend():
+        extra = {}
+        if prologue:
+            extra = dict(eps=w.eps, theta=w.theta, q_norm_weight=qw.data_ptr(),
+                         k_norm_weight=kw.data_ptr())
         if w.layout == "padded":
-            rt.attention_padded_device(q_in.data_ptr(), k_in.data_ptr(), v.data_ptr(),
+            rt.attention_padded_device(q.data_ptr(), k.data_ptr(), v.data_ptr(),
                                        lengths.data_ptr(), out.data_ptr(), batch=B, seq=L,
                                        heads=H, kv_heads=KV, dim=D, in_dtype=in_code,
                                        out_dtype=TX_F32, causal=w.causal, scale=w.scale,
                                        lengths_host=lengths_host, stream=sptr, **extra)
         else:
-            rt.attention_varlen_device(q_in.data_ptr(), k_in.data_ptr(), v.data_ptr(),
+            rt.attention_varlen_device(q.data_ptr(), k.data_ptr(), v.data_ptr(),
                                        cu.data_ptr(), out.data_ptr(), nseq=nseq, total=total,
                                        max_len=w.seq, heads=H, kv_heads=KV, dim=D,
                                        in_dtype=in_code, out_dtype=TX_F32, causal=w.causal,
@@ -446,44 +436,10 @@ def run_ours(args):
     def step():
         # One library call: with both norm weights the library normalises and rotates the
         # valid k rows (one launch) and runs the attention kernel, which applies the q
-        # prologue to each Q tile in shared memory, as a programmatic dependent of it.
-        attend(k, prologue)
-
-    def split_step(mid):
-        # The same two kernels as separate calls with an event between them (for the
-        # per-kernel rooflines): the k prologue into kn, then the attention on kn (fp32:
-        # the q and k prologue into qn and kn, every row as the library does, then the
-        # attention on them).
-        if f32_prologue:
-            layout = (dict(seq=L) if w.layout == "padded" else
-                      dict(seq=w.seq, cu_seqlens=cu.data_ptr(), nseq=nseq))
-            rt.qk_norm_rope_device(q.data_ptr(), k.data_ptr(), qn.data_ptr(), kn.data_ptr(),
-                                   tokens=tokens_in_layout, heads=H, kv_heads=KV, dim=D,
-                                   q_norm_weight=qw.data_ptr(), k_norm_weight=kw.data_ptr(),
-                                   in_dtype=in_code, out_dtype=in_code, eps=w.eps,
-                                   theta=w.theta, stream=sptr, **layout)
-            mid.record(stream)
-            attend(kn, False, q_in=qn)
-        elif prologue and not fused:
-            if w.layout == "padded":
-                rt.qk_norm_rope_device(None, k.data_ptr(), None, kn.data_ptr(),
-                                       tokens=tokens_in_layout, seq=L, heads=H, kv_heads=KV,
-                                       dim=D, q_norm_weight=None, k_norm_weight=kw.data_ptr(),
-                                       lengths=lengths.data_ptr(), in_dtype=in_code,
-                                       out_dtype=in_code, eps=w.eps, theta=w.theta,
-                                       stream=sptr)
-            else:
-                rt.qk_norm_rope_device(None, k.data_ptr(), None, kn.data_ptr(),
-                                       tokens=tokens_in_layout, seq=w.seq, heads=H,
-                                       kv_heads=KV, dim=D, q_norm_weight=None,
-                                       k_norm_weight=kw.data_ptr(), cu_seqlens=cu.data_ptr(),
-                                       nseq=nseq, in_dtype=in_code, out_dtype=in_code,
-                                       eps=w.eps, theta=w.theta, stream=sptr)
-            mid.record(stream)
-            attend(kn, False)
-        else:
-            mid.record(stream)
-            step()
+        # prologue to each Q tile in shared memory, as a programmatic dependent of it
+        # (sequences of at most 32 tokens: one launch of the short-sequence kernel with
+        # the q and k prologue inside; fp32: one q/k prologue launch, then the attention).
+        attend()
 
     for _ in range(max(args.warmup, 3)):
         flush.zero_()
@@ -524,20 +480,22 @@ def run_ours(args):
     clocks = sampler.stop()
     rt.sync(sptr)  # device status word (bounded-wait timeouts) must be clean
 
-    # Split of a step between the two kernels, from separate untimed steps with an event
-    # between the launches (used for the per-kernel rooflines, not for `value`).
-    s_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    s_mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    s_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    # Per-kernel device times of the same call, from separate untimed steps with the
+    # library's kernel timing on (an event pair around each launch, which also keeps the
+    # attention kernel from starting before the prologue ends): the per-kernel rooflines,
+    # not `value`.
+    rt.kernel_timing(True)
+    pro_ms, att_ms = [], []
     for i in range(args.steps):
         flush.zero_()
-        s_starts[i].record(stream)
-        split_step(s_mids[i])
-        s_ends[i].record(stream)
+        step()
+        times = rt.kernel_times()
+        att_ms.append(times[-1] * 1e3)
+        if len(times) > 1:
+            pro_ms.append(times[0] * 1e3)
+    rt.kernel_timing(False)
     torch.cuda.synchronize()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends, strict=True)]
-    pro_ms = [s.elapsed_time(m) for s, m in zip(s_starts, s_mids, strict=True)]
-    att_ms = [m.elapsed_time(e) for m, e in zip(s_mids, s_ends, strict=True)]
     total_s = sum(step_ms) * 1e-3
     tokens = w.valid_tokens() * args.steps
     flops = w.useful_flops()
@@ -611,8 +569,8 @@ def run_ours(args):
     d2h = result.nbytes
 
     roof, prologue_roof = rooflines(w, name, kernel, statistics.mean(att_ms) * 1e-3,
-                                    statistics.mean(pro_ms) * 1e-3 if prologue and not fused
-                                    else None, pro_qk=f32_prologue)
+                                    statistics.mean(pro_ms) * 1e-3 if pro_ms else None,
+                                    pro_qk=f32_prologue)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -644,6 +602,8 @@ def run_ours(args):
         if prologue_roof:
             line["prologue_roofline"] = prologue_roof
             line["prologue_ms"] = statistics.mean(pro_ms)
+        line["kernel_timing"] = ("per-kernel times from separate steps of the same call with "
+                                 "the library's kernel timing on (tx_kernel_times)")
         print(json.dumps(line), flush=True)
     rt.close()
     if dist:

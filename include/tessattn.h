@@ -145,6 +145,17 @@ double tx_gpu_seconds(void *ctx);
 int tx_profile_enable(void *ctx, int enabled);
 int tx_profile_read(void *ctx, double *seconds, uint32_t count);
 
+/* Per-kernel device times of the typed attention entry points (no reference
+ * counterpart; the typed calls have no command to profile).  While enabled, every
+ * kernel launch of a tx_attention_* call is bracketed by a CUDA event pair on the
+ * call's stream (which also keeps the attention kernel from overlapping the prologue
+ * launch before it); tx_kernel_times waits for the last call's launches (the last chunk
+ * of a host-buffer call) and writes their durations in launch order: the q/k prologue
+ * when the call ran one, then the attention kernel.  *count = number of launches;
+ * TX_EINVAL when cap is smaller. */
+int tx_kernel_timing(void *ctx, int enabled);
+int tx_kernel_times(void *ctx, double *seconds, uint32_t cap, uint32_t *count);
+
 /* ---- typed attention entry points -------------------------------------------------
 
  * These replace the Params-block route for callers that hold device pointers.  They

@@ -12,13 +12,14 @@
 //
 // Warp roles (576 threads, one CTA per SM), specialised so that each serial per-unit
 // step runs beside the others instead of in front of them:
-//   warps 0-3   softmax of head slot 0 (thread t = query row t)
-//   warps 4-7   softmax of head slot 1
-//   warps 8-11  per work unit k, for head slot 0: the q prologue of unit k+1 (RMSNorm +
-//               RoPE of its Q tile in shared memory, as soon as it lands), then the
-//               epilogue of unit k (O from tensor memory, scaled, staged swizzled in a
-//               per-warp 32-row chunk, sent by TMA bulk-tensor stores)
-//   warps 12-15 the same for head slot 1
+//   warps 0-3   softmax of head slot 0 (thread t = query row t), and after a unit's last
+//               P.V its epilogue (O from tensor memory, scaled by the row sum the thread
+//               holds, staged swizzled in a per-warp 32-row chunk, sent by TMA
+//               bulk-tensor stores)
+//   warps 4-7   the same for head slot 1
+//   warps 8-15  the q prologue of the next unit (RMSNorm + RoPE of its Q tiles in shared
+//               memory, as soon as they land; warpgroup h takes rows 64h..64h+63 of both
+//               heads, two lanes per row)
 //   warp 16     TMA producer: Q tiles of the unit two ahead (into the buffer whose last
 //               Q.K^T has run), K and V tiles of 128 keys through a 2-slot ring, and L2
 //               prefetches of the next units' tiles
@@ -29,7 +30,7 @@
 // the tensor-memory A operand, so P needs no shared memory.  Shared memory: two unit
 // buffers of Q tiles (2 x 128x128 bf16 each, so the next unit's Q is loaded and
 // transformed while this one runs), 2 ring slots (128x128 bf16: K or V), and one output
-// staging chunk per epilogue warp (32 rows x 128 bytes), all in the 128-byte-swizzled
+// staging chunk per softmax warp (32 rows x 128 bytes), all in the 128-byte-swizzled
 // layout that TMA and UMMA use (a 128-byte row holds 64 bf16 or 32 fp32).
 //
 // Key tile j of a unit (every MMA is M=128 x N=128 x K=16, issued 8 at a time): the
@@ -99,8 +100,7 @@ enum : uint32_t {
   kBarSFull = kBarKVEmpty + kStages,  // + h: S_h of the next key tile (commit)
   kBarPFull = kBarSFull + 2,          // + h: P_h written over S_h (128 arrivals)
   kBarPVDone = kBarPFull + 2,         // + h: P_h.V ran (commit)
-  kBarLReady = kBarPVDone + 2,        // + 2h + unit parity: row sums published (128 arrivals)
-  kBarOFree = kBarLReady + 4,         // + h: O_h read out (128 arrivals)
+  kBarOFree = kBarPVDone + 2,         // + h: O_h read out (128 arrivals)
   kBarDrain = kBarOFree + 2,
   kNumBars = kBarDrain + 1
 };
@@ -108,16 +108,15 @@ constexpr uint32_t kOffTmemSlot = kNumBars * 8;   // uint32 TMEM base address
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;  // int abort flag
 constexpr uint32_t kOffQw = 512;                  // bf16 q-norm weight [128]
 constexpr uint32_t kOffInvFreq = 768;             // float inverse frequencies [64]
-constexpr uint32_t kOffRowSum = 1024;             // float [head slot][unit parity][128]
 static_assert(kOffAbort + 4 <= kOffQw, "misc area overflow");
-static_assert(kOffRowSum + 2 * 2 * 128 * 4 <= kMiscBytes, "misc area overflow");
+static_assert(kOffInvFreq + 64 * 4 <= kMiscBytes, "misc area overflow");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 static_assert(kOffKV % 1024 == 0 && kOffStage % 1024 == 0, "swizzled tiles need 1024 B alignment");
 
 // Wait sites, reported in the status word for diagnosis.
 enum : int {
   kSiteQEmpty = 1, kSiteKVEmpty = 2, kSiteQReady = 3, kSiteKVFull = 4, kSitePFull = 5,
-  kSiteSFull = 6, kSitePVDone = 7, kSiteQFull = 8, kSiteLReady = 9, kSiteOFree = 10
+  kSiteSFull = 6, kSitePVDone = 7, kSiteQFull = 8, kSiteOFree = 10
 };
 
 // ---- unit encoding --------------------------------------------------------------------
@@ -151,6 +150,7 @@ struct Params {
   float scale_log2;
   int *status;
   const uint16_t *q_norm_w;  // fused q prologue when non-NULL
+  const uint16_t *k_norm_w;  // weights of the k RMSNorm applied to k (NULL: none known)
   float eps;
   long long wait_cycles;     // limit of every bounded wait, in SM clock cycles
   float inv_freq[64];        // RoPE theta^(-2c/128), c < 64
@@ -401,7 +401,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int *abort_flag = (volatile int *)(misc + kOffAbort);
   uint16_t *qw_s = (uint16_t *)(misc + kOffQw);
   float *invf_s = (float *)(misc + kOffInvFreq);
-  float *rowsum_s = (float *)(misc + kOffRowSum);
   auto bar = [&](uint32_t i) { return bars + 8u * i; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -416,7 +415,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(kBarPFull + h), 128);
       mbar_init(bar(kBarPVDone + h), 1);
       mbar_init(bar(kBarOFree + h), 128);
-      for (int s = 0; s < 2; ++s) mbar_init(bar(kBarLReady + 2 * h + s), 128);
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(kBarKVFull + s), 1);
@@ -660,8 +658,126 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = (wq * 32u) << 16;
     const uint32_t tS = tmem + lane_base + h * 256;
     const uint32_t tO = tS + 128;
-    uint32_t tiles = 0, units_seen = 0;  // key tiles and work units processed
+    uint32_t tiles = 0;   // key tiles processed
+    uint32_t chunks = 0;  // staging chunks this warp has sent
     bool ok = true;
+    const uint32_t srow = (uint32_t)lane * 128, sw = (uint32_t)lane & 7;
+    const uint32_t stage0 = sbase + kOffStage + (uint32_t)warp * kStageSlots * kChunkBytes;
+    // The staging slot for this warp's next chunk, once the store that last read it is done.
+    auto take_slot = [&]() -> uint32_t {
+      if (lane == 0) bulk_wait_read<kStageSlots - 1>();
+      __syncwarp();
+      return stage0 + (chunks++ % kStageSlots) * kChunkBytes;
+    };
+    // Sends this warp's staged 32 rows (chunk at `slot`) to columns [x, ..) of `head`.
+    auto send = [&](uint32_t slot, int x, uint32_t head, uint32_t row0) {
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_3d(&tm_o, slot, x, (int)head, (int)row0);
+        bulk_commit();
+      }
+    };
+    // Epilogue of unit v for head slot h, once its last P.V ran: O read out of tensor
+    // memory 32 columns at a time (after the last read O is released to the next unit),
+    // normalised by the row sum l, stored.  Warps whose 32 rows all lie inside the
+    // sequence stage each 32-row chunk in shared memory and send it with a TMA bulk-tensor
+    // store; a warp at a ragged end stores row by row.
+    auto epilogue = [&](const Unit &v, float l) {
+      const uint32_t qpos = v.q0 + r;
+      const bool store = qpos < v.rows;
+      const uint32_t wrow0 = v.q0 + wq * 32;
+      const bool bulk = wrow0 + 32 <= v.rows;
+      const float inv = 1.0f / l;
+      const uint32_t head = v.head0 + h;
+      const size_t orow = ((size_t)(v.tok0 + qpos) * p.heads + head) * 128;
+      if (!kOutBf16) {
+        // Chunk c + 1 is read out of tensor memory and scaled while the store of chunk c
+        // still reads the staging slot.
+        uint32_t x[32];
+        tmem_ld32(tO, x);
+        tmem_ld_wait();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) x[t] = __float_as_uint(__uint_as_float(x[t]) * inv);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {  // 32 fp32 columns = one 128-byte staging row
+          if (bulk) {
+            const uint32_t slot = take_slot();
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+              st_shared_v4(slot + srow + (((uint32_t)g ^ sw) << 4), x[4 * g], x[4 * g + 1],
+                           x[4 * g + 2], x[4 * g + 3]);
+            send(slot, c * 32, head, v.tok0 + wrow0);
+          } else if (store) {
+            float4 *o = (float4 *)((float *)p.out + orow + c * 32);
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+              o[g] = make_float4(__uint_as_float(x[4 * g]), __uint_as_float(x[4 * g + 1]),
+                                 __uint_as_float(x[4 * g + 2]), __uint_as_float(x[4 * g + 3]));
+          }
+          if (c < 3) {
+            tmem_ld32(tO + (c + 1) * 32, x);
+            tmem_ld_wait();
+            if (c == 2) {  // O read out: released to the next unit's P.V
+              tc_fence_before();
+              mbar_arrive(bar(kBarOFree + h));
+            }
+#pragma unroll
+            for (int t = 0; t < 32; ++t) x[t] = __float_as_uint(__uint_as_float(x[t]) * inv);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {  // 64 bf16 columns = one 128-byte staging row
+          const uint32_t slot = bulk ? take_slot() : 0u;
+#pragma unroll 1
+          for (int half = 0; half < 2; ++half) {  // 32 columns = 4 16-byte units
+            uint32_t x[32], w[16];
+            tmem_ld32(tO + c * 64 + half * 32, x);
+            tmem_ld_wait();
+            if (c == 1 && half == 1) {
+              tc_fence_before();
+              mbar_arrive(bar(kBarOFree + h));
+            }
+#pragma unroll
+            for (int t = 0; t < 16; ++t)
+              w[t] = pack_bf16x2(__uint_as_float(x[2 * t]) * inv,
+                                 __uint_as_float(x[2 * t + 1]) * inv);
+            if (bulk) {
+#pragma unroll
+              for (int g = 0; g < 4; ++g)
+                st_shared_v4(slot + srow + (((uint32_t)(4 * half + g) ^ sw) << 4), w[4 * g],
+                             w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+            } else if (store) {
+              uint4 *o = (uint4 *)((uint16_t *)p.out + orow + c * 64 + half * 32);
+#pragma unroll
+              for (int g = 0; g < 4; ++g)
+                o[g] = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+            }
+          }
+          if (bulk) send(slot, c * 64, head, v.tok0 + wrow0);
+        }
+      }
+    };
+    // With the weights of both RMSNorms known, every score is bounded: an RMSNorm output
+    // over 128 columns has norm <= max|w| sqrt(128) (the rotation keeps it), so
+    // |q.k| scale log2(e) <= 128 max|w_q| max|w_k| scale log2(e), with 2^-6 of slack for
+    // the bf16 roundings.  Up to 64, exp2 of a score with the fixed reference 0 lies in
+    // [2^-64, 2^64]: one pass over each tile, no row maximum, no rescaling.
+    bool single = false;
+    if (p.q_norm_w && p.k_norm_w) {
+      float wq = 0.f, wk = 0.f;
+      for (int i = lane; i < 128; i += 32) {
+        wq = fmaxf(wq, fabsf(__uint_as_float((uint32_t)qw_s[i] << 16)));
+        wk = fmaxf(wk, fabsf(__uint_as_float((uint32_t)p.k_norm_w[i] << 16)));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        wq = fmaxf(wq, __shfl_xor_sync(0xffffffffu, wq, o));
+        wk = fmaxf(wk, __shfl_xor_sync(0xffffffffu, wk, o));
+      }
+      single = 128.0f * wq * wk * p.scale_log2 * 1.0157f <= 64.0f;
+    }
     for (UnitCursor uc(p); ok && h < nh && uc.more();) {
       const Unit u = uc.take(p);
       if (!u.nt) continue;
@@ -683,54 +799,58 @@ __global__ void __launch_bounds__(kThreads, 1)
           continue;
         }
         const int valid = (int)min(max((int)end - (int)(j * kKeys), 0), kKeys);
-        // Pass 1: the tile's row maximum (64 columns in registers at a time).
-        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (single) {
+          m_ref = 0.f;
+        } else {
+          // Pass 1: the tile's row maximum (64 columns in registers at a time).
+          float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          // Keys masked for every row of the warp (causal diagonal, ragged end) are skipped.
-          if (__all_sync(0xffffffffu, half * 64 >= valid)) break;
-          uint32_t xa[32], xb[32];
-          tmem_ld32(tS + half * 64, xa);
-          tmem_ld32(tS + half * 64 + 32, xb);
-          tmem_ld_wait();
-          const float ninf = -INFINITY;
+          for (int half = 0; half < 2; ++half) {
+            // Keys masked for every row of the warp (causal diagonal, ragged end) are skipped.
+            if (__all_sync(0xffffffffu, half * 64 >= valid)) break;
+            uint32_t xa[32], xb[32];
+            tmem_ld32(tS + half * 64, xa);
+            tmem_ld32(tS + half * 64 + 32, xb);
+            tmem_ld_wait();
+            const float ninf = -INFINITY;
 #pragma unroll
-          for (int t = 0; t < 32; t += 2) {  // keys at or past `valid` do not count
-            const int ka = half * 64 + t, kb = ka + 32;
-            mq[t & 2 ? 1 : 0] = fmax3(mq[t & 2 ? 1 : 0],
-                                      ka < valid ? __uint_as_float(xa[t]) : ninf,
-                                      ka + 1 < valid ? __uint_as_float(xa[t + 1]) : ninf);
-            mq[t & 2 ? 3 : 2] = fmax3(mq[t & 2 ? 3 : 2],
-                                      kb < valid ? __uint_as_float(xb[t]) : ninf,
-                                      kb + 1 < valid ? __uint_as_float(xb[t + 1]) : ninf);
+            for (int t = 0; t < 32; t += 2) {  // keys at or past `valid` do not count
+              const int ka = half * 64 + t, kb = ka + 32;
+              mq[t & 2 ? 1 : 0] = fmax3(mq[t & 2 ? 1 : 0],
+                                        ka < valid ? __uint_as_float(xa[t]) : ninf,
+                                        ka + 1 < valid ? __uint_as_float(xa[t + 1]) : ninf);
+              mq[t & 2 ? 3 : 2] = fmax3(mq[t & 2 ? 3 : 2],
+                                        kb < valid ? __uint_as_float(xb[t]) : ninf,
+                                        kb + 1 < valid ? __uint_as_float(xb[t + 1]) : ninf);
+            }
           }
-        }
-        const float mt = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * p.scale_log2;
-        if (j > 0) {
-          // Rescale decision is per row; TMEM access is warp-wide (.sync.aligned), so the
-          // warp rescales when any of its rows needs it (others scale by 1).  S of this
-          // tile was committed after P.V of the previous one, so O_h is complete.
-          float corr = 1.0f;
-          const bool need = mt > m_ref + kRescaleThreshold;
-          if (need) {
-            corr = ex2(m_ref - mt);
-            l *= corr;
+          const float mt = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * p.scale_log2;
+          if (j > 0) {
+            // Rescale decision is per row; TMEM access is warp-wide (.sync.aligned), so the
+            // warp rescales when any of its rows needs it (others scale by 1).  S of this
+            // tile was committed after P.V of the previous one, so O_h is complete.
+            float corr = 1.0f;
+            const bool need = mt > m_ref + kRescaleThreshold;
+            if (need) {
+              corr = ex2(m_ref - mt);
+              l *= corr;
+              m_ref = mt;
+            }
+            if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+              for (int c = 0; c < 8; ++c) {  // 16 columns at a time
+                uint32_t o[16];
+                tmem_ld16(tO + c * 16, o);
+                tmem_ld_wait();
+#pragma unroll
+                for (int t = 0; t < 16; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * corr);
+                tmem_st16(tO + c * 16, o);
+              }
+              tmem_st_wait();
+            }
+          } else {
             m_ref = mt;
           }
-          if (__any_sync(0xffffffffu, need)) {
-#pragma unroll 1
-            for (int c = 0; c < 8; ++c) {  // 16 columns at a time
-              uint32_t o[16];
-              tmem_ld16(tO + c * 16, o);
-              tmem_ld_wait();
-#pragma unroll
-              for (int t = 0; t < 16; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * corr);
-              tmem_st16(tO + c * 16, o);
-            }
-            tmem_st_wait();
-          }
-        } else {
-          m_ref = mt;
         }
         // Pass 2: P = exp2(S*scale*log2e - m) as bf16 pairs over the first 64 columns
         // (keys 32c..32c+31 in columns 16c..16c+15; each chunk is read before the chunk
@@ -754,26 +874,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(bar(kBarPFull + h));
       }
       if (!ok) break;
-      // Row sum of the unit for the epilogue warps.
-      rowsum_s[(h * 2 + (units_seen & 1)) * 128 + r] = l;
-      mbar_arrive(bar(kBarLReady + 2 * h + (units_seen & 1)));
-      ++units_seen;
+      // The unit's last P.V ran: O_h out of tensor memory, normalised, stored.
+      ok = __all_sync(0xffffffffu, wait_phase(bar(kBarPVDone + h), (tiles - 1) & 1, abort_flag,
+                                              p.status, kSitePVDone, p.wait_cycles));
+      if (!ok) break;
+      tc_fence_after();
+      epilogue(u, l);
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   } else {
-    // ---------------- q prologue and epilogue --------------------------------------------
+    // ---------------- q prologue ---------------------------------------------------------
     // Warpgroup h transforms rows [64h, 64h + 64) of every head tile of the next unit (two
-    // lanes per row), then writes the epilogue of head slot h (thread = row = TMEM lane).
+    // lanes per row), as soon as its tiles land; the warpgroup of head slot h also writes
+    // the NaN rows of units without valid keys.
     const uint32_t h = (uint32_t)(warp - kEpiWarp0) >> 2;
     const uint32_t wq = (uint32_t)warp & 3;
     const uint32_t r = wq * 32 + lane;
     const uint32_t xrow = 64 * h + (r >> 1), xhalf = r & 1;  // this thread's transform share
-    const uint32_t lane_base = (wq * 32u) << 16;
-    uint32_t lcount = 0;  // work units whose row sums were taken
-    uint32_t tiles = 0;   // key tiles of the work units finished so far
-    uint32_t chunks = 0;  // staging chunks this warp has sent
     bool ok = true;
-    const uint32_t srow = (uint32_t)lane * 128, sw = (uint32_t)lane & 7;
-    const uint32_t stage0 = sbase + kOffStage + (h * 4 + wq) * kStageSlots * kChunkBytes;
     // Wait for fill `phase` of buffer b, apply the q prologue to this thread's share of
     // the unit's tiles, hand them to the issuer (which waits for all 256 threads).
     auto prepare = [&](uint32_t ui, uint32_t b, uint32_t phase) {
@@ -789,115 +908,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mbar_arrive(bar(kBarQReady + b));
     };
-    // The staging slot for this warp's next chunk, once the store that last read it is done.
-    auto take_slot = [&]() -> uint32_t {
-      if (lane == 0) bulk_wait_read<kStageSlots - 1>();
-      __syncwarp();
-      return stage0 + (chunks++ % kStageSlots) * kChunkBytes;
-    };
-    // Sends this warp's staged 32 rows (chunk at `slot`) to columns [x, ..) of `head`.
-    auto send = [&](uint32_t slot, int x, uint32_t head, uint32_t row0) {
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) {
-        tma_store_3d(&tm_o, slot, x, (int)head, (int)row0);
-        bulk_commit();
-      }
-    };
-    // Epilogue of unit v for head slot h: wait for its row sums and last P.V, read O out of
-    // tensor memory 32 columns at a time (after the last read O is released to the next
-    // unit), normalise, store.  Warps whose 32 rows all lie inside the sequence stage
-    // each 32-row chunk in shared memory and send it with a TMA bulk-tensor store; a warp at
-    // a ragged end stores row by row.
-    auto epilogue = [&](const Unit &v) {
-      const uint32_t qpos = v.q0 + r;
-      const bool store = qpos < v.rows;
-      const uint32_t wrow0 = v.q0 + wq * 32;
-      const bool bulk = wrow0 + 32 <= v.rows;
-      const uint32_t last_pv = tiles + v.nt - 1;  // index of the unit's last P.V per head
-      {
-        // Row sums: one barrier per unit parity (the softmax warps of a head cannot run
-        // two units ahead of this epilogue: their next-but-one unit needs O_h freed).
-        ok = __all_sync(0xffffffffu,
-                        wait_phase(bar(kBarLReady + 2 * h + (lcount & 1)), (lcount >> 1) & 1,
-                                   abort_flag, p.status, kSiteLReady, p.wait_cycles));
-        if (!ok) return;
-        const float l = rowsum_s[(h * 2 + (lcount & 1)) * 128 + r];
-        ok = __all_sync(0xffffffffu, wait_phase(bar(kBarPVDone + h), last_pv & 1, abort_flag,
-                                                p.status, kSitePVDone, p.wait_cycles));
-        if (!ok) return;
-        tc_fence_after();
-        const float inv = 1.0f / l;
-        const uint32_t tO = tmem + lane_base + h * 256 + 128;
-        const uint32_t head = v.head0 + h;
-        const size_t orow = ((size_t)(v.tok0 + qpos) * p.heads + head) * 128;
-        if (!kOutBf16) {
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {  // 32 fp32 columns = one 128-byte staging row
-            uint32_t x[32];
-            tmem_ld32(tO + c * 32, x);
-            tmem_ld_wait();
-            if (c == 3) {
-              tc_fence_before();
-              mbar_arrive(bar(kBarOFree + h));
-            }
-#pragma unroll
-            for (int t = 0; t < 32; ++t) x[t] = __float_as_uint(__uint_as_float(x[t]) * inv);
-            if (bulk) {
-              const uint32_t slot = take_slot();
-#pragma unroll
-              for (int g = 0; g < 8; ++g)
-                st_shared_v4(slot + srow + (((uint32_t)g ^ sw) << 4), x[4 * g], x[4 * g + 1],
-                             x[4 * g + 2], x[4 * g + 3]);
-              send(slot, c * 32, head, v.tok0 + wrow0);
-            } else if (store) {
-              float4 *o = (float4 *)((float *)p.out + orow + c * 32);
-#pragma unroll
-              for (int g = 0; g < 8; ++g)
-                o[g] = make_float4(__uint_as_float(x[4 * g]), __uint_as_float(x[4 * g + 1]),
-                                   __uint_as_float(x[4 * g + 2]), __uint_as_float(x[4 * g + 3]));
-            }
-          }
-        } else {
-#pragma unroll 1
-          for (int c = 0; c < 2; ++c) {  // 64 bf16 columns = one 128-byte staging row
-            const uint32_t slot = bulk ? take_slot() : 0u;
-#pragma unroll 1
-            for (int half = 0; half < 2; ++half) {  // 32 columns = 4 16-byte units
-              uint32_t x[32], w[16];
-              tmem_ld32(tO + c * 64 + half * 32, x);
-              tmem_ld_wait();
-              if (c == 1 && half == 1) {
-                tc_fence_before();
-                mbar_arrive(bar(kBarOFree + h));
-              }
-#pragma unroll
-              for (int t = 0; t < 16; ++t)
-                w[t] = pack_bf16x2(__uint_as_float(x[2 * t]) * inv,
-                                   __uint_as_float(x[2 * t + 1]) * inv);
-              if (bulk) {
-#pragma unroll
-                for (int g = 0; g < 4; ++g)
-                  st_shared_v4(slot + srow + (((uint32_t)(4 * half + g) ^ sw) << 4), w[4 * g],
-                               w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
-              } else if (store) {
-                uint4 *o = (uint4 *)((uint16_t *)p.out + orow + c * 64 + half * 32);
-#pragma unroll
-                for (int g = 0; g < 4; ++g)
-                  o[g] = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
-              }
-            }
-            if (bulk) send(slot, c * 64, head, v.tok0 + wrow0);
-          }
-        }
-      }
-      ++lcount;
-      tiles += v.nt;
-    };
-    // The q prologue of work unit 0, then per work unit k: the q prologue of work unit
-    // k+1 (whose tiles the producer loaded while unit k-1 ran), then the epilogue of k.
-    // Both warpgroups transform every unit; a warpgroup whose head slot is unused (one
-    // head per unit) writes no epilogue.
+    // The q prologue of work unit 0, then per work unit k the q prologue of work unit k+1
+    // (whose tiles the producer loads once unit k-1's last Q.K^T has run).  Both
+    // warpgroups transform every unit.
     const bool epi = h < nh;
     uint32_t next = next_work(p, p.offsets[blockIdx.x]);
     if (next < p.n_units) prepare(next, 0, 0);
@@ -927,11 +940,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         next = next_work(p, next + 1);
       }
-      if (epi) epilogue(u);
       ++k;
     }
-    if (lane == 0) bulk_wait_all();
-    __syncwarp();
   }
 
   tc_fence_before();
@@ -1183,7 +1193,8 @@ cudaError_t tc_preload() {
 cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uint32_t n_units,
                                 int num_sms, int *status, const uint16_t *q_norm_w, float eps,
                                 float theta, cudaStream_t stream, bool after_prologue,
-                                long long wait_cycles, bool exact_units) {
+                                long long wait_cycles, bool exact_units,
+                                const uint16_t *k_norm_w) {
   if (!n_units) return cudaSuccess;
   CUtensorMap mq, mk, mv, mo;
   const uint32_t rows = p.total;
@@ -1214,6 +1225,7 @@ cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uin
   prm.scale_log2 = p.scale * 1.4426950408889634f;
   prm.status = status;
   prm.q_norm_w = q_norm_w;
+  prm.k_norm_w = q_norm_w ? k_norm_w : nullptr;
   prm.eps = eps;
   prm.wait_cycles = wait_cycles > 0 ? wait_cycles : tc::kWaitCycles;
   for (int i = 0; i < 64; ++i)

@@ -95,10 +95,14 @@ bool tc_attention_supported(const AttnProblem &p);
 // prologue (the launch may then overlap its tail, programmatic dependent launch).
 // wait_cycles: limit of each bounded wait in SM cycles (<= 0: about a second).
 // exact_units: the work list was built with host lengths (tc_units_exact).
+// k_norm_w: the weights of the k RMSNorm the prologue applied to k in this call (NULL when
+// k was not normalised here); with q_norm_w they bound every score, and the kernel then
+// takes one pass over each score tile (no row maximum).
 cudaError_t launch_attention_tc(const AttnProblem &p, const uint32_t *units, uint32_t n_units,
                                 int num_sms, int *status, const uint16_t *q_norm_w, float eps,
                                 float theta, cudaStream_t stream, bool after_prologue,
-                                long long wait_cycles, bool exact_units);
+                                long long wait_cycles, bool exact_units,
+                                const uint16_t *k_norm_w = nullptr);
 // Whether tc_build_units writes units with their lengths (host lengths or cu_seqlens of
 // the problem's layout given).
 inline bool tc_units_exact(const AttnProblem &p, const uint32_t *lengths_host,

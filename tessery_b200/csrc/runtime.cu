@@ -21,7 +21,7 @@
 
 namespace {
 
-constexpr uint32_t kAbiVersion = 8;
+constexpr uint32_t kAbiVersion = 9;
 constexpr uint32_t kHostChunks = 8;              // most chunks of a host-buffer call
 constexpr size_t kHostChunkBytes = 16u << 20;     // bytes moved per chunk, at least
 
@@ -48,6 +48,11 @@ struct Ctx {
   std::vector<cudaEvent_t> prof_events;  // pairs
   size_t prof_used = 0;
   std::vector<double> prof_seconds;
+  // per-kernel timing of the typed entry points: an event pair around each launch of
+  // the last call (at most kKernelMarks / 2 launches)
+  bool ktime = false;
+  cudaEvent_t kt_ev[8] = {};
+  int kt_n = 0;
   // device status word
   int *status = nullptr;
   // scratch
@@ -162,6 +167,14 @@ struct Params64 {
 };
 static_assert(sizeof(Params64) == 64, "Params block is 64 bytes");
 
+constexpr int kKernelMarks = 8;
+// Event marks around one kernel launch of a typed call, when kernel timing is on.
+void kt_mark(Ctx *c, cudaStream_t stream) {
+  if (!c->ktime || c->kt_n >= kKernelMarks) return;
+  if (!c->kt_ev[c->kt_n] && cudaEventCreate(&c->kt_ev[c->kt_n]) != cudaSuccess) return;
+  cudaEventRecord(c->kt_ev[c->kt_n++], stream);
+}
+
 // Core of the typed entry points (padded when cu == nullptr).
 // `units_dev` / `units_n`: a work list already on the device (host-buffer calls upload
 // every chunk's list in one copy ahead of the data); NULL builds and uploads it here.
@@ -201,6 +214,7 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
         if (lengths_host[b] > p.seq) return fail(c, TX_EINVAL, "length exceeds seq");
     p.total = p.batch * p.seq;
   }
+  c->kt_n = 0;
   if (!p.total) return TX_OK;
   if ((uint64_t)p.total * p.heads * p.dim >= (1ull << 40))
     return fail(c, TX_EINVAL, "problem too large");
@@ -209,9 +223,11 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
   if (p.in_dtype == TX_BF16 && tx::short_attention_supported(p)) {
     cudaError_t e = cudaSetDevice(c->device);
     if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
+    kt_mark(c, stream);
     if ((e = tx::launch_attention_short(p, q_w, k_w, eps, theta, c->status, stream)) !=
         cudaSuccess)
       return cuda_fail(c, e, "attention launch");
+    kt_mark(c, stream);
     c->last_kernel = "short_d128";
     ++c->launches;
     return TX_OK;
@@ -286,19 +302,23 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
     pp.in_dtype = p.in_dtype; pp.out_dtype = mid;
     pp.q_w = q_w; pp.k_w = k_w; pp.eps = eps; pp.theta = theta;
     pp.lengths = tc_path && !p.cu_seqlens ? p.lengths : nullptr;
+    kt_mark(c, stream);
     if ((e = tx::launch_qk_norm_rope(pp, stream)) != cudaSuccess)
       return cuda_fail(c, e, "prologue launch");
+    kt_mark(c, stream);
     ++c->launches;
     if (pro_q) p.q = qs;
     if (pro_k) p.k = ks;
   }
 
+  kt_mark(c, stream);
   if (tc_path) {
     // pro_k: the k prologue was the launch just before on this stream.
     if ((e = tx::launch_attention_tc(p, units_dev ? units_dev : c->units,
                                      units_dev ? units_n : c->units_count, c->sms, c->status,
                                      tc_q_w, eps, theta, stream, pro_k, c->wait_cycles,
-                                     tx::tc_units_exact(p, lengths_host, cu_host))) !=
+                                     tx::tc_units_exact(p, lengths_host, cu_host),
+                                     pro_k ? k_w : nullptr)) !=
         cudaSuccess)
       return cuda_fail(c, e, "attention launch");
     c->last_kernel = "tc_bf16_d128";
@@ -324,6 +344,7 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
     c->last_kernel = "simt";
     ++c->launches;
   }
+  kt_mark(c, stream);
   if (uses_scratch && (e = scratch_release(c, stream)) != cudaSuccess)
     return cuda_fail(c, e, "scratch event");
   return TX_OK;
@@ -641,6 +662,8 @@ void tx_destroy(void *ctx) {
     if (c->units) cudaFree(c->units);
     if (c->status) cudaFree(c->status);
     for (cudaEvent_t ev : c->prof_events) cudaEventDestroy(ev);
+    for (cudaEvent_t ev : c->kt_ev)
+      if (ev) cudaEventDestroy(ev);
     if (c->ev_begin) cudaEventDestroy(c->ev_begin);
     if (c->ev_end) cudaEventDestroy(c->ev_end);
     if (c->scratch_done) cudaEventDestroy(c->scratch_done);
@@ -1120,6 +1143,34 @@ int tx_profile_enable(void *ctx, int enabled) {
   c->profile = enabled != 0;
   c->prof_used = 0;
   c->prof_seconds.clear();
+  return TX_OK;
+}
+
+int tx_kernel_timing(void *ctx, int enabled) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  c->ktime = enabled != 0;
+  c->kt_n = 0;
+  return TX_OK;
+}
+
+int tx_kernel_times(void *ctx, double *seconds, uint32_t cap, uint32_t *count) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c || !count) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  const uint32_t n = (uint32_t)c->kt_n / 2;
+  *count = n;
+  if (n > cap || (n && !seconds)) return fail(c, TX_EINVAL, "kernel times: capacity");
+  if (!n) return TX_OK;
+  cudaError_t e = cudaEventSynchronize(c->kt_ev[2 * n - 1]);
+  if (e != cudaSuccess) return cuda_fail(c, e, "kernel times");
+  for (uint32_t i = 0; i < n; ++i) {
+    float ms = 0.f;
+    if ((e = cudaEventElapsedTime(&ms, c->kt_ev[2 * i], c->kt_ev[2 * i + 1])) != cudaSuccess)
+      return cuda_fail(c, e, "kernel times");
+    seconds[i] = ms * 1e-3;
+  }
   return TX_OK;
 }
 

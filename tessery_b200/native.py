@@ -16,7 +16,7 @@ from typing import Any
 
 from .errors import NativeBuildError
 
-ABI_VERSION = 8
+ABI_VERSION = 9
 LIBRARY_NAME = "libtessattn.so"
 
 TX_OK, TX_EINVAL, TX_ECUDA, TX_ETIMEOUT = 0, 1, 2, 3
@@ -92,6 +92,8 @@ SIGNATURES: dict[str, tuple[list[Any], Any]] = {
     "tx_gpu_seconds": ([_vp], ct.c_double),
     "tx_profile_enable": ([_vp, _i32], _i32),
     "tx_profile_read": ([_vp, ct.POINTER(ct.c_double), _u32], _i32),
+    "tx_kernel_timing": ([_vp, _i32], _i32),
+    "tx_kernel_times": ([_vp, ct.POINTER(ct.c_double), _u32, ct.POINTER(_u32)], _i32),
     "tx_attention_padded": (
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _i32, _i32, _i32,
          _f32, _vp, _vp, _f32, _f32, _vp],

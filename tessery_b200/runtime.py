@@ -154,6 +154,21 @@ class CudaRuntime:
         """Kernels launched by this runtime's context so far."""
         return int(self._lib.tx_launch_count(self._pointer))
 
+    def kernel_timing(self, enabled: bool) -> None:
+        """While enabled, each kernel launch of the typed attention calls is bracketed by
+        a CUDA event pair (tx_kernel_timing); kernel_times() reads the last call's."""
+        self._check_open()
+        _raise_for(self._lib.tx_kernel_timing(self._pointer, int(bool(enabled))))
+
+    def kernel_times(self) -> list[float]:
+        """Device seconds of each kernel of the last typed attention call, in launch
+        order (the q/k prologue when it ran, then the attention kernel); waits for them."""
+        self._check_open()
+        seconds = (ct.c_double * 8)()
+        count = ct.c_uint32(0)
+        _raise_for(self._lib.tx_kernel_times(self._pointer, seconds, 8, ct.byref(count)))
+        return [float(seconds[i]) for i in range(count.value)]
+
     def set_wait_limit(self, cycles: int) -> None:
         """Limit, in SM clock cycles, of each bounded wait of the tensor-core kernel
         (0 restores the default, about a second).  A wait that runs out is reported as
