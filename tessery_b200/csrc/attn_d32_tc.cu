@@ -4,28 +4,32 @@
 // kernels.metal:78-103 (a query at position p of a sequence of length n attends to
 // [0, causal ? min(p + 1, n) : n); padded query rows included).
 //
-// The scores go to the tensor cores, the rest stays on the FP32 pipe: with padded query
-// rows counted the head_dim-32 problem is ~23 FLOP per byte of I/O, above the fp32 SIMT
-// ridge, and half of those FLOPs are Q.K^T.  Per CTA (one per 128 query rows, head,
-// sequence), per tile of 128 keys:
-//   - every thread loads one query row (once) and one key row, scales q by
-//     scale * log2(e), splits each value into a TF32 pair (hi = value rounded to TF32,
-//     lo = value - hi) and stores both parts into shared memory in the 128-byte-swizzled
-//     K-major layout the tensor core reads (a 32-float row is one 128-byte row); value
-//     rows are stored as they are;
-//   - one thread issues S = Qhi.Khi + Qhi.Klo + Qlo.Khi (tcgen05.mma kind::tf32,
-//     M=128, N=128, K=8, twelve instructions) into 128 tensor-memory columns: about 22
-//     significant bits per operand, so the scores carry fp32-level error;
-//   - thread t (tensor-memory lane t = query row t) reads its row of S, takes the
-//     masked maximum and forms exp2(s - m); threads 2i and 2i+1 exchange these and each
-//     accumulates both rows' p * v for its half of the head dimension with packed f32x2
-//     FMAs (every value row read as a shared-memory broadcast feeds two rows); the
-//     softmax is online across tiles with a lazily updated reference maximum (rescaled
-//     only when a chunk maximum exceeds it by more than 8), so every probability stays
-//     at most 2^8.
+// Both products on the tensor cores, as three-product TF32 splits (hi = value rounded to
+// TF32, lo = value - hi; hi.hi + hi.lo + lo.hi keeps about 22 significant bits per
+// operand, fp32-level error); the FP32 pipe keeps only the softmax.  With padded query
+// rows counted the head_dim-32 problem is ~23 FLOP per byte of I/O, and on the FP32 pipe
+// alone P.V by itself would take longer than the HBM traffic.  One CTA (4 warps, thread t
+// = query row t = tensor-memory lane t) per (128 query rows, head, sequence), two CTAs
+// per SM; per tile of 64 keys:
+//   - thread t stages query row t once (scaled by scale * log2(e)), then per tile
+//     threads 0-63 key row c0 + t and threads 64-127 value row c0 + t - 64, as TF32
+//     pairs in the 128-byte-swizzled K-major layouts the tensor core reads: Q and K one
+//     128-byte row per token, V transposed (V^T: one row per head-dimension column, 32
+//     keys per 128-byte block).  Two K/V buffers: tile j + 2 is staged once P.V of tile
+//     j has run, tile j + 1 is in place when Q.K^T of tile j + 1 is issued;
+//   - one thread issues S = Qhi.Khi + Qhi.Klo + Qlo.Khi (M=128, N=64, K=8, twelve
+//     instructions) into 64 tensor-memory columns;
+//   - thread t reads its row of S, takes the masked tile maximum (the reference maximum
+//     moves only when it exceeds it by more than 8, so every probability stays at most
+//     2^8), forms p = exp2(s - m) and writes its TF32 pair into tensor memory, hi over S
+//     and lo beside it;
+//   - one thread issues O_t = Phi.Vhi (into 32 columns) and Phi.Vlo + Plo.Vhi (into 32
+//     more) with P as the tensor-memory A operand (M=128, N=32, K=8, 24 instructions);
+//   - with the next tile's scores thread t reads both partial outputs of the previous
+//     tile and adds them to its row's fp32 accumulators, rescaled with the maximum.
 // Key and value rows at or past a sequence's end are never read (zeros are staged), so
-// padded rows may hold anything.  The single wait (scores ready) is bounded; a wait that
-// gives up records TX_ETIMEOUT | site << 8 and the CTA returns after its MMAs drained.
+// padded rows may hold anything.  Every wait is bounded; a wait that gives up records
+// TX_ETIMEOUT | site << 8 and the CTA returns once the products it issued have drained.
 #include <cuda.h>
 
 #include "../../include/tessattn.h"
@@ -38,60 +42,99 @@ namespace d32tc {
 
 using namespace ptx;
 
-constexpr int kRows = 128;       // query rows per CTA = threads = tensor-memory lanes
-constexpr int kKeys = 128;       // keys per tile (N of the score MMA)
-constexpr uint32_t kTile = kRows * 128;  // one operand part: 128 rows x 128 bytes
-// Shared memory: Q hi, Q lo, K hi, K lo (swizzled, 16 KB each), V (16 KB), barrier.
-constexpr uint32_t kOffQ = 0, kOffQlo = kTile, kOffK = 2 * kTile, kOffKlo = 3 * kTile,
-                   kOffV = 4 * kTile, kOffBar = 5 * kTile;
+constexpr int kRows = 128;  // query rows per CTA = threads = tensor-memory lanes
+constexpr int kKeys = 64;   // keys per tile (N of the score MMA, K of the output MMA)
+constexpr int kD = 32;
+constexpr uint32_t kQPart = kRows * 128;   // Q hi or lo: 128 rows x 128 B
+constexpr uint32_t kKPart = kKeys * 128;   // K hi or lo: 64 rows x 128 B
+constexpr uint32_t kVBlock = kD * 128;     // V^T block of 32 keys: 32 rows x 128 B
+constexpr uint32_t kVPart = 2 * kVBlock;   // V^T hi or lo: two blocks of 32 keys
+constexpr uint32_t kKVBuf = 2 * kKPart + 2 * kVPart;  // K hi, K lo, V^T hi, V^T lo
+// Shared memory: Q hi, Q lo, then two K/V buffers, then the barriers.
+constexpr uint32_t kOffQ = 0, kOffQlo = kQPart, kOffKV = 2 * kQPart,
+                   kOffBar = kOffKV + 2 * kKVBuf;
 constexpr uint32_t kSmemBytes = kOffBar + 1024 + 64;  // + alignment slack
-constexpr uint32_t kTmemCols = 128;
+static_assert(2 * kSmemBytes <= 232448, "two CTAs per SM");
+// Tensor memory: S / P hi [0, 64), P lo [64, 128), O main [128, 160), O corr [160, 192).
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColPlo = 64, kColOm = 128, kColOc = 160;
 constexpr long long kWaitCycles = 2000000000ll;
 // kind::tf32: D = f32 (bit 4), A and B TF32 (2 at bits 7 and 10), K-major, N >> 3 at bit
 // 17, M >> 4 at bit 24.
-constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kKeys >> 3) << 17) |
-                            ((uint32_t)(kRows >> 4) << 24);
-constexpr int kSiteScores = 1;
+constexpr uint32_t idesc_tf32(uint32_t n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((n >> 3) << 17) | ((uint32_t)(kRows >> 4) << 24);
+}
+constexpr uint32_t kIdescQK = idesc_tf32(kKeys), kIdescPV = idesc_tf32(kD);
+constexpr int kSiteScores = 1, kSiteOutput = 2;
 
-// Stores a 32-float row (r of 128) as a TF32 pair into the swizzled hi and lo tiles:
-// 16-byte chunk j of row r sits at chunk j ^ (r % 8) of the row's 128 bytes.
-__device__ __forceinline__ void store_split_row(uint32_t hi_tile, uint32_t lo_tile, uint32_t r,
-                                                const float (&x)[32]) {
-  const uint32_t row = r * 128, sw = r & 7;
+// D (+)= A B, A (TF32, lane = row, one element per column) read from tensor memory.
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// A 32-float row (8 float4 from global memory, or zeros), scaled.
+__device__ __forceinline__ void load_row(const float *src, bool ok, float scale,
+                                         float4 (&x)[8]) {
 #pragma unroll
-  for (uint32_t j = 0; j < 8; ++j) {
-    float h[4], l[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      h[e] = tf32_round(x[4 * j + e]);
-      l[e] = x[4 * j + e] - h[e];
-    }
-    const uint32_t off = row + ((j ^ sw) << 4);
-    st_shared_v4(hi_tile + off, __float_as_uint(h[0]), __float_as_uint(h[1]),
-                 __float_as_uint(h[2]), __float_as_uint(h[3]));
-    st_shared_v4(lo_tile + off, __float_as_uint(l[0]), __float_as_uint(l[1]),
-                 __float_as_uint(l[2]), __float_as_uint(l[3]));
+  for (int j = 0; j < 8; ++j) {
+    float4 t = ok ? __ldg(reinterpret_cast<const float4 *>(src) + j)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+    x[j] = make_float4(t.x * scale, t.y * scale, t.z * scale, t.w * scale);
   }
 }
 
-__device__ __forceinline__ void load_row(const float *p, bool ok, float (&x)[32]) {
+// Row r of a K-major operand (128 B per row) as a TF32 pair: 16-byte chunk j of row r at
+// chunk j ^ (r % 8).
+__device__ __forceinline__ void store_split_row(uint32_t hi, uint32_t lo, uint32_t r,
+                                                const float4 (&x)[8]) {
+  const uint32_t row = r * 128, sw = r & 7;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float4 t = ok ? __ldg(reinterpret_cast<const float4 *>(p) + j)
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
-    x[4 * j] = t.x, x[4 * j + 1] = t.y, x[4 * j + 2] = t.z, x[4 * j + 3] = t.w;
+  for (uint32_t j = 0; j < 8; ++j) {
+    const float h0 = tf32_round(x[j].x), h1 = tf32_round(x[j].y), h2 = tf32_round(x[j].z),
+                h3 = tf32_round(x[j].w);
+    const uint32_t off = row + ((j ^ sw) << 4);
+    st_shared_v4(hi + off, __float_as_uint(h0), __float_as_uint(h1), __float_as_uint(h2),
+                 __float_as_uint(h3));
+    st_shared_v4(lo + off, __float_as_uint(x[j].x - h0), __float_as_uint(x[j].y - h1),
+                 __float_as_uint(x[j].z - h2), __float_as_uint(x[j].w - h3));
+  }
+}
+
+// Value row `key` (of 64) as column `key` of V^T, a TF32 pair: V^T row d (head-dimension
+// column d) holds the keys of a 32-key block in 128 bytes, 16-byte chunk j (keys 4j..4j+3
+// of the block) at chunk j ^ (d % 8).  Threads of a warp hold 32 consecutive keys, so
+// each 4-byte store of a warp fills one 128-byte row without bank conflicts.
+__device__ __forceinline__ void store_split_col(uint32_t hi, uint32_t lo, uint32_t key,
+                                                const float4 (&x)[8]) {
+  const uint32_t blk = (key >> 5) * kVBlock, k = key & 31, j = k >> 2, e = (k & 3) * 4;
+#pragma unroll
+  for (uint32_t c = 0; c < 8; ++c) {
+    const float v[4] = {x[c].x, x[c].y, x[c].z, x[c].w};
+#pragma unroll
+    for (uint32_t i = 0; i < 4; ++i) {
+      const uint32_t d = 4 * c + i;
+      const uint32_t off = blk + d * 128 + ((j ^ (d & 7)) << 4) + e;
+      const float h = tf32_round(v[i]);
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(hi + off), "r"(__float_as_uint(h)));
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(lo + off), "r"(__float_as_uint(v[i] - h)));
+    }
   }
 }
 
 __global__ void __launch_bounds__(kRows, 2) attn_d32_tc_kernel(AttnProblem p, int *status) {
   extern __shared__ uint8_t smem_raw[];
-  // 1024-byte aligned window for the swizzled tiles.
+  // 1024-byte aligned window for the swizzled operands.
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t sbase = (raw + 1023u) & ~1023u;
   uint8_t *smem = smem_raw + (sbase - raw);
-  const uint32_t bar = sbase + kOffBar;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 8);
-  const float *vs = reinterpret_cast<const float *>(smem + kOffV);
+  const uint32_t bar_s = sbase + kOffBar, bar_o = bar_s + 8, bar_d = bar_s + 16;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 24);
 
   const uint32_t tid = threadIdx.x, warp = tid >> 5;
   const uint32_t qblock = blockIdx.x, head = blockIdx.y, seqi = blockIdx.z;
@@ -115,12 +158,15 @@ __global__ void __launch_bounds__(kRows, 2) attn_d32_tc_kernel(AttnProblem p, in
   const uint32_t end = act ? (p.causal ? min(pos + 1, len) : len) : 0u;
   const uint32_t last = min(q0 + kRows, rows) - 1;
   const uint32_t kend = p.causal ? min(last + 1, len) : len;
+  const uint32_t ntiles = (kend + kKeys - 1) / kKeys;
   const float *q = static_cast<const float *>(p.q), *k = static_cast<const float *>(p.k),
               *v = static_cast<const float *>(p.v);
   float *out = static_cast<float *>(p.out);
 
   if (tid == 0) {
-    mbar_init(bar, 1);
+    mbar_init(bar_s, 1);
+    mbar_init(bar_o, 1);
+    mbar_init(bar_d, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
@@ -130,153 +176,188 @@ __global__ void __launch_bounds__(kRows, 2) attn_d32_tc_kernel(AttnProblem p, in
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // This thread's query row, pre-scaled into log2 units, as a TF32 pair.
+  // Tile j of keys for K/V buffer j % 2: threads 0-63 a key row, 64-127 a value row;
+  // rows at or past kend are zeros.  Loads and stores are separate steps so that the
+  // first tiles' loads are all in flight at once.
+  const uint32_t r_kv = tid & (kKeys - 1);
+  auto load_tile = [&](uint32_t j, float4 (&x)[8]) {
+    const uint32_t key = j * kKeys + r_kv;
+    const uint64_t row = ((base + key) * p.kv_heads + kvhead) * kD;
+    load_row((tid < (uint32_t)kKeys ? k : v) + row, key < kend, 1.0f, x);
+  };
+  auto store_tile = [&](uint32_t j, const float4 (&x)[8]) {
+    const uint32_t buf = sbase + kOffKV + (j & 1) * kKVBuf;
+    if (tid < (uint32_t)kKeys)
+      store_split_row(buf, buf + kKPart, r_kv, x);
+    else
+      store_split_col(buf + 2 * kKPart, buf + 2 * kKPart + kVPart, r_kv, x);
+  };
+  auto stage = [&](uint32_t j) {
+    float4 x[8];
+    load_tile(j, x);
+    store_tile(j, x);
+  };
   {
-    float x[32];
-    load_row(q + ((base + pos) * p.heads + head) * 32, act, x);
-    const float qs = p.scale * 1.4426950408889634f;
-#pragma unroll
-    for (int e = 0; e < 32; ++e) x[e] *= qs;
-    store_split_row(sbase + kOffQ, sbase + kOffQlo, tid, x);
+    float4 xq[8], x0[8], x1[8];
+    load_row(q + ((base + pos) * p.heads + head) * kD, act, p.scale * 1.4426950408889634f, xq);
+    load_tile(0, x0);  // rows past kend (no tile) are zeros and never stored
+    load_tile(1, x1);
+    store_split_row(sbase + kOffQ, sbase + kOffQlo, tid, xq);
+    if (ntiles > 0) store_tile(0, x0);
+    if (ntiles > 1) store_tile(1, x1);
   }
+  fence_proxy_async();  // generic stores seen by the tensor core
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem + ((warp * 32u) << 16);
+  const uint32_t tL = tmem + ((warp * 32u) << 16);  // this warp's lanes
 
-  // Threads 2i and 2i+1 (rows 2i and 2i+1) share the output accumulators of both rows,
-  // each for one half of the head dimension (h), so every value-row read from shared
-  // memory feeds two rows; each thread keeps the softmax state of its own row.
-  const uint32_t h = tid & 1;
-  uint64_t acc_e[8], acc_o[8];  // rows 2i and 2i+1, columns 16h..16h+15, packed pairs
+  // S = Q K_j^T, three TF32 products over the 32 columns (4 steps of 8).
+  auto issue_qk = [&](uint32_t j) {
+    const uint32_t buf = sbase + kOffKV + (j & 1) * kKVBuf;
+    const uint64_t qd = sw128_desc(sbase + kOffQ, 16, 1024);
+    const uint64_t qld = sw128_desc(sbase + kOffQlo, 16, 1024);
+    const uint64_t kd = sw128_desc(buf, 16, 1024), kld = sw128_desc(buf + kKPart, 16, 1024);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc_e[i] = acc_o[i] = f2(0.f, 0.f);
+    for (uint32_t ks = 0; ks < 4; ++ks) {
+      const uint64_t o = (uint64_t)(ks * 2);  // 8 elements = 32 bytes of the swizzled row
+      umma_tf32(tmem, qd + o, kd + o, kIdescQK, ks > 0 ? 1u : 0u);
+      umma_tf32(tmem, qd + o, kld + o, kIdescQK, 1u);
+      umma_tf32(tmem, qld + o, kd + o, kIdescQK, 1u);
+    }
+    umma_commit(bar_s);
+  };
+  // O_j = P V_j over the tile's 64 keys (8 steps of 8): Phi.Vhi into the main columns,
+  // Phi.Vlo + Plo.Vhi into the correction columns.
+  auto issue_pv = [&](uint32_t j) {
+    const uint32_t vb = sbase + kOffKV + (j & 1) * kKVBuf + 2 * kKPart;
+#pragma unroll
+    for (uint32_t ks = 0; ks < 8; ++ks) {
+      const uint32_t blk = (ks >> 2) * kVBlock;
+      const uint64_t o = (uint64_t)((ks & 3) * 2);
+      const uint64_t vd = sw128_desc(vb + blk, 16, 1024) + o;
+      const uint64_t vld = sw128_desc(vb + kVPart + blk, 16, 1024) + o;
+      umma_tf32_ts(tmem + kColOm, tmem + 8 * ks, vd, kIdescPV, ks > 0 ? 1u : 0u);
+      umma_tf32_ts(tmem + kColOc, tmem + 8 * ks, vld, kIdescPV, ks > 0 ? 1u : 0u);
+      umma_tf32_ts(tmem + kColOc, tmem + kColPlo + 8 * ks, vd, kIdescPV, 1u);
+    }
+    umma_commit(bar_o);
+  };
+  // Bounded wait for phase `parity` of barrier b.
+  auto wait_bar = [&](uint32_t b, uint32_t parity) -> bool {
+    const long long t0 = clock64();
+    while (!mbar_test(b, parity))
+      if (clock64() - t0 > kWaitCycles) return false;
+    return true;
+  };
+
+  if (tid == 0 && ntiles > 0) issue_qk(0);
+  float acc[kD];
+#pragma unroll
+  for (int d = 0; d < kD; ++d) acc[d] = 0.f;
   float m = -INFINITY, l = 0.f;
   bool ok = true;
-  uint32_t phase = 0;
-  for (uint32_t c0 = 0; c0 < kend; c0 += kKeys, phase ^= 1) {
-    // Stage key row c0 + tid (split) and value row c0 + tid; rows past the end are zeros.
-    {
-      const uint32_t key = c0 + tid;
-      const bool kin = key < kend;
-      const uint64_t row = ((base + key) * p.kv_heads + kvhead) * 32;
-      float x[32];
-      load_row(k + row, kin, x);
-      store_split_row(sbase + kOffK, sbase + kOffKlo, tid, x);
-      load_row(v + row, kin, x);
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        st_shared_v4(sbase + kOffV + tid * 128 + j * 16, __float_as_uint(x[4 * j]),
-                     __float_as_uint(x[4 * j + 1]), __float_as_uint(x[4 * j + 2]),
-                     __float_as_uint(x[4 * j + 3]));
-    }
-    fence_proxy_async();  // generic stores seen by the tensor core
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (tid == 0) {
-      const uint64_t qd = sw128_desc(sbase + kOffQ, 16, 1024), qld = sw128_desc(sbase + kOffQlo, 16, 1024);
-      const uint64_t kd = sw128_desc(sbase + kOffK, 16, 1024), kld = sw128_desc(sbase + kOffKlo, 16, 1024);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {  // 8 elements of K = 32 bytes of the swizzled row
-        const uint64_t o = (uint64_t)(ks * 2);
-        umma_tf32(tmem, qd + o, kd + o, kIdesc, ks > 0 ? 1u : 0u);
-        umma_tf32(tmem, qd + o, kld + o, kIdesc, 1u);
-        umma_tf32(tmem, qld + o, kd + o, kIdesc, 1u);
-      }
-      umma_commit(bar);
-    }
-    // Scores ready (bounded wait).
-    {
-      const long long t0 = clock64();
-      while (!mbar_test(bar, phase) && ok)
-        if (clock64() - t0 > kWaitCycles) ok = false;
-    }
-    if (!__syncthreads_and(ok)) {
-      // The issued MMAs complete by themselves: wait for them before the columns are
-      // freed, then return without output.
-      if (tid == 0) report_status(status, kStatusTimeout | (kSiteScores << 8));
-      const long long t0 = clock64();
-      while (!mbar_test(bar, phase) && clock64() - t0 < kWaitCycles) {
-      }
+  int site = 0;
+  for (uint32_t j = 0; j < ntiles; ++j) {
+    // S_j ready: committed after P.V of tile j - 1, so that one ran too.
+    if (!__syncthreads_and(wait_bar(bar_s, j & 1))) {
       ok = false;
+      site = kSiteScores;
       break;
     }
     tc_fence_after();
-    // This row's scores, 32 keys at a time: masked maximum of the chunk (the reference
-    // maximum moves only when it exceeds it by more than 8), then exp2(s - m) * v.
-    const int valid = (int)min(max((int)end - (int)c0, 0), kKeys);
-#pragma unroll 1
-    for (int c = 0; c < kKeys / 32; ++c) {
-      if (c0 + c * 32 >= kend) break;  // uniform: no row has keys there
-      uint32_t r[32];
-      tmem_ld32(tS + c * 32, r);
+    uint32_t sr[64];
+    tmem_ld32(tL, *reinterpret_cast<uint32_t(*)[32]>(sr));
+    tmem_ld32(tL + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+    if (j > 0) {  // tile j - 1's partial outputs into the accumulators
+      uint32_t om[32], oc[32];
+      tmem_ld32(tL + kColOm, om);
+      tmem_ld32(tL + kColOc, oc);
       tmem_ld_wait();
-      float mc = -INFINITY;
 #pragma unroll
-      for (int t = 0; t < 32; ++t)
-        if (c * 32 + t < valid) mc = fmaxf(mc, __uint_as_float(r[t]));
-      float cr = 1.0f;  // rescale factor of this thread's row (1: none)
-      if (mc > m + 8.0f) {  // also the first chunk with a valid key (m = -inf)
-        cr = ex2(m - mc);
-        l *= cr;
-        m = mc;
-      }
-      const float cr_pair = __shfl_xor_sync(0xffffffffu, cr, 1);
-      if (__any_sync(0xffffffffu, cr != 1.0f || cr_pair != 1.0f)) {
-        const float ce = h ? cr_pair : cr, co = h ? cr : cr_pair;
-        const uint64_t ce2 = f2(ce, ce), co2 = f2(co, co);
+      for (int d = 0; d < kD; ++d) acc[d] += __uint_as_float(om[d]) + __uint_as_float(oc[d]);
+    } else {
+      tmem_ld_wait();
+    }
+    const int valid = (int)min(max((int)end - (int)(j * kKeys), 0), kKeys);
+    float mc = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          acc_e[i] = mul2(acc_e[i], ce2);
-          acc_o[i] = mul2(acc_o[i], co2);
-        }
-      }
-      const float *vc = vs + c * 32 * 32 + 16 * h;
+    for (int t = 0; t < 64; ++t)
+      if (t < valid) mc = fmaxf(mc, __uint_as_float(sr[t]));
+    if (mc > m + 8.0f) {  // also the first tile with a valid key (m = -inf)
+      const float cr = ex2(m - mc);
+      l *= cr;
+#pragma unroll
+      for (int d = 0; d < kD; ++d) acc[d] *= cr;
+      m = mc;
+    }
+    // P as a TF32 pair: hi over S, lo beside it (32 keys at a time).
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t ph[32], pl[32];
 #pragma unroll
       for (int t = 0; t < 32; ++t) {
-        const float pj = c * 32 + t < valid ? ex2(__uint_as_float(r[t]) - m) : 0.f;
+        const float pj = 32 * h + t < valid ? ex2(__uint_as_float(sr[32 * h + t]) - m) : 0.f;
         l += pj;
-        const float pp = __shfl_xor_sync(0xffffffffu, pj, 1);
-        const float pe = h ? pp : pj, po = h ? pj : pp;
-        const uint64_t pe2 = f2(pe, pe), po2 = f2(po, po);
-        const float4 *vr = reinterpret_cast<const float4 *>(vc + t * 32);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float4 vv = vr[i];
-          const uint64_t va = f2(vv.x, vv.y), vb = f2(vv.z, vv.w);
-          acc_e[2 * i] = fma2(pe2, va, acc_e[2 * i]);
-          acc_e[2 * i + 1] = fma2(pe2, vb, acc_e[2 * i + 1]);
-          acc_o[2 * i] = fma2(po2, va, acc_o[2 * i]);
-          acc_o[2 * i + 1] = fma2(po2, vb, acc_o[2 * i + 1]);
-        }
+        const float hi = tf32_round(pj);
+        ph[t] = __float_as_uint(hi);
+        pl[t] = __float_as_uint(pj - hi);
       }
+      tmem_st32(tL + 32 * h, ph);
+      tmem_st32(tL + kColPlo + 32 * h, pl);
     }
-    // Shared memory and the score columns are reused by the next tile.
+    tmem_st_wait();
     tc_fence_before();
-    __syncthreads();
-  }
-  {
-    // This thread's half of rows 2i and 2i+1 (zero valid keys: 0/0, as the reference's
-    // sums give).
-    const float l_pair = __shfl_xor_sync(0xffffffffu, l, 1);
-    const float inv_e = 1.0f / (h ? l_pair : l), inv_o = 1.0f / (h ? l : l_pair);
-    const uint32_t pos_e = q0 + (tid & ~1u);
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const uint32_t prow = pos_e + r;
-      if (!ok || prow >= rows) continue;
-      const uint64_t(&a)[8] = r ? acc_o : acc_e;
-      const float inv = r ? inv_o : inv_e;
-      float4 *op =
-          reinterpret_cast<float4 *>(out + ((base + prow) * p.heads + head) * 32 + 16 * h);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 x0 = f2_unpack(a[2 * i]), x1 = f2_unpack(a[2 * i + 1]);
-        op[i] = make_float4(x0.x * inv, x0.y * inv, x1.x * inv, x1.y * inv);
-      }
+    __syncthreads();  // P complete in every lane; tile j + 1 staged
+    tc_fence_after();
+    if (tid == 0) {
+      issue_pv(j);
+      if (j + 1 < ntiles) issue_qk(j + 1);
     }
+    if (j + 2 < ntiles) {
+      // Tile j + 2 into this tile's buffer once P.V of tile j (the last reader) ran; the
+      // next iteration's barrier orders the stores before its Q.K^T is issued.
+      if (!__syncthreads_and(wait_bar(bar_o, j & 1))) {
+        ok = false;
+        site = kSiteOutput;
+        break;
+      }
+      stage(j + 2);
+      fence_proxy_async();
+    }
+  }
+  if (ok && ntiles > 0) {
+    // The last tile's partial outputs.
+    if (__syncthreads_and(wait_bar(bar_o, (ntiles - 1) & 1))) {
+      tc_fence_after();
+      uint32_t om[32], oc[32];
+      tmem_ld32(tL + kColOm, om);
+      tmem_ld32(tL + kColOc, oc);
+      tmem_ld_wait();
+#pragma unroll
+      for (int d = 0; d < kD; ++d) acc[d] += __uint_as_float(om[d]) + __uint_as_float(oc[d]);
+    } else {
+      ok = false;
+      site = kSiteOutput;
+    }
+  }
+  if (!ok) {
+    // Every product issued completes by itself: wait for them (one commit tracks all of
+    // the issuing thread's) before the columns are freed; no output.
+    if (tid == 0) {
+      report_status(status, kStatusTimeout | (site << 8));
+      umma_commit(bar_d);
+      wait_bar(bar_d, 0);
+    }
+  } else if (act) {
+    // Zero valid keys: 0/0, as the reference's sums give.
+    const float inv = 1.0f / l;
+    float4 *op = reinterpret_cast<float4 *>(out + ((base + pos) * p.heads + head) * kD);
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      op[c] = make_float4(acc[4 * c] * inv, acc[4 * c + 1] * inv, acc[4 * c + 2] * inv,
+                          acc[4 * c + 3] * inv);
   }
   tc_fence_before();
   __syncthreads();

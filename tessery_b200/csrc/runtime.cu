@@ -233,12 +233,8 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
     return TX_OK;
   }
   const bool tc_path = p.in_dtype == TX_BF16 && p.scale > 0.f && tx::tc_attention_supported(p);
-  // head_dim 32, fp32: the tensor-core scores kernel while the problem fits one wave of
-  // CTAs (it shortens each CTA: config 1, 24.2 -> 16.6 us); beyond, the packed-FMA
-  // kernel, four CTAs per SM against two, has the higher throughput (batch 4096: 1.74 ms
-  // against 2.00 ms).
-  const uint64_t d32_ctas = (uint64_t)((p.seq + 127) / 128) * p.heads * p.batch;
-  const bool d32tc_path = !tc_path && tx::d32_tc_supported(p) && d32_ctas <= 2ull * c->sms;
+  // head_dim 32, fp32: both products on the tensor cores (three-product TF32 splits).
+  const bool d32tc_path = !tc_path && tx::d32_tc_supported(p);
   const bool d32_path = !tc_path && !d32tc_path && p.dim == 32 &&
                         p.batch <= 65535u && p.heads <= 65535u &&
                         (uintptr_t)p.q % 16 == 0 && (uintptr_t)p.k % 16 == 0 &&

@@ -87,9 +87,8 @@ def test_attention_route_follows_head_dim(runtime):
 
 # ---- BGE d32 fp32 ---------------------------------------------------------------------
 def d32_route(runtime, batch, seq, heads=12):
-    """fp32 head_dim 32: tensor-core scores within one wave of CTAs, packed FMA beyond."""
-    ctas = -(-seq // 128) * heads * batch
-    return "d32_tc" if ctas <= 2 * runtime.sms else "d32"
+    """fp32 head_dim 32: the tensor-core kernel (both products, TF32 splits) at any size."""
+    return "d32_tc"
 
 
 @pytest.mark.parametrize("batch,seq", [(4, 128), (3, 200), (2, 520), (30, 128)])
