@@ -1128,7 +1128,7 @@ def run_forward(args):
                 "config": spec.config(world), "roofline": roof,
                 "tokens_per_s": int(lengths.sum()) * world * args.steps / total_s,
                 "route": "linear_kernel + attn_tc_kernel + row kernels" if spec.qwen
-                         else "linear_kernel (TF32) + attention_d32_kernel + row kernels",
+                         else "linear_kernel (TF32) + attn_d32_tc_kernel + row kernels",
                 "cpu_baseline": cpu,
                 "e2e": {"value": e2e_value, "unit": "texts/s",
                         "h2d_bytes_per_step": int(lengths.sum()) * 4 + (lengths.size + 1) * 4,

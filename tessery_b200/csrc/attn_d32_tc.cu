@@ -9,22 +9,23 @@
 // operand, fp32-level error); the FP32 pipe keeps only the softmax.  With padded query
 // rows counted the head_dim-32 problem is ~23 FLOP per byte of I/O, and on the FP32 pipe
 // alone P.V by itself would take longer than the HBM traffic.  One CTA (4 warps, thread t
-// = query row t = tensor-memory lane t) per (128 query rows, head, sequence), two CTAs
-// per SM; per tile of 64 keys:
+// = query row t = tensor-memory lane t) per (128 query rows, head, sequence); per tile of
+// T keys (T = 64, two CTAs per SM, for launches within one wave; T = 32, three CTAs per
+// SM, beyond):
 //   - thread t stages query row t once (scaled by scale * log2(e)), then per tile
-//     threads 0-63 key row c0 + t and threads 64-127 value row c0 + t - 64, as TF32
+//     threads [0, T) key row c0 + t and threads [T, 2T) value row c0 + t - T, as TF32
 //     pairs in the 128-byte-swizzled K-major layouts the tensor core reads: Q and K one
 //     128-byte row per token, V transposed (V^T: one row per head-dimension column, 32
 //     keys per 128-byte block).  Two K/V buffers: tile j + 2 is staged once P.V of tile
 //     j has run, tile j + 1 is in place when Q.K^T of tile j + 1 is issued;
-//   - one thread issues S = Qhi.Khi + Qhi.Klo + Qlo.Khi (M=128, N=64, K=8, twelve
-//     instructions) into 64 tensor-memory columns;
+//   - one thread issues S = Qhi.Khi + Qhi.Klo + Qlo.Khi (M=128, N=T, K=8, twelve
+//     instructions) into T tensor-memory columns;
 //   - thread t reads its row of S, takes the masked tile maximum (the reference maximum
 //     moves only when it exceeds it by more than 8, so every probability stays at most
 //     2^8), forms p = exp2(s - m) and writes its TF32 pair into tensor memory, hi over S
 //     and lo beside it;
 //   - one thread issues O_t = Phi.Vhi (into 32 columns) and Phi.Vlo + Plo.Vhi (into 32
-//     more) with P as the tensor-memory A operand (M=128, N=32, K=8, 24 instructions);
+//     more) with P as the tensor-memory A operand (M=128, N=32, K=8, 3T/8 instructions);
 //   - with the next tile's scores thread t reads both partial outputs of the previous
 //     tile and adds them to its row's fp32 accumulators, rescaled with the maximum.
 // Key and value rows at or past a sequence's end are never read (zeros are staged), so
@@ -43,29 +44,37 @@ namespace d32tc {
 using namespace ptx;
 
 constexpr int kRows = 128;  // query rows per CTA = threads = tensor-memory lanes
-constexpr int kKeys = 64;   // keys per tile (N of the score MMA, K of the output MMA)
 constexpr int kD = 32;
 constexpr uint32_t kQPart = kRows * 128;   // Q hi or lo: 128 rows x 128 B
-constexpr uint32_t kKPart = kKeys * 128;   // K hi or lo: 64 rows x 128 B
 constexpr uint32_t kVBlock = kD * 128;     // V^T block of 32 keys: 32 rows x 128 B
-constexpr uint32_t kVPart = 2 * kVBlock;   // V^T hi or lo: two blocks of 32 keys
-constexpr uint32_t kKVBuf = 2 * kKPart + 2 * kVPart;  // K hi, K lo, V^T hi, V^T lo
-// Shared memory: Q hi, Q lo, then two K/V buffers, then the barriers.
-constexpr uint32_t kOffQ = 0, kOffQlo = kQPart, kOffKV = 2 * kQPart,
-                   kOffBar = kOffKV + 2 * kKVBuf;
-constexpr uint32_t kSmemBytes = kOffBar + 1024 + 64;  // + alignment slack
-static_assert(2 * kSmemBytes <= 232448, "two CTAs per SM");
-// Tensor memory: S / P hi [0, 64), P lo [64, 128), O main [128, 160), O corr [160, 192).
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColPlo = 64, kColOm = 128, kColOc = 160;
+constexpr uint32_t kOffQ = 0, kOffQlo = kQPart, kOffKV = 2 * kQPart;
 constexpr long long kWaitCycles = 2000000000ll;
 // kind::tf32: D = f32 (bit 4), A and B TF32 (2 at bits 7 and 10), K-major, N >> 3 at bit
 // 17, M >> 4 at bit 24.
 constexpr uint32_t idesc_tf32(uint32_t n) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((n >> 3) << 17) | ((uint32_t)(kRows >> 4) << 24);
 }
-constexpr uint32_t kIdescQK = idesc_tf32(kKeys), kIdescPV = idesc_tf32(kD);
 constexpr int kSiteScores = 1, kSiteOutput = 2;
+
+// Layout for tiles of kKeys keys (N of the score MMA, K of the output MMA): 64-key tiles
+// take fewer round trips per CTA (the one-wave latency case), 32-key tiles fit three
+// CTAs per SM (128 tensor-memory columns, 65 KB of shared memory, <= 168 registers).
+template <int kKeys>
+struct Cfg {
+  static_assert(kKeys == 32 || kKeys == 64, "tile of 32 or 64 keys");
+  static constexpr int kChunks = kKeys / 32;            // 32-column chunks of a score row
+  static constexpr uint32_t kKPart = kKeys * 128;       // K hi or lo: 128 B per key
+  static constexpr uint32_t kVPart = kChunks * kVBlock;  // V^T hi or lo: a block per 32 keys
+  static constexpr uint32_t kKVBuf = 2 * kKPart + 2 * kVPart;  // K hi, K lo, V^T hi, V^T lo
+  // Shared memory: Q hi, Q lo, then two K/V buffers, then the barriers.
+  static constexpr uint32_t kOffBar = kOffKV + 2 * kKVBuf;
+  static constexpr uint32_t kSmemBytes = kOffBar + 1024 + 64;  // + alignment slack
+  // Tensor memory: S / P hi [0, kKeys), P lo [kKeys, 2 kKeys), O main and O corr.
+  static constexpr uint32_t kColPlo = kKeys, kColOm = 2 * kKeys, kColOc = 2 * kKeys + kD;
+  static constexpr uint32_t kTmemCols = kColOc + kD <= 128 ? 128 : 256;  // a power of two
+  static constexpr int kCtasPerSm = kTmemCols == 128 ? 3 : 2;
+  static constexpr uint32_t kIdescQK = idesc_tf32(kKeys), kIdescPV = idesc_tf32(kD);
+};
 
 // D (+)= A B, A (TF32, lane = row, one element per column) read from tensor memory.
 __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
@@ -127,7 +136,15 @@ __device__ __forceinline__ void store_split_col(uint32_t hi, uint32_t lo, uint32
   }
 }
 
-__global__ void __launch_bounds__(kRows, 2) attn_d32_tc_kernel(AttnProblem p, int *status) {
+template <int kKeys>
+__global__ void __launch_bounds__(kRows, Cfg<kKeys>::kCtasPerSm)
+    attn_d32_tc_kernel(AttnProblem p, int *status) {
+  using C = Cfg<kKeys>;
+  constexpr int kChunks = C::kChunks;
+  constexpr uint32_t kKPart = C::kKPart, kVPart = C::kVPart, kKVBuf = C::kKVBuf,
+                     kOffBar = C::kOffBar, kColPlo = C::kColPlo, kColOm = C::kColOm,
+                     kColOc = C::kColOc, kTmemCols = C::kTmemCols, kIdescQK = C::kIdescQK,
+                     kIdescPV = C::kIdescPV;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned window for the swizzled operands.
   const uint32_t raw = smem_addr(smem_raw);
@@ -176,20 +193,21 @@ __global__ void __launch_bounds__(kRows, 2) attn_d32_tc_kernel(AttnProblem p, in
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // Tile j of keys for K/V buffer j % 2: threads 0-63 a key row, 64-127 a value row;
+  // Tile j of keys for K/V buffer j % 2: threads [0, kKeys) a key row, [kKeys, 2 kKeys) a
+  // value row;
   // rows at or past kend are zeros.  Loads and stores are separate steps so that the
   // first tiles' loads are all in flight at once.
   const uint32_t r_kv = tid & (kKeys - 1);
   auto load_tile = [&](uint32_t j, float4 (&x)[8]) {
     const uint32_t key = j * kKeys + r_kv;
     const uint64_t row = ((base + key) * p.kv_heads + kvhead) * kD;
-    load_row((tid < (uint32_t)kKeys ? k : v) + row, key < kend, 1.0f, x);
+    load_row((tid < (uint32_t)kKeys ? k : v) + row, key < kend && tid < 2u * kKeys, 1.0f, x);
   };
   auto store_tile = [&](uint32_t j, const float4 (&x)[8]) {
     const uint32_t buf = sbase + kOffKV + (j & 1) * kKVBuf;
     if (tid < (uint32_t)kKeys)
       store_split_row(buf, buf + kKPart, r_kv, x);
-    else
+    else if (tid < 2u * kKeys)
       store_split_col(buf + 2 * kKPart, buf + 2 * kKPart + kVPart, r_kv, x);
   };
   auto stage = [&](uint32_t j) {
@@ -228,12 +246,12 @@ __global__ void __launch_bounds__(kRows, 2) attn_d32_tc_kernel(AttnProblem p, in
     }
     umma_commit(bar_s);
   };
-  // O_j = P V_j over the tile's 64 keys (8 steps of 8): Phi.Vhi into the main columns,
+  // O_j = P V_j over the tile's keys (steps of 8): Phi.Vhi into the main columns,
   // Phi.Vlo + Plo.Vhi into the correction columns.
   auto issue_pv = [&](uint32_t j) {
     const uint32_t vb = sbase + kOffKV + (j & 1) * kKVBuf + 2 * kKPart;
 #pragma unroll
-    for (uint32_t ks = 0; ks < 8; ++ks) {
+    for (uint32_t ks = 0; ks < kKeys / 8; ++ks) {
       const uint32_t blk = (ks >> 2) * kVBlock;
       const uint64_t o = (uint64_t)((ks & 3) * 2);
       const uint64_t vd = sw128_desc(vb + blk, 16, 1024) + o;
@@ -267,9 +285,10 @@ __global__ void __launch_bounds__(kRows, 2) attn_d32_tc_kernel(AttnProblem p, in
       break;
     }
     tc_fence_after();
-    uint32_t sr[64];
-    tmem_ld32(tL, *reinterpret_cast<uint32_t(*)[32]>(sr));
-    tmem_ld32(tL + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+    uint32_t sr[kKeys];
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c)
+      tmem_ld32(tL + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(sr + 32 * c));
     if (j > 0) {  // tile j - 1's partial outputs into the accumulators
       uint32_t om[32], oc[32];
       tmem_ld32(tL + kColOm, om);
@@ -283,7 +302,7 @@ __global__ void __launch_bounds__(kRows, 2) attn_d32_tc_kernel(AttnProblem p, in
     const int valid = (int)min(max((int)end - (int)(j * kKeys), 0), kKeys);
     float mc = -INFINITY;
 #pragma unroll
-    for (int t = 0; t < 64; ++t)
+    for (int t = 0; t < kKeys; ++t)
       if (t < valid) mc = fmaxf(mc, __uint_as_float(sr[t]));
     if (mc > m + 8.0f) {  // also the first tile with a valid key (m = -inf)
       const float cr = ex2(m - mc);
@@ -294,7 +313,7 @@ __global__ void __launch_bounds__(kRows, 2) attn_d32_tc_kernel(AttnProblem p, in
     }
     // P as a TF32 pair: hi over S, lo beside it (32 keys at a time).
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < kChunks; ++h) {
       uint32_t ph[32], pl[32];
 #pragma unroll
       for (int t = 0; t < 32; ++t) {
@@ -377,17 +396,30 @@ bool d32_tc_supported(const AttnProblem &p) {
          (uintptr_t)p.out % 16 == 0 && p.scale > 0.f;
 }
 
-cudaError_t launch_attention_d32_tc(const AttnProblem &p, int *status, cudaStream_t stream) {
+namespace {
+template <int kKeys>
+cudaError_t launch_d32_tc(const AttnProblem &p, int *status, cudaStream_t stream, dim3 grid) {
+  constexpr uint32_t bytes = d32tc::Cfg<kKeys>::kSmemBytes;
+  cudaError_t e = cudaFuncSetAttribute(d32tc::attn_d32_tc_kernel<kKeys>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) return e;
+  d32tc::attn_d32_tc_kernel<kKeys><<<grid, d32tc::kRows, bytes, stream>>>(p, status);
+  return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_attention_d32_tc(const AttnProblem &p, int *status, cudaStream_t stream,
+                                    int num_sms) {
   if (!d32_tc_supported(p)) return cudaErrorInvalidValue;
   const uint32_t qblocks = (p.seq + d32tc::kRows - 1) / d32tc::kRows;
   if (!qblocks || qblocks > 65535u) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(d32tc::attn_d32_tc_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)d32tc::kSmemBytes);
-  if (e != cudaSuccess) return e;
   const dim3 grid(qblocks, p.heads, p.batch);
-  d32tc::attn_d32_tc_kernel<<<grid, d32tc::kRows, d32tc::kSmemBytes, stream>>>(p, status);
-  return cudaGetLastError();
+  // Within one wave at two CTAs per SM the CTA's own latency decides: 64-key tiles (BGE
+  // config 1: 14.9 us against 18.4); beyond, three CTAs per SM with 32-key tiles (batch
+  // 4096: 1.44 ms against 1.68).
+  const uint64_t ctas = (uint64_t)qblocks * p.heads * p.batch;
+  if (ctas <= 2ull * (uint64_t)num_sms) return launch_d32_tc<64>(p, status, stream, grid);
+  return launch_d32_tc<32>(p, status, stream, grid);
 }
 
 }  // namespace tx

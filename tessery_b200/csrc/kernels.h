@@ -29,10 +29,13 @@ cudaError_t launch_rope(float *x, uint32_t n, uint32_t heads, uint32_t seq, uint
                         float theta, cudaStream_t stream);
 // General attention: any dim <= 256, f32/bf16 in, f32/bf16 out, padded or varlen.
 cudaError_t launch_attention_simt(const AttnProblem &p, cudaStream_t stream);
-// head_dim 32, fp32 in and out: scores on tensor cores (TF32 split operands), the softmax
-// and P.V on the FP32 pipe (attn_d32_tc.cu).  `status`: the device status word.
+// head_dim 32, fp32 in and out: Q.K^T and P.V on tensor cores (TF32 split operands), the
+// softmax on the FP32 pipe (attn_d32_tc.cu); 64-key tiles while the grid fits one wave
+// at two CTAs per SM, 32-key tiles at three CTAs per SM beyond.  `status`: the device
+// status word.
 bool d32_tc_supported(const AttnProblem &p);
-cudaError_t launch_attention_d32_tc(const AttnProblem &p, int *status, cudaStream_t stream);
+cudaError_t launch_attention_d32_tc(const AttnProblem &p, int *status, cudaStream_t stream,
+                                    int num_sms);
 // head_dim 128, fp32 in and out: scores on tensor cores (TF32 split operands), the softmax
 // and P.V on the FP32 pipe (attn_f32_tc.cu).
 bool f32_tc_supported(const AttnProblem &p);

@@ -320,7 +320,7 @@ int run_attention(Ctx *c, tx::AttnProblem p, const uint32_t *lengths_host,
     c->last_kernel = "tc_bf16_d128";
     ++c->launches;
   } else if (d32tc_path) {
-    if ((e = tx::launch_attention_d32_tc(p, c->status, stream)) != cudaSuccess)
+    if ((e = tx::launch_attention_d32_tc(p, c->status, stream, c->sms)) != cudaSuccess)
       return cuda_fail(c, e, "attention launch");
     c->last_kernel = "d32_tc";
     ++c->launches;
