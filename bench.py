@@ -534,6 +534,8 @@ def run_ours(args):
     for _ in range(args.e2e_steps):
         result = e2e_step()
     e2e_s = time.perf_counter() - t0
+    # Bytes the library's copies moved in the last call (per step), both directions.
+    h2d, d2h = rt.host_copy_bytes()
     first = int(w.seq_lengths[0])
     check = result[0, :first] if w.layout == "padded" else result[:first]
     assert np.isfinite(check).all()
@@ -558,15 +560,6 @@ def run_ours(args):
     if dist:
         dist.all_reduce(pageable, op=dist.ReduceOp.MAX)
     pageable_value = e2e_tokens_all / float(pageable[0])
-    # Bytes that cross the link: in the padded layout the library copies only the valid
-    # k and v rows (the padded ones are never read).
-    kv_bytes = hk.nbytes + hv.nbytes
-    if w.layout == "padded":
-        kv_bytes = 2 * w.valid_tokens() * w.kv_heads * w.dim * hk.itemsize
-    h2d = hq.nbytes + kv_bytes + sum(
-        a.nbytes for a in [*hsel.values(), *[x for x in hpro.values()
-                                             if isinstance(x, np.ndarray)]])
-    d2h = result.nbytes
 
     roof, prologue_roof = rooflines(w, name, kernel, statistics.mean(att_ms) * 1e-3,
                                     statistics.mean(pro_ms) * 1e-3 if pro_ms else None,
@@ -1199,8 +1192,7 @@ def run_one_process(args):
         extra["pageable"] = pageable_step
 
         units, unit, metric = w.valid_tokens(), "tokens/s", metric_of(args.workload)
-        kv_rows = w.valid_tokens() if w.layout == "padded" else w.k.shape[0]
-        h2d = w.q.nbytes + 2 * kv_rows * w.kv_heads * w.dim * w.k.itemsize
+        h2d = 0  # counted by the library after the timed calls
         config = config_block(args.workload, w, n)
     else:
         raise SystemExit("--one-process takes qwen_padded, qwen_varlen, qwen_forward or "
@@ -1212,6 +1204,8 @@ def run_one_process(args):
         result = step()
     seconds = time.perf_counter() - t0
     value = units * args.e2e_steps / seconds
+    if model is None:  # attention: the bytes every device's copies moved in the last step
+        h2d = sum(rt_.host_copy_bytes()[0] for rt_ in group.runtimes)
     pageable = extra.pop("pageable", None)
     if pageable is not None:
         pageable()

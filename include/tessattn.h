@@ -212,8 +212,9 @@ int tx_attention_varlen(void *ctx, const void *q, const void *k, const void *v,
  * the dispatch (metal.py:532-569) and the read-back (metal.py:650-662) -- in one call.
  * The sequences are split into chunks of whole sequences; chunk i's rows are copied in
  * while chunk i-1 is computed and chunk i-2 copied out, so transfer in both directions
- * overlaps and the kernels hide behind it.  In the padded layout only the valid k and v
- * rows are copied (the rest are never attended).  Results equal the
+ * overlaps and the kernels hide behind it.  In the padded layout the valid k and v rows
+ * are copied, in spans that take short padding gaps between sequences along (fewer
+ * copies; padded rows are never attended).  Results equal the
  * device-pointer entry points' bit for bit.  Returns when the output is in `out` (kernel errors included); device
  * memory for the copies is kept by the context and grows to the largest call. */
 int tx_attention_padded_host(void *ctx, const void *q, const void *k, const void *v,
@@ -227,6 +228,13 @@ int tx_attention_varlen_host(void *ctx, const void *q, const void *k, const void
                              uint32_t heads, uint32_t kv_heads, uint32_t dim, int in_dtype,
                              int out_dtype, int causal, float scale, const uint16_t *q_norm_w,
                              const uint16_t *k_norm_w, float eps, float theta);
+
+/* Bytes the last host-buffer attention call of this context copied: out[0] host to
+ * device (q rows, the k/v spans, lengths or cu_seqlens, norm weights, work lists),
+ * out[1] device to host (the output rows).  No reference counterpart: the reference's
+ * uploads are whole Buffers (metal.py:94-119); this reports what the chunked copies of
+ * the two entry points above moved, for throughput accounting. */
+int tx_host_copy_bytes(void *ctx, uint64_t *out);
 
 /* Standalone fused q/k prologue (qwen3.py:216-237 as one pass): RMSNorm with bf16
  * weights then split-half RoPE, reading q/k in `in_dtype` and writing bf16 or f32

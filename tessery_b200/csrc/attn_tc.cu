@@ -41,7 +41,9 @@
 // head's products.  Because S_h of tile j+1 is committed after P_h.V of tile j, a
 // softmax warp that sees S_h full also knows that O_h holds every earlier tile.  Tiles
 // above the causal diagonal and beyond each sequence's length are never visited; the
-// diagonal and the last tile are masked per row.  The running maximum is updated
+// diagonal and the last tile are masked per row.  In a sequence's last key tile, P.V
+// runs only over the 16-key steps that hold keys before the end, and the V rows past the
+// end are set to zero on chip.  The running maximum is updated
 // lazily: O is rescaled only when a tile maximum exceeds the reference maximum by more
 // than 8 (log2 units), so every probability stays below 2^8 and the normalised result
 // is unchanged.
@@ -578,25 +580,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       issued = true;
     };
-    // O_h (+)= P_h V with P_h (bf16, 128 keys) in the first 64 columns of S_h.
-    auto pv_head = [&](uint32_t h, uint32_t slot, uint32_t acc) {
+    // O_h (+)= P_h V with P_h (bf16, 128 keys) in the first 64 columns of S_h, over the
+    // first `steps` 16-key steps of the tile (the steps past a sequence's end hold only
+    // zero probabilities and are not issued).
+    auto pv_head = [&](uint32_t h, uint32_t slot, uint32_t acc, uint32_t steps) {
       if (leader) {
         const uint64_t vd = mnmajor_desc(sbase + kOffKV + slot * kKVBytes, 0);
         const uint32_t pt = tmem + h * 256, d = tmem + h * 256 + 128;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          umma_ts(d, pt + ks * 8, vd + (uint64_t)(ks * (2048 >> 4)), kIdescPV,
-                  (acc || ks > 0) ? 1u : 0u);
+          if ((uint32_t)ks < steps)
+            umma_ts(d, pt + ks * 8, vd + (uint64_t)(ks * (2048 >> 4)), kIdescPV,
+                    (acc || ks > 0) ? 1u : 0u);
         umma_commit(bar(kBarPVDone + h));
       }
     };
-    // Rows [first, 128) of the V tile in ring slot `slot` set to zero: those keys lie at or
-    // past the sequence's end (padding, or the next packed sequence), their probabilities
-    // are zero, and zero times a non-finite value would not be.  Whole 128-byte rows of
-    // both 64-column atoms, so the swizzle does not matter.
-    auto clear_v_rows = [&](uint32_t slot, uint32_t first) {
+    // Rows [first, last) of the V tile in ring slot `slot` set to zero: those keys lie at
+    // or past the sequence's end (padding, or the next packed sequence), their
+    // probabilities are zero, and zero times a non-finite value would not be.  Whole
+    // 128-byte rows of both 64-column atoms, so the swizzle does not matter.  (Clearing
+    // only the rows inside the last 16-key step that P.V reads was measured: faster at
+    // the padded benchmark shape, slower at the packed one.)
+    auto clear_v_rows = [&](uint32_t slot, uint32_t first, uint32_t last) {
       const uint32_t base = sbase + kOffKV + slot * kKVBytes;
-      for (uint32_t i = first * 16 + lane; i < 128u * 16u; i += 32) {
+      for (uint32_t i = first * 16 + lane; i < last * 16; i += 32) {
         const uint32_t row = i >> 4, atom = (i >> 3) & 1u, c = i & 7u;
         st_shared_v4(base + atom * kKVAtom + row * 128 + c * 16, 0u, 0u, 0u, 0u);
       }
@@ -619,7 +626,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (uint32_t j = 0; ok && j < u.nt; ++j) {
         uint32_t slotV;
         if (!take(&slotV)) break;
-        if (u.n < (j + 1) * kKeys) clear_v_rows(slotV, u.n - j * kKeys);
+        // Keys of this tile before the sequence's end (a visited tile holds at least one),
+        // and the 16-key steps of P.V that cover them.
+        const uint32_t vkeys = min(u.n - j * kKeys, (uint32_t)kKeys);
+        const uint32_t vsteps = (vkeys + 15) / 16;
+        if (vkeys < (uint32_t)kKeys) clear_v_rows(slotV, vkeys, kKeys);
         const bool more = j + 1 < u.nt;
         for (uint32_t h = 0; h < nh && ok; ++h) {
           if (!(ok = wait_all(bar(kBarPFull + h), bit(pbits, h), kSitePFull))) break;
@@ -630,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             obits ^= 1u << h;
           }
           tc_fence_after();
-          pv_head(h, slotV, j > 0);
+          pv_head(h, slotV, j > 0, vsteps);
           if (more) {
             if (h == 0 && !take(&slotK)) break;
             qk_head(h, slotK);

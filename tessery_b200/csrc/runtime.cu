@@ -21,9 +21,15 @@
 
 namespace {
 
-constexpr uint32_t kAbiVersion = 9;
+constexpr uint32_t kAbiVersion = 10;
 constexpr uint32_t kHostChunks = 8;              // most chunks of a host-buffer call
 constexpr size_t kHostChunkBytes = 16u << 20;     // bytes moved per chunk, at least
+// Padded layout, host-buffer calls: the valid k/v rows of consecutive sequences are
+// copied as one span, padded rows between them included, while the padding between two
+// sequences is at most this many bytes (fewer copies against more bytes: at the Qwen
+// padded benchmark shape 256 KB measured best of 0, 256 KB and 1 MB, by ~3 %); the
+// padded rows copied are never attended.
+constexpr size_t kMergeGapBytes = 256u << 10;
 
 struct Ctx;
 
@@ -80,6 +86,7 @@ struct Ctx {
   cudaStream_t hp_up = nullptr, hp_down = nullptr;
   cudaEvent_t hp_ev[2 * kHostChunks] = {};
   std::vector<int32_t> hp_cu;  // per-chunk cu_seqlens, rebased to each chunk's first row
+  uint64_t hp_h2d = 0, hp_d2h = 0;  // bytes the last host-buffer call copied each way
 };
 
 std::mutex g_create_mu;
@@ -491,6 +498,9 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
   // Nothing of an earlier call may still read these buffers.
   if ((e = cudaStreamWaitEvent(c->hp_up, c->scratch_done, 0)) != cudaSuccess)
     return cuda_fail(c, e, "stream wait");
+  c->hp_h2d = meta + (q_w ? (size_t)p.dim * 2 : 0) + (k_w ? (size_t)p.dim * 2 : 0) +
+              wl_used * 4;
+  c->hp_d2h = 0;
   if (cu)
     e = cudaMemcpyAsync(dev + om, c->hp_cu.data(), meta, cudaMemcpyHostToDevice, c->hp_up);
   else
@@ -510,27 +520,38 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
   const uint16_t *dkw = k_w ? (const uint16_t *)(dev + ow + up256((size_t)p.dim * 2)) : nullptr;
   for (uint32_t i = 0; i < nch; ++i) {
     const size_t r0 = row_of(first[i]), r1 = row_of(first[i + 1]), n = r1 - r0;
-    // k and v rows of the chunk.  Padded layout: only each sequence's valid rows cross the
-    // link (a run of full sequences in one copy); its rows at or past the length are never
-    // attended, and every kernel either skips them or clears them on chip, so the device
-    // rows there may hold whatever an earlier call left.
+    // k and v rows of the chunk.  Padded layout: each sequence's valid rows cross the
+    // link, in spans over consecutive sequences that take the padded rows between them
+    // along while a gap is at most kMergeGapBytes (fewer, larger copies); rows at or past
+    // a length are never attended, and every kernel either skips them or clears them on
+    // chip, so the device rows there may hold anything (an earlier call's rows, or the
+    // caller's padding copied along).
     auto copy_kv = [&](size_t region, const uint8_t *h) -> cudaError_t {
-      if (cu)
+      if (cu) {
+        c->hp_h2d += n * kvrow;
         return cudaMemcpyAsync(dev + region + r0 * kvrow, h + r0 * kvrow, n * kvrow,
                                cudaMemcpyHostToDevice, c->hp_up);
+      }
       cudaError_t err = cudaSuccess;
       for (uint32_t b = first[i]; b < first[i + 1] && err == cudaSuccess;) {
         const size_t s0 = (size_t)b * p.seq;
-        uint32_t b1 = b;  // sequences b .. b1 are full except possibly b1
-        while (b1 + 1 < first[i + 1] && lengths[b1] == p.seq) ++b1;
-        const size_t nv = (size_t)(b1 - b) * p.seq + lengths[b1];
-        if (nv)
-          err = cudaMemcpyAsync(dev + region + s0 * kvrow, h + s0 * kvrow, nv * kvrow,
+        size_t end = s0 + std::min(lengths[b], p.seq);  // rows [s0, end) are copied
+        uint32_t b1 = b;
+        while (b1 + 1 < first[i + 1] &&
+               ((size_t)(b1 + 1) * p.seq - end) * kvrow <= kMergeGapBytes) {
+          ++b1;
+          end = (size_t)b1 * p.seq + std::min(lengths[b1], p.seq);
+        }
+        if (end > s0) {
+          c->hp_h2d += (end - s0) * kvrow;
+          err = cudaMemcpyAsync(dev + region + s0 * kvrow, h + s0 * kvrow, (end - s0) * kvrow,
                                 cudaMemcpyHostToDevice, c->hp_up);
+        }
         b = b1 + 1;
       }
       return err;
     };
+    c->hp_h2d += n * qrow;
     if ((e = cudaMemcpyAsync(dev + oq + r0 * qrow, hq + r0 * qrow, n * qrow,
                              cudaMemcpyHostToDevice, c->hp_up)) != cudaSuccess ||
         (e = copy_kv(ok, hk)) != cudaSuccess || (e = copy_kv(ov, hv)) != cudaSuccess ||
@@ -556,6 +577,7 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
       drain();
       return cuda_fail(c, e, "copy out");
     }
+    c->hp_d2h += n * orow;
   }
   // The next call's copies in wait for this one's kernels and copies out.
   if ((e = cudaEventRecord(c->scratch_done, c->hp_down)) != cudaSuccess) {
@@ -751,6 +773,15 @@ int tx_memory_stats(void *ctx, uint64_t *out) {
   out[1] = c->mem_peak;
   out[2] = c->mem_allocs;
   out[3] = c->mem_alloc_bytes;
+  return TX_OK;
+}
+
+int tx_host_copy_bytes(void *ctx, uint64_t *out) {
+  Ctx *c = (Ctx *)ctx;
+  if (!c || !out) return TX_EINVAL;
+  std::lock_guard<std::recursive_mutex> g(c->mu);
+  out[0] = c->hp_h2d;
+  out[1] = c->hp_d2h;
   return TX_OK;
 }
 

@@ -16,7 +16,7 @@ from typing import Any
 
 from .errors import NativeBuildError
 
-ABI_VERSION = 9
+ABI_VERSION = 10
 LIBRARY_NAME = "libtessattn.so"
 
 TX_OK, TX_EINVAL, TX_ECUDA, TX_ETIMEOUT = 0, 1, 2, 3
@@ -79,6 +79,7 @@ SIGNATURES: dict[str, tuple[list[Any], Any]] = {
     "tx_buffer": ([_vp, _vp, _u64], _vp),
     "tx_free": ([_vp], None),
     "tx_memory_stats": ([_vp, ct.POINTER(_u64)], _i32),
+    "tx_host_copy_bytes": ([_vp, ct.POINTER(_u64)], _i32),
     "tx_read": ([_vp, _vp, _u64], _i32),
     "tx_write": ([_vp, _vp, _u64], _i32),
     "tx_buffer_device_ptr": ([_vp], _vp),

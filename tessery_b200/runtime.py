@@ -169,6 +169,14 @@ class CudaRuntime:
         _raise_for(self._lib.tx_kernel_times(self._pointer, seconds, 8, ct.byref(count)))
         return [float(seconds[i]) for i in range(count.value)]
 
+    def host_copy_bytes(self) -> tuple[int, int]:
+        """(host-to-device, device-to-host) bytes the last host-buffer attention call
+        copied (tx_host_copy_bytes)."""
+        self._check_open()
+        out = (ct.c_uint64 * 2)()
+        _raise_for(self._lib.tx_host_copy_bytes(self._pointer, out))
+        return int(out[0]), int(out[1])
+
     def set_wait_limit(self, cycles: int) -> None:
         """Limit, in SM clock cycles, of each bounded wait of the tensor-core kernel
         (0 restores the default, about a second).  A wait that runs out is reported as

@@ -641,6 +641,26 @@ def test_host_buffer_entry_points_match_device_path(runtime):
         assert np.array_equal(hout, want), w.layout
 
 
+def test_host_buffer_copies_padding_spans_and_counts_bytes(runtime):
+    """The padded host-buffer call copies each chunk's valid k/v rows in spans that take
+    short padding gaps along; the caller's padded rows (NaN k, Inf v here) then reach the
+    device and are still never attended: every row equals the device call on clean
+    padding bit for bit.  tx_host_copy_bytes reports what crossed the link: at least the
+    q rows and the valid k/v rows, at most the whole arrays, and the output rows back."""
+    w = workloads.qwen_padded(batch=16, seq=512, seed=31)
+    want = _device_path(runtime, w)
+    k = _poison_padding(w.k, w.lengths, np.uint16(0x7FC0))  # bf16 NaN
+    v = _poison_padding(w.v, w.lengths, np.uint16(0x7F80))  # bf16 +Inf
+    got = attention(w.q, k, v, lengths=w.lengths, causal=w.causal, scale=w.scale,
+                    q_norm_weight=w.q_norm_weight, k_norm_weight=w.k_norm_weight, eps=w.eps,
+                    theta=w.theta, runtime=runtime)
+    assert np.array_equal(got, want)
+    h2d, d2h = runtime.host_copy_bytes()
+    valid_kv = 2 * int(np.sum(w.lengths)) * w.kv_heads * w.dim * 2
+    assert w.q.nbytes + valid_kv <= h2d <= w.q.nbytes + k.nbytes + v.nbytes + (1 << 20)
+    assert d2h == got.nbytes
+
+
 def test_composed_prologue_matches_one_call(runtime):
     """k-only prologue over the valid rows (tx_qk_norm_rope with device lengths), then
     attention with only the q weight, against the one-call path.  The one call knows both
