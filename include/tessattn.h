@@ -206,8 +206,9 @@ int tx_attention_varlen(void *ctx, const void *q, const void *k, const void *v,
                         const uint16_t *k_norm_w, float eps, float theta, void *stream);
 
 /* Host-buffer forms of the two entry points above: q, k, v, out, lengths / cu_seqlens and
- * the norm weights are HOST pointers (page-locked memory, e.g. from tx_host_alloc, lets the
- * copies overlap; pageable memory works too).  They stand in for the reference's
+ * the norm weights are HOST pointers (page-locked memory, e.g. from tx_host_alloc, is
+ * copied directly; pageable q/k/v/out go through page-locked staging the context keeps,
+ * copied by a few host threads chunk by chunk beside the transfers).  They stand in for the reference's
  * host-side sequence around one attention dispatch -- Buffer uploads (metal.py:94-119),
  * the dispatch (metal.py:532-569) and the read-back (metal.py:650-662) -- in one call.
  * The sequences are split into chunks of whole sequences; chunk i's rows are copied in

@@ -17,6 +17,7 @@ from numpy.typing import NDArray
 
 from . import native
 from .errors import InvalidInputError
+from .host import result_empty
 from .runtime import CudaRuntime, _raise_for
 
 _default: CudaRuntime | None = None
@@ -72,7 +73,9 @@ def attention(
     RMSNorm'd and rotated (RoPE, positions = padded index or index within the sequence)
     first.
     Returns float32 (or uint16 bf16 bits when out_dtype == "bf16") in q's layout,
-    written into `out` when given (e.g. a page-locked array from host.pinned_empty).
+    written into `out` when given (e.g. a page-locked array from host.pinned_empty), else
+    into a new array (page-locked memory recycled from dropped results, host.result_empty).
+    Pageable inputs are copied through the library's page-locked staging.
     """
     rt = runtime or default_runtime()
     q, k, v = (np.ascontiguousarray(a) for a in (q, k, v))
@@ -115,11 +118,12 @@ def attention(
             raise InvalidInputError()
         sel["cu_seqlens"] = cu
     if out is None:
-        out = np.empty(q.shape, dtype=out_np_dtype)
+        out = result_empty(q.shape, out_np_dtype)
     elif out.shape != q.shape or out.dtype != out_np_dtype or not out.flags.c_contiguous:
         raise InvalidInputError()
     # Host arrays straight into the host-buffer entry point: the library moves the
-    # sequences through in chunks whose copies in, kernels and copies out overlap.
+    # sequences through in chunks whose copies in, kernels and copies out overlap
+    # (pageable arrays through its page-locked staging).
     rt.attention_host(q, k, v, out, in_dtype=code, out_dtype=out_code, causal=causal,
                       scale=scale, q_norm_weight=qw, k_norm_weight=kw, eps=eps, theta=theta,
                       **sel)

@@ -9,11 +9,14 @@
 
 #include <algorithm>
 #include <cmath>
+#include <condition_variable>
 #include <cstdio>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <set>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/tessattn.h"
@@ -32,6 +35,84 @@ constexpr size_t kHostChunkBytes = 16u << 20;     // bytes moved per chunk, at l
 constexpr size_t kMergeGapBytes = 256u << 10;
 
 struct Ctx;
+
+// Host memcpy over a few worker threads and the calling thread, for the staging of
+// pageable host arrays through page-locked memory (one thread copies ~15 GB/s on the
+// B200 hosts measured; four reach the ~50 GB/s the host gives).  copy() hands out 1 MB
+// pieces of its segments and returns once every piece has been copied.
+class CopyPool {
+ public:
+  struct Seg {
+    uint8_t *dst;
+    const uint8_t *src;
+    size_t bytes;
+  };
+  explicit CopyPool(unsigned workers) {
+    for (unsigned i = 0; i < workers; ++i) threads_.emplace_back([this] { loop(); });
+  }
+  ~CopyPool() {
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      stop_ = true;
+    }
+    wake_.notify_all();
+    for (std::thread &t : threads_) t.join();
+  }
+  void copy(const std::vector<Seg> &segs) {
+    std::vector<Seg> pieces;
+    for (const Seg &sg : segs)
+      for (size_t o = 0; o < sg.bytes; o += kPiece)
+        pieces.push_back({sg.dst + o, sg.src + o, std::min(kPiece, sg.bytes - o)});
+    if (pieces.empty()) return;
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      jobs_ = &pieces;
+      next_ = 0;
+      left_ = pieces.size();
+      ++gen_;
+    }
+    wake_.notify_all();
+    work();
+    std::unique_lock<std::mutex> lk(mu_);
+    done_.wait(lk, [&] { return left_ == 0; });
+    jobs_ = nullptr;
+  }
+
+ private:
+  static constexpr size_t kPiece = 1u << 20;
+  void work() {
+    for (;;) {
+      Seg sg;
+      {
+        std::lock_guard<std::mutex> g(mu_);
+        if (!jobs_ || next_ >= jobs_->size()) return;
+        sg = (*jobs_)[next_++];
+      }
+      std::memcpy(sg.dst, sg.src, sg.bytes);
+      std::lock_guard<std::mutex> g(mu_);
+      if (--left_ == 0) done_.notify_all();
+    }
+  }
+  void loop() {
+    uint64_t seen = 0;
+    for (;;) {
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        wake_.wait(lk, [&] { return stop_ || gen_ != seen; });
+        if (stop_) return;
+        seen = gen_;
+      }
+      work();
+    }
+  }
+  std::vector<std::thread> threads_;
+  std::mutex mu_;
+  std::condition_variable wake_, done_;
+  const std::vector<Seg> *jobs_ = nullptr;
+  size_t next_ = 0, left_ = 0;
+  uint64_t gen_ = 0;
+  bool stop_ = false;
+};
 
 struct Buf {
   Ctx *ctx;
@@ -87,6 +168,12 @@ struct Ctx {
   cudaEvent_t hp_ev[2 * kHostChunks] = {};
   std::vector<int32_t> hp_cu;  // per-chunk cu_seqlens, rebased to each chunk's first row
   uint64_t hp_h2d = 0, hp_d2h = 0;  // bytes the last host-buffer call copied each way
+  // pageable host arrays: page-locked staging (the device copies' layout), the copy
+  // threads, and per chunk an event after its copy out
+  uint8_t *st_mem = nullptr;
+  size_t st_bytes = 0;
+  std::unique_ptr<CopyPool> st_pool;
+  cudaEvent_t hp_out_ev[kHostChunks] = {};
 };
 
 std::mutex g_create_mu;
@@ -465,6 +552,9 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
     for (cudaEvent_t &ev : c->hp_ev)
       if ((e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess)
         return cuda_fail(c, e, "copy events");
+    for (cudaEvent_t &ev : c->hp_out_ev)
+      if ((e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess)
+        return cuda_fail(c, e, "copy events");
   }
   uint8_t *dev = (uint8_t *)c->hp_mem;
   // Work lists of the chunks that take the tensor-core kernel, built here and uploaded in
@@ -487,8 +577,40 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
                                  c->units_host.data(), c->hp_units + wl_used);
     wl_used += tx::tc_work_words(pc, c->sms);
   }
+  // Pageable host arrays go through page-locked staging laid out like the device copies
+  // (a DMA from pageable memory is staged by the driver a piece at a time at a fraction
+  // of the link's speed): chunk i's input rows are copied into the staging by the copy
+  // threads before its copies in are queued, and its output rows out of it once its copy
+  // out has landed, while the device works on the neighbouring chunks.
+  auto pageable = [](const void *ptr) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+      cudaGetLastError();
+      return true;
+    }
+    return a.type == cudaMemoryTypeUnregistered;
+  };
+  const bool sq = pageable(p.q), sk = pageable(p.k), sv = pageable(p.v), so = pageable(p.out);
+  if (sq || sk || sv || so) {
+    if (c->st_bytes < om) {  // every earlier call has drained: nothing reads it
+      if (c->st_mem) cudaFreeHost(c->st_mem);
+      c->st_mem = nullptr;
+      c->st_bytes = 0;
+      if ((e = cudaHostAlloc((void **)&c->st_mem, om, cudaHostAllocDefault)) != cudaSuccess)
+        return cuda_fail(c, e, "page-locked staging");
+      c->st_bytes = om;
+    }
+    if (!c->st_pool) {
+      const unsigned hw = std::thread::hardware_concurrency();
+      c->st_pool.reset(new CopyPool(std::max(1u, std::min(4u, hw / 2))));
+    }
+  }
+  uint8_t *st = c->st_mem;
   const uint8_t *hq = (const uint8_t *)p.q, *hk = (const uint8_t *)p.k, *hv = (const uint8_t *)p.v;
   uint8_t *ho = (uint8_t *)p.out;
+  // Sources of the copies in and destination of the copies out.
+  const uint8_t *cq = sq ? st + oq : hq, *ck = sk ? st + ok : hk, *cv = sv ? st + ov : hv;
+  uint8_t *co = so ? st + oo : ho;
   // Drains every stream of this call (no copy may touch the caller's memory after return).
   auto drain = [&]() {
     cudaStreamSynchronize(c->hp_up);
@@ -518,43 +640,65 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
   }
   const uint16_t *dqw = q_w ? (const uint16_t *)(dev + ow) : nullptr;
   const uint16_t *dkw = k_w ? (const uint16_t *)(dev + ow + up256((size_t)p.dim * 2)) : nullptr;
+  // k and v rows of chunk i as (first byte, bytes) spans of the k (or v) array.  Padded
+  // layout: each sequence's valid rows cross the link, in spans over consecutive sequences
+  // that take the padded rows between them along while a gap is at most kMergeGapBytes
+  // (fewer, larger copies); rows at or past a length are never attended, and every kernel
+  // either skips them or clears them on chip, so the device rows there may hold anything
+  // (an earlier call's rows, or the caller's padding copied along).
+  std::vector<std::pair<size_t, size_t>> kv_spans;
+  auto spans_of = [&](uint32_t i) {
+    kv_spans.clear();
+    const size_t r0 = row_of(first[i]), r1 = row_of(first[i + 1]);
+    if (cu) {
+      kv_spans.push_back({r0 * kvrow, (r1 - r0) * kvrow});
+      return;
+    }
+    for (uint32_t b = first[i]; b < first[i + 1];) {
+      const size_t s0 = (size_t)b * p.seq;
+      size_t end = s0 + std::min(lengths[b], p.seq);  // rows [s0, end) are copied
+      uint32_t b1 = b;
+      while (b1 + 1 < first[i + 1] &&
+             ((size_t)(b1 + 1) * p.seq - end) * kvrow <= kMergeGapBytes) {
+        ++b1;
+        end = (size_t)b1 * p.seq + std::min(lengths[b1], p.seq);
+      }
+      if (end > s0) kv_spans.push_back({s0 * kvrow, (end - s0) * kvrow});
+      b = b1 + 1;
+    }
+  };
+  // Output rows of chunk j from the staging into the caller's array, once they landed.
+  auto unstage_out = [&](uint32_t j) -> cudaError_t {
+    const size_t r0 = row_of(first[j]), n = row_of(first[j + 1]) - r0;
+    const cudaError_t err = cudaEventSynchronize(c->hp_out_ev[j]);
+    if (err == cudaSuccess) c->st_pool->copy({{ho + r0 * orow, co + r0 * orow, n * orow}});
+    return err;
+  };
   for (uint32_t i = 0; i < nch; ++i) {
     const size_t r0 = row_of(first[i]), r1 = row_of(first[i + 1]), n = r1 - r0;
-    // k and v rows of the chunk.  Padded layout: each sequence's valid rows cross the
-    // link, in spans over consecutive sequences that take the padded rows between them
-    // along while a gap is at most kMergeGapBytes (fewer, larger copies); rows at or past
-    // a length are never attended, and every kernel either skips them or clears them on
-    // chip, so the device rows there may hold anything (an earlier call's rows, or the
-    // caller's padding copied along).
-    auto copy_kv = [&](size_t region, const uint8_t *h) -> cudaError_t {
-      if (cu) {
-        c->hp_h2d += n * kvrow;
-        return cudaMemcpyAsync(dev + region + r0 * kvrow, h + r0 * kvrow, n * kvrow,
-                               cudaMemcpyHostToDevice, c->hp_up);
+    spans_of(i);
+    if (sq || sk || sv) {
+      std::vector<CopyPool::Seg> segs;
+      if (sq) segs.push_back({st + oq + r0 * qrow, hq + r0 * qrow, n * qrow});
+      for (const auto &sp : kv_spans) {
+        if (sk) segs.push_back({st + ok + sp.first, hk + sp.first, sp.second});
+        if (sv) segs.push_back({st + ov + sp.first, hv + sp.first, sp.second});
       }
-      cudaError_t err = cudaSuccess;
-      for (uint32_t b = first[i]; b < first[i + 1] && err == cudaSuccess;) {
-        const size_t s0 = (size_t)b * p.seq;
-        size_t end = s0 + std::min(lengths[b], p.seq);  // rows [s0, end) are copied
-        uint32_t b1 = b;
-        while (b1 + 1 < first[i + 1] &&
-               ((size_t)(b1 + 1) * p.seq - end) * kvrow <= kMergeGapBytes) {
-          ++b1;
-          end = (size_t)b1 * p.seq + std::min(lengths[b1], p.seq);
-        }
-        if (end > s0) {
-          c->hp_h2d += (end - s0) * kvrow;
-          err = cudaMemcpyAsync(dev + region + s0 * kvrow, h + s0 * kvrow, (end - s0) * kvrow,
-                                cudaMemcpyHostToDevice, c->hp_up);
-        }
-        b = b1 + 1;
-      }
-      return err;
-    };
+      c->st_pool->copy(segs);
+    }
     c->hp_h2d += n * qrow;
-    if ((e = cudaMemcpyAsync(dev + oq + r0 * qrow, hq + r0 * qrow, n * qrow,
-                             cudaMemcpyHostToDevice, c->hp_up)) != cudaSuccess ||
-        (e = copy_kv(ok, hk)) != cudaSuccess || (e = copy_kv(ov, hv)) != cudaSuccess ||
+    e = cudaMemcpyAsync(dev + oq + r0 * qrow, cq + r0 * qrow, n * qrow, cudaMemcpyHostToDevice,
+                        c->hp_up);
+    for (const auto &sp : kv_spans) {
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(dev + ok + sp.first, ck + sp.first, sp.second,
+                            cudaMemcpyHostToDevice, c->hp_up);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(dev + ov + sp.first, cv + sp.first, sp.second,
+                            cudaMemcpyHostToDevice, c->hp_up);
+      c->hp_h2d += 2 * sp.second;
+    }
+    if (e != cudaSuccess ||
         (e = cudaEventRecord(c->hp_ev[2 * i], c->hp_up)) != cudaSuccess ||
         (e = cudaStreamWaitEvent(c->stream, c->hp_ev[2 * i], 0)) != cudaSuccess) {
       drain();
@@ -572,12 +716,18 @@ int run_attention_host(Ctx *c, tx::AttnProblem p, const uint32_t *lengths, const
     }
     if ((e = cudaEventRecord(c->hp_ev[2 * i + 1], c->stream)) != cudaSuccess ||
         (e = cudaStreamWaitEvent(c->hp_down, c->hp_ev[2 * i + 1], 0)) != cudaSuccess ||
-        (e = cudaMemcpyAsync(ho + r0 * orow, dev + oo + r0 * orow, n * orow,
-                             cudaMemcpyDeviceToHost, c->hp_down)) != cudaSuccess) {
+        (e = cudaMemcpyAsync(co + r0 * orow, dev + oo + r0 * orow, n * orow,
+                             cudaMemcpyDeviceToHost, c->hp_down)) != cudaSuccess ||
+        (e = cudaEventRecord(c->hp_out_ev[i], c->hp_down)) != cudaSuccess ||
+        (so && i > 0 && (e = unstage_out(i - 1)) != cudaSuccess)) {
       drain();
       return cuda_fail(c, e, "copy out");
     }
     c->hp_d2h += n * orow;
+  }
+  if (so && (e = unstage_out(nch - 1)) != cudaSuccess) {
+    drain();
+    return cuda_fail(c, e, "copy out");
   }
   // The next call's copies in wait for this one's kernels and copies out.
   if ((e = cudaEventRecord(c->scratch_done, c->hp_down)) != cudaSuccess) {
@@ -689,6 +839,10 @@ void tx_destroy(void *ctx) {
     if (c->hp_units) cudaFreeHost(c->hp_units);
     for (cudaEvent_t ev : c->hp_ev)
       if (ev) cudaEventDestroy(ev);
+    for (cudaEvent_t ev : c->hp_out_ev)
+      if (ev) cudaEventDestroy(ev);
+    if (c->st_mem) cudaFreeHost(c->st_mem);
+    c->st_pool.reset();
     if (c->hp_up) cudaStreamDestroy(c->hp_up);
     if (c->hp_down) cudaStreamDestroy(c->hp_down);
     if (c->stream) cudaStreamDestroy(c->stream);
