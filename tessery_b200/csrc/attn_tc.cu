@@ -21,8 +21,9 @@
 //               memory, as soon as they land; warpgroup h takes rows 64h..64h+63 of both
 //               heads, two lanes per row)
 //   warp 16     TMA producer: Q tiles of the unit two ahead (into the buffer whose last
-//               Q.K^T has run), K and V tiles of 128 keys through a 2-slot ring, and L2
-//               prefetches of the next units' tiles
+//               Q.K^T has run) and K and V tiles of 128 keys through a 2-slot ring; no L2
+//               prefetches (prefetching the next unit's tiles competed with the loads on
+//               the critical path: 3-9 % slower, measured)
 //   warp 17     TMEM allocator and single-thread tcgen05.mma issuer
 // Tensor memory (512 columns x 128 lanes, fp32), per head slot h at column 256h:
 //   [0,128) S_h, [128,256) O_h.
@@ -450,7 +451,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kTmaWarp) {
     // ---------------- TMA producer ----------------
-    // Q tiles of the first two work units, then per work unit k: its K/V tiles in the
+    // Q tiles of the first work unit, its first K tile, then the second unit's Q tiles
+    // (so that the first unit's tiles, which everything waits for at the start, do not
+    // share the memory system with them); then per work unit k: its K/V tiles in the
     // order the issuer consumes them (K_0, then V_j, K_{j+1} for j = 0..), and the Q tiles
     // of work unit k+2 into buffer k%2 once the last Q.K^T of unit k has run.
     if (lane == 0) {
@@ -484,23 +487,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         armed ^= 1u << (16 + b);
         armed |= 1u << (18 + b);
       };
-      // L2 prefetch of a unit's Q tiles (and, with kv, of its K/V tiles).
-      auto prefetch_unit = [&](uint32_t ui, bool kv) {
-        const Unit v = decode(p, p.units[ui]);
-        for (uint32_t h = 0; h < nh; ++h)
-          for (int a = 0; a < 2; ++a)
-            tma_prefetch_3d(&tm_q, a * 64, (int)(v.head0 + h), (int)(v.tok0 + v.q0));
-        if (kv)
-          for (uint32_t j = 0; j < v.nt; ++j)
-            for (int a = 0; a < 2; ++a) {
-              tma_prefetch_3d(&tm_k, a * 64, (int)v.kvh, (int)(v.tok0 + j * kKeys));
-              tma_prefetch_3d(&tm_v, a * 64, (int)v.kvh, (int)(v.tok0 + j * kKeys));
-            }
-      };
       uint32_t cur = next_work(p, p.offsets[blockIdx.x]);
       uint32_t nxt = cur < p.n_units ? next_work(p, cur + 1) : p.n_units;
       if (cur < p.n_units) load_q(cur, 0);
-      if (nxt < p.n_units) load_q(nxt, 1);
       // K may be written by the kernel launched just before this one (the k prologue):
       // with a programmatic dependent launch this grid starts while that one drains, so
       // wait for it before the first K load.  Q, V, the lengths and the work list were in
@@ -509,9 +498,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (uint32_t k = 0; ok && cur < p.n_units; ++k) {
         const Unit u = decode(p, p.units[cur]);
         const uint32_t ahead = nxt < p.n_units ? next_work(p, nxt + 1) : p.n_units;
-        if (ahead < p.n_units) prefetch_unit(ahead, false);
-        if (nxt < p.n_units) prefetch_unit(nxt, true);
         load_kv(&tm_k, u, 0);
+        if (k == 0 && nxt < p.n_units) load_q(nxt, 1);
         for (uint32_t j = 0; ok && j < u.nt; ++j) {
           load_kv(&tm_v, u, j);
           if (ok && j + 1 < u.nt) load_kv(&tm_k, u, j + 1);
