@@ -45,7 +45,7 @@
 // above the causal diagonal and beyond each sequence's length are never visited; the
 // diagonal and the last tile are masked per row.  In a sequence's last key tile, P.V
 // runs only over the 16-key steps that hold keys before the end, and the V rows past the
-// end are set to zero on chip.  The running maximum is updated
+// end inside the last such step are set to zero on chip.  The running maximum is updated
 // lazily: O is rescaled only when a tile maximum exceeds the reference maximum by more
 // than 8 (log2 units), so every probability stays below 2^8 and the normalised result
 // is unchanged.
@@ -591,12 +591,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(bar(kBarPVDone + h));
       }
     };
-    // Rows [first, last) of the V tile in ring slot `slot` set to zero: those keys lie at
-    // or past the sequence's end (padding, or the next packed sequence), their
-    // probabilities are zero, and zero times a non-finite value would not be.  Whole
-    // 128-byte rows of both 64-column atoms, so the swizzle does not matter.  (Clearing
-    // only the rows inside the last 16-key step that P.V reads was measured: faster at
-    // the padded benchmark shape, slower at the packed one.)
+    // Rows [first, last) of the V tile in ring slot `slot` set to zero (at most 15 rows:
+    // the rest of the last 16-key step that P.V reads): those keys lie at or past the
+    // sequence's end (padding, or the next packed sequence), their probabilities are zero,
+    // and zero times a non-finite value would not be.  Whole 128-byte rows of both
+    // 64-column atoms, so the swizzle does not matter.
     auto clear_v_rows = [&](uint32_t slot, uint32_t first, uint32_t last) {
       const uint32_t base = sbase + kOffKV + slot * kKVBytes;
       for (uint32_t i = first * 16 + lane; i < last * 16; i += 32) {
@@ -626,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // and the 16-key steps of P.V that cover them.
         const uint32_t vkeys = min(u.n - j * kKeys, (uint32_t)kKeys);
         const uint32_t vsteps = (vkeys + 15) / 16;
-        if (vkeys < (uint32_t)kKeys) clear_v_rows(slotV, vkeys, kKeys);
+        if (vkeys < vsteps * 16) clear_v_rows(slotV, vkeys, vsteps * 16);
         const bool more = j + 1 < u.nt;
         for (uint32_t h = 0; h < nh && ok; ++h) {
           if (!(ok = wait_all(bar(kBarPFull + h), bit(pbits, h), kSitePFull))) break;
