@@ -1030,8 +1030,10 @@ uint32_t unit_tiles(const AttnProblem &p, const uint32_t *lengths_host, const in
   return std::min((kend + tc::kKeys - 1) / tc::kKeys, 511u);
 }
 
-// Relative cost of a unit for the load balance: about 9k cycles per key tile and 4.5k
-// per unit (loading and transforming its Q tiles, the epilogue), measured on B200.
+// Relative cost of a unit for the load balance.  Traced on B200 at the padded Qwen
+// benchmark shape, a unit's time on the softmax warps is ~8k / 16k / 27k / 38k cycles for
+// 1 / 2 / 3 / 4 key tiles; costs closer to that (tiles, 5 tiles - 1) and with a larger
+// fixed part (tiles + 2, tiles + 3, 2 tiles + 3) balanced no better than this one.
 uint32_t unit_cost(uint32_t tiles) { return 2 * tiles + 1; }
 
 // Min-heap of (load << 16 | cta) keys over the CTAs (grid <= 65535).
