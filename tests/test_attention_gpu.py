@@ -661,6 +661,31 @@ def test_host_buffer_copies_padding_spans_and_counts_bytes(runtime):
     assert d2h == got.nbytes
 
 
+def test_host_buffer_mixed_pageable_and_page_locked_arrays(runtime):
+    """Each host array is staged through page-locked memory only when it is pageable:
+    page-locked inputs with a pageable `out`, pageable inputs with a page-locked `out`,
+    and everything pageable all give the device call's rows bit for bit (the output
+    rows of a pageable `out` are copied out of the staging chunk by chunk)."""
+    from tessery_b200.host import pinned_copy, pinned_empty
+
+    padded = workloads.qwen_padded(batch=12, seq=512, seed=33)
+    packed = workloads.qwen_varlen(seed=34, lengths=workloads.varlen_lengths(48, 34))
+    for w in (padded, packed):
+        want = _device_path(runtime, w)
+        sel = ({"lengths": w.lengths.astype(np.uint32)} if w.layout == "padded"
+               else {"cu_seqlens": w.cu_seqlens.astype(np.int32)})
+        kw = dict(causal=w.causal, scale=w.scale, q_norm_weight=w.q_norm_weight,
+                  k_norm_weight=w.k_norm_weight, eps=w.eps, theta=w.theta, runtime=runtime,
+                  **sel)
+        pinned_in = [pinned_copy(a) for a in (w.q, w.k, w.v)]
+        for inputs, out in ((pinned_in, np.empty(w.q.shape, np.float32)),
+                            ((w.q, w.k, w.v), pinned_empty(w.q.shape, np.float32)),
+                            ((w.q, w.k, w.v), np.empty(w.q.shape, np.float32))):
+            out[...] = np.nan
+            attention(*inputs, out=out, **kw)
+            assert np.array_equal(out, want), w.layout
+
+
 def test_composed_prologue_matches_one_call(runtime):
     """k-only prologue over the valid rows (tx_qk_norm_rope with device lengths), then
     attention with only the q weight, against the one-call path.  The one call knows both
